@@ -1,0 +1,612 @@
+// Device-resident flow-matching head: velocity MLP integrated with Euler /
+// Heun / RK4 (reference: src/core/heads/flow/flow.cc:64-323).
+//
+//   h = SiLU(W_in x + W_t [sin(t f) | cos(t f)] + c_emb),  c_emb = W_c cond
+//   h = SiLU(W_l h)  (mlp_layers times),  v = W_out h        (no biases)
+//
+// Rows of a batch are independent samples sharing the weights.  One ODE step
+// (1, 2 or 4 velocity evaluations) is captured as a CUDA graph per (batch,
+// method, path); the step index lives in device memory and is advanced by the
+// graph itself, so a resumable solve replays the same graph.  Small batches
+// use the weight-streaming CUDA-core GEMV (fp32 or bf16 weights); batches of
+// 128+ rows in bf16 mode use the tcgen05 GEMM with SiLU / time / condition
+// terms in its epilogue.
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+#include <map>
+#include <tuple>
+
+#include "runtime.cuh"
+#include "simt.cuh"
+
+namespace feb {
+namespace {
+
+constexpr int kTcMinRows = 128;
+
+std::uint16_t to_bf16(float v) {
+  std::uint32_t u;
+  std::memcpy(&u, &v, 4);
+  if ((u & 0x7FFFFFFFu) > 0x7F800000u) return 0x7FC0;
+  u += 0x7FFFu + ((u >> 16) & 1u);
+  return static_cast<std::uint16_t>(u >> 16);
+}
+
+struct Mat {
+  int rows = 0, rows_pad = 0, cols = 0, cols_pad = 0;
+  void* w = nullptr;  // [rows_pad][cols_pad]
+  SimtSlice* slices = nullptr;
+  int nslices = 0;
+};
+
+// t of velocity evaluation `stage` within step `step` (flow.cc:275-300)
+__device__ __forceinline__ float stage_time(int step, int steps, int method, int stage) {
+  const float dt = 1.0f / static_cast<float>(steps);
+  const float t = static_cast<float>(step) * dt;
+  if (method == 1) return stage == 0 ? t : t + dt;
+  if (method == 2) {
+    const float half = 0.5f * dt;
+    return stage == 0 ? t : (stage == 3 ? t + dt : t + half);
+  }
+  return t;
+}
+
+// tp[h] = sum_j Wt[h][j] * [sin(t f) | cos(t f)]_j
+__global__ void time_proj_kernel(const int* step_idx, int steps, int method, int stage, const float* freqs, int half,
+                                 const float* wt, int H, float* tp) {
+  extern __shared__ float sinu[];
+  const float t = stage_time(*step_idx, steps, method, stage);
+  for (int j = threadIdx.x; j < half; j += blockDim.x) {
+    sinu[j] = sinf(t * freqs[j]);
+    sinu[half + j] = cosf(t * freqs[j]);
+  }
+  __syncthreads();
+  for (int h = blockIdx.x * blockDim.x + threadIdx.x; h < H; h += gridDim.x * blockDim.x) {
+    float acc = 0.0f;
+    for (int j = 0; j < 2 * half; ++j) acc = fmaf(wt[h * 2 * half + j], sinu[j], acc);
+    tp[h] = acc;
+  }
+}
+
+// ODE stage update after velocity evaluation `stage` wrote k[stage]
+// (span_ops.h:33-56 expression order).  Writes the next evaluation's input
+// (probe or x) into `next_in` (fp32 or bf16, padded width ld_in).
+struct OdeParams {
+  int B, A, ld;  // rows, action dim, row stride of the fp32 state buffers
+  int method, stage, steps;
+  const int* step_idx;
+  int* step_out;  // incremented after the last stage (null: no increment)
+  float* x;
+  float* probe;
+  const float* k[4];
+  void* next_in;
+  int ld_in;
+  int next_bf16;
+};
+
+__global__ void ode_stage_kernel(const OdeParams p) {
+  const float dt = 1.0f / static_cast<float>(p.steps);
+  const long long total = static_cast<long long>(p.B) * p.A;
+  const int last = p.method == 0 ? 0 : (p.method == 1 ? 1 : 3);
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const int b = static_cast<int>(i / p.A);
+    const int a = static_cast<int>(i - static_cast<long long>(b) * p.A);
+    const long long o = static_cast<long long>(b) * p.ld + a;
+    float nxt;
+    if (p.method == 0) {
+      nxt = p.x[o] + dt * p.k[0][o];
+      p.x[o] = nxt;
+    } else if (p.method == 1) {
+      if (p.stage == 0) {
+        nxt = p.x[o] + (dt * p.k[0][o]);
+        p.probe[o] = nxt;
+      } else {
+        nxt = p.x[o] + 0.5f * dt * (p.k[0][o] + p.k[1][o]);
+        p.x[o] = nxt;
+      }
+    } else {
+      const float half = 0.5f * dt;
+      if (p.stage == 0) {
+        nxt = p.x[o] + (half * p.k[0][o]);
+        p.probe[o] = nxt;
+      } else if (p.stage == 1) {
+        nxt = p.x[o] + (half * p.k[1][o]);
+        p.probe[o] = nxt;
+      } else if (p.stage == 2) {
+        nxt = p.x[o] + (dt * p.k[2][o]);
+        p.probe[o] = nxt;
+      } else {
+        nxt = p.x[o] + (dt / 6.0f) * (p.k[0][o] + (2.0f * p.k[1][o]) + (2.0f * p.k[2][o]) + p.k[3][o]);
+        p.x[o] = nxt;
+      }
+    }
+    const long long ii = static_cast<long long>(b) * p.ld_in + a;
+    if (p.next_bf16) static_cast<__nv_bfloat16*>(p.next_in)[ii] = __float2bfloat16_rn(nxt);
+    else static_cast<float*>(p.next_in)[ii] = nxt;
+  }
+  if (p.step_out != nullptr && p.stage == last && blockIdx.x == 0 && threadIdx.x == 0) *p.step_out = *p.step_idx + 1;
+}
+
+// fp32 [B][A] (dense) -> padded fp32 state and padded next-input buffer
+__global__ void load_rows_kernel(const float* src, int B, int A, float* dst, int ld, void* in, int ld_in, int in_bf16) {
+  const long long total = static_cast<long long>(B) * ld_in;
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const int b = static_cast<int>(i / ld_in);
+    const int a = static_cast<int>(i - static_cast<long long>(b) * ld_in);
+    const float v = a < A ? src[static_cast<long long>(b) * A + a] : 0.0f;
+    if (dst != nullptr && a < ld) dst[static_cast<long long>(b) * ld + a] = v;
+    if (in_bf16) static_cast<__nv_bfloat16*>(in)[i] = __float2bfloat16_rn(v);
+    else static_cast<float*>(in)[i] = v;
+  }
+}
+
+__global__ void store_rows_kernel(const float* src, int B, int A, int ld, float* dst) {
+  const long long total = static_cast<long long>(B) * A;
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const int b = static_cast<int>(i / A);
+    const int a = static_cast<int>(i - static_cast<long long>(b) * A);
+    dst[i] = src[static_cast<long long>(b) * ld + a];
+  }
+}
+
+class Flow final : public FlowDevice {
+ public:
+  Flow(std::shared_ptr<DeviceContext> ctx, Precision prec) : ctx_(std::move(ctx)), prec_(prec) {}
+  ~Flow() override {
+    for (auto& [k, g] : graphs_) cudaGraphExecDestroy(g);
+    if (pinned_ != nullptr) cudaFreeHost(pinned_);
+  }
+  bool load(const TensorTable& t, std::string& err);
+  const FlowConfig& config() const noexcept override { return cfg_; }
+  std::size_t capacity() const noexcept override { return cap_; }
+  int reserve(std::size_t batch, std::string& err) noexcept override;
+  int begin(const float* condition, const float* x0, std::size_t batch, std::size_t steps, int method,
+            bool condition_on_device, std::string& err) noexcept override;
+  int advance(std::size_t first, std::size_t count, float* out, std::string& err) noexcept override;
+  int sample_device(const float* condition, const float* x0, std::size_t batch, std::size_t steps, int method,
+                    float* out, void* stream, std::string& err) noexcept override;
+
+ private:
+  bool use_tc(std::size_t batch) const { return prec_ == Precision::kBF16 && static_cast<int>(batch) >= kTcMinRows; }
+  bool gemm(const Mat& m, const void* in, int in_ld, std::size_t batch, float* out_f32, void* out_bf16, int out_ld,
+            const float* add_vec, const float* add_tok, int act, bool tc, cudaStream_t st, std::string& err);
+  bool record_step(std::size_t batch, int method, bool tc, cudaStream_t st, std::string& err);
+  bool prepare(const float* condition, const float* x0, std::size_t batch, bool cond_device, bool x_device,
+               cudaStream_t st, std::string& err);
+
+  std::shared_ptr<DeviceContext> ctx_;
+  Precision prec_;
+  FlowConfig cfg_{};
+  int a_pad_ = 0, c_pad_ = 0;
+  DeviceArena wts_;
+  Mat in_, cond_, out_;
+  std::vector<Mat> layers_;
+  float* wt_ = nullptr;     // [H][td] fp32
+  float* freqs_ = nullptr;  // [td/2]
+  DeviceArena ws_;
+  std::size_t cap_ = 0, cap_rows_ = 0;
+  float *x_ = nullptr, *probe_ = nullptr, *k_[4] = {}, *cemb_ = nullptr, *tp_ = nullptr, *part_ = nullptr;
+  float* in_cond_ = nullptr;
+  void *xin_ = nullptr, *h0_ = nullptr, *h1_ = nullptr, *cin_ = nullptr;
+  int* step_ = nullptr;
+  std::size_t part_elems_ = 0;
+  float* pinned_ = nullptr;
+  std::size_t batch_ = 0, steps_ = 0;
+  int method_ = 0;
+  std::map<std::tuple<std::size_t, int, bool, std::size_t>, cudaGraphExec_t> graphs_;
+};
+
+bool Flow::load(const TensorTable& t, std::string& err) {
+  const HostTensor* in = t.find("flow.in_proj.weight");
+  const HostTensor* tp = t.find("flow.time_proj.weight");
+  const HostTensor* cp = t.find("flow.cond_proj.weight");
+  const HostTensor* op = t.find("flow.out_proj.weight");
+  if (in == nullptr || tp == nullptr || cp == nullptr || op == nullptr || in->ndim != 2 || tp->ndim != 2 ||
+      cp->ndim != 2 || op->ndim != 2) {
+    err = "flow.* projections missing";
+    return false;
+  }
+  cfg_.hidden = in->shape[0];
+  cfg_.action_dim = in->shape[1];
+  cfg_.time_dim = tp->shape[1];
+  cfg_.cond_dim = cp->shape[1];
+  if (cfg_.hidden == 0 || cfg_.action_dim == 0 || cfg_.time_dim == 0 || cfg_.cond_dim == 0 ||
+      cfg_.time_dim % 2 != 0 || tp->shape[0] != cfg_.hidden || cp->shape[0] != cfg_.hidden ||
+      op->shape[0] != cfg_.action_dim || op->shape[1] != cfg_.hidden) {
+    err = "flow.* projection shapes are inconsistent";
+    return false;
+  }
+  std::vector<const HostTensor*> layer_t;
+  for (std::size_t n = 0; n < 8; ++n) {
+    const HostTensor* lw = t.find("flow.layers." + std::to_string(n) + ".weight");
+    if (lw == nullptr) break;
+    if (lw->ndim != 2 || lw->shape[0] != cfg_.hidden || lw->shape[1] != cfg_.hidden) {
+      err = "flow layer shape mismatch";
+      return false;
+    }
+    layer_t.push_back(lw);
+  }
+  cfg_.mlp_layers = layer_t.size();
+  const int H = static_cast<int>(cfg_.hidden);
+  a_pad_ = static_cast<int>((cfg_.action_dim + 63) / 64 * 64);
+  c_pad_ = static_cast<int>((cfg_.cond_dim + 63) / 64 * 64);
+  if (H % 64 != 0) {
+    err = "flow hidden width must be a multiple of 64";
+    return false;
+  }
+  const bool bf = prec_ == Precision::kBF16;
+  ArenaPlan plan;
+  auto plan_mat = [&](int rows, int cols) {
+    const int rp = (rows + 127) / 128 * 128;
+    const int cp2 = (cols + 63) / 64 * 64;
+    plan.add(static_cast<std::size_t>(rp) * cp2 * (bf ? 2 : 4));
+    plan.add_n<SimtSlice>(static_cast<std::size_t>((cp2 + 255) / 256));
+  };
+  plan_mat(H, static_cast<int>(cfg_.action_dim));
+  plan_mat(H, static_cast<int>(cfg_.cond_dim));
+  plan_mat(static_cast<int>(cfg_.action_dim), H);
+  for (std::size_t i = 0; i < cfg_.mlp_layers; ++i) plan_mat(H, H);
+  plan.add_n<float>(cfg_.hidden * cfg_.time_dim + cfg_.time_dim);
+  if (!wts_.init(plan.total(), err)) return false;
+  auto put_mat = [&](const HostTensor* src, Mat& m) {
+    m.rows = static_cast<int>(src->shape[0]);
+    m.cols = static_cast<int>(src->shape[1]);
+    m.rows_pad = (m.rows + 127) / 128 * 128;
+    m.cols_pad = (m.cols + 63) / 64 * 64;
+    const auto w = widen_f32(*src);  // bf16 files widen exactly (flow.cc:41-58)
+    std::vector<float> padded(static_cast<std::size_t>(m.rows_pad) * m.cols_pad, 0.0f);
+    for (int r = 0; r < m.rows; ++r)
+      std::memcpy(&padded[static_cast<std::size_t>(r) * m.cols_pad], &w[static_cast<std::size_t>(r) * m.cols],
+                  static_cast<std::size_t>(m.cols) * 4);
+    if (bf) {
+      std::vector<std::uint16_t> h(padded.size());
+      for (std::size_t i = 0; i < h.size(); ++i) h[i] = to_bf16(padded[i]);
+      m.w = wts_.take(h.size() * 2);
+      cudaMemcpy(m.w, h.data(), h.size() * 2, cudaMemcpyHostToDevice);
+    } else {
+      m.w = wts_.take(padded.size() * 4);
+      cudaMemcpy(m.w, padded.data(), padded.size() * 4, cudaMemcpyHostToDevice);
+    }
+    std::vector<SimtSlice> sl;
+    for (int c = 0; c < m.cols_pad; c += 256) sl.push_back(SimtSlice{0, 0, c, std::min(256, m.cols_pad - c), c});
+    m.nslices = static_cast<int>(sl.size());
+    m.slices = wts_.take_n<SimtSlice>(sl.size());
+    cudaMemcpy(m.slices, sl.data(), sl.size() * sizeof(SimtSlice), cudaMemcpyHostToDevice);
+  };
+  put_mat(in, in_);
+  put_mat(cp, cond_);
+  put_mat(op, out_);
+  layers_.resize(cfg_.mlp_layers);
+  for (std::size_t i = 0; i < cfg_.mlp_layers; ++i) put_mat(layer_t[i], layers_[i]);
+  const auto wt = widen_f32(*tp);
+  wt_ = wts_.take_n<float>(wt.size());
+  cudaMemcpy(wt_, wt.data(), wt.size() * 4, cudaMemcpyHostToDevice);
+  // f_j = 10000^(-j / half) in float pow (flow.cc:104)
+  const std::size_t half = cfg_.time_dim / 2;
+  std::vector<float> f(half);
+  for (std::size_t j = 0; j < half; ++j)
+    f[j] = std::pow(10000.0f, -static_cast<float>(j) / static_cast<float>(half));
+  freqs_ = wts_.take_n<float>(half);
+  cudaMemcpy(freqs_, f.data(), half * 4, cudaMemcpyHostToDevice);
+  if (cudaDeviceSynchronize() != cudaSuccess) {
+    err = "flow weight upload failed";
+    return false;
+  }
+  return true;
+}
+
+int Flow::reserve(std::size_t batch, std::string& err) noexcept {
+  if (batch == 0) batch = 1;
+  if (batch <= cap_) return 0;
+  for (auto& [k, g] : graphs_) cudaGraphExecDestroy(g);
+  graphs_.clear();
+  const std::size_t rows = (batch + 255) / 256 * 256;
+  const std::size_t H = cfg_.hidden;
+  const std::size_t nsl = static_cast<std::size_t>(std::max({in_.nslices, cond_.nslices, out_.nslices,
+                                                             layers_.empty() ? 1 : layers_[0].nslices}));
+  part_elems_ = nsl * batch * std::max<std::size_t>(H, static_cast<std::size_t>(out_.rows_pad));
+  ArenaPlan plan;
+  for (int i = 0; i < 6; ++i) plan.add_n<float>(rows * static_cast<std::size_t>(a_pad_));
+  plan.add_n<float>(rows * H);           // c_emb
+  plan.add_n<float>(H);                  // tp
+  plan.add_n<float>(part_elems_);
+  plan.add_n<float>(rows * static_cast<std::size_t>(c_pad_));
+  plan.add_n<float>(rows * static_cast<std::size_t>(a_pad_));  // xin
+  plan.add_n<float>(rows * H);                                 // h0
+  plan.add_n<float>(rows * H);                                 // h1
+  plan.add_n<float>(rows * static_cast<std::size_t>(c_pad_));  // cin
+  plan.add_n<int>(4);
+  ws_.release();
+  if (!ws_.init(plan.total(), err)) {
+    cap_ = 0;
+    return 2;
+  }
+  x_ = ws_.take_n<float>(rows * a_pad_);
+  probe_ = ws_.take_n<float>(rows * a_pad_);
+  for (auto& k : k_) k = ws_.take_n<float>(rows * a_pad_);
+  cemb_ = ws_.take_n<float>(rows * H);
+  tp_ = ws_.take_n<float>(H);
+  part_ = ws_.take_n<float>(part_elems_);
+  in_cond_ = ws_.take_n<float>(rows * c_pad_);
+  xin_ = ws_.take(rows * a_pad_ * 4);
+  h0_ = ws_.take(rows * H * 4);
+  h1_ = ws_.take(rows * H * 4);
+  cin_ = ws_.take(rows * c_pad_ * 4);
+  step_ = ws_.take_n<int>(4);
+  cudaMemset(x_, 0, ws_.used());
+  if (pinned_ != nullptr) cudaFreeHost(pinned_);
+  pinned_ = nullptr;
+  if (counted_host_malloc(reinterpret_cast<void**>(&pinned_), batch * (cfg_.cond_dim + 2 * cfg_.action_dim) * 4) !=
+      cudaSuccess) {
+    err = "pinned host allocation failed";
+    return 2;
+  }
+  cap_ = batch;
+  cap_rows_ = rows;
+  return cudaDeviceSynchronize() == cudaSuccess ? 0 : 2;
+}
+
+bool Flow::gemm(const Mat& m, const void* in, int in_ld, std::size_t batch, float* out_f32, void* out_bf16, int out_ld,
+                const float* add_vec, const float* add_tok, int act, bool tc, cudaStream_t st, std::string& err) {
+  if (tc) {
+    TcLaunch l;
+    l.A = m.w;
+    l.M_rows = m.rows_pad;
+    l.K = m.cols_pad;
+    l.src[0] = TcSource{in, in_ld, 1, static_cast<int>(cap_rows_)};
+    l.L = 1;
+    l.n_samples = static_cast<int>(batch);
+    l.m_valid = m.rows;
+    l.segs = {tc::Seg{0, 0, 0, m.cols_pad / 64, 0}};
+    l.add_vec = add_vec;
+    l.add_tok = add_tok;
+    l.add_ld = static_cast<int>(cfg_.hidden);
+    l.act = act;
+    l.out_f32 = out_f32 != nullptr;
+    l.out = out_f32 != nullptr ? static_cast<void*>(out_f32) : out_bf16;
+    l.out_ld = out_ld;
+    return tc_gemm(l, *ctx_, st, err) == cudaSuccess;
+  }
+  SimtConvParams p{};
+  p.W = m.w;
+  p.M = m.rows;
+  p.K = m.cols_pad;
+  p.src[0] = SimtSource{static_cast<const float*>(in), in_ld, 1};
+  p.stride = 1;
+  p.L_out = 1;
+  p.n_tokens = static_cast<int>(batch);
+  p.slices = m.slices;
+  p.partial = part_;
+  const int nt = p.n_tokens >= 16 ? 16 : (p.n_tokens >= 8 ? 8 : 4);
+  const dim3 grid(static_cast<unsigned>(m.nslices), static_cast<unsigned>((m.rows + 127) / 128),
+                  static_cast<unsigned>((p.n_tokens + nt - 1) / nt));
+  const bool bf = prec_ == Precision::kBF16;
+  if (nt == 16) bf ? simt_conv_kernel<16, true><<<grid, 128, 0, st>>>(p) : simt_conv_kernel<16, false><<<grid, 128, 0, st>>>(p);
+  else if (nt == 8) bf ? simt_conv_kernel<8, true><<<grid, 128, 0, st>>>(p) : simt_conv_kernel<8, false><<<grid, 128, 0, st>>>(p);
+  else bf ? simt_conv_kernel<4, true><<<grid, 128, 0, st>>>(p) : simt_conv_kernel<4, false><<<grid, 128, 0, st>>>(p);
+  ReduceParams r{};
+  r.partial = part_;
+  r.nslices = m.nslices;
+  r.n_tokens = static_cast<int>(batch);
+  r.M = m.rows;
+  r.add_vec = add_vec;
+  r.add_tok = add_tok;
+  r.act = act;
+  r.out = out_f32 != nullptr ? out_f32 : static_cast<float*>(out_bf16);
+  r.out_ld = out_ld;
+  reduce_partials_kernel<<<ew_grid(static_cast<long long>(batch) * m.rows, 256, *ctx_), 256, 0, st>>>(r);
+  return cudaGetLastError() == cudaSuccess;
+}
+
+bool Flow::record_step(std::size_t batch, int method, bool tc, cudaStream_t st, std::string& err) {
+  const int H = static_cast<int>(cfg_.hidden);
+  const int A = static_cast<int>(cfg_.action_dim);
+  const int half = static_cast<int>(cfg_.time_dim / 2);
+  const int stages = method == 0 ? 1 : (method == 1 ? 2 : 4);
+  for (int s = 0; s < stages; ++s) {
+    time_proj_kernel<<<(H + 255) / 256, 256, static_cast<std::size_t>(2 * half) * 4, st>>>(
+        step_, static_cast<int>(steps_), method, s, freqs_, half, wt_, H, tp_);
+    // h = SiLU(W_in x + tp + c_emb)
+    void* hin = h0_;
+    void* hout = h1_;
+    if (!gemm(in_, xin_, a_pad_, batch, tc ? nullptr : static_cast<float*>(hin), tc ? hin : nullptr, H, tp_, cemb_,
+              tc::kActSilu, tc, st, err))
+      return false;
+    for (const Mat& l : layers_) {
+      if (!gemm(l, hin, H, batch, tc ? nullptr : static_cast<float*>(hout), tc ? hout : nullptr, H, nullptr, nullptr,
+                tc::kActSilu, tc, st, err))
+        return false;
+      std::swap(hin, hout);
+    }
+    if (!gemm(out_, hin, H, batch, k_[s], nullptr, a_pad_, nullptr, nullptr, tc::kActNone, tc, st, err)) return false;
+    OdeParams p{};
+    p.B = static_cast<int>(batch);
+    p.A = A;
+    p.ld = a_pad_;
+    p.method = method;
+    p.stage = s;
+    p.steps = static_cast<int>(steps_);
+    p.step_idx = step_;
+    p.step_out = s == stages - 1 ? step_ + 1 : nullptr;
+    p.x = x_;
+    p.probe = probe_;
+    for (int i = 0; i < 4; ++i) p.k[i] = k_[i];
+    p.next_in = xin_;
+    p.ld_in = a_pad_;
+    p.next_bf16 = tc ? 1 : 0;
+    ode_stage_kernel<<<ew_grid(static_cast<long long>(batch) * A, 256, *ctx_), 256, 0, st>>>(p);
+  }
+  // step_[0] <- step_[1] (next step index) for the next replay
+  cudaMemcpyAsync(step_, step_ + 1, sizeof(int), cudaMemcpyDeviceToDevice, st);
+  return cudaGetLastError() == cudaSuccess;
+}
+
+bool Flow::prepare(const float* condition, const float* x0, std::size_t batch, bool cond_device, bool x_device,
+                   cudaStream_t st, std::string& err) {
+  const bool tc = use_tc(batch);
+  const int C = static_cast<int>(cfg_.cond_dim), A = static_cast<int>(cfg_.action_dim);
+  float* pc = pinned_;
+  float* px = pinned_ + batch * cfg_.cond_dim;
+  const float* dcond = condition;
+  const float* dx = x0;
+  float* staging = k_[3];  // dense [B][A] staging for x0 (reused, overwritten by the solve)
+  if (!cond_device) {
+    std::memcpy(pc, condition, batch * C * 4);
+    cudaMemcpyAsync(probe_, pc, batch * C * 4, cudaMemcpyHostToDevice, st);
+    dcond = probe_;  // probe_ holds >= rows * a_pad floats; cond fits when C <= a_pad (else use part_)
+    if (static_cast<std::size_t>(C) > static_cast<std::size_t>(a_pad_)) {
+      cudaMemcpyAsync(part_, pc, batch * C * 4, cudaMemcpyHostToDevice, st);
+      dcond = part_;
+    }
+  }
+  if (!x_device) {
+    std::memcpy(px, x0, batch * A * 4);
+    cudaMemcpyAsync(staging, px, batch * A * 4, cudaMemcpyHostToDevice, st);
+    dx = staging;
+  }
+  // condition -> padded input (fp32 or bf16), then c_emb = W_c cond (flow.cc:256)
+  load_rows_kernel<<<ew_grid(static_cast<long long>(batch) * c_pad_, 256, *ctx_), 256, 0, st>>>(
+      dcond, static_cast<int>(batch), C, nullptr, 0, tc ? cin_ : static_cast<void*>(in_cond_), c_pad_, tc ? 1 : 0);
+  if (!gemm(cond_, tc ? cin_ : static_cast<void*>(in_cond_), c_pad_, batch, cemb_, nullptr,
+            static_cast<int>(cfg_.hidden), nullptr, nullptr, tc::kActNone, tc, st, err))
+    return false;
+  load_rows_kernel<<<ew_grid(static_cast<long long>(batch) * a_pad_, 256, *ctx_), 256, 0, st>>>(
+      dx, static_cast<int>(batch), A, x_, a_pad_, xin_, a_pad_, tc ? 1 : 0);
+  cudaMemsetAsync(step_, 0, 2 * sizeof(int), st);
+  return cudaGetLastError() == cudaSuccess;
+}
+
+int Flow::begin(const float* condition, const float* x0, std::size_t batch, std::size_t steps, int method,
+                bool condition_on_device, std::string& err) noexcept {
+  if (batch == 0 || steps == 0 || method < 0 || method > 2) {
+    err = "invalid flow arguments";
+    return 1;
+  }
+  if (batch > cap_ && reserve(batch, err) != 0) return 2;
+  cudaSetDevice(ctx_->device);
+  batch_ = batch;
+  steps_ = steps;
+  method_ = method;
+  if (!prepare(condition, x0, batch, condition_on_device, false, ctx_->stream, err)) return 2;
+  return 0;
+}
+
+int Flow::advance(std::size_t first, std::size_t count, float* out, std::string& err) noexcept {
+  cudaSetDevice(ctx_->device);
+  cudaStream_t st = ctx_->stream;
+  const bool tc = use_tc(batch_);
+  if (count > 0) {
+    const auto key = std::make_tuple(batch_, method_, tc, steps_);
+    auto it = graphs_.find(key);
+    if (it == graphs_.end()) {
+      cudaStream_t cap = nullptr;
+      cudaStreamCreateWithFlags(&cap, cudaStreamNonBlocking);
+      cudaStreamSynchronize(st);
+      cudaGraph_t graph = nullptr;
+      cudaStreamBeginCapture(cap, cudaStreamCaptureModeThreadLocal);
+      const bool ok = record_step(batch_, method_, tc, cap, err);
+      const cudaError_t end = cudaStreamEndCapture(cap, &graph);
+      cudaStreamDestroy(cap);
+      if (!ok || end != cudaSuccess) {
+        if (graph != nullptr) cudaGraphDestroy(graph);
+        if (err.empty()) err = "flow graph capture failed";
+        cudaGetLastError();
+        return 2;
+      }
+      cudaGraphExec_t exec = nullptr;
+      const cudaError_t inst = cudaGraphInstantiate(&exec, graph, 0);
+      cudaGraphDestroy(graph);
+      if (inst != cudaSuccess) {
+        err = "flow graph instantiation failed";
+        return 2;
+      }
+      it = graphs_.emplace(key, exec).first;
+    }
+    const int first_i = static_cast<int>(first);
+    cudaMemcpyAsync(step_, &first_i, sizeof(int), cudaMemcpyHostToDevice, st);
+    for (std::size_t i = 0; i < count; ++i)
+      if (cudaGraphLaunch(it->second, st) != cudaSuccess) {
+        err = "flow graph launch failed";
+        return 2;
+      }
+  }
+  if (out != nullptr) {
+    const int A = static_cast<int>(cfg_.action_dim);
+    float* stage = k_[3];
+    store_rows_kernel<<<ew_grid(static_cast<long long>(batch_) * A, 256, *ctx_), 256, 0, st>>>(
+        x_, static_cast<int>(batch_), A, a_pad_, stage);
+    float* px = pinned_ + batch_ * cfg_.cond_dim;
+    cudaMemcpyAsync(px, stage, batch_ * A * 4, cudaMemcpyDeviceToHost, st);
+    if (cudaStreamSynchronize(st) != cudaSuccess) {
+      err = std::string("flow solve failed: ") + cudaGetErrorString(cudaGetLastError());
+      return 2;
+    }
+    if (take_device_error(*ctx_, st) != 0) {
+      err = "a device pipeline wait timed out";
+      return 2;
+    }
+    std::memcpy(out, px, batch_ * A * 4);
+  }
+  return 0;
+}
+
+int Flow::sample_device(const float* condition, const float* x0, std::size_t batch, std::size_t steps, int method,
+                        float* out, void* stream, std::string& err) noexcept {
+  if (batch == 0 || steps == 0 || method < 0 || method > 2) {
+    err = "invalid flow arguments";
+    return 1;
+  }
+  if (batch > cap_) {
+    err = "batch exceeds the reserved capacity (call fe_engine_reserve_batch first)";
+    return 2;
+  }
+  cudaSetDevice(ctx_->device);
+  cudaStream_t st = stream != nullptr ? static_cast<cudaStream_t>(stream) : ctx_->stream;
+  batch_ = batch;
+  steps_ = steps;
+  method_ = method;
+  if (!prepare(condition, x0, batch, true, true, st, err)) return 2;
+  const bool tc = use_tc(batch);
+  const auto key = std::make_tuple(batch, method, tc, steps);
+  auto it = graphs_.find(key);
+  if (it == graphs_.end()) {
+    // record on the caller's stream ordering: capture on a private stream
+    cudaStream_t cap = nullptr;
+    cudaStreamCreateWithFlags(&cap, cudaStreamNonBlocking);
+    cudaStreamSynchronize(st);
+    cudaGraph_t graph = nullptr;
+    cudaStreamBeginCapture(cap, cudaStreamCaptureModeThreadLocal);
+    const bool ok = record_step(batch, method, tc, cap, err);
+    cudaStreamEndCapture(cap, &graph);
+    cudaStreamDestroy(cap);
+    if (!ok || graph == nullptr) {
+      if (graph != nullptr) cudaGraphDestroy(graph);
+      return 2;
+    }
+    cudaGraphExec_t exec = nullptr;
+    cudaGraphInstantiate(&exec, graph, 0);
+    cudaGraphDestroy(graph);
+    it = graphs_.emplace(key, exec).first;
+  }
+  for (std::size_t i = 0; i < steps; ++i) cudaGraphLaunch(it->second, st);
+  store_rows_kernel<<<ew_grid(static_cast<long long>(batch) * cfg_.action_dim, 256, *ctx_), 256, 0, st>>>(
+      x_, static_cast<int>(batch), static_cast<int>(cfg_.action_dim), a_pad_, out);
+  return cudaGetLastError() == cudaSuccess ? 0 : 2;
+}
+
+}  // namespace
+
+std::unique_ptr<FlowDevice> make_flow_device(const TensorTable& tensors, std::shared_ptr<DeviceContext> ctx,
+                                             Precision precision, std::string& err) {
+  cudaSetDevice(ctx->device);
+  auto f = std::make_unique<Flow>(std::move(ctx), precision);
+  if (!f->load(tensors, err)) return nullptr;
+  if (f->reserve(1, err) != 0) return nullptr;
+  return f;
+}
+
+}  // namespace feb

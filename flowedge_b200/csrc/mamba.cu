@@ -1,0 +1,672 @@
+// Device-resident Mamba encoder (reference: src/core/models/mamba/mamba.cc).
+//
+// Per layer, tokens of all sequences at once (token-major [B*L][width]):
+//   normed = RMSNorm(hidden)                     rmsnorm_kernel
+//   [x | z] = normed W_in^T                      GEMM (fp32 out)
+//   u = SiLU(causal depthwise conv(x) + b)       causal_conv_kernel
+//   [dt_in | B | C] = u W_x^T                    GEMM (fp32 out)
+//   scan: dt = softplus(dt_in W_dt^T + b_dt) fused into the selective scan,
+//         y = (D u + sum_n h_n C_n) * SiLU(z)   scan_kernel
+//   hidden += y W_out^T                          GEMM (fp32 accumulate)
+// then a final RMSNorm.  GEMMs use the weight-streaming CUDA-core kernel for
+// short token counts and the tcgen05 GEMM (bf16 operands) for long ones in
+// bf16 mode.  Streaming decode keeps the per-layer conv window and SSM state
+// on the device in the reference's snapshot layout ([di][dc] window, newest
+// last, then [ds][di] state).
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+
+#include "runtime.cuh"
+#include "simt.cuh"
+
+namespace feb {
+namespace {
+
+constexpr int kTcMinTokens = 256;
+constexpr int kMaxState = 16;
+constexpr int kMaxRank = 64;
+
+std::uint16_t bf16_of(float v) {
+  std::uint32_t u;
+  std::memcpy(&u, &v, 4);
+  if ((u & 0x7FFFFFFFu) > 0x7F800000u) return 0x7FC0;
+  u += 0x7FFFu + ((u >> 16) & 1u);
+  return static_cast<std::uint16_t>(u >> 16);
+}
+
+struct Mat {
+  int rows = 0, rows_pad = 0, cols = 0, cols_pad = 0;
+  void* w = nullptr;
+  SimtSlice* slices = nullptr;
+  int nslices = 0;
+};
+
+struct Layer {
+  float* norm = nullptr;
+  Mat in_proj, x_proj, out_proj;
+  float* conv_w = nullptr;  // [di][dc]
+  float* conv_b = nullptr;
+  float* dt_w = nullptr;    // [di][dr] fp32 (widened)
+  float* dt_b = nullptr;
+  float* a_neg = nullptr;   // [ds][di] = -exp(A_log)^T (mamba.cc:167-176)
+  float* d = nullptr;
+};
+
+// one warp per row; RMSNorm with eps 1e-5 (kernels_scalar.cc:48-60); optional
+// bf16 copy for the tensor-core GEMM
+__global__ void rmsnorm_kernel(const float* in, const float* w, int rows, int dim, float* out, __nv_bfloat16* out_bf) {
+  const int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  const float* x = in + static_cast<long long>(row) * dim;
+  float ss = 0.0f;
+  for (int i = lane; i < dim; i += 32) ss = fmaf(x[i], x[i], ss);
+  for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+  const float scale = 1.0f / sqrtf((ss / static_cast<float>(dim)) + 1e-5f);
+  for (int i = lane; i < dim; i += 32) {
+    const float v = x[i] * scale * w[i];
+    if (out != nullptr) out[static_cast<long long>(row) * dim + i] = v;
+    if (out_bf != nullptr) out_bf[static_cast<long long>(row) * dim + i] = __float2bfloat16_rn(v);
+  }
+}
+
+// u[b][t][c] = SiLU(bias[c] + sum_k w[c][k] * x[b][t - (dc-1) + k][c]), x is the
+// first di columns of xz (row stride 2*di) (kernels_scalar.cc:10-27)
+__global__ void causal_conv_kernel(const float* xz, int B, int L, int di, int dc, const float* w, const float* bias,
+                                   float* u, __nv_bfloat16* u_bf) {
+  const long long total = static_cast<long long>(B) * L * di;
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const long long tok = i / di;
+    const int c = static_cast<int>(i - tok * di);
+    const int t = static_cast<int>(tok % L);
+    float acc = bias[c];
+    for (int k = 0; k < dc; ++k) {
+      const int ti = t - (dc - 1) + k;
+      if (ti >= 0) acc += w[c * dc + k] * xz[(tok - t + ti) * 2 * di + c];
+    }
+    const float v = silu_f(acc);
+    u[i] = v;
+    if (u_bf != nullptr) u_bf[i] = __float2bfloat16_rn(v);
+  }
+}
+
+// Selective scan with the dt projection fused in.  One thread per (sequence,
+// channel), states in registers, sequential over t (kernels_scalar.cc:133-169):
+//   dt = softplus(b_dt[c] + sum_r W_dt[c][r] dbl[t][r])
+//   h_n = exp(dt A_n) h_n + dt B_n u ;  y = (D u + sum_n h_n C_n) * SiLU(z)
+// dbl rows of the block's sequence are staged in shared memory.
+template <int DS, int DR>
+__global__ void __launch_bounds__(256) scan_kernel(const float* dbl, int wd, const float* u, const float* xz, int L,
+                                                   int di, const float* dt_w, const float* dt_b, const float* a_neg,
+                                                   const float* dsk, float* state, float* y, __nv_bfloat16* y_bf) {
+  extern __shared__ float sdbl[];  // [L][wd]
+  const int b = blockIdx.y;
+  const int c = blockIdx.x * blockDim.x + threadIdx.x;
+  const float* drow = dbl + static_cast<long long>(b) * L * wd;
+  for (int i = threadIdx.x; i < L * wd; i += blockDim.x) sdbl[i] = drow[i];
+  __syncthreads();
+  if (c >= di) return;
+  float wdt[DR], an[DS], h[DS];
+#pragma unroll
+  for (int r = 0; r < DR; ++r) wdt[r] = dt_w[c * DR + r];
+#pragma unroll
+  for (int n = 0; n < DS; ++n) {
+    an[n] = a_neg[n * di + c];
+    h[n] = state != nullptr ? state[(static_cast<long long>(b) * DS + n) * di + c] : 0.0f;
+  }
+  const float bdt = dt_b[c], dk = dsk[c];
+  for (int t = 0; t < L; ++t) {
+    const float* row = sdbl + t * wd;
+    float acc = 0.0f;
+#pragma unroll
+    for (int r = 0; r < DR; ++r) acc += row[r] * wdt[r];
+    const float dt = softplus_f(acc + bdt);
+    const long long tok = static_cast<long long>(b) * L + t;
+    const float uv = u[tok * di + c];
+    float yv = dk * uv;
+#pragma unroll
+    for (int n = 0; n < DS; ++n) {
+      const float da = expf(dt * an[n]);
+      const float dbu = dt * row[DR + n] * uv;
+      h[n] = (da * h[n]) + dbu;
+      yv += h[n] * row[DR + DS + n];
+    }
+    const float zv = xz[tok * 2 * di + di + c];
+    const float out = yv * (zv / (1.0f + expf(-zv)));
+    y[tok * di + c] = out;
+    if (y_bf != nullptr) y_bf[tok * di + c] = __float2bfloat16_rn(out);
+  }
+  if (state != nullptr)
+#pragma unroll
+    for (int n = 0; n < DS; ++n) state[(static_cast<long long>(b) * DS + n) * di + c] = h[n];
+}
+
+// hidden[b][t] = embedding[token[b][t]]
+__global__ void embed_kernel(const int* tokens, long long n_tok, const float* emb, int dm, float* hidden) {
+  const long long total = n_tok * dm;
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const long long tok = i / dm;
+    const int c = static_cast<int>(i - tok * dm);
+    hidden[i] = emb[static_cast<long long>(tokens[tok]) * dm + c];
+  }
+}
+
+// last position of each sequence -> dense [B][dm]
+__global__ void gather_last_kernel(const float* hidden, int B, int L, int dm, float* out) {
+  const long long total = static_cast<long long>(B) * dm;
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const long long b = i / dm;
+    const int c = static_cast<int>(i - b * dm);
+    out[i] = hidden[((b * L) + L - 1) * dm + c];
+  }
+}
+
+// decode: shift the conv window, append x, conv + SiLU (mamba.cc:353-360)
+__global__ void conv_step_kernel(const float* xz, int di, int dc, float* window, const float* w, const float* bias,
+                                 float* u) {
+  const int c = blockIdx.x * blockDim.x + threadIdx.x;
+  if (c >= di) return;
+  float* wc = window + c * dc;
+  for (int k = 0; k + 1 < dc; ++k) wc[k] = wc[k + 1];
+  wc[dc - 1] = xz[c];
+  float acc = bias[c];
+  for (int k = 0; k < dc; ++k) acc += w[c * dc + k] * wc[k];
+  u[c] = silu_f(acc);
+}
+
+class Mamba final : public MambaDevice {
+ public:
+  Mamba(std::shared_ptr<DeviceContext> ctx, Precision prec) : ctx_(std::move(ctx)), prec_(prec) {}
+  ~Mamba() override {
+    if (pinned_ != nullptr) cudaFreeHost(pinned_);
+  }
+  bool load(const TensorTable& t, std::string& err);
+  const MambaConfig& config() const noexcept override { return cfg_; }
+  std::size_t capacity() const noexcept override { return cap_tokens_; }
+  int reserve(std::size_t batch, std::size_t max_len, std::string& err) noexcept override;
+  int forward(const std::int32_t* tokens, std::size_t batch, std::size_t len, float* hidden, bool last_only,
+              std::string& err) noexcept override;
+  const float* last_hidden_device() const noexcept override { return last_; }
+  int forward_device(const std::int32_t* tokens, std::size_t batch, std::size_t len, float* last_hidden, void* stream,
+                     std::string& err) noexcept override;
+  int step(std::int32_t token, float* out, std::string& err) noexcept override;
+  void reset() noexcept override;
+  std::size_t state_floats() const noexcept override {
+    return cfg_.n_layers * cfg_.d_inner * (cfg_.d_conv + cfg_.d_state);
+  }
+  int read_state(float* dst, std::string& err) noexcept override;
+  int write_state(const float* src, std::string& err) noexcept override;
+
+ private:
+  bool gemm(const Mat& m, const void* in, int in_ld, long long n_tok, float* out, int out_ld, bool accumulate,
+            bool tc, cudaStream_t st, std::string& err);
+  bool run_layers(long long n_tok, int B, int L, bool tc, cudaStream_t st, std::string& err);
+
+  std::shared_ptr<DeviceContext> ctx_;
+  Precision prec_;
+  MambaConfig cfg_{};
+  DeviceArena wts_, ws_;
+  float* emb_ = nullptr;
+  float* norm_f_ = nullptr;
+  std::vector<Layer> layers_;
+  std::size_t cap_tokens_ = 0, cap_batch_ = 0, cap_rows_ = 0;
+  int* tokens_ = nullptr;
+  float *hidden_ = nullptr, *xz_ = nullptr, *u_ = nullptr, *dbl_ = nullptr, *y_ = nullptr, *part_ = nullptr;
+  float* last_ = nullptr;
+  float* out_ = nullptr;
+  __nv_bfloat16 *nb_ = nullptr, *ub_ = nullptr, *yb_ = nullptr;
+  float* state_ = nullptr;  // decode state (snapshot layout)
+  float* dh_ = nullptr;     // decode scratch
+  std::size_t part_elems_ = 0;
+  float* pinned_ = nullptr;
+  std::size_t pinned_floats_ = 0;
+};
+
+bool Mamba::load(const TensorTable& t, std::string& err) {
+  const HostTensor* emb = t.find("backbone.embeddings.weight");
+  const HostTensor* a0 = t.find("backbone.layers.0.mixer.A_log");
+  const HostTensor* cv0 = t.find("backbone.layers.0.mixer.conv1d.weight");
+  const HostTensor* xp0 = t.find("backbone.layers.0.mixer.x_proj.weight");
+  const HostTensor* nf = t.find("backbone.norm_f.weight");
+  if (emb == nullptr || a0 == nullptr || cv0 == nullptr || xp0 == nullptr || nf == nullptr || emb->ndim != 2 ||
+      a0->ndim != 2 || cv0->ndim != 3 || xp0->ndim != 2 || emb->dtype != DType::F32 || a0->dtype != DType::F32) {
+    err = "backbone.* tensors missing or malformed";
+    return false;
+  }
+  cfg_.vocab = emb->shape[0];
+  cfg_.d_model = emb->shape[1];
+  cfg_.d_inner = a0->shape[0];
+  cfg_.d_state = a0->shape[1];
+  cfg_.d_conv = cv0->shape[2];
+  if (xp0->shape[0] < 2 * cfg_.d_state) {
+    err = "x_proj is narrower than 2 * d_state";
+    return false;
+  }
+  cfg_.dt_rank = xp0->shape[0] - 2 * cfg_.d_state;
+  if (cfg_.d_state > static_cast<std::size_t>(kMaxState) || cfg_.dt_rank > static_cast<std::size_t>(kMaxRank) ||
+      cfg_.d_model % 8 != 0 || cfg_.d_inner % 8 != 0) {
+    err = "Mamba dimensions outside this build's limits (d_state <= 16, dt_rank <= 64)";
+    return false;
+  }
+  const std::size_t dm = cfg_.d_model, di = cfg_.d_inner, ds = cfg_.d_state, dc = cfg_.d_conv, dr = cfg_.dt_rank;
+  std::size_t n = 0;
+  while (n < 64 && t.find("backbone.layers." + std::to_string(n) + ".norm.weight") != nullptr) ++n;
+  cfg_.n_layers = n;
+  if (n == 0) {
+    err = "no Mamba layers";
+    return false;
+  }
+  const bool bf = prec_ == Precision::kBF16;
+  auto mat_bytes = [&](std::size_t rows, std::size_t cols) {
+    const std::size_t rp = (rows + 127) / 128 * 128, cp = (cols + 63) / 64 * 64;
+    return rp * cp * (bf ? 2 : 4) + ((cp + 255) / 256) * sizeof(SimtSlice) + 512;
+  };
+  ArenaPlan plan;
+  plan.add_n<float>(cfg_.vocab * dm + dm);
+  for (std::size_t i = 0; i < n; ++i) {
+    plan.add(mat_bytes(2 * di, dm));
+    plan.add(mat_bytes(dr + 2 * ds, di));
+    plan.add(mat_bytes(dm, di));
+    plan.add_n<float>(dm + di * dc + di + di * dr + di + ds * di + di);
+  }
+  if (!wts_.init(plan.total(), err)) return false;
+  auto get = [&](std::size_t layer, const std::string& sub, std::initializer_list<std::size_t> shape,
+                 bool allow_bf16, std::vector<float>& out) {
+    const std::string name = "backbone.layers." + std::to_string(layer) + "." + sub;
+    const HostTensor* h = t.find(name);
+    if (h == nullptr || h->ndim != static_cast<int>(shape.size()) || (!allow_bf16 && h->dtype != DType::F32)) {
+      err = "tensor " + name + " missing or malformed";
+      return false;
+    }
+    int i = 0;
+    for (std::size_t s : shape)
+      if (h->shape[static_cast<std::size_t>(i++)] != s) {
+        err = "tensor " + name + " has an unexpected shape";
+        return false;
+      }
+    out = widen_f32(*h);
+    return true;
+  };
+  auto put = [&](const std::vector<float>& h) {
+    float* d = wts_.take_n<float>(h.size());
+    cudaMemcpy(d, h.data(), h.size() * 4, cudaMemcpyHostToDevice);
+    return d;
+  };
+  auto put_mat = [&](const std::vector<float>& w, int rows, int cols, Mat& m) {
+    m.rows = rows;
+    m.cols = cols;
+    m.rows_pad = (rows + 127) / 128 * 128;
+    m.cols_pad = (cols + 63) / 64 * 64;
+    std::vector<float> padded(static_cast<std::size_t>(m.rows_pad) * m.cols_pad, 0.0f);
+    for (int r = 0; r < rows; ++r)
+      std::memcpy(&padded[static_cast<std::size_t>(r) * m.cols_pad], &w[static_cast<std::size_t>(r) * cols],
+                  static_cast<std::size_t>(cols) * 4);
+    if (bf) {
+      std::vector<std::uint16_t> hb(padded.size());
+      for (std::size_t i = 0; i < hb.size(); ++i) hb[i] = bf16_of(padded[i]);
+      m.w = wts_.take(hb.size() * 2);
+      cudaMemcpy(m.w, hb.data(), hb.size() * 2, cudaMemcpyHostToDevice);
+    } else {
+      m.w = put(padded);
+    }
+    std::vector<SimtSlice> sl;
+    for (int c = 0; c < m.cols_pad; c += 256) sl.push_back(SimtSlice{0, 0, c, std::min(256, m.cols_pad - c), c});
+    m.nslices = static_cast<int>(sl.size());
+    m.slices = wts_.take_n<SimtSlice>(sl.size());
+    cudaMemcpy(m.slices, sl.data(), sl.size() * sizeof(SimtSlice), cudaMemcpyHostToDevice);
+  };
+  emb_ = put(widen_f32(*emb));
+  {
+    const HostTensor* nfw = t.find("backbone.norm_f.weight");
+    if (nfw->ndim != 1 || nfw->shape[0] != dm || nfw->dtype != DType::F32) {
+      err = "backbone.norm_f.weight malformed";
+      return false;
+    }
+    norm_f_ = put(widen_f32(*nfw));
+  }
+  layers_.resize(n);
+  for (std::size_t i = 0; i < n; ++i) {
+    Layer& L = layers_[i];
+    std::vector<float> v;
+    if (!get(i, "norm.weight", {dm}, false, v)) return false;
+    L.norm = put(v);
+    if (!get(i, "mixer.in_proj.weight", {2 * di, dm}, true, v)) return false;
+    put_mat(v, static_cast<int>(2 * di), static_cast<int>(dm), L.in_proj);
+    if (!get(i, "mixer.conv1d.weight", {di, 1, dc}, false, v)) return false;
+    L.conv_w = put(v);
+    if (!get(i, "mixer.conv1d.bias", {di}, false, v)) return false;
+    L.conv_b = put(v);
+    if (!get(i, "mixer.x_proj.weight", {dr + 2 * ds, di}, true, v)) return false;
+    put_mat(v, static_cast<int>(dr + 2 * ds), static_cast<int>(di), L.x_proj);
+    if (!get(i, "mixer.dt_proj.weight", {di, dr}, true, v)) return false;
+    if (bf) {  // the bf16 mode rounds every projection weight
+      for (float& x : v) {
+        const std::uint32_t bits = static_cast<std::uint32_t>(bf16_of(x)) << 16;
+        std::memcpy(&x, &bits, 4);
+      }
+    }
+    L.dt_w = put(v);
+    if (!get(i, "mixer.dt_proj.bias", {di}, false, v)) return false;
+    L.dt_b = put(v);
+    if (!get(i, "mixer.A_log", {di, ds}, false, v)) return false;
+    std::vector<float> an(ds * di);
+    for (std::size_t s = 0; s < ds; ++s)
+      for (std::size_t c = 0; c < di; ++c) an[s * di + c] = -std::exp(v[c * ds + s]);
+    L.a_neg = put(an);
+    if (!get(i, "mixer.D", {di}, false, v)) return false;
+    L.d = put(v);
+    if (!get(i, "mixer.out_proj.weight", {dm, di}, true, v)) return false;
+    put_mat(v, static_cast<int>(dm), static_cast<int>(di), L.out_proj);
+  }
+  cudaFuncSetAttribute(scan_kernel<16, 32>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+  cudaFuncSetAttribute(scan_kernel<8, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+  cudaFuncSetAttribute(scan_kernel<4, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+  if (cudaDeviceSynchronize() != cudaSuccess) {
+    err = "Mamba weight upload failed";
+    return false;
+  }
+  return true;
+}
+
+int Mamba::reserve(std::size_t batch, std::size_t max_len, std::string& err) noexcept {
+  if (batch == 0) batch = 1;
+  if (max_len == 0) max_len = 512;
+  const std::size_t tokens = batch * max_len;
+  if (tokens <= cap_tokens_ && batch <= cap_batch_) return 0;
+  const std::size_t dm = cfg_.d_model, di = cfg_.d_inner, wd = cfg_.dt_rank + 2 * cfg_.d_state;
+  const std::size_t rows = (tokens + 255) / 256 * 256;
+  std::size_t nsl = 1;
+  for (const Layer& L : layers_)
+    nsl = std::max({nsl, static_cast<std::size_t>(L.in_proj.nslices), static_cast<std::size_t>(L.x_proj.nslices),
+                    static_cast<std::size_t>(L.out_proj.nslices)});
+  // split-K partials are only used on the CUDA-core path (short inputs)
+  const std::size_t simt_tokens = std::min<std::size_t>(tokens, 4096);
+  part_elems_ = nsl * simt_tokens * 2 * di;
+  ArenaPlan plan;
+  plan.add_n<int>(rows);
+  plan.add_n<float>(rows * dm);       // hidden
+  plan.add_n<float>(rows * 2 * di);   // xz
+  plan.add_n<float>(rows * di);       // u
+  plan.add_n<float>(rows * wd);       // dbl
+  plan.add_n<float>(rows * di);       // y
+  plan.add_n<float>(part_elems_);
+  plan.add_n<float>(batch * dm);      // last
+  plan.add_n<float>(rows * dm);       // out
+  plan.add_n<__nv_bfloat16>(rows * dm);
+  plan.add_n<__nv_bfloat16>(rows * di);
+  plan.add_n<__nv_bfloat16>(rows * di);
+  plan.add_n<float>(state_floats());
+  plan.add_n<float>(dm + 2 * di + di + wd + di + di + dm + 64);
+  // keep the decode state across a re-reserve
+  std::vector<float> saved;
+  if (state_ != nullptr) {
+    saved.resize(state_floats());
+    cudaMemcpy(saved.data(), state_, saved.size() * 4, cudaMemcpyDeviceToHost);
+  }
+  ws_.release();
+  if (!ws_.init(plan.total(), err)) {
+    cap_tokens_ = 0;
+    return 2;
+  }
+  tokens_ = ws_.take_n<int>(rows);
+  hidden_ = ws_.take_n<float>(rows * dm);
+  xz_ = ws_.take_n<float>(rows * 2 * di);
+  u_ = ws_.take_n<float>(rows * di);
+  dbl_ = ws_.take_n<float>(rows * wd);
+  y_ = ws_.take_n<float>(rows * di);
+  part_ = ws_.take_n<float>(part_elems_);
+  last_ = ws_.take_n<float>(batch * dm);
+  out_ = ws_.take_n<float>(rows * dm);
+  nb_ = ws_.take_n<__nv_bfloat16>(rows * dm);
+  ub_ = ws_.take_n<__nv_bfloat16>(rows * di);
+  yb_ = ws_.take_n<__nv_bfloat16>(rows * di);
+  state_ = ws_.take_n<float>(state_floats());
+  dh_ = ws_.take_n<float>(dm + 2 * di + di + wd + di + di + dm + 64);
+  cudaMemset(tokens_, 0, ws_.used());
+  if (!saved.empty()) cudaMemcpy(state_, saved.data(), saved.size() * 4, cudaMemcpyHostToDevice);
+  const std::size_t need = tokens * (dm + 1) + state_floats();
+  if (pinned_floats_ < need) {
+    if (pinned_ != nullptr) cudaFreeHost(pinned_);
+    pinned_ = nullptr;
+    if (counted_host_malloc(reinterpret_cast<void**>(&pinned_), need * 4) != cudaSuccess) {
+      err = "pinned host allocation failed";
+      return 2;
+    }
+    pinned_floats_ = need;
+  }
+  cap_tokens_ = tokens;
+  cap_batch_ = batch;
+  cap_rows_ = rows;
+  return cudaDeviceSynchronize() == cudaSuccess ? 0 : 2;
+}
+
+bool Mamba::gemm(const Mat& m, const void* in, int in_ld, long long n_tok, float* out, int out_ld, bool accumulate,
+                 bool tc, cudaStream_t st, std::string& err) {
+  if (tc) {
+    TcLaunch l;
+    l.A = m.w;
+    l.M_rows = m.rows_pad;
+    l.K = m.cols_pad;
+    l.src[0] = TcSource{in, in_ld, 1, static_cast<int>(cap_rows_)};
+    l.L = 1;
+    l.n_samples = static_cast<int>(n_tok);
+    l.m_valid = m.rows;
+    l.segs = {tc::Seg{0, 0, 0, m.cols_pad / 64, 0}};
+    l.out_f32 = true;
+    l.out_accumulate = accumulate;
+    l.out = out;
+    l.out_ld = out_ld;
+    return tc_gemm(l, *ctx_, st, err) == cudaSuccess;
+  }
+  // CUDA-core path, chunks of <= 4096 tokens through the partial buffer
+  for (long long t0 = 0; t0 < n_tok; t0 += 4096) {
+    const long long nt_tok = std::min<long long>(4096, n_tok - t0);
+    SimtConvParams p{};
+    p.W = m.w;
+    p.M = m.rows;
+    p.K = m.cols_pad;
+    p.src[0] = SimtSource{static_cast<const float*>(in) + t0 * in_ld, in_ld, 1};
+    p.stride = 1;
+    p.L_out = 1;
+    p.n_tokens = static_cast<int>(nt_tok);
+    p.slices = m.slices;
+    p.partial = part_;
+    const int nt = p.n_tokens >= 16 ? 16 : (p.n_tokens >= 8 ? 8 : 4);
+    const dim3 grid(static_cast<unsigned>(m.nslices), static_cast<unsigned>((m.rows + 127) / 128),
+                    static_cast<unsigned>((p.n_tokens + nt - 1) / nt));
+    const bool bf = prec_ == Precision::kBF16;
+    if (nt == 16) bf ? simt_conv_kernel<16, true><<<grid, 128, 0, st>>>(p) : simt_conv_kernel<16, false><<<grid, 128, 0, st>>>(p);
+    else if (nt == 8) bf ? simt_conv_kernel<8, true><<<grid, 128, 0, st>>>(p) : simt_conv_kernel<8, false><<<grid, 128, 0, st>>>(p);
+    else bf ? simt_conv_kernel<4, true><<<grid, 128, 0, st>>>(p) : simt_conv_kernel<4, false><<<grid, 128, 0, st>>>(p);
+    ReduceParams r{};
+    r.partial = part_;
+    r.nslices = m.nslices;
+    r.n_tokens = p.n_tokens;
+    r.M = m.rows;
+    r.act = 0;
+    r.out = out + t0 * out_ld;
+    r.out_ld = out_ld;
+    r.accumulate = accumulate ? 1 : 0;
+    reduce_partials_kernel<<<ew_grid(nt_tok * m.rows, 256, *ctx_), 256, 0, st>>>(r);
+  }
+  return cudaGetLastError() == cudaSuccess;
+}
+
+bool Mamba::run_layers(long long n_tok, int B, int L, bool tc, cudaStream_t st, std::string& err) {
+  const int dm = static_cast<int>(cfg_.d_model), di = static_cast<int>(cfg_.d_inner);
+  const int ds = static_cast<int>(cfg_.d_state), dc = static_cast<int>(cfg_.d_conv);
+  const int dr = static_cast<int>(cfg_.dt_rank), wd = dr + 2 * ds;
+  float* normed = out_;  // fp32 normed rows share the output buffer until the final norm
+  for (const Layer& Ly : layers_) {
+    rmsnorm_kernel<<<static_cast<unsigned>((n_tok * 32 + 255) / 256), 256, 0, st>>>(hidden_, Ly.norm,
+                                                                                      static_cast<int>(n_tok), dm,
+                                                                                      tc ? nullptr : normed,
+                                                                                      tc ? nb_ : nullptr);
+    if (!gemm(Ly.in_proj, tc ? static_cast<const void*>(nb_) : normed, dm, n_tok, xz_, 2 * di, false, tc, st, err))
+      return false;
+    causal_conv_kernel<<<ew_grid(n_tok * di, 256, *ctx_), 256, 0, st>>>(xz_, B, L, di, dc, Ly.conv_w, Ly.conv_b, u_,
+                                                                        tc ? ub_ : nullptr);
+    if (!gemm(Ly.x_proj, tc ? static_cast<const void*>(ub_) : u_, di, n_tok, dbl_, wd, false, tc, st, err))
+      return false;
+    const dim3 grid(static_cast<unsigned>((di + 255) / 256), static_cast<unsigned>(B));
+    const std::size_t smem = static_cast<std::size_t>(L) * wd * 4;
+    if (ds == 16 && dr == 32)
+      scan_kernel<16, 32><<<grid, 256, smem, st>>>(dbl_, wd, u_, xz_, L, di, Ly.dt_w, Ly.dt_b, Ly.a_neg, Ly.d, nullptr,
+                                                   y_, tc ? yb_ : nullptr);
+    else if (ds == 4 && dr == 4)
+      scan_kernel<4, 4><<<grid, 256, smem, st>>>(dbl_, wd, u_, xz_, L, di, Ly.dt_w, Ly.dt_b, Ly.a_neg, Ly.d, nullptr, y_,
+                                                 tc ? yb_ : nullptr);
+    else if (ds == 8 && dr == 4)
+      scan_kernel<8, 4><<<grid, 256, smem, st>>>(dbl_, wd, u_, xz_, L, di, Ly.dt_w, Ly.dt_b, Ly.a_neg, Ly.d, nullptr, y_,
+                                                 tc ? yb_ : nullptr);
+    else {
+      err = "no scan instantiation for this (d_state, dt_rank)";
+      return false;
+    }
+    if (!gemm(Ly.out_proj, tc ? static_cast<const void*>(yb_) : y_, di, n_tok, hidden_, dm, true, tc, st, err))
+      return false;
+  }
+  rmsnorm_kernel<<<static_cast<unsigned>((n_tok * 32 + 255) / 256), 256, 0, st>>>(hidden_, norm_f_,
+                                                                                    static_cast<int>(n_tok), dm, out_,
+                                                                                    nullptr);
+  return cudaGetLastError() == cudaSuccess;
+}
+
+int Mamba::forward_device(const std::int32_t* tokens, std::size_t batch, std::size_t len, float* last_hidden,
+                          void* stream, std::string& err) noexcept {
+  const long long n_tok = static_cast<long long>(batch * len);
+  if (batch * len > cap_tokens_ || batch > cap_batch_) {
+    err = "batch * sequence exceeds the reserved capacity";
+    return 2;
+  }
+  cudaSetDevice(ctx_->device);
+  cudaStream_t st = stream != nullptr ? static_cast<cudaStream_t>(stream) : ctx_->stream;
+  const bool tc = prec_ == Precision::kBF16 && n_tok >= kTcMinTokens;
+  if (tokens != tokens_) cudaMemcpyAsync(tokens_, tokens, n_tok * 4, cudaMemcpyDeviceToDevice, st);
+  const int dm = static_cast<int>(cfg_.d_model);
+  embed_kernel<<<ew_grid(n_tok * dm, 256, *ctx_), 256, 0, st>>>(tokens_, n_tok, emb_, dm, hidden_);
+  if (!run_layers(n_tok, static_cast<int>(batch), static_cast<int>(len), tc, st, err)) return 2;
+  gather_last_kernel<<<ew_grid(static_cast<long long>(batch) * dm, 256, *ctx_), 256, 0, st>>>(
+      out_, static_cast<int>(batch), static_cast<int>(len), dm, last_hidden != nullptr ? last_hidden : last_);
+  return cudaGetLastError() == cudaSuccess ? 0 : 2;
+}
+
+int Mamba::forward(const std::int32_t* tokens, std::size_t batch, std::size_t len, float* hidden, bool last_only,
+                   std::string& err) noexcept {
+  if ((batch * len > cap_tokens_ || batch > cap_batch_) && reserve(batch, std::max<std::size_t>(len, 512), err) != 0)
+    return 2;
+  cudaSetDevice(ctx_->device);
+  cudaStream_t st = ctx_->stream;
+  const long long n_tok = static_cast<long long>(batch * len);
+  auto* ptok = reinterpret_cast<std::int32_t*>(pinned_);
+  std::memcpy(ptok, tokens, n_tok * 4);
+  cudaMemcpyAsync(tokens_, ptok, n_tok * 4, cudaMemcpyHostToDevice, st);
+  if (forward_device(tokens_, batch, len, nullptr, st, err) != 0) return 2;
+  const std::size_t dm = cfg_.d_model;
+  float* ph = pinned_ + n_tok;
+  if (!last_only && hidden != nullptr) cudaMemcpyAsync(ph, out_, n_tok * dm * 4, cudaMemcpyDeviceToHost, st);
+  if (cudaStreamSynchronize(st) != cudaSuccess) {
+    err = std::string("Mamba forward failed: ") + cudaGetErrorString(cudaGetLastError());
+    return 2;
+  }
+  if (take_device_error(*ctx_, st) != 0) {
+    err = "a device pipeline wait timed out";
+    return 2;
+  }
+  if (!last_only && hidden != nullptr) std::memcpy(hidden, ph, n_tok * dm * 4);
+  return 0;
+}
+
+int Mamba::step(std::int32_t token, float* out, std::string& err) noexcept {
+  cudaSetDevice(ctx_->device);
+  cudaStream_t st = ctx_->stream;
+  const int dm = static_cast<int>(cfg_.d_model), di = static_cast<int>(cfg_.d_inner);
+  const int ds = static_cast<int>(cfg_.d_state), dc = static_cast<int>(cfg_.d_conv);
+  const int dr = static_cast<int>(cfg_.dt_rank), wd = dr + 2 * ds;
+  float* x = dh_;                // [dm] hidden
+  float* xz = x + dm;            // [2 di]
+  float* u = xz + 2 * di;        // [di]
+  float* dbl = u + di;           // [wd]
+  float* y = dbl + wd;           // [di]
+  float* normed = y + di + di;   // [dm]
+  auto* tok = reinterpret_cast<int*>(pinned_);
+  *tok = token;
+  cudaMemcpyAsync(tokens_, tok, 4, cudaMemcpyHostToDevice, st);
+  embed_kernel<<<1, 256, 0, st>>>(tokens_, 1, emb_, dm, x);
+  const std::size_t per = static_cast<std::size_t>(di) * (dc + ds);
+  for (std::size_t li = 0; li < layers_.size(); ++li) {
+    const Layer& Ly = layers_[li];
+    float* window = state_ + li * per;
+    float* h = window + static_cast<std::size_t>(di) * dc;
+    rmsnorm_kernel<<<1, 32, 0, st>>>(x, Ly.norm, 1, dm, normed, nullptr);
+    if (!gemm(Ly.in_proj, normed, dm, 1, xz, 2 * di, false, false, st, err)) return 2;
+    conv_step_kernel<<<(di + 255) / 256, 256, 0, st>>>(xz, di, dc, window, Ly.conv_w, Ly.conv_b, u);
+    if (!gemm(Ly.x_proj, u, di, 1, dbl, wd, false, false, st, err)) return 2;
+    const dim3 grid(static_cast<unsigned>((di + 255) / 256), 1);
+    const std::size_t smem = static_cast<std::size_t>(wd) * 4;
+    if (ds == 16 && dr == 32)
+      scan_kernel<16, 32><<<grid, 256, smem, st>>>(dbl, wd, u, xz, 1, di, Ly.dt_w, Ly.dt_b, Ly.a_neg, Ly.d, h, y, nullptr);
+    else if (ds == 4 && dr == 4)
+      scan_kernel<4, 4><<<grid, 256, smem, st>>>(dbl, wd, u, xz, 1, di, Ly.dt_w, Ly.dt_b, Ly.a_neg, Ly.d, h, y, nullptr);
+    else if (ds == 8 && dr == 4)
+      scan_kernel<8, 4><<<grid, 256, smem, st>>>(dbl, wd, u, xz, 1, di, Ly.dt_w, Ly.dt_b, Ly.a_neg, Ly.d, h, y, nullptr);
+    else {
+      err = "no scan instantiation for this (d_state, dt_rank)";
+      return 2;
+    }
+    if (!gemm(Ly.out_proj, y, di, 1, x, dm, true, false, st, err)) return 2;
+  }
+  rmsnorm_kernel<<<1, 32, 0, st>>>(x, norm_f_, 1, dm, normed, nullptr);
+  float* ph = pinned_ + 1;
+  cudaMemcpyAsync(ph, normed, dm * 4, cudaMemcpyDeviceToHost, st);
+  if (cudaStreamSynchronize(st) != cudaSuccess) {
+    err = std::string("Mamba step failed: ") + cudaGetErrorString(cudaGetLastError());
+    return 2;
+  }
+  std::memcpy(out, ph, dm * 4);
+  return 0;
+}
+
+void Mamba::reset() noexcept {
+  cudaSetDevice(ctx_->device);
+  cudaMemsetAsync(state_, 0, state_floats() * 4, ctx_->stream);
+  cudaStreamSynchronize(ctx_->stream);
+}
+
+int Mamba::read_state(float* dst, std::string& err) noexcept {
+  cudaSetDevice(ctx_->device);
+  if (cudaMemcpyAsync(pinned_, state_, state_floats() * 4, cudaMemcpyDeviceToHost, ctx_->stream) != cudaSuccess ||
+      cudaStreamSynchronize(ctx_->stream) != cudaSuccess) {
+    err = "decode state copy failed";
+    return 2;
+  }
+  std::memcpy(dst, pinned_, state_floats() * 4);
+  return 0;
+}
+
+int Mamba::write_state(const float* src, std::string& err) noexcept {
+  cudaSetDevice(ctx_->device);
+  std::memcpy(pinned_, src, state_floats() * 4);
+  if (cudaMemcpyAsync(state_, pinned_, state_floats() * 4, cudaMemcpyHostToDevice, ctx_->stream) != cudaSuccess ||
+      cudaStreamSynchronize(ctx_->stream) != cudaSuccess) {
+    err = "decode state copy failed";
+    return 2;
+  }
+  return 0;
+}
+
+}  // namespace
+
+std::unique_ptr<MambaDevice> make_mamba_device(const TensorTable& tensors, std::shared_ptr<DeviceContext> ctx,
+                                               Precision precision, std::string& err) {
+  cudaSetDevice(ctx->device);
+  auto m = std::make_unique<Mamba>(std::move(ctx), precision);
+  if (!m->load(tensors, err)) return nullptr;
+  return m;
+}
+
+}  // namespace feb

@@ -1,0 +1,256 @@
+#include <cstring>
+#include <mutex>
+
+#include "runtime.cuh"
+
+namespace feb {
+namespace {
+
+std::atomic<std::uint64_t> g_device_mallocs{0};
+std::atomic<std::uint64_t> g_host_mallocs{0};
+
+using EncodeTiled = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                 const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                 CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiled encode_fn() {
+  static EncodeTiled fn = [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult status{};
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &status) != cudaSuccess ||
+        status != cudaDriverEntryPointSuccess)
+      ptr = nullptr;
+    return reinterpret_cast<EncodeTiled>(ptr);
+  }();
+  return fn;
+}
+
+bool encode_2d(CUtensorMap* map, const void* ptr, std::uint64_t inner, std::uint64_t outer, std::uint32_t box_inner,
+               std::uint32_t box_outer, std::string& err) {
+  const cuuint64_t dims[2] = {inner, outer};
+  const cuuint64_t strides[1] = {inner * 2};
+  const cuuint32_t box[2] = {box_inner, box_outer};
+  const cuuint32_t estr[2] = {1, 1};
+  const CUresult rc = encode_fn()(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides,
+                                  box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (rc != CUDA_SUCCESS) {
+    err = "cuTensorMapEncodeTiled (weights) failed: " + std::to_string(static_cast<int>(rc));
+    return false;
+  }
+  return true;
+}
+
+bool encode_3d(CUtensorMap* map, const TcSource& s, std::uint32_t box_l, std::uint32_t box_s, std::string& err) {
+  const cuuint64_t dims[3] = {static_cast<cuuint64_t>(s.channels), static_cast<cuuint64_t>(s.length),
+                              static_cast<cuuint64_t>(s.samples)};
+  const cuuint64_t strides[2] = {static_cast<cuuint64_t>(s.channels) * 2,
+                                 static_cast<cuuint64_t>(s.channels) * s.length * 2};
+  const cuuint32_t box[3] = {64, box_l, box_s};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  const CUresult rc = encode_fn()(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(s.ptr), dims, strides,
+                                  box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (rc != CUDA_SUCCESS) {
+    err = "cuTensorMapEncodeTiled (activations) failed: " + std::to_string(static_cast<int>(rc));
+    return false;
+  }
+  return true;
+}
+
+}  // namespace
+
+std::uint64_t device_malloc_count() noexcept { return g_device_mallocs.load(); }
+std::uint64_t host_malloc_count() noexcept { return g_host_mallocs.load(); }
+
+cudaError_t counted_malloc(void** ptr, std::size_t bytes) {
+  g_device_mallocs.fetch_add(1);
+  return cudaMalloc(ptr, bytes);
+}
+
+cudaError_t counted_host_malloc(void** ptr, std::size_t bytes) {
+  g_host_mallocs.fetch_add(1);
+  return cudaMallocHost(ptr, bytes);
+}
+
+DeviceContext::~DeviceContext() {
+  if (stream != nullptr) {
+    cudaSetDevice(device);
+    cudaStreamSynchronize(stream);
+    cudaStreamDestroy(stream);
+  }
+  if (d_err != nullptr) cudaFree(d_err);
+}
+
+std::shared_ptr<DeviceContext> make_device_context(int device, std::string& err) {
+  int count = 0;
+  if (cudaGetDeviceCount(&count) != cudaSuccess || count == 0) {
+    cudaGetLastError();
+    err = "no CUDA device is available (this library has no CPU fallback)";
+    return nullptr;
+  }
+  if (device < 0 || device >= count) {
+    err = "FLOWEDGE_DEVICE is out of range";
+    return nullptr;
+  }
+  cudaDeviceProp prop{};
+  if (cudaGetDeviceProperties(&prop, device) != cudaSuccess) {
+    err = "cudaGetDeviceProperties failed";
+    return nullptr;
+  }
+  if (prop.major != 10 || prop.minor != 0) {
+    err = "this library is built for sm_100a (B200); found compute capability " + std::to_string(prop.major) + "." +
+          std::to_string(prop.minor);
+    return nullptr;
+  }
+  if (encode_fn() == nullptr) {
+    err = "driver entry point cuTensorMapEncodeTiled is unavailable";
+    return nullptr;
+  }
+  auto ctx = std::make_shared<DeviceContext>();
+  ctx->device = device;
+  ctx->sm_count = prop.multiProcessorCount;
+  cudaSetDevice(device);
+  if (cudaStreamCreateWithFlags(&ctx->stream, cudaStreamNonBlocking) != cudaSuccess) {
+    err = "cudaStreamCreate failed";
+    return nullptr;
+  }
+  if (counted_malloc(reinterpret_cast<void**>(&ctx->d_err), 256) != cudaSuccess ||
+      cudaMemset(ctx->d_err, 0, 256) != cudaSuccess) {
+    err = "device allocation failed";
+    return nullptr;
+  }
+  if (cudaFuncSetAttribute(tc::tc_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, tc::SMEM_BYTES) !=
+      cudaSuccess) {
+    err = "cannot enable the tensor-core kernel's shared memory";
+    return nullptr;
+  }
+  return ctx;
+}
+
+int context_device(const DeviceContext& ctx) noexcept { return ctx.device; }
+
+int synchronize_context(DeviceContext& ctx) noexcept {
+  cudaSetDevice(ctx.device);
+  if (cudaStreamSynchronize(ctx.stream) != cudaSuccess) return 2;
+  return take_device_error(ctx, ctx.stream) == 0 ? 0 : 2;
+}
+
+int take_device_error(DeviceContext& ctx, cudaStream_t stream) {
+  int host = 0;
+  if (cudaMemcpyAsync(&host, ctx.d_err, sizeof(int), cudaMemcpyDeviceToHost, stream) != cudaSuccess) return -1;
+  if (cudaStreamSynchronize(stream) != cudaSuccess) return -1;
+  if (host != 0) cudaMemsetAsync(ctx.d_err, 0, sizeof(int), stream);
+  return host;
+}
+
+DeviceArena::~DeviceArena() { release(); }
+
+bool DeviceArena::init(std::size_t bytes, std::string& err) {
+  release();
+  if (bytes == 0) bytes = 256;
+  if (counted_malloc(reinterpret_cast<void**>(&base_), bytes) != cudaSuccess) {
+    cudaGetLastError();
+    base_ = nullptr;
+    err = "device allocation of " + std::to_string(bytes >> 20) + " MiB failed";
+    return false;
+  }
+  size_ = bytes;
+  used_ = 0;
+  return true;
+}
+
+void* DeviceArena::take(std::size_t bytes) {
+  const std::size_t aligned = (bytes + 255) & ~std::size_t(255);
+  if (base_ == nullptr || used_ + aligned > size_) return nullptr;
+  void* p = base_ + used_;
+  used_ += aligned;
+  return p;
+}
+
+void DeviceArena::release() noexcept {
+  if (base_ != nullptr) cudaFree(base_);
+  base_ = nullptr;
+  size_ = used_ = 0;
+}
+
+std::vector<float> widen_f32(const HostTensor& t) {
+  std::vector<float> out(t.numel());
+  if (t.dtype == DType::F32) {
+    std::memcpy(out.data(), t.data, out.size() * sizeof(float));
+  } else {
+    const auto* bits = static_cast<const std::uint16_t*>(t.data);
+    for (std::size_t i = 0; i < out.size(); ++i) {
+      const std::uint32_t w = static_cast<std::uint32_t>(bits[i]) << 16;
+      std::memcpy(&out[i], &w, sizeof(float));
+    }
+  }
+  return out;
+}
+
+cudaError_t tc_gemm(const TcLaunch& l, DeviceContext& ctx, cudaStream_t stream, std::string& err) {
+  if (l.M_rows % tc::BM != 0 || l.K % tc::BK != 0 || l.L < 1 || l.L > tc::BN || (l.L & (l.L - 1)) != 0 ||
+      l.segs.empty() || static_cast<int>(l.segs.size()) > tc::MAX_SEGS) {
+    err = "tc_gemm: unsupported geometry";
+    return cudaErrorInvalidValue;
+  }
+  tc::Params p{};
+  p.L = l.L;
+  p.tile_samples = tc::BN / l.L;
+  if (l.stats != nullptr && (p.tile_samples > tc::MAX_TILE_SAMPLES || l.group_ch % 32 != 0 ||
+                             (l.group_ch > tc::BM && l.group_ch % tc::BM != 0) ||
+                             (l.group_ch < tc::BM && tc::BM % l.group_ch != 0))) {
+    err = "tc_gemm: unsupported GroupNorm geometry";
+    return cudaErrorInvalidValue;
+  }
+  p.n_tiles_m = l.M_rows / tc::BM;
+  p.n_tiles_n = (l.n_samples + p.tile_samples - 1) / p.tile_samples;
+  p.total_tiles = p.n_tiles_m * p.n_tiles_n;
+  p.n_samples = l.n_samples;
+  p.m_valid = l.m_valid;
+  p.nseg = static_cast<int>(l.segs.size());
+  for (int i = 0; i < p.nseg; ++i) {
+    p.seg[i] = l.segs[static_cast<std::size_t>(i)];
+    const TcSource& s = l.src[p.seg[i].src];
+    if (s.ptr == nullptr || s.channels % 64 != 0 || s.length != l.L || s.samples < p.tile_samples ||
+        p.seg[i].ch_off % 64 != 0 || p.seg[i].ch_off + p.seg[i].kblocks * 64 > s.channels ||
+        p.seg[i].a_k + p.seg[i].kblocks * 64 > l.K) {
+      err = "tc_gemm: segment does not fit its source";
+      return cudaErrorInvalidValue;
+    }
+  }
+  p.bias = l.bias;
+  p.add_vec = l.add_vec;
+  p.add_tok = l.add_tok;
+  p.add_ld = l.add_ld;
+  p.act = l.act;
+  p.out_f32 = l.out_f32 ? 1 : 0;
+  p.out_accumulate = l.out_accumulate ? 1 : 0;
+  p.out = l.out;
+  p.out_ld = l.out_ld;
+  p.out_rps = l.out_rps;
+  p.out_tmul = l.out_tmul;
+  p.out_tadd = l.out_tadd;
+  p.out_ch_off = l.out_ch_off;
+  p.stats = l.stats;
+  p.group_ch = l.group_ch;
+  p.groups = l.groups;
+  p.parts = l.group_ch > tc::BM ? l.group_ch / tc::BM : 1;
+  p.err = ctx.d_err;
+
+  CUtensorMap ta{}, tb[3]{};
+  if (!encode_2d(&ta, l.A, static_cast<std::uint64_t>(l.K), static_cast<std::uint64_t>(l.M_rows), 64, tc::BM, err))
+    return cudaErrorInvalidValue;
+  for (int i = 0; i < 3; ++i) {
+    const TcSource& s = l.src[i].ptr != nullptr ? l.src[i] : l.src[0];
+    if (!encode_3d(&tb[i], s, static_cast<std::uint32_t>(l.L), static_cast<std::uint32_t>(p.tile_samples), err))
+      return cudaErrorInvalidValue;
+  }
+  const int grid = p.total_tiles < ctx.sm_count ? p.total_tiles : ctx.sm_count;
+  tc::tc_gemm_kernel<<<grid, tc::THREADS, tc::SMEM_BYTES, stream>>>(ta, tb[0], tb[1], tb[2], p);
+  const cudaError_t rc = cudaGetLastError();
+  if (rc != cudaSuccess) err = std::string("tc_gemm launch: ") + cudaGetErrorString(rc);
+  return rc;
+}
+
+}  // namespace feb

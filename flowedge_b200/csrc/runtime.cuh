@@ -1,0 +1,116 @@
+// CUDA-side runtime shared by the head modules: device context, counted
+// allocations, a bump arena over one allocation, TMA descriptor encoding and
+// the launcher of the tcgen05 GEMM.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <string>
+#include <vector>
+
+#include "device.h"
+#include "tc_gemm.cuh"
+
+namespace feb {
+
+struct DeviceContext {
+  int device = 0;
+  cudaStream_t stream = nullptr;
+  int sm_count = 0;
+  int* d_err = nullptr;  // device error word written by kernels (never trapped)
+  ~DeviceContext();
+};
+
+// cudaMalloc / cudaFree with the allocation counter.
+cudaError_t counted_malloc(void** ptr, std::size_t bytes);
+cudaError_t counted_host_malloc(void** ptr, std::size_t bytes);
+
+// One device allocation carved by a bump pointer (256-byte aligned pieces).
+class DeviceArena {
+ public:
+  DeviceArena() = default;
+  DeviceArena(const DeviceArena&) = delete;
+  DeviceArena& operator=(const DeviceArena&) = delete;
+  ~DeviceArena();
+  bool init(std::size_t bytes, std::string& err);
+  void* take(std::size_t bytes);
+  template <typename T>
+  T* take_n(std::size_t n) {
+    return static_cast<T*>(take(n * sizeof(T)));
+  }
+  [[nodiscard]] std::size_t used() const noexcept { return used_; }
+  [[nodiscard]] std::size_t size() const noexcept { return size_; }
+  void reset() noexcept { used_ = 0; }
+  void release() noexcept;
+
+ private:
+  char* base_ = nullptr;
+  std::size_t size_ = 0;
+  std::size_t used_ = 0;
+};
+
+// Sizing pass: the same sequence of take() calls against a counting arena.
+class ArenaPlan {
+ public:
+  void add(std::size_t bytes) { total_ += (bytes + 255) & ~std::size_t(255); }
+  template <typename T>
+  void add_n(std::size_t n) {
+    add(n * sizeof(T));
+  }
+  [[nodiscard]] std::size_t total() const noexcept { return total_; }
+
+ private:
+  std::size_t total_ = 0;
+};
+
+// --- tcgen05 GEMM launch ----------------------------------------------------
+
+struct TcSource {
+  const void* ptr = nullptr;  // bf16 [samples][length][channels]
+  int channels = 0;
+  int length = 0;
+  int samples = 0;  // extent of the buffer (>= tile samples)
+};
+
+struct TcLaunch {
+  const void* A = nullptr;  // bf16 [M_rows][K], M_rows multiple of 128, K multiple of 64
+  int M_rows = 0;
+  int K = 0;
+  TcSource src[3];
+  int L = 1;          // tokens per sample in the N tile (power of two <= 256)
+  int n_samples = 0;  // valid samples
+  int m_valid = 0;
+  std::vector<tc::Seg> segs;
+  const float* bias = nullptr;
+  const float* add_vec = nullptr;
+  const float* add_tok = nullptr;
+  int add_ld = 0;
+  int act = tc::kActNone;
+  bool out_f32 = false;
+  bool out_accumulate = false;
+  void* out = nullptr;
+  long long out_ld = 0;
+  int out_rps = 1, out_tmul = 1, out_tadd = 0, out_ch_off = 0;
+  double* stats = nullptr;
+  int group_ch = 0, groups = 0;
+};
+
+cudaError_t tc_gemm(const TcLaunch& launch, DeviceContext& ctx, cudaStream_t stream, std::string& err);
+
+// grid size for grid-stride elementwise kernels
+inline int ew_grid(long long total, int threads, const DeviceContext& ctx) {
+  long long blocks = (total + threads - 1) / threads;
+  const long long cap = static_cast<long long>(ctx.sm_count) * 8;
+  if (blocks > cap) blocks = cap;
+  return static_cast<int>(blocks < 1 ? 1 : blocks);
+}
+
+// Reads and clears the device error word; non-zero means a bounded wait in a
+// kernel gave up.
+int take_device_error(DeviceContext& ctx, cudaStream_t stream);
+
+std::vector<float> widen_f32(const HostTensor& t);
+
+}  // namespace feb

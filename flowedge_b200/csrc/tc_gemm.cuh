@@ -1,0 +1,327 @@
+// Persistent tcgen05 implicit-GEMM for sm_100a.
+//
+//   out[token][m] = epilogue( sum_seg sum_c A[m][seg.a_k + c] * B_seg[token](c) )
+//
+// A is a K-major bf16 weight matrix [M_total][K_total].  B is gathered per
+// "segment": a TMA box of 64 channels from a bf16 activation tensor laid out
+// [samples][length][channels], read at a time offset `t_off` and channel
+// offset `ch_off`.  A 1-D convolution with k taps is k segments (one per tap,
+// t_off = tap - pad); a channel concatenation is one segment per source; a
+// stride-2 convolution reads a [samples][length/2][2*channels] view of its
+// input.  TMA zero-fills rows whose time index falls outside [0, length) and
+// samples beyond the batch, which is exactly the convolution's zero padding.
+//
+// Tile: 128 (M) x 256 (N tokens) x 64 (K) per stage, 4 stages, fp32
+// accumulators double-buffered in TMEM (2 x 256 columns).  Warp roles:
+//   warp 0: TMA producer (one lane)
+//   warp 1: TMEM allocator + MMA issuer (one lane)
+//   warps 2-5: epilogue (TMEM -> registers -> global), one accumulator row
+//              (= one output channel) per thread.
+// Every mbarrier wait is bounded; a timeout sets an error code, raises a
+// shared abort flag, drains in-flight copies/MMAs with bounded waits, frees
+// TMEM and returns.
+#pragma once
+
+#include "common.cuh"
+
+namespace feb {
+namespace tc {
+
+constexpr int BM = 128;
+constexpr int BN = 256;
+constexpr int BK = 64;
+constexpr int STAGES = 4;
+constexpr int A_BYTES = BM * BK * 2;
+constexpr int B_BYTES = BN * BK * 2;
+constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+constexpr int MAX_SEGS = 12;
+constexpr int MAX_TILE_SAMPLES = 64;  // samples per N tile when GN statistics are gathered
+constexpr int THREADS = 192;
+constexpr int TMEM_COLS = 512;
+constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + 256 + 4 * MAX_TILE_SAMPLES * 16;
+
+enum Act : int { kActNone = 0, kActSilu = 1, kActSoftplus = 2 };
+
+struct Seg {
+  int src;      // which B tensor map (0..2)
+  int t_off;    // time offset of the tap
+  int ch_off;   // first channel within the source
+  int kblocks;  // number of 64-channel blocks
+  int a_k;      // K offset of this segment in A
+};
+
+struct Params {
+  int n_tiles_m, n_tiles_n, total_tiles;
+  int L;            // tokens per sample inside an N tile (TMA box length)
+  int tile_samples; // BN / L
+  int n_samples;    // valid samples (tokens of samples >= this are skipped)
+  int m_valid;      // rows >= m_valid are not stored
+  int nseg;
+  Seg seg[MAX_SEGS];
+  // epilogue
+  const float* bias;      // [m] or null
+  const float* add_vec;   // [m] or null
+  const float* add_tok;   // [row][add_ld] fp32 or null (indexed like the output row)
+  int add_ld;
+  int act;
+  int out_f32;            // 1: fp32 output, 0: bf16
+  int out_accumulate;     // fp32 output only: out += value
+  void* out;
+  long long out_ld;       // elements per output row
+  int out_rps;            // output rows per sample
+  int out_tmul, out_tadd; // output row within sample = t * tmul + tadd
+  int out_ch_off;
+  // GroupNorm partial statistics (sum, sum of squares) per (sample, group, part)
+  double* stats;          // null: no statistics
+  int group_ch;           // channels per group (multiple of 32)
+  int groups;             // groups of the layer
+  int parts;              // max(1, group_ch / 128)
+  int* err;
+};
+
+__device__ __forceinline__ void epilogue_store(const Params& p, int tok_b, int tok_t, int m, float v) {
+  const long long row = static_cast<long long>(tok_b) * p.out_rps + tok_t * p.out_tmul + p.out_tadd;
+  const long long idx = row * p.out_ld + p.out_ch_off + m;
+  if (p.out_f32) {
+    float* out = static_cast<float*>(p.out);
+    if (p.out_accumulate) v += out[idx];
+    out[idx] = v;
+  } else {
+    static_cast<__nv_bfloat16*>(p.out)[idx] = __float2bfloat16_rn(v);
+  }
+}
+
+static __global__ void __launch_bounds__(THREADS, 1)
+    tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB0,
+                   const __grid_constant__ CUtensorMap tmB1, const __grid_constant__ CUtensorMap tmB2,
+                   const __grid_constant__ Params p) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
+  uint64_t* empty = full + STAGES;
+  uint64_t* tfull = empty + STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* drain = tempty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  double2* red = reinterpret_cast<double2*>(smem + STAGES * STAGE_BYTES + 256);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull[a], 1);
+      mbar_init(&tempty[a], 128);
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    prefetch_tmap(&tmA);
+    prefetch_tmap(&tmB0);
+    prefetch_tmap(&tmB1);
+    prefetch_tmap(&tmB2);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  const int total_kb = [&] {
+    int n = 0;
+    for (int s = 0; s < p.nseg; ++s) n += p.seg[s].kblocks;
+    return n;
+  }();
+
+  if (warp == 0) {
+    // ---------------- TMA producer ----------------
+    if (lane == 0) {
+      uint32_t kb_iter = 0;
+      int armed[STAGES];
+      for (int s = 0; s < STAGES; ++s) armed[s] = -1;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < p.total_tiles && ok; tile += gridDim.x) {
+        const int m_blk = tile % p.n_tiles_m;
+        const int n_blk = tile / p.n_tiles_m;
+        for (int s = 0; s < p.nseg && ok; ++s) {
+          const Seg sg = p.seg[s];
+          const CUtensorMap* mapB = sg.src == 0 ? &tmB0 : (sg.src == 1 ? &tmB1 : &tmB2);
+          for (int kb = 0; kb < sg.kblocks; ++kb, ++kb_iter) {
+            const int stage = kb_iter % STAGES;
+            const uint32_t phase = (kb_iter / STAGES) & 1;
+            if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag)) {
+              ok = false;
+              break;
+            }
+            uint8_t* a_dst = smem + stage * STAGE_BYTES;
+            uint8_t* b_dst = a_dst + A_BYTES;
+            mbar_arrive_expect_tx(&full[stage], STAGE_BYTES);
+            armed[stage] = static_cast<int>(phase);
+            tma_load_2d(a_dst, &tmA, sg.a_k + kb * BK, m_blk * BM, &full[stage]);
+            tma_load_3d(b_dst, mapB, sg.ch_off + kb * BK, sg.t_off, n_blk * p.tile_samples, &full[stage]);
+          }
+        }
+      }
+      if (!ok) {
+        atomicCAS(p.err, 0, kErrWaitTimeoutProducer);
+        *abort_flag = 1;
+        for (int s = 0; s < STAGES; ++s)
+          if (armed[s] >= 0) {
+            for (uint32_t spin = 0; spin < kSpinLimit && !mbar_try_wait(&full[s], armed[s]); ++spin) {
+            }
+          }
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_bf16_f32(BM, BN);
+      uint32_t kb_iter = 0;
+      uint32_t acc_iter = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < p.total_tiles && ok; tile += gridDim.x, ++acc_iter) {
+        const int acc = acc_iter & 1;
+        const uint32_t acc_phase = (acc_iter >> 1) & 1;
+        if (!mbar_wait(&tempty[acc], acc_phase ^ 1, abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * BN;
+        for (int kb = 0; kb < total_kb; ++kb, ++kb_iter) {
+          const int stage = kb_iter % STAGES;
+          const uint32_t phase = (kb_iter / STAGES) & 1;
+          if (!mbar_wait(&full[stage], phase, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(smem + stage * STAGE_BYTES);
+          const uint32_t b_addr = a_addr + A_BYTES;
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k) {
+            umma_bf16(d_tmem, sw128_desc(a_addr + k * 32), sw128_desc(b_addr + k * 32), idesc,
+                      (kb > 0 || k > 0) ? 1u : 0u);
+          }
+          umma_commit(&empty[stage]);
+        }
+        if (!ok) break;
+        umma_commit(&tfull[acc]);
+      }
+      if (!ok) {
+        atomicCAS(p.err, 0, kErrWaitTimeoutMma);
+        *abort_flag = 1;
+      }
+      // Make sure every issued MMA finished before TMEM is released.
+      umma_commit(drain);
+      for (uint32_t spin = 0; spin < kSpinLimit && !mbar_try_wait(drain, 0); ++spin) {
+      }
+    }
+  } else {
+    // ---------------- epilogue (warps 2..5) ----------------
+    const int q = warp & 3;  // TMEM lane quadrant this warp may access
+    const int row = q * 32 + lane;
+    uint32_t acc_iter = 0;
+    const bool gather_stats = p.stats != nullptr;
+    for (int tile = blockIdx.x; tile < p.total_tiles; tile += gridDim.x, ++acc_iter) {
+      const int m_blk = tile % p.n_tiles_m;
+      const int n_blk = tile / p.n_tiles_m;
+      const int acc = acc_iter & 1;
+      const uint32_t acc_phase = (acc_iter >> 1) & 1;
+      if (!mbar_wait(&tfull[acc], acc_phase, abort_flag)) {
+        atomicCAS(p.err, 0, kErrWaitTimeoutEpilogue);
+        *abort_flag = 1;
+        break;
+      }
+      tc_fence_after();
+      const int m = m_blk * BM + row;
+      const bool m_ok = m < p.m_valid;
+      const float bias = (p.bias != nullptr && m_ok) ? p.bias[m] : 0.0f;
+      const float addv = (p.add_vec != nullptr && m_ok) ? p.add_vec[m] : 0.0f;
+      const int sample0 = n_blk * p.tile_samples;
+      float s1 = 0.0f, s2 = 0.0f;
+      for (int chunk = 0; chunk < BN / 32; ++chunk) {
+        float v[32];
+        tmem_ld32(tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * BN + chunk * 32, v);
+#pragma unroll 4
+        for (int j = 0; j < 32; ++j) {
+          const int n = chunk * 32 + j;
+          const int ls = n / p.L;
+          const int t = n - ls * p.L;
+          const int b = sample0 + ls;
+          float y = v[j] + bias + addv;
+          if (p.add_tok != nullptr && m_ok && b < p.n_samples) {
+            const long long arow = static_cast<long long>(b) * p.out_rps + t * p.out_tmul + p.out_tadd;
+            y += p.add_tok[arow * p.add_ld + m];
+          }
+          if (p.act == kActSilu) y = silu_f(y);
+          else if (p.act == kActSoftplus) y = softplus_f(y);
+          if (m_ok && b < p.n_samples) epilogue_store(p, b, t, m, y);
+          if (gather_stats) {
+            s1 += y;
+            s2 += y * y;
+            if (t == p.L - 1) {
+              double d1 = s1, d2 = s2;
+#pragma unroll
+              for (int off = 16; off > 0; off >>= 1) {
+                d1 += __shfl_xor_sync(0xffffffffu, d1, off);
+                d2 += __shfl_xor_sync(0xffffffffu, d2, off);
+              }
+              if (lane == 0) red[q * MAX_TILE_SAMPLES + ls] = make_double2(d1, d2);
+              s1 = 0.0f;
+              s2 = 0.0f;
+            }
+          }
+        }
+      }
+      // TMEM buffer may be overwritten by the next tile's MMAs from here on.
+      tc_fence_before();
+      mbar_arrive(&tempty[acc]);
+      if (gather_stats) {
+        named_barrier(1, 128);
+        // combine the 4 warps' partials into (sample, group) sums
+        const int tid = threadIdx.x - 64;
+        const int warps_per_group = p.group_ch >= BM ? 4 : p.group_ch / 32;
+        const int groups_in_tile = BM / (warps_per_group * 32);
+        const int items = p.tile_samples * groups_in_tile;
+        for (int it = tid; it < items; it += 128) {
+          const int ls = it / groups_in_tile;
+          const int gl = it - ls * groups_in_tile;
+          const int b = sample0 + ls;
+          if (b >= p.n_samples) continue;
+          double d1 = 0.0, d2 = 0.0;
+          for (int w = 0; w < warps_per_group; ++w) {
+            const double2 r = red[(gl * warps_per_group + w) * MAX_TILE_SAMPLES + ls];
+            d1 += r.x;
+            d2 += r.y;
+          }
+          const int row0 = m_blk * BM + gl * warps_per_group * 32;
+          const int g = row0 / p.group_ch;
+          const int part = (row0 % p.group_ch) / BM;
+          double* dst = p.stats + (((static_cast<long long>(b) * p.groups + g) * p.parts + part) * 2);
+          dst[0] = d1;
+          dst[1] = d2;
+        }
+        named_barrier(1, 128);
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tmem_base, TMEM_COLS);
+}
+
+}  // namespace tc
+}  // namespace feb

@@ -1,0 +1,1204 @@
+// Device-resident Diffusion Policy ConditionalUnet1D with the DDIM / DDPM
+// sampler (reference: src/core/heads/diffusion/diffusion.cc:383-1035).
+//
+// Two execution paths share one weight layout (tap-major packed GEMM rows,
+// [out][tap][in], input channels padded to 64):
+//   * tensor path (bf16 weights, batch * horizon >= kTcMinTokens): every conv
+//     is one tcgen05 implicit GEMM whose epilogue adds the bias and gathers
+//     GroupNorm statistics; GroupNorm + Mish + FiLM / residual is one bf16
+//     elementwise pass; the output 1x1 conv is fused with the DDIM / DDPM
+//     update.
+//   * weight-streaming path (fp32 or bf16 weights, small batch): split-K
+//     CUDA-core convolution whose partial sums are reduced inside the
+//     GroupNorm kernel (fixed order, deterministic).
+// FiLM is split as W_t * mish(temb(t)) + W_c * mish(cond) + b: the time part
+// is tabulated for every training timestep at load, the condition part is
+// computed once per sample call.  The whole sampling loop of one call is
+// captured as one CUDA graph per (batch, steps, scheduler).
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+#include <map>
+#include <numbers>
+#include <tuple>
+
+#include "runtime.cuh"
+#include "simt.cuh"
+
+namespace feb {
+namespace {
+
+constexpr int kSliceCh = 256;
+constexpr long long kTcMinTokens = 512;
+constexpr std::size_t kFinalNormGroups = 8;
+
+std::uint16_t bf16_bits(float v) {
+  std::uint32_t u;
+  std::memcpy(&u, &v, 4);
+  if ((u & 0x7FFFFFFFu) > 0x7F800000u) return 0x7FC0;
+  u += 0x7FFFu + ((u >> 16) & 1u);
+  return static_cast<std::uint16_t>(u >> 16);
+}
+
+struct Part {
+  int channels;  // actual input channels of this concatenated part
+  int padded;    // channels in the activation tensor (multiple of 64)
+};
+
+enum class ConvKind { kSame, kDown, kUp0, kUp1, kPoint };
+
+struct ConvDev {
+  ConvKind kind{};
+  int oc = 0, oc_rows = 0, K = 0, ic_total = 0, taps = 0;
+  void* w = nullptr;  // [oc_rows][K] (weight dtype)
+  float* bias = nullptr;
+  SimtSlice* slices = nullptr;
+  int nslices = 0;
+  std::vector<tc::Seg> segs;
+  int stride = 1;
+  // host staging before upload
+  std::vector<float> host_w;
+  std::vector<float> host_b;
+  std::vector<SimtSlice> host_slices;
+};
+
+struct BlockDev {
+  ConvDev c1, c2, res;
+  bool has_res = false;
+  float *g1 = nullptr, *b1 = nullptr, *g2 = nullptr, *b2 = nullptr;
+  std::vector<float> hg1, hb1, hg2, hb2;
+  int oc = 0;
+  int film_off = 0;
+};
+
+// tap list: (kernel index into the stored weight, time offset)
+std::vector<std::pair<int, int>> taps_for(ConvKind kind, int k) {
+  std::vector<std::pair<int, int>> taps;
+  switch (kind) {
+    case ConvKind::kSame:
+      for (int j = 0; j < k; ++j) taps.emplace_back(j, j - k / 2);
+      break;
+    case ConvKind::kDown:  // k3 s2 p1: input t = 2*t_out + j - 1
+      for (int j = 0; j < 3; ++j) taps.emplace_back(j, j - 1);
+      break;
+    case ConvKind::kUp0:  // convT k4 s2 p1, even outputs 2s: x[s] * W1 + x[s-1] * W3
+      taps = {{1, 0}, {3, -1}};
+      break;
+    case ConvKind::kUp1:  // odd outputs 2s+1: x[s+1] * W0 + x[s] * W2
+      taps = {{0, 1}, {2, 0}};
+      break;
+    case ConvKind::kPoint:
+      taps = {{0, 0}};
+      break;
+  }
+  return taps;
+}
+
+// Pack one convolution.  `w` is [oc][ic][k] (conv) or [ic][oc][4] (convT).
+void pack_conv(ConvDev& c, ConvKind kind, const std::vector<float>& w, const std::vector<float>& b, int oc,
+               const std::vector<Part>& parts, int k) {
+  c.kind = kind;
+  c.oc = oc;
+  c.oc_rows = (oc + 127) / 128 * 128;
+  int ic_actual = 0, ic_pad = 0;
+  for (const Part& p : parts) {
+    ic_actual += p.channels;
+    ic_pad += p.padded;
+  }
+  c.ic_total = ic_pad;
+  const auto taps = taps_for(kind, k);
+  c.taps = static_cast<int>(taps.size());
+  c.K = c.taps * ic_pad;
+  c.host_w.assign(static_cast<std::size_t>(c.oc_rows) * c.K, 0.0f);
+  const bool transposed = kind == ConvKind::kUp0 || kind == ConvKind::kUp1;
+  for (int o = 0; o < oc; ++o)
+    for (int j = 0; j < c.taps; ++j) {
+      const int kk = taps[static_cast<std::size_t>(j)].first;
+      int src_ic = 0, dst = 0;
+      for (const Part& p : parts) {
+        for (int i = 0; i < p.channels; ++i) {
+          const int ic = src_ic + i;
+          const float v = transposed ? w[(static_cast<std::size_t>(ic) * oc + o) * 4 + kk]
+                                     : w[(static_cast<std::size_t>(o) * ic_actual + ic) * k + kk];
+          c.host_w[static_cast<std::size_t>(o) * c.K + static_cast<std::size_t>(j) * ic_pad + dst + i] = v;
+        }
+        src_ic += p.channels;
+        dst += p.padded;
+      }
+    }
+  c.host_b = b;
+  c.stride = kind == ConvKind::kDown ? 2 : 1;
+  // weight-streaming slices and tensor-core segments
+  for (int j = 0; j < c.taps; ++j) {
+    const int t_off = taps[static_cast<std::size_t>(j)].second;
+    int off = 0;
+    for (int q = 0; q < static_cast<int>(parts.size()); ++q) {
+      const int pc = parts[static_cast<std::size_t>(q)].padded;
+      for (int ch = 0; ch < pc; ch += kSliceCh)
+        c.host_slices.push_back(SimtSlice{q, t_off, ch, std::min(kSliceCh, pc - ch), j * ic_pad + off + ch});
+      if (kind == ConvKind::kDown) {
+        // [B][L/2][2C] pair view: x[2s + d] = view[s][d * C + c]
+        const int pair_t = j == 0 ? -1 : 0;
+        const int ch_off = j == 1 ? 0 : pc;
+        c.segs.push_back(tc::Seg{0, pair_t, ch_off, pc / 64, j * ic_pad + off});
+      } else {
+        c.segs.push_back(tc::Seg{q, t_off, 0, pc / 64, j * ic_pad + off});
+      }
+      off += pc;
+    }
+  }
+  c.nslices = static_cast<int>(c.host_slices.size());
+}
+
+struct Act {
+  void* p = nullptr;
+  int C = 0;
+  int L = 0;
+};
+
+struct StepPlan {
+  int timestep;
+  int previous;
+  StepScalars scalars;
+};
+
+class Unet final : public UnetDevice {
+ public:
+  Unet(std::shared_ptr<DeviceContext> ctx, Precision prec) : ctx_(std::move(ctx)), prec_(prec) {}
+  ~Unet() override {
+    for (auto& [key, g] : graphs_) {
+      cudaGraphExecDestroy(g.exec);
+    }
+    if (pinned_ != nullptr) cudaFreeHost(pinned_);
+  }
+
+  bool load(const TensorTable& t, std::string& err);
+
+  const DiffusionConfig& config() const noexcept override { return cfg_; }
+  Precision precision() const noexcept override { return prec_; }
+  std::size_t capacity() const noexcept override { return cap_; }
+  std::uint64_t kernel_launches() const noexcept override { return launches_; }
+  int reserve(std::size_t batch, std::string& err) noexcept override;
+  int denoise(const float* condition, const float* sample, float timestep, float* eps, std::size_t batch,
+              std::string& err) noexcept override;
+  int sample(const float* condition, const float* noise, std::size_t batch, std::size_t steps, int scheduler,
+             std::uint64_t seed, float* action, std::string& err) noexcept override;
+  int sample_device(const float* condition, const float* noise, std::size_t batch, std::size_t steps,
+                    int scheduler, std::uint64_t seed, float* action, void* stream,
+                    std::string& err) noexcept override;
+
+ private:
+  bool use_tc(std::size_t batch) const {
+    return prec_ == Precision::kBF16 && tc_ok_ &&
+           static_cast<long long>(batch) * static_cast<long long>(cfg_.horizon) >= kTcMinTokens;
+  }
+  bool bf16_weights() const { return prec_ == Precision::kBF16; }
+  void upload_conv(ConvDev& c);
+  bool build_plan(std::string& err);
+  std::vector<StepPlan> plan_steps(std::size_t steps, int scheduler) const;
+  bool record_sample(std::size_t batch, const std::vector<StepPlan>& plan, cudaStream_t st, std::string& err);
+  bool record_forward(std::size_t batch, bool tc, const float* film_time_row, cudaStream_t st, std::string& err);
+  bool record_film_cond(std::size_t batch, bool tc, cudaStream_t st, std::string& err);
+  bool simt_conv(const ConvDev& c, const std::vector<Act>& srcs, int L_out, std::size_t batch, float* partial,
+                 cudaStream_t st, std::string& err);
+  void simt_reduce(const ConvDev& c, const float* partial, std::size_t batch, int L_tok, Act out, int rps, int tmul,
+                   int tadd, cudaStream_t st);
+  void simt_gn(const ConvDev& c, const float* partial, std::size_t batch, int L, const float* gamma,
+               const float* beta, int groups, const BlockDev* film_block, const float* film_time_row,
+               const float* res_tensor, const ConvDev* res_conv, const float* res_partial, Act out, cudaStream_t st);
+  bool tc_conv(const ConvDev& c, const std::vector<Act>& srcs, int L_out, std::size_t batch, void* out,
+               long long out_ld, int rps, int tmul, int tadd, bool stats, int groups, bool out_f32, cudaStream_t st,
+               std::string& err);
+  void tc_gn(const Act& y, std::size_t batch, int groups, int parts, const float* gamma, const float* beta,
+             const BlockDev* film_block, const float* film_time_row, const void* res, Act out, cudaStream_t st);
+  bool block(const BlockDev& blk, const std::vector<Act>& in, int L, std::size_t batch, bool tc,
+             const float* film_time_row, Act out, cudaStream_t st, std::string& err);
+  template <typename Kernel, typename... Args>
+  void launch(Kernel k, dim3 grid, dim3 block, std::size_t smem, cudaStream_t st, Args... args) {
+    k<<<grid, block, smem, st>>>(args...);
+    ++recorded_;
+  }
+
+  std::shared_ptr<DeviceContext> ctx_;
+  Precision prec_;
+  DiffusionConfig cfg_{};
+  bool tc_ok_ = false;
+  int cin_pad_ = 64, cond_pad_ = 64, F_ = 0;
+  std::vector<float> alphas_;
+  // weights
+  DeviceArena wts_;
+  std::vector<std::array<BlockDev, 2>> down_;
+  std::vector<ConvDev> ds_;
+  std::array<BlockDev, 2> mid_;
+  std::vector<std::array<BlockDev, 2>> up_;
+  std::vector<std::array<ConvDev, 2>> us_;
+  ConvDev fc_;
+  float *fn_g_ = nullptr, *fn_b_ = nullptr, *fo_w_ = nullptr, *fo_b_ = nullptr;
+  std::vector<float> h_fn_g_, h_fn_b_, h_fo_w_, h_fo_b_;
+  ConvDev film_;  // W_c of every block's FiLM, [F][cond_pad]
+  float* film_time_ = nullptr;  // [T][F]
+  float *te1_w_ = nullptr, *te1_b_ = nullptr, *te2_w_ = nullptr, *te2_b_ = nullptr, *wt_ = nullptr;
+  float *amin_ = nullptr, *amax_ = nullptr;
+  // workspace (reserve)
+  DeviceArena ws_;
+  std::size_t cap_ = 0;
+  std::size_t cap_tc_ = 0;  // capacity rounded for TMA boxes
+  float* in_cond_ = nullptr;   // [cap][C]
+  float* in_noise_ = nullptr;  // [cap][H][A]
+  float* out_action_ = nullptr;
+  float* x_master_ = nullptr;
+  float* eps_ = nullptr;
+  std::uint64_t* seeds_ = nullptr;
+  std::uint64_t* seed0_ = nullptr;
+  float* tstep_ = nullptr;  // timestep scalar for denoise()
+  float* tm_row_ = nullptr;
+  float* ft_row_ = nullptr;  // film_time row for denoise()
+  void* mcond_ = nullptr;
+  float* film_cond_ = nullptr;
+  void* x_in_ = nullptr;
+  std::vector<void*> acts_;  // per-layer outputs
+  void* h1_ = nullptr;
+  void* y1_ = nullptr;
+  void* y2_ = nullptr;
+  void* yr_ = nullptr;
+  float *p1_ = nullptr, *p2_ = nullptr, *p3_ = nullptr;
+  double* stats_ = nullptr;
+  std::size_t act_elems_ = 0;   // elements per activation buffer
+  std::size_t part_elems_ = 0;  // elements per partial buffer
+  float* pinned_ = nullptr;
+  std::size_t pinned_floats_ = 0;
+  struct Graph {
+    cudaGraphExec_t exec = nullptr;
+    std::uint64_t launches = 0;
+  };
+  std::map<std::tuple<std::size_t, std::size_t, int, bool>, Graph> graphs_;
+  std::uint64_t launches_ = 0;
+  std::uint64_t recorded_ = 0;
+};
+
+bool Unet::load(const TensorTable& t, std::string& err) {
+  const HostTensor* meta = t.find("dp.meta");
+  const HostTensor* dims = t.find("dp.dims");
+  if (meta == nullptr || dims == nullptr || meta->dtype != DType::F32 || meta->numel() != 16 ||
+      dims->dtype != DType::F32) {
+    err = "dp.meta / dp.dims missing or malformed";
+    return false;
+  }
+  const auto mv = widen_f32(*meta);
+  auto sz = [&](int i) { return static_cast<std::size_t>(mv[static_cast<std::size_t>(i)]); };
+  for (int i : {0, 1, 2, 3, 4, 5, 6, 7, 8, 9, 10, 11, 12, 13, 15}) {
+    const float v = mv[static_cast<std::size_t>(i)];
+    if (!std::isfinite(v) || v < 0 || std::floor(v) != v) {
+      err = "dp.meta holds a non-integer size";
+      return false;
+    }
+  }
+  cfg_.action_dim = sz(1);
+  cfg_.horizon = sz(2);
+  cfg_.action_steps = sz(3);
+  cfg_.observation_steps = sz(4);
+  cfg_.condition_dim = sz(5);
+  cfg_.stages = sz(6);
+  cfg_.kernel = sz(7);
+  cfg_.groups = sz(8);
+  cfg_.timestep_dim = sz(9);
+  cfg_.train_timesteps = sz(10);
+  cfg_.clip_sample = sz(13) != 0;
+  cfg_.clip_sample_range = mv[14];
+  // same validation as DiffusionHead::DiffusionHead (diffusion.cc:383-426)
+  if (sz(0) != 1 || sz(11) != 0 || sz(12) != 0 || sz(15) != 0 || sz(13) > 1 || cfg_.action_dim == 0 ||
+      cfg_.horizon == 0 || cfg_.action_steps == 0 || cfg_.observation_steps == 0 ||
+      cfg_.observation_steps > cfg_.horizon || cfg_.action_steps > cfg_.horizon - cfg_.observation_steps + 1 ||
+      cfg_.condition_dim == 0 || cfg_.stages < 2 || cfg_.stages > 8 || cfg_.kernel == 0 || cfg_.kernel % 2 == 0 ||
+      cfg_.groups == 0 || cfg_.timestep_dim < 4 || cfg_.timestep_dim % 2 != 0 || cfg_.train_timesteps == 0 ||
+      dims->numel() != cfg_.stages || !std::isfinite(cfg_.clip_sample_range) || cfg_.clip_sample_range <= 0) {
+    err = "dp.meta describes an unsupported Diffusion Policy configuration";
+    return false;
+  }
+  const auto dv = widen_f32(*dims);
+  for (float d : dv) {
+    if (!(d > 0) || std::floor(d) != d || static_cast<std::size_t>(d) % cfg_.groups != 0) {
+      err = "dp.dims entries must be positive multiples of the group count";
+      return false;
+    }
+    cfg_.dims.push_back(static_cast<std::size_t>(d));
+  }
+  if (cfg_.dims[0] % kFinalNormGroups != 0 || cfg_.horizon % (std::size_t(1) << (cfg_.stages - 1)) != 0) {
+    err = "U-Net geometry does not match the horizon";
+    return false;
+  }
+  const int A = static_cast<int>(cfg_.action_dim);
+  const int Cd = static_cast<int>(cfg_.condition_dim);
+  const int td = static_cast<int>(cfg_.timestep_dim);
+  const int k = static_cast<int>(cfg_.kernel);
+  cin_pad_ = (A + 63) / 64 * 64;
+  cond_pad_ = (Cd + 63) / 64 * 64;
+
+  auto get = [&](const std::string& name, std::initializer_list<std::size_t> shape, bool allow_bf16,
+                 std::vector<float>& out) {
+    const HostTensor* h = t.find(name);
+    if (h == nullptr) {
+      err = "missing tensor " + name;
+      return false;
+    }
+    if (h->ndim != static_cast<int>(shape.size()) || (!allow_bf16 && h->dtype != DType::F32)) {
+      err = "tensor " + name + " has an unsupported shape or dtype";
+      return false;
+    }
+    int i = 0;
+    for (std::size_t s : shape)
+      if (h->shape[static_cast<std::size_t>(i++)] != s) {
+        err = "tensor " + name + " has an unexpected shape";
+        return false;
+      }
+    out = widen_f32(*h);
+    return true;
+  };
+  // Conv weights: the reference accepts F32 only; BF16 convs are this build's
+  // added precision mode.
+  auto conv_t = [&](const std::string& pfx, int oc, int ic, int kk, std::vector<float>& w, std::vector<float>& b) {
+    return get(pfx + ".w", {static_cast<std::size_t>(oc), static_cast<std::size_t>(ic), static_cast<std::size_t>(kk)},
+               true, w) &&
+           get(pfx + ".b", {static_cast<std::size_t>(oc)}, false, b);
+  };
+  std::vector<float> te1w, te1b, te2w, te2b, amin, amax;
+  if (!get("dp.te1.w", {static_cast<std::size_t>(4 * td), static_cast<std::size_t>(td)}, true, te1w) ||
+      !get("dp.te1.b", {static_cast<std::size_t>(4 * td)}, false, te1b) ||
+      !get("dp.te2.w", {static_cast<std::size_t>(td), static_cast<std::size_t>(4 * td)}, true, te2w) ||
+      !get("dp.te2.b", {static_cast<std::size_t>(td)}, false, te2b) ||
+      !get("dp.action_min", {static_cast<std::size_t>(A)}, false, amin) ||
+      !get("dp.action_max", {static_cast<std::size_t>(A)}, false, amax))
+    return false;
+  for (int a = 0; a < A; ++a)
+    if (!std::isfinite(amin[a]) || !std::isfinite(amax[a]) || !(amax[a] > amin[a])) {
+      err = "action normalisation statistics are invalid";
+      return false;
+    }
+
+  std::vector<float> wt_all, wc_all, fb_all;  // FiLM: [F][td], [F][cond_pad], [F]
+  F_ = 0;
+  auto load_block = [&](BlockDev& blk, const std::string& pfx, std::vector<Part> in_parts, int oc) {
+    int ic = 0;
+    for (const Part& p : in_parts) ic += p.channels;
+    std::vector<float> w, b;
+    blk.oc = oc;
+    if (!conv_t(pfx + ".c1", oc, ic, k, w, b)) return false;
+    pack_conv(blk.c1, ConvKind::kSame, w, b, oc, in_parts, k);
+    if (!get(pfx + ".n1.w", {static_cast<std::size_t>(oc)}, false, blk.hg1) ||
+        !get(pfx + ".n1.b", {static_cast<std::size_t>(oc)}, false, blk.hb1))
+      return false;
+    std::vector<float> fw, fbias;
+    if (!get(pfx + ".film.w", {static_cast<std::size_t>(2 * oc), static_cast<std::size_t>(td + Cd)}, true, fw) ||
+        !get(pfx + ".film.b", {static_cast<std::size_t>(2 * oc)}, false, fbias))
+      return false;
+    blk.film_off = F_;
+    for (int r = 0; r < 2 * oc; ++r) {
+      for (int j = 0; j < td; ++j) wt_all.push_back(fw[static_cast<std::size_t>(r) * (td + Cd) + j]);
+      for (int j = 0; j < cond_pad_; ++j)
+        wc_all.push_back(j < Cd ? fw[static_cast<std::size_t>(r) * (td + Cd) + td + j] : 0.0f);
+      fb_all.push_back(fbias[static_cast<std::size_t>(r)]);
+    }
+    F_ += 2 * oc;
+    if (!conv_t(pfx + ".c2", oc, oc, k, w, b)) return false;
+    pack_conv(blk.c2, ConvKind::kSame, w, b, oc, {{oc, oc}}, k);
+    if (!get(pfx + ".n2.w", {static_cast<std::size_t>(oc)}, false, blk.hg2) ||
+        !get(pfx + ".n2.b", {static_cast<std::size_t>(oc)}, false, blk.hb2))
+      return false;
+    blk.has_res = ic != oc;
+    if (blk.has_res) {
+      if (!conv_t(pfx + ".res", oc, ic, 1, w, b)) return false;
+      pack_conv(blk.res, ConvKind::kPoint, w, b, oc, in_parts, 1);
+    }
+    return true;
+  };
+
+  const int S = static_cast<int>(cfg_.stages);
+  down_.resize(static_cast<std::size_t>(S));
+  ds_.resize(static_cast<std::size_t>(S));
+  for (int s = 0; s < S; ++s) {
+    const int oc = static_cast<int>(cfg_.dims[static_cast<std::size_t>(s)]);
+    const std::vector<Part> in0 = s == 0 ? std::vector<Part>{{A, cin_pad_}}
+                                         : std::vector<Part>{{static_cast<int>(cfg_.dims[s - 1]),
+                                                              static_cast<int>(cfg_.dims[s - 1])}};
+    if (!load_block(down_[s][0], "dp.d" + std::to_string(s) + ".r0", in0, oc) ||
+        !load_block(down_[s][1], "dp.d" + std::to_string(s) + ".r1", {{oc, oc}}, oc))
+      return false;
+    if (s + 1 < S) {
+      std::vector<float> w, b;
+      if (!conv_t("dp.d" + std::to_string(s) + ".ds", oc, oc, 3, w, b)) return false;
+      pack_conv(ds_[s], ConvKind::kDown, w, b, oc, {{oc, oc}}, 3);
+    }
+  }
+  const int top = static_cast<int>(cfg_.dims.back());
+  for (int m = 0; m < 2; ++m)
+    if (!load_block(mid_[m], "dp.m" + std::to_string(m), {{top, top}}, top)) return false;
+  up_.resize(static_cast<std::size_t>(S - 1));
+  us_.resize(static_cast<std::size_t>(S - 1));
+  for (int s = 0; s + 1 < S; ++s) {
+    const int high = static_cast<int>(cfg_.dims[static_cast<std::size_t>(S - 1 - s)]);
+    const int low = static_cast<int>(cfg_.dims[static_cast<std::size_t>(S - 2 - s)]);
+    if (!load_block(up_[s][0], "dp.u" + std::to_string(s) + ".r0", {{high, high}, {high, high}}, low) ||
+        !load_block(up_[s][1], "dp.u" + std::to_string(s) + ".r1", {{low, low}}, low))
+      return false;
+    std::vector<float> w, b;
+    if (!get("dp.u" + std::to_string(s) + ".us.w",
+             {static_cast<std::size_t>(low), static_cast<std::size_t>(low), 4}, true, w) ||
+        !get("dp.u" + std::to_string(s) + ".us.b", {static_cast<std::size_t>(low)}, false, b))
+      return false;
+    pack_conv(us_[s][0], ConvKind::kUp0, w, b, low, {{low, low}}, 4);
+    pack_conv(us_[s][1], ConvKind::kUp1, w, b, low, {{low, low}}, 4);
+  }
+  const int c0 = static_cast<int>(cfg_.dims[0]);
+  {
+    std::vector<float> w, b;
+    if (!conv_t("dp.f.c", c0, c0, k, w, b)) return false;
+    pack_conv(fc_, ConvKind::kSame, w, b, c0, {{c0, c0}}, k);
+    if (!get("dp.f.n.w", {static_cast<std::size_t>(c0)}, false, h_fn_g_) ||
+        !get("dp.f.n.b", {static_cast<std::size_t>(c0)}, false, h_fn_b_) ||
+        !conv_t("dp.f.o", A, c0, 1, h_fo_w_, h_fo_b_))
+      return false;
+  }
+  // FiLM condition projection as one GEMM over all blocks
+  film_.kind = ConvKind::kPoint;
+  film_.oc = F_;
+  film_.oc_rows = (F_ + 127) / 128 * 128;
+  film_.K = cond_pad_;
+  film_.taps = 1;
+  film_.ic_total = cond_pad_;
+  film_.host_w.assign(static_cast<std::size_t>(film_.oc_rows) * cond_pad_, 0.0f);
+  std::copy(wc_all.begin(), wc_all.end(), film_.host_w.begin());
+  film_.host_b = fb_all;
+  for (int ch = 0; ch < cond_pad_; ch += kSliceCh)
+    film_.host_slices.push_back(SimtSlice{0, 0, ch, std::min(kSliceCh, cond_pad_ - ch), ch});
+  film_.nslices = static_cast<int>(film_.host_slices.size());
+  film_.segs.push_back(tc::Seg{0, 0, 0, cond_pad_ / 64, 0});
+
+  // alphas_cumprod: squaredcos_cap_v2 betas in double, cumulative product in
+  // float (diffusion.cc:186-191, 529-541)
+  auto alpha_bar = [](double time) {
+    const double c = std::cos(((time + 0.008) / 1.008) * (std::numbers::pi / 2.0));
+    return c * c;
+  };
+  float cumulative = 1.0f;
+  const std::size_t T = cfg_.train_timesteps;
+  for (std::size_t s = 0; s < T; ++s) {
+    const double begin = static_cast<double>(s) / static_cast<double>(T);
+    const double end = static_cast<double>(s + 1) / static_cast<double>(T);
+    const float beta = static_cast<float>(std::min(1.0 - (alpha_bar(end) / alpha_bar(begin)), 0.999));
+    cumulative *= 1.0f - beta;
+    alphas_.push_back(cumulative);
+  }
+
+  // tensor-path geometry: 64-multiple channels, whole groups per 128-row tile,
+  // L >= 4 at the deepest stage.
+  tc_ok_ = true;
+  for (std::size_t d : cfg_.dims) {
+    const std::size_t gc = d / cfg_.groups;
+    if (d % 128 != 0 || gc % 32 != 0 || (gc < 128 && 128 % gc != 0) || (gc > 128 && gc % 128 != 0)) tc_ok_ = false;
+  }
+  if ((cfg_.dims[0] / kFinalNormGroups) % 32 != 0 || cfg_.horizon > 256 ||
+      (cfg_.horizon & (cfg_.horizon - 1)) != 0 || (cfg_.horizon >> (cfg_.stages - 1)) < 4)
+    tc_ok_ = false;
+
+  // ---- upload everything into one arena
+  ArenaPlan plan;
+  const std::size_t wbytes = bf16_weights() ? 2 : 4;
+  auto plan_conv = [&](const ConvDev& c) {
+    plan.add(c.host_w.size() * wbytes);
+    plan.add_n<float>(c.host_b.size());
+    plan.add_n<SimtSlice>(c.host_slices.size());
+  };
+  auto plan_block = [&](const BlockDev& b) {
+    plan_conv(b.c1);
+    plan_conv(b.c2);
+    if (b.has_res) plan_conv(b.res);
+    plan.add_n<float>(4 * static_cast<std::size_t>(b.oc));
+  };
+  for (auto& st : down_) plan_block(st[0]), plan_block(st[1]);
+  for (auto& c : ds_) plan_conv(c);
+  plan_block(mid_[0]);
+  plan_block(mid_[1]);
+  for (auto& st : up_) plan_block(st[0]), plan_block(st[1]);
+  for (auto& pr : us_) plan_conv(pr[0]), plan_conv(pr[1]);
+  plan_conv(fc_);
+  plan_conv(film_);
+  plan.add_n<float>(2 * c0 + A * c0 + A + 2 * A);
+  plan.add_n<float>(T * static_cast<std::size_t>(F_));
+  plan.add_n<float>(te1w.size() + te1b.size() + te2w.size() + te2b.size() + wt_all.size());
+  plan.add_n<float>(T + T * td);
+  if (!wts_.init(plan.total(), err)) return false;
+
+  cudaStream_t st = ctx_->stream;
+  auto put = [&](const std::vector<float>& h) -> float* {
+    float* d = wts_.take_n<float>(h.size());
+    cudaMemcpyAsync(d, h.data(), h.size() * sizeof(float), cudaMemcpyHostToDevice, st);
+    return d;
+  };
+  std::vector<std::uint16_t> bf_stage;
+  auto put_conv = [&](ConvDev& c) {
+    if (bf16_weights()) {
+      bf_stage.resize(c.host_w.size());
+      for (std::size_t i = 0; i < c.host_w.size(); ++i) bf_stage[i] = bf16_bits(c.host_w[i]);
+      c.w = wts_.take(bf_stage.size() * 2);
+      cudaMemcpy(c.w, bf_stage.data(), bf_stage.size() * 2, cudaMemcpyHostToDevice);
+    } else {
+      c.w = put(c.host_w);
+    }
+    c.bias = put(c.host_b);
+    c.slices = wts_.take_n<SimtSlice>(c.host_slices.size());
+    cudaMemcpyAsync(c.slices, c.host_slices.data(), c.host_slices.size() * sizeof(SimtSlice), cudaMemcpyHostToDevice,
+                    st);
+    cudaStreamSynchronize(st);
+    std::vector<float>().swap(c.host_w);
+  };
+  auto put_block = [&](BlockDev& b) {
+    put_conv(b.c1);
+    put_conv(b.c2);
+    if (b.has_res) put_conv(b.res);
+    b.g1 = put(b.hg1);
+    b.b1 = put(b.hb1);
+    b.g2 = put(b.hg2);
+    b.b2 = put(b.hb2);
+  };
+  for (auto& stg : down_) put_block(stg[0]), put_block(stg[1]);
+  for (int s = 0; s + 1 < S; ++s) put_conv(ds_[s]);
+  put_block(mid_[0]);
+  put_block(mid_[1]);
+  for (auto& stg : up_) put_block(stg[0]), put_block(stg[1]);
+  for (auto& pr : us_) put_conv(pr[0]), put_conv(pr[1]);
+  put_conv(fc_);
+  put_conv(film_);
+  fn_g_ = put(h_fn_g_);
+  fn_b_ = put(h_fn_b_);
+  fo_w_ = put(h_fo_w_);
+  fo_b_ = put(h_fo_b_);
+  amin_ = put(amin);
+  amax_ = put(amax);
+  film_time_ = wts_.take_n<float>(T * static_cast<std::size_t>(F_));
+  te1_w_ = put(te1w);
+  te1_b_ = put(te1b);
+  te2_w_ = put(te2w);
+  te2_b_ = put(te2b);
+  wt_ = put(wt_all);
+  std::vector<float> ts(T);
+  for (std::size_t i = 0; i < T; ++i) ts[i] = static_cast<float>(i);
+  float* d_ts = put(ts);
+  float* d_tm = wts_.take_n<float>(T * static_cast<std::size_t>(td));
+  temb_kernel<<<static_cast<unsigned>(T), 128, static_cast<std::size_t>(5 * td) * sizeof(float), st>>>(
+      d_ts, static_cast<int>(T), td, te1_w_, te1_b_, te2_w_, te2_b_, d_tm);
+  film_time_kernel<<<ew_grid(static_cast<long long>(T) * F_, 256, *ctx_), 256, 0, st>>>(d_tm, static_cast<int>(T), td,
+                                                                                        wt_, F_, film_time_);
+  if (cudaStreamSynchronize(st) != cudaSuccess) {
+    err = std::string("weight upload failed: ") + cudaGetErrorString(cudaGetLastError());
+    return false;
+  }
+  return true;
+}
+
+int Unet::reserve(std::size_t batch, std::string& err) noexcept {
+  if (batch == 0) batch = 1;
+  if (batch <= cap_) return 0;
+  // drop graphs recorded against the old workspace
+  for (auto& [key, g] : graphs_) cudaGraphExecDestroy(g.exec);
+  graphs_.clear();
+  const std::size_t H = cfg_.horizon, A = cfg_.action_dim;
+  const std::size_t cap_tc = (batch + 255) / 256 * 256;
+  std::size_t max_c = 0;
+  for (std::size_t d : cfg_.dims) max_c = std::max(max_c, d);
+  // largest activation: C * L at any stage is at most max(dims[s] * H >> s), plus concat (2 * high * L)
+  std::size_t per_sample = static_cast<std::size_t>(cin_pad_) * H;
+  for (std::size_t s = 0; s < cfg_.stages; ++s) {
+    per_sample = std::max(per_sample, cfg_.dims[s] * (H >> s));
+  }
+  act_elems_ = per_sample * cap_tc;
+  // split-K partials: nslices * n_tokens * M for the largest conv
+  std::size_t part = 0;
+  auto pc = [&](const ConvDev& c, std::size_t L) {
+    part = std::max(part, static_cast<std::size_t>(c.nslices) * batch * L * static_cast<std::size_t>(c.oc));
+  };
+  for (std::size_t s = 0; s < cfg_.stages; ++s) {
+    const std::size_t L = H >> s;
+    for (auto& b : down_[s]) {
+      pc(b.c1, L), pc(b.c2, L);
+      if (b.has_res) pc(b.res, L);
+    }
+    if (s + 1 < cfg_.stages) pc(ds_[s], L / 2);
+  }
+  const std::size_t Lm = H >> (cfg_.stages - 1);
+  for (auto& b : mid_) pc(b.c1, Lm), pc(b.c2, Lm);
+  for (std::size_t s = 0; s + 1 < cfg_.stages; ++s) {
+    const std::size_t L = H >> (cfg_.stages - 1 - s);
+    for (auto& b : up_[s]) {
+      pc(b.c1, L), pc(b.c2, L);
+      if (b.has_res) pc(b.res, L);
+    }
+    pc(us_[s][0], L), pc(us_[s][1], L);
+  }
+  pc(fc_, H);
+  pc(film_, 1);
+  part_elems_ = part;
+  // outputs: 3 per down stage (r0, r1, downsample), 2 middle, 3 per up stage
+  const std::size_t n_layers = 6 * cfg_.stages;
+  const std::size_t ebytes = 4;  // activation buffers sized for fp32 (bf16 uses half)
+  ArenaPlan plan;
+  plan.add_n<float>(batch * cfg_.condition_dim);
+  plan.add_n<float>(batch * H * A);
+  plan.add_n<float>(batch * H * A);
+  plan.add_n<float>(batch * H * A);
+  plan.add_n<float>(batch * H * A);
+  plan.add_n<std::uint64_t>(batch);
+  plan.add_n<std::uint64_t>(1);
+  plan.add_n<float>(1);
+  plan.add_n<float>(cfg_.timestep_dim);
+  plan.add_n<float>(static_cast<std::size_t>(F_));
+  plan.add(cap_tc * static_cast<std::size_t>(cond_pad_) * ebytes);
+  plan.add_n<float>(batch * static_cast<std::size_t>(F_));
+  plan.add(cap_tc * H * static_cast<std::size_t>(cin_pad_) * ebytes);
+  for (std::size_t i = 0; i < n_layers + 4; ++i) plan.add(act_elems_ * ebytes);
+  for (int i = 0; i < 3; ++i) plan.add_n<float>(part_elems_);
+  plan.add_n<double>(cap_tc * 8 * 2 * 2 + 64);
+  ws_.release();
+  if (!ws_.init(plan.total(), err)) {
+    cap_ = 0;
+    return 2;
+  }
+  in_cond_ = ws_.take_n<float>(batch * cfg_.condition_dim);
+  in_noise_ = ws_.take_n<float>(batch * H * A);
+  out_action_ = ws_.take_n<float>(batch * H * A);
+  x_master_ = ws_.take_n<float>(batch * H * A);
+  eps_ = ws_.take_n<float>(batch * H * A);
+  seeds_ = ws_.take_n<std::uint64_t>(batch);
+  seed0_ = ws_.take_n<std::uint64_t>(1);
+  tstep_ = ws_.take_n<float>(1);
+  tm_row_ = ws_.take_n<float>(cfg_.timestep_dim);
+  ft_row_ = ws_.take_n<float>(static_cast<std::size_t>(F_));
+  mcond_ = ws_.take(cap_tc * static_cast<std::size_t>(cond_pad_) * ebytes);
+  film_cond_ = ws_.take_n<float>(batch * static_cast<std::size_t>(F_));
+  x_in_ = ws_.take(cap_tc * H * static_cast<std::size_t>(cin_pad_) * ebytes);
+  acts_.clear();
+  for (std::size_t i = 0; i < n_layers; ++i) acts_.push_back(ws_.take(act_elems_ * ebytes));
+  h1_ = ws_.take(act_elems_ * ebytes);
+  y1_ = ws_.take(act_elems_ * ebytes);
+  y2_ = ws_.take(act_elems_ * ebytes);
+  yr_ = ws_.take(act_elems_ * ebytes);
+  p1_ = ws_.take_n<float>(part_elems_);
+  p2_ = ws_.take_n<float>(part_elems_);
+  p3_ = ws_.take_n<float>(part_elems_);
+  stats_ = ws_.take_n<double>(cap_tc * 8 * 2 * 2 + 64);
+  // zero everything once so padded channels / padded samples read as zeros
+  cudaMemsetAsync(in_cond_, 0, ws_.used(), ctx_->stream);
+  // pinned staging for host calls
+  const std::size_t need = batch * (cfg_.condition_dim + 2 * H * A);
+  if (pinned_floats_ < need) {
+    if (pinned_ != nullptr) cudaFreeHost(pinned_);
+    pinned_ = nullptr;
+    if (counted_host_malloc(reinterpret_cast<void**>(&pinned_), need * sizeof(float)) != cudaSuccess) {
+      err = "pinned host allocation failed";
+      pinned_floats_ = 0;
+      return 2;
+    }
+    pinned_floats_ = need;
+  }
+  if (cudaStreamSynchronize(ctx_->stream) != cudaSuccess) {
+    err = "workspace initialisation failed";
+    return 2;
+  }
+  cap_ = batch;
+  cap_tc_ = cap_tc;
+  return 0;
+}
+
+bool Unet::simt_conv(const ConvDev& c, const std::vector<Act>& srcs, int L_out, std::size_t batch, float* partial,
+                     cudaStream_t st, std::string& err) {
+  SimtConvParams p{};
+  p.W = c.w;
+  p.M = c.oc;
+  p.K = c.K;
+  for (std::size_t i = 0; i < srcs.size() && i < 3; ++i)
+    p.src[i] = SimtSource{static_cast<const float*>(srcs[i].p), srcs[i].C, srcs[i].L};
+  p.stride = c.stride;
+  p.L_out = L_out;
+  p.n_tokens = static_cast<int>(batch) * L_out;
+  p.slices = c.slices;
+  p.partial = partial;
+  const int nt = p.n_tokens >= 16 ? 16 : (p.n_tokens >= 8 ? 8 : 4);
+  const dim3 grid(static_cast<unsigned>(c.nslices), static_cast<unsigned>((c.oc + 127) / 128),
+                  static_cast<unsigned>((p.n_tokens + nt - 1) / nt));
+  const bool bf = bf16_weights();
+  if (nt == 16) {
+    if (bf) launch(simt_conv_kernel<16, true>, grid, dim3(128), 0, st, p);
+    else launch(simt_conv_kernel<16, false>, grid, dim3(128), 0, st, p);
+  } else if (nt == 8) {
+    if (bf) launch(simt_conv_kernel<8, true>, grid, dim3(128), 0, st, p);
+    else launch(simt_conv_kernel<8, false>, grid, dim3(128), 0, st, p);
+  } else {
+    if (bf) launch(simt_conv_kernel<4, true>, grid, dim3(128), 0, st, p);
+    else launch(simt_conv_kernel<4, false>, grid, dim3(128), 0, st, p);
+  }
+  (void)err;
+  return true;
+}
+
+void Unet::simt_reduce(const ConvDev& c, const float* partial, std::size_t batch, int L_tok, Act out, int rps,
+                       int tmul, int tadd, cudaStream_t st) {
+  // generic reduce with a row mapping: token (b, t) -> out row b * rps + t * tmul + tadd
+  ReduceParams p{};
+  p.partial = partial;
+  p.nslices = c.nslices;
+  p.n_tokens = static_cast<int>(batch) * L_tok;
+  p.M = c.oc;
+  p.bias = c.bias;
+  p.act = 0;
+  p.accumulate = 0;
+  if (rps == L_tok && tmul == 1 && tadd == 0) {
+    p.out = static_cast<float*>(out.p);
+    p.out_ld = out.C;
+    launch(reduce_partials_kernel, dim3(ew_grid(static_cast<long long>(p.n_tokens) * p.M, 256, *ctx_)), dim3(256), 0,
+           st, p);
+    return;
+  }
+  // strided rows (conv-transpose phases): one launch per sample row pattern via out_ld trick:
+  // out row for (b, t) = b * rps + t * tmul + tadd; with rps == L_tok * tmul this is
+  // (b * L_tok + t) * tmul + tadd, i.e. a fixed stride of tmul rows.
+  p.out = static_cast<float*>(out.p) + static_cast<long long>(tadd) * out.C;
+  p.out_ld = out.C * tmul;
+  launch(reduce_partials_kernel, dim3(ew_grid(static_cast<long long>(p.n_tokens) * p.M, 256, *ctx_)), dim3(256), 0,
+         st, p);
+}
+
+void Unet::simt_gn(const ConvDev& c, const float* partial, std::size_t batch, int L, const float* gamma,
+                   const float* beta, int groups, const BlockDev* film_block, const float* film_time_row,
+                   const float* res_tensor, const ConvDev* res_conv, const float* res_partial, Act out,
+                   cudaStream_t st) {
+  GnParams p{};
+  p.partial = partial;
+  p.nslices = c.nslices;
+  p.n_tokens = static_cast<int>(batch) * L;
+  p.C = c.oc;
+  p.L = L;
+  p.bias = c.bias;
+  p.gamma = gamma;
+  p.beta = beta;
+  p.groups = groups;
+  p.mish = 1;
+  if (film_block != nullptr) {
+    p.film_cond = film_cond_;
+    p.film_time = film_time_row;
+    p.film_F = F_;
+    p.film_off = film_block->film_off;
+  }
+  p.res = res_tensor;
+  if (res_conv != nullptr) {
+    p.res_partial = res_partial;
+    p.res_nslices = res_conv->nslices;
+    p.res_bias = res_conv->bias;
+  }
+  p.out = static_cast<float*>(out.p);
+  launch(gn_partials_kernel, dim3(static_cast<unsigned>(batch), static_cast<unsigned>(groups)), dim3(256), 0, st, p);
+}
+
+bool Unet::tc_conv(const ConvDev& c, const std::vector<Act>& srcs, int L_out, std::size_t batch, void* out,
+                   long long out_ld, int rps, int tmul, int tadd, bool stats, int groups, bool out_f32,
+                   cudaStream_t st, std::string& err) {
+  TcLaunch l;
+  l.A = c.w;
+  l.M_rows = c.oc_rows;
+  l.K = c.K;
+  for (std::size_t i = 0; i < srcs.size() && i < 3; ++i) {
+    l.src[i].ptr = srcs[i].p;
+    l.src[i].channels = srcs[i].C;
+    l.src[i].length = srcs[i].L;
+    l.src[i].samples = static_cast<int>(cap_tc_);
+  }
+  if (c.kind == ConvKind::kDown) {  // pair view of the input
+    l.src[0].channels = srcs[0].C * 2;
+    l.src[0].length = srcs[0].L / 2;
+  }
+  l.L = L_out;
+  l.n_samples = static_cast<int>(batch);
+  l.m_valid = c.oc;
+  l.segs = c.segs;
+  l.bias = c.bias;
+  l.out = out;
+  l.out_ld = out_ld;
+  l.out_rps = rps;
+  l.out_tmul = tmul;
+  l.out_tadd = tadd;
+  l.out_f32 = out_f32;
+  if (stats) {
+    l.stats = stats_;
+    l.groups = groups;
+    l.group_ch = c.oc / groups;
+  }
+  ++recorded_;
+  return tc_gemm(l, *ctx_, st, err) == cudaSuccess;
+}
+
+void Unet::tc_gn(const Act& y, std::size_t batch, int groups, int parts, const float* gamma, const float* beta,
+                 const BlockDev* film_block, const float* film_time_row, const void* res, Act out, cudaStream_t st) {
+  GnBf16Params p{};
+  p.y = static_cast<const __nv_bfloat16*>(y.p);
+  p.n_tokens = static_cast<long long>(batch) * y.L;
+  p.C = y.C;
+  p.L = y.L;
+  p.groups = groups;
+  p.parts = parts;
+  p.stats = stats_;
+  p.gamma = gamma;
+  p.beta = beta;
+  if (film_block != nullptr) {
+    p.film_cond = film_cond_;
+    p.film_time = film_time_row;
+    p.film_F = F_;
+    p.film_off = film_block->film_off;
+  }
+  p.res = static_cast<const __nv_bfloat16*>(res);
+  p.out = static_cast<__nv_bfloat16*>(out.p);
+  launch(gn_bf16_kernel, dim3(ew_grid(p.n_tokens * (p.C / 8), 256, *ctx_)), dim3(256), 0, st, p);
+}
+
+bool Unet::block(const BlockDev& blk, const std::vector<Act>& in, int L, std::size_t batch, bool tc,
+                 const float* film_time_row, Act out, cudaStream_t st, std::string& err) {
+  const int G = static_cast<int>(cfg_.groups);
+  const int oc = blk.oc;
+  Act h1{h1_, oc, L};
+  if (!tc) {
+    if (!simt_conv(blk.c1, in, L, batch, p1_, st, err)) return false;
+    simt_gn(blk.c1, p1_, batch, L, blk.g1, blk.b1, G, &blk, film_time_row, nullptr, nullptr, nullptr, h1, st);
+    if (!simt_conv(blk.c2, {h1}, L, batch, p2_, st, err)) return false;
+    if (blk.has_res) {
+      if (!simt_conv(blk.res, in, L, batch, p3_, st, err)) return false;
+      simt_gn(blk.c2, p2_, batch, L, blk.g2, blk.b2, G, nullptr, nullptr, nullptr, &blk.res, p3_, out, st);
+    } else {
+      simt_gn(blk.c2, p2_, batch, L, blk.g2, blk.b2, G, nullptr, nullptr, static_cast<const float*>(in[0].p), nullptr,
+              nullptr, out, st);
+    }
+    return true;
+  }
+  const int parts = (oc / G) > 128 ? (oc / G) / 128 : 1;
+  Act y1{y1_, oc, L}, y2{y2_, oc, L}, yr{yr_, oc, L};
+  if (!tc_conv(blk.c1, in, L, batch, y1_, oc, L, 1, 0, true, G, false, st, err)) return false;
+  tc_gn(y1, batch, G, parts, blk.g1, blk.b1, &blk, film_time_row, nullptr, h1, st);
+  if (!tc_conv(blk.c2, {h1}, L, batch, y2_, oc, L, 1, 0, true, G, false, st, err)) return false;
+  const void* res = in[0].p;
+  if (blk.has_res) {
+    if (!tc_conv(blk.res, in, L, batch, yr_, oc, L, 1, 0, false, 0, false, st, err)) return false;
+    res = yr_;
+  }
+  tc_gn(y2, batch, G, parts, blk.g2, blk.b2, nullptr, nullptr, res, out, st);
+  (void)yr;
+  return true;
+}
+
+bool Unet::record_film_cond(std::size_t batch, bool tc, cudaStream_t st, std::string& err) {
+  launch(prep_cond_kernel, dim3(ew_grid(static_cast<long long>(batch) * cond_pad_, 256, *ctx_)), dim3(256), 0, st,
+         static_cast<const float*>(in_cond_), static_cast<int>(batch), static_cast<int>(cfg_.condition_dim), mcond_,
+         cond_pad_, tc ? 1 : 0);
+  Act mc{mcond_, cond_pad_, 1};
+  if (tc) return tc_conv(film_, {mc}, 1, batch, film_cond_, F_, 1, 1, 0, false, 0, true, st, err);
+  if (!simt_conv(film_, {mc}, 1, batch, p1_, st, err)) return false;
+  simt_reduce(film_, p1_, batch, 1, Act{film_cond_, F_, 1}, 1, 1, 0, st);
+  return true;
+}
+
+bool Unet::record_forward(std::size_t batch, bool tc, const float* ft_row, cudaStream_t st, std::string& err) {
+  const std::size_t S = cfg_.stages;
+  const int H = static_cast<int>(cfg_.horizon);
+  std::size_t li = 0;
+  Act x{x_in_, cin_pad_, H};
+  std::vector<Act> skips(S);
+  int L = H;
+  for (std::size_t s = 0; s < S; ++s) {
+    const int oc = static_cast<int>(cfg_.dims[s]);
+    Act o0{acts_[li++], oc, L}, o1{acts_[li++], oc, L};
+    if (!block(down_[s][0], {x}, L, batch, tc, ft_row, o0, st, err)) return false;
+    if (!block(down_[s][1], {o0}, L, batch, tc, ft_row, o1, st, err)) return false;
+    skips[s] = o1;
+    x = o1;
+    if (s + 1 < S) {
+      Act d{acts_[li++], oc, L / 2};
+      if (tc) {
+        if (!tc_conv(ds_[s], {x}, L / 2, batch, d.p, oc, L / 2, 1, 0, false, 0, false, st, err)) return false;
+      } else {
+        if (!simt_conv(ds_[s], {x}, L / 2, batch, p1_, st, err)) return false;
+        simt_reduce(ds_[s], p1_, batch, L / 2, d, L / 2, 1, 0, st);
+      }
+      x = d;
+      L /= 2;
+    } else {
+      ++li;
+    }
+  }
+  for (int m = 0; m < 2; ++m) {
+    Act o{acts_[li++], x.C, L};
+    if (!block(mid_[m], {x}, L, batch, tc, ft_row, o, st, err)) return false;
+    x = o;
+  }
+  for (std::size_t s = 0; s + 1 < S; ++s) {
+    const Act skip = skips[S - 1 - s];
+    const int low = static_cast<int>(cfg_.dims[S - 2 - s]);
+    Act o0{acts_[li++], low, L}, o1{acts_[li++], low, L};
+    if (!block(up_[s][0], {x, skip}, L, batch, tc, ft_row, o0, st, err)) return false;
+    if (!block(up_[s][1], {o0}, L, batch, tc, ft_row, o1, st, err)) return false;
+    Act u{acts_[li++], low, 2 * L};
+    for (int ph = 0; ph < 2; ++ph) {
+      if (tc) {
+        if (!tc_conv(us_[s][ph], {o1}, L, batch, u.p, low, 2 * L, 2, ph, false, 0, false, st, err)) return false;
+      } else {
+        if (!simt_conv(us_[s][ph], {o1}, L, batch, p1_, st, err)) return false;
+        simt_reduce(us_[s][ph], p1_, batch, L, u, 2 * L, 2, ph, st);
+      }
+    }
+    x = u;
+    L *= 2;
+  }
+  // final conv -> GN(8) + Mish -> z in h1_
+  const int c0 = static_cast<int>(cfg_.dims[0]);
+  Act z{h1_, c0, H};
+  if (tc) {
+    if (!tc_conv(fc_, {x}, H, batch, y1_, c0, H, 1, 0, true, static_cast<int>(kFinalNormGroups), false, st, err))
+      return false;
+    tc_gn(Act{y1_, c0, H}, batch, static_cast<int>(kFinalNormGroups), 1, fn_g_, fn_b_, nullptr, nullptr, nullptr, z, st);
+  } else {
+    if (!simt_conv(fc_, {x}, H, batch, p1_, st, err)) return false;
+    simt_gn(fc_, p1_, batch, H, fn_g_, fn_b_, static_cast<int>(kFinalNormGroups), nullptr, nullptr, nullptr, nullptr,
+            nullptr, z, st);
+  }
+  return true;
+}
+
+std::vector<StepPlan> Unet::plan_steps(std::size_t steps, int scheduler) const {
+  std::vector<StepPlan> plan;
+  const std::size_t ratio = cfg_.train_timesteps / steps;
+  for (std::size_t i = 0; i < steps; ++i) {
+    const std::size_t timestep = (steps - 1 - i) * ratio;
+    const long long previous = static_cast<long long>(timestep) - static_cast<long long>(ratio);
+    // scalar arithmetic exactly as DiffusionHead::sample (diffusion.cc:997-1024)
+    const float alpha_t = alphas_[timestep];
+    const float alpha_prev = previous >= 0 ? alphas_[static_cast<std::size_t>(previous)] : 1.0f;
+    const float beta_t = 1.0f - alpha_t;
+    StepScalars s{};
+    s.sqrt_alpha = std::sqrt(alpha_t);
+    s.sqrt_beta = std::sqrt(beta_t);
+    s.sqrt_alpha_prev = std::sqrt(alpha_prev);
+    s.sqrt_one_minus_prev = std::sqrt(1.0f - alpha_prev);
+    s.clip = cfg_.clip_sample ? 1 : 0;
+    s.clip_range = cfg_.clip_sample_range;
+    s.ddpm = scheduler == 1 ? 1 : 0;
+    if (s.ddpm) {
+      const float current_alpha = alpha_t / alpha_prev;
+      const float current_beta = 1.0f - current_alpha;
+      s.orig_coef = std::sqrt(alpha_prev) * current_beta / std::max(beta_t, 1e-20f);
+      s.sample_coef = std::sqrt(current_alpha) * (1.0f - alpha_prev) / std::max(beta_t, 1e-20f);
+      const float variance = ((1.0f - alpha_prev) / std::max(beta_t, 1e-20f)) * current_beta;
+      s.noise_std = std::sqrt(std::max(variance, 1e-20f));
+      s.add_noise = previous >= 0 ? 1 : 0;
+      s.noise_draw = static_cast<int>(i);
+    }
+    plan.push_back(StepPlan{static_cast<int>(timestep), static_cast<int>(previous), s});
+  }
+  return plan;
+}
+
+__global__ void seeds_kernel(const std::uint64_t* seed0, std::uint64_t* seeds, int n) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) seeds[i] = *seed0 + static_cast<std::uint64_t>(i);
+}
+
+bool Unet::record_sample(std::size_t batch, const std::vector<StepPlan>& plan, cudaStream_t st, std::string& err) {
+  const bool tc = use_tc(batch);
+  const int H = static_cast<int>(cfg_.horizon), A = static_cast<int>(cfg_.action_dim);
+  const int n_tokens = static_cast<int>(batch) * H;
+  launch(seeds_kernel, dim3((static_cast<unsigned>(batch) + 255) / 256), dim3(256), 0, st,
+         static_cast<const std::uint64_t*>(seed0_), seeds_, static_cast<int>(batch));
+  launch(prep_sample_kernel, dim3(ew_grid(static_cast<long long>(n_tokens) * cin_pad_, 256, *ctx_)), dim3(256), 0, st,
+         static_cast<const float*>(in_noise_), n_tokens, A, x_master_, x_in_, cin_pad_, tc ? 1 : 0);
+  if (!record_film_cond(batch, tc, st, err)) return false;
+  const int c0 = static_cast<int>(cfg_.dims[0]);
+  for (const StepPlan& sp : plan) {
+    const float* ft_row = film_time_ + static_cast<std::size_t>(sp.timestep) * static_cast<std::size_t>(F_);
+    if (!record_forward(batch, tc, ft_row, st, err)) return false;
+    const unsigned blocks = static_cast<unsigned>((n_tokens * 32 + 255) / 256);
+    if (tc) {
+      OutParams<__nv_bfloat16> p{};
+      p.z = static_cast<const __nv_bfloat16*>(h1_);
+      p.C = c0, p.A = A, p.H = H, p.n_tokens = n_tokens;
+      p.W = fo_w_, p.bias = fo_b_, p.x_master = x_master_, p.eps_out = nullptr, p.update = 1;
+      p.step = sp.scalars, p.seeds = seeds_, p.x_in = x_in_, p.Cin = cin_pad_, p.x_in_bf16 = 1;
+      if (A <= 16) launch(out_update_kernel<__nv_bfloat16, 16>, dim3(blocks), dim3(256), 0, st, p);
+      else launch(out_update_kernel<__nv_bfloat16, 64>, dim3(blocks), dim3(256), 0, st, p);
+    } else {
+      OutParams<float> p{};
+      p.z = static_cast<const float*>(h1_);
+      p.C = c0, p.A = A, p.H = H, p.n_tokens = n_tokens;
+      p.W = fo_w_, p.bias = fo_b_, p.x_master = x_master_, p.eps_out = nullptr, p.update = 1;
+      p.step = sp.scalars, p.seeds = seeds_, p.x_in = x_in_, p.Cin = cin_pad_, p.x_in_bf16 = 0;
+      if (A <= 16) launch(out_update_kernel<float, 16>, dim3(blocks), dim3(256), 0, st, p);
+      else launch(out_update_kernel<float, 64>, dim3(blocks), dim3(256), 0, st, p);
+    }
+  }
+  launch(unnormalize_kernel, dim3(ew_grid(static_cast<long long>(n_tokens) * A, 256, *ctx_)), dim3(256), 0, st,
+         static_cast<const float*>(x_master_), n_tokens, A, static_cast<const float*>(amin_),
+         static_cast<const float*>(amax_), out_action_);
+  return true;
+}
+
+int Unet::sample_device(const float* condition, const float* noise, std::size_t batch, std::size_t steps,
+                        int scheduler, std::uint64_t seed, float* action, void* stream, std::string& err) noexcept {
+  if (batch == 0 || steps == 0 || steps > cfg_.train_timesteps || (scheduler != 0 && scheduler != 1)) {
+    err = "invalid diffusion sampling arguments";
+    return 1;
+  }
+  if (batch > cap_) {
+    err = "batch exceeds the reserved capacity (call fe_engine_reserve_batch first)";
+    return 2;
+  }
+  cudaSetDevice(ctx_->device);
+  cudaStream_t st = stream != nullptr ? static_cast<cudaStream_t>(stream) : ctx_->stream;
+  const std::size_t H = cfg_.horizon, A = cfg_.action_dim;
+  if (condition != in_cond_)
+    cudaMemcpyAsync(in_cond_, condition, batch * cfg_.condition_dim * sizeof(float), cudaMemcpyDeviceToDevice, st);
+  if (noise != in_noise_)
+    cudaMemcpyAsync(in_noise_, noise, batch * H * A * sizeof(float), cudaMemcpyDeviceToDevice, st);
+  cudaMemcpyAsync(seed0_, &seed, sizeof(seed), cudaMemcpyHostToDevice, st);
+  const auto key = std::make_tuple(batch, steps, scheduler, use_tc(batch));
+  auto it = graphs_.find(key);
+  if (it == graphs_.end()) {
+    // record once per (batch, steps, scheduler) on a private capture stream
+    cudaStream_t cap = nullptr;
+    cudaStreamCreateWithFlags(&cap, cudaStreamNonBlocking);
+    cudaStreamSynchronize(st);
+    cudaGraph_t graph = nullptr;
+    recorded_ = 0;
+    if (cudaStreamBeginCapture(cap, cudaStreamCaptureModeThreadLocal) != cudaSuccess) {
+      err = "cudaStreamBeginCapture failed";
+      cudaStreamDestroy(cap);
+      return 2;
+    }
+    const bool ok = record_sample(batch, plan_steps(steps, scheduler), cap, err);
+    const cudaError_t end = cudaStreamEndCapture(cap, &graph);
+    cudaStreamDestroy(cap);
+    if (!ok || end != cudaSuccess || graph == nullptr) {
+      if (graph != nullptr) cudaGraphDestroy(graph);
+      if (err.empty()) err = std::string("graph capture failed: ") + cudaGetErrorString(end);
+      cudaGetLastError();
+      return 2;
+    }
+    Graph g;
+    const cudaError_t inst = cudaGraphInstantiate(&g.exec, graph, 0);
+    cudaGraphDestroy(graph);
+    if (inst != cudaSuccess) {
+      err = std::string("cudaGraphInstantiate failed: ") + cudaGetErrorString(inst);
+      return 2;
+    }
+    g.launches = recorded_;
+    it = graphs_.emplace(key, g).first;
+  }
+  if (cudaGraphLaunch(it->second.exec, st) != cudaSuccess) {
+    err = "cudaGraphLaunch failed";
+    return 2;
+  }
+  launches_ += it->second.launches;
+  if (action != out_action_)
+    cudaMemcpyAsync(action, out_action_, batch * H * A * sizeof(float), cudaMemcpyDeviceToDevice, st);
+  return 0;
+}
+
+int Unet::sample(const float* condition, const float* noise, std::size_t batch, std::size_t steps, int scheduler,
+                 std::uint64_t seed, float* action, std::string& err) noexcept {
+  if (batch > cap_) {
+    const int rc = reserve(batch, err);
+    if (rc != 0) return rc;
+  }
+  cudaSetDevice(ctx_->device);
+  cudaStream_t st = ctx_->stream;
+  const std::size_t H = cfg_.horizon, A = cfg_.action_dim, Cd = cfg_.condition_dim;
+  float* pc = pinned_;
+  float* pn = pinned_ + batch * Cd;
+  float* pa = pn + batch * H * A;
+  std::memcpy(pc, condition, batch * Cd * sizeof(float));
+  std::memcpy(pn, noise, batch * H * A * sizeof(float));
+  cudaMemcpyAsync(in_cond_, pc, batch * Cd * sizeof(float), cudaMemcpyHostToDevice, st);
+  cudaMemcpyAsync(in_noise_, pn, batch * H * A * sizeof(float), cudaMemcpyHostToDevice, st);
+  const int rc = sample_device(in_cond_, in_noise_, batch, steps, scheduler, seed, out_action_, st, err);
+  if (rc != 0) return rc;
+  cudaMemcpyAsync(pa, out_action_, batch * H * A * sizeof(float), cudaMemcpyDeviceToHost, st);
+  if (cudaStreamSynchronize(st) != cudaSuccess) {
+    err = std::string("diffusion sampling failed on the device: ") + cudaGetErrorString(cudaGetLastError());
+    return 2;
+  }
+  if (take_device_error(*ctx_, st) != 0) {
+    err = "a device pipeline wait timed out";
+    return 2;
+  }
+  std::memcpy(action, pa, batch * H * A * sizeof(float));
+  return 0;
+}
+
+int Unet::denoise(const float* condition, const float* sample, float timestep, float* eps, std::size_t batch,
+                  std::string& err) noexcept {
+  if (!std::isfinite(timestep) || batch == 0) {
+    err = "invalid denoise arguments";
+    return 1;
+  }
+  if (batch > cap_) {
+    const int rc = reserve(batch, err);
+    if (rc != 0) return rc;
+  }
+  cudaSetDevice(ctx_->device);
+  cudaStream_t st = ctx_->stream;
+  const std::size_t H = cfg_.horizon, A = cfg_.action_dim, Cd = cfg_.condition_dim;
+  const bool tc = use_tc(batch);
+  const int n_tokens = static_cast<int>(batch * H);
+  cudaMemcpyAsync(in_cond_, condition, batch * Cd * sizeof(float), cudaMemcpyHostToDevice, st);
+  cudaMemcpyAsync(in_noise_, sample, batch * H * A * sizeof(float), cudaMemcpyHostToDevice, st);
+  cudaMemcpyAsync(tstep_, &timestep, sizeof(float), cudaMemcpyHostToDevice, st);
+  const int td = static_cast<int>(cfg_.timestep_dim);
+  temb_kernel<<<1, 128, static_cast<std::size_t>(5 * td) * sizeof(float), st>>>(tstep_, 1, td, te1_w_, te1_b_,
+                                                                                 te2_w_, te2_b_, tm_row_);
+  film_time_kernel<<<ew_grid(F_, 256, *ctx_), 256, 0, st>>>(tm_row_, 1, td, wt_, F_, ft_row_);
+  prep_sample_kernel<<<ew_grid(static_cast<long long>(n_tokens) * cin_pad_, 256, *ctx_), 256, 0, st>>>(
+      in_noise_, n_tokens, static_cast<int>(A), x_master_, x_in_, cin_pad_, tc ? 1 : 0);
+  if (!record_film_cond(batch, tc, st, err) || !record_forward(batch, tc, ft_row_, st, err)) return 2;
+  const unsigned blocks = static_cast<unsigned>((n_tokens * 32 + 255) / 256);
+  const int c0 = static_cast<int>(cfg_.dims[0]);
+  if (tc) {
+    OutParams<__nv_bfloat16> p{};
+    p.z = static_cast<const __nv_bfloat16*>(h1_);
+    p.C = c0, p.A = static_cast<int>(A), p.H = static_cast<int>(H), p.n_tokens = n_tokens;
+    p.W = fo_w_, p.bias = fo_b_, p.x_master = x_master_, p.eps_out = eps_, p.update = 0;
+    if (A <= 16) out_update_kernel<__nv_bfloat16, 16><<<blocks, 256, 0, st>>>(p);
+    else out_update_kernel<__nv_bfloat16, 64><<<blocks, 256, 0, st>>>(p);
+  } else {
+    OutParams<float> p{};
+    p.z = static_cast<const float*>(h1_);
+    p.C = c0, p.A = static_cast<int>(A), p.H = static_cast<int>(H), p.n_tokens = n_tokens;
+    p.W = fo_w_, p.bias = fo_b_, p.x_master = x_master_, p.eps_out = eps_, p.update = 0;
+    if (A <= 16) out_update_kernel<float, 16><<<blocks, 256, 0, st>>>(p);
+    else out_update_kernel<float, 64><<<blocks, 256, 0, st>>>(p);
+  }
+  float* pe = pinned_;
+  cudaMemcpyAsync(pe, eps_, batch * H * A * sizeof(float), cudaMemcpyDeviceToHost, st);
+  if (cudaStreamSynchronize(st) != cudaSuccess) {
+    err = std::string("diffusion denoise failed on the device: ") + cudaGetErrorString(cudaGetLastError());
+    return 2;
+  }
+  if (take_device_error(*ctx_, st) != 0) {
+    err = "a device pipeline wait timed out";
+    return 2;
+  }
+  std::memcpy(eps, pe, batch * H * A * sizeof(float));
+  return 0;
+}
+
+}  // namespace
+
+std::unique_ptr<UnetDevice> make_unet_device(const TensorTable& tensors, std::shared_ptr<DeviceContext> ctx,
+                                             Precision precision, std::string& err) {
+  auto unet = std::make_unique<Unet>(std::move(ctx), precision);
+  if (!unet->load(tensors, err)) return nullptr;
+  if (unet->reserve(1, err) != 0) return nullptr;
+  return unet;
+}
+
+}  // namespace feb

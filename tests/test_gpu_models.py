@@ -1,0 +1,183 @@
+"""End-to-end parity of the CUDA path (through the C ABI) with the reference.
+
+* golden fixtures (tests/golden/): the reference's own outputs on its own
+  converted checkpoints - fp32 mode must match within 1e-4..1e-3;
+* the compiled reference core (oracle/_ref) on a PushT-shaped checkpoint
+  - DDIM-10 actions within max-abs 1e-3 (fp32);
+* bf16 mode (this build's added precision) within max-abs 2e-2 of the fp32
+  reference, as the north star sets for bf16 weights with fp32 accumulation.
+"""
+
+import numpy as np
+import pytest
+
+from flowedge_b200 import Engine
+from flowedge_b200 import checkpoint as ck
+from flowedge_b200.engine import device_malloc_count
+from oracle import restate
+
+pytestmark = pytest.mark.gpu
+
+GOLD = "tests/golden"
+
+
+def _engine(name, **kw):
+    return Engine(f"{GOLD}/{name}.safetensors", threads=0, device=0, **kw)
+
+
+@pytest.mark.parametrize("name", ["unet_tiny", "unet_small"])
+def test_unet_golden_fp32(golden, name):
+    _, _, g = golden(name)
+    e = _engine(name, precision="fp32")
+    assert e.model_metadata["model_digest"] == bytes(g["digest"])
+    for i, ts in enumerate(g["timesteps"]):
+        np.testing.assert_allclose(e.diffusion_denoise(g["cond"][0], g["noise"][0], float(ts)), g["eps"][i],
+                                   atol=1e-4, rtol=1e-4)
+    for steps in (1, 5, 10):
+        for i in range(3):
+            out = e.sample_diffusion(g["cond"][i], g["noise"][i], steps, "ddim")
+            np.testing.assert_allclose(out, g[f"ddim_{steps}"][i], atol=1e-4, rtol=1e-4)
+    for i in range(3):
+        out = e.sample_diffusion(g["cond"][i], g["noise"][i], 5, "ddpm", seed=int(g["ddpm_seeds"][i]))
+        np.testing.assert_allclose(out, g["ddpm_5"][i], atol=5e-4, rtol=5e-4)
+    e.close()
+
+
+@pytest.mark.parametrize("name", ["unet_tiny", "unet_small"])
+def test_unet_golden_bf16(golden, name):
+    _, _, g = golden(name)
+    e = _engine(name, precision="bf16")
+    for i in range(3):
+        out = e.sample_diffusion(g["cond"][i], g["noise"][i], 10, "ddim")
+        np.testing.assert_allclose(out, g["ddim_10"][i], atol=2e-2 * 4.0)  # action range up to 4 (unnormalised)
+    e.close()
+
+
+def test_unet_batched_matches_single_and_is_deterministic(golden):
+    _, _, g = golden("unet_small")
+    e = _engine("unet_small", precision="fp32", max_batch=3)
+    batch = e.sample_diffusion_batch(g["cond"], g["noise"], 10, "ddim")
+    np.testing.assert_allclose(batch, g["ddim_10"], atol=1e-4, rtol=1e-4)
+    again = e.sample_diffusion_batch(g["cond"], g["noise"], 10, "ddim")
+    np.testing.assert_array_equal(batch, again)
+    ddpm = e.sample_diffusion_batch(g["cond"], g["noise"], 5, "ddpm", seed=42)
+    np.testing.assert_allclose(ddpm, g["ddpm_5"], atol=5e-4, rtol=5e-4)  # sample b uses seed 42 + b
+    e.close()
+
+
+def test_no_allocation_after_warmup(golden):
+    _, _, g = golden("unet_small")
+    e = _engine("unet_small", precision="fp32", max_batch=3)
+    e.sample_diffusion_batch(g["cond"], g["noise"], 10, "ddim")
+    e.sample_diffusion(g["cond"][0], g["noise"][0], 10, "ddpm", seed=1)
+    before = device_malloc_count()
+    for _ in range(3):
+        e.sample_diffusion_batch(g["cond"], g["noise"], 10, "ddim")
+        e.sample_diffusion(g["cond"][0], g["noise"][0], 10, "ddpm", seed=1)
+    assert device_malloc_count() == before
+    e.close()
+
+
+def test_unet_metadata_and_errors(golden):
+    e = _engine("unet_tiny", precision="fp32")
+    md = e.diffusion_metadata
+    assert md["action_dim"] == 2 and md["horizon"] == 8 and md["train_timesteps"] == 20
+    assert e.cuda_resident and e.action_horizon == 8 and e.condition_dim == 6
+    with pytest.raises(RuntimeError, match="status 1"):
+        e.sample_diffusion(np.zeros(6), np.zeros((8, 2)), 21)
+    with pytest.raises(RuntimeError, match="status 5"):
+        e.lib.fe_engine_sample_diffusion and e._check(
+            e.lib.fe_engine_sample_diffusion(e.handle, np.zeros(6, np.float32).ctypes.data_as(
+                __import__("ctypes").POINTER(__import__("ctypes").c_float)),
+                np.zeros(16, np.float32).ctypes.data_as(__import__("ctypes").POINTER(__import__("ctypes").c_float)),
+                10, 7, 0, np.zeros(16, np.float32).ctypes.data_as(
+                    __import__("ctypes").POINTER(__import__("ctypes").c_float))))
+    with pytest.raises(RuntimeError, match="status 4"):
+        e.sample_condition(np.zeros(6), np.zeros(2))
+    e.close()
+
+
+@pytest.mark.parametrize("name", ["mamba_flow_tiny", "mamba_flow_bf16"])
+def test_mamba_flow_golden(golden, name):
+    _, _, g = golden(name)
+    e = _engine(name, precision="fp32")
+    assert e.model_metadata["model_digest"] == bytes(g["digest"])
+    np.testing.assert_allclose(e.run(g["tokens"]), g["hidden"], atol=2e-5, rtol=1e-4)
+    for solver, steps in (("euler", 10), ("heun", 3), ("rk4", 4)):
+        for i in range(2):
+            out = e.sample_condition(g["cond"][i], g["noise"][i], steps=steps, method=solver)
+            np.testing.assert_allclose(out, g[f"{solver}_{steps}"][i], atol=2e-5, rtol=1e-4)
+    np.testing.assert_allclose(e.sample(g["tokens"], g["noise"][0], 10, "euler"), g["pipeline_euler_10"],
+                               atol=2e-5, rtol=1e-4)
+    e.reset()
+    for i, tok in enumerate(g["tokens"][:5]):
+        np.testing.assert_allclose(e.step(tok), g["decoded"][i], atol=2e-5, rtol=1e-4)
+    snap = e.decode_state()
+    assert snap[:96] == bytes(g["snapshot"][:96])
+    np.testing.assert_allclose(np.frombuffer(snap[96:], np.float32), g["snapshot"][96:].view(np.float32),
+                               atol=2e-5, rtol=1e-4)
+    e.close()
+
+
+def test_flow_resumable_and_cancel(golden):
+    _, _, g = golden("mamba_flow_tiny")
+    e = _engine("mamba_flow_tiny", precision="fp32")
+    out = np.empty(6, np.float32)
+    e.flow_begin(g["cond"][0], g["noise"][0], steps=10, method="euler")
+    remaining = 10
+    while remaining:
+        remaining = e.flow_advance(out, step_budget=3)
+    np.testing.assert_allclose(out, g["euler_10"][0], atol=2e-5, rtol=1e-4)
+    assert e.flow_metadata["status"] == 1  # FE_ACTION_COMPLETE
+    e.flow_begin(g["cond"][0], g["noise"][0], steps=10, method="euler", generation=5)
+    e.flow_advance(out, step_budget=2)
+    e.cancel_before(6)
+    with pytest.raises(RuntimeError, match="status 8"):
+        e.flow_advance(out, step_budget=2)
+    assert e.flow_metadata["status"] == 2  # FE_ACTION_CANCELLED
+    e.close()
+
+
+def test_decode_snapshot_round_trip(golden):
+    _, _, g = golden("mamba_flow_tiny")
+    e = _engine("mamba_flow_tiny", precision="fp32")
+    e.reset()
+    for tok in g["tokens"][:3]:
+        e.step(tok)
+    snap = e.decode_state()
+    a = e.step(g["tokens"][3])
+    e.restore_decode_state(snap)
+    b = e.step(g["tokens"][3])
+    np.testing.assert_array_equal(a, b)
+    corrupt = bytearray(snap)
+    corrupt[100] ^= 0xFF
+    with pytest.raises(RuntimeError, match="status 10"):
+        e.restore_decode_state(bytes(corrupt))
+    e.close()
+
+
+def test_pusht_ddim10_matches_reference_core(tmp_path):
+    """BASELINE config 1 at full size against the compiled reference core."""
+    from oracle import reference
+
+    if not reference.available():
+        pytest.skip("oracle/_ref not built")
+    tensors, meta = ck.diffusion_tensors(ck.PUSHT, seed=0)
+    path = tmp_path / "pusht.safetensors"
+    ck.write_checkpoint(path, tensors, metadata=meta)
+    rng = np.random.default_rng(0)
+    cond = rng.standard_normal((2, 132)).astype(np.float32)
+    noise = rng.standard_normal((2, 16, 2)).astype(np.float32)
+    ref = reference.ReferenceEngine(path, threads=8)
+    expected = np.stack([ref.sample_diffusion(cond[i], noise[i], 10) for i in range(2)])
+    eps_ref = ref.diffusion_denoise(cond[0], noise[0], 90.0)
+    ref.close()
+    e = Engine(path, threads=0, device=0, precision="fp32", max_batch=2)
+    np.testing.assert_allclose(e.diffusion_denoise(cond[0], noise[0], 90.0), eps_ref, atol=1e-4, rtol=1e-4)
+    out = np.stack([e.sample_diffusion(cond[i], noise[i], 10) for i in range(2)])
+    assert np.abs(out - expected).max() <= 1e-3
+    e.close()
+    eb = Engine(path, threads=0, device=0, precision="bf16", max_batch=2)
+    outb = eb.sample_diffusion_batch(cond, noise, 10)
+    assert np.abs(outb - expected).max() <= 2e-2
+    eb.close()
