@@ -1,0 +1,340 @@
+#!/usr/bin/env python3
+"""Benchmark of the policy-sampling hot path on B200.
+
+Workload: bimanual Diffusion Policy ConditionalUnet1D
+(action 14, horizon 64, condition 284, dims 512/1024/2048, kernel 5, 8 groups,
+step embedding 128), bf16 weights / fp32 accumulation, 10-step DDIM (eta 0),
+global batch 4096 sharded over the ranks (strong scaling), seeded synthetic
+inputs and PyTorch-default random-init weights (no datasets or checkpoints are
+reachable).  One step = one complete DDIM-10 sample of the rank's shard.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Rank 0 prints one JSON line.  `value` is device-timed (CUDA events on the
+launching stream, inputs resident in HBM, max over ranks); `e2e` is the same
+metric through the host-buffer C ABI (host->device inputs and device->host
+actions inside the timed region).  `--impl reference` times the reference's own
+CPU core (oracle/_ref) on the host cores on a bounded sample of the workload.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+REPO = Path(__file__).resolve().parent
+sys.path.insert(0, str(REPO))
+
+from flowedge_b200 import checkpoint as ck  # noqa: E402
+
+METRIC = "DDIM action chunks/s at b=4096 (bimanual U-Net, 10-step DDIM)"
+UNIT = "chunks/s"
+GLOBAL_BATCH = 4096
+STEPS = 10
+SEED = 0
+
+
+def _dist():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+def _checkpoint(path: Path, spec, bf16_round: bool):
+    """Seeded random-init U-Net; with bf16_round the 2-D/3-D weights are
+    rounded to bf16 and stored as fp32, so the bf16 engine and the fp32
+    reference core run identical weights."""
+    if path.exists():
+        return path
+    tensors, meta = ck.diffusion_tensors(spec, seed=SEED)
+    if bf16_round:
+        tensors = {k: (ck.bf16_bits_to_f32(ck.to_bf16_bits(v)) if v.ndim >= 2 else v) for k, v in tensors.items()}
+    tmp = path.with_suffix(f".tmp{os.getpid()}")
+    ck.write_checkpoint(tmp, tensors, metadata=meta)
+    os.replace(tmp, path)
+    return path
+
+
+def _inputs(spec, batch, offset=0):
+    rng = np.random.default_rng(SEED + 1)
+    cond = rng.standard_normal((GLOBAL_BATCH, spec.condition_dim), dtype=np.float32)
+    noise = rng.standard_normal((GLOBAL_BATCH, spec.horizon, spec.action_dim), dtype=np.float32)
+    return (np.ascontiguousarray(cond[offset:offset + batch]),
+            np.ascontiguousarray(noise[offset:offset + batch]))
+
+
+class ClockSampler:
+    """nvidia-smi sampling of SM clocks and throttle reasons during a region."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device: int):
+        self.device = device
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.device}", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        self.lines = []
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                out, _ = self.proc.communicate()
+            self.lines = [l for l in out.splitlines() if l.strip()]
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in getattr(self, "lines", []):
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for name, val in zip(names, f[5:9]):
+                if val.lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def _peaks():
+    path = REPO / "MEASURED_PEAKS.json"
+    if path.exists():
+        data = json.loads(path.read_text())
+        return data.get("bf16_tflops_sustained", data.get("bf16_tflops")), "measured (sustained bf16)"
+    return 1590.0, "fallback"
+
+
+# ---------------------------------------------------------------------------
+# CPU: the reference core on the host cores
+
+
+def _reference_throughput(path: Path, spec, chunks: int, threads: int, rounds: int = 1):
+    """`threads` engines sharing one weight store, threads=0 each (one chunk
+    per engine per round); returns (chunks/s, seconds)."""
+    from oracle import reference
+
+    lib = reference.lib()
+    weights = lib.fe_weights_load(str(path).encode())
+    if not weights:
+        raise RuntimeError(lib.fe_engine_last_error().decode())
+    engines = [reference.ReferenceEngine.from_weights(weights, 0) for _ in range(threads)]
+    cond, noise = _inputs(spec, chunks)
+    done = []
+
+    def work(i):
+        e = engines[i % threads]
+        for j in range(i, chunks, threads):
+            e.sample_diffusion(cond[j], noise[j], STEPS)
+            done.append(j)
+
+    t0 = time.perf_counter()
+    for _ in range(rounds):
+        pool = [threading.Thread(target=work, args=(i,)) for i in range(threads)]
+        for t in pool:
+            t.start()
+        for t in pool:
+            t.join()
+    elapsed = time.perf_counter() - t0
+    for e in engines:
+        e.close()
+    lib.fe_weights_free(weights)
+    return chunks * rounds / elapsed, elapsed
+
+
+def run_reference(args):
+    world, rank, _ = _dist()
+    if rank != 0:
+        return 0
+    spec = ck.BIMANUAL
+    path = _checkpoint(Path(args.workdir) / "bench_c4_bf16w.safetensors", spec, True)
+    threads = os.cpu_count() or 1
+    chunks = threads  # one DDIM-10 chunk per host thread per step
+    for _ in range(args.warmup):
+        _reference_throughput(path, spec, max(1, threads // 4), threads)
+    times = []
+    for _ in range(args.steps):
+        _, secs = _reference_throughput(path, spec, chunks, threads)
+        times.append(secs)
+    total = sum(times)
+    value = chunks * args.steps / total
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": 1000 * total / args.steps, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "C4 bimanual U-Net DDIM-10 (reference fp32 CPU core on the bf16-rounded weights)",
+                   "global_batch": GLOBAL_BATCH, "horizon": spec.horizon, "action_dim": spec.action_dim},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "reference",
+                         "sample": f"{chunks} chunks per step, {threads} engines x 1 thread, shared weights"},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ---------------------------------------------------------------------------
+# GPU
+
+
+def run_ours(args):
+    import torch
+
+    world, rank, local = _dist()
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
+                                device_id=torch.device("cuda", local))
+    from flowedge_b200 import Engine
+    from flowedge_b200.engine import device_malloc_count
+
+    spec = ck.BIMANUAL
+    workdir = Path(args.workdir)
+    workdir.mkdir(parents=True, exist_ok=True)
+    path = workdir / "bench_c4_bf16w.safetensors"
+    if rank == 0:
+        _checkpoint(path, spec, True)
+    if dist is not None:
+        dist.barrier()
+    assert GLOBAL_BATCH % world == 0
+    shard = GLOBAL_BATCH // world
+    cond, noise = _inputs(spec, shard, offset=rank * shard)
+    engine = Engine(path, threads=0, device=local, precision="bf16", max_batch=shard)
+
+    stream = torch.cuda.current_stream()
+    d_cond = torch.from_numpy(cond).cuda()
+    d_noise = torch.from_numpy(noise).cuda()
+    d_action = torch.empty((shard, spec.horizon, spec.action_dim), dtype=torch.float32, device="cuda")
+
+    def step():
+        engine.sample_diffusion_device(d_cond.data_ptr(), d_noise.data_ptr(), shard, d_action.data_ptr(), STEPS,
+                                       "ddim", SEED + rank * shard, stream.cuda_stream)
+
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize()
+    mallocs0 = device_malloc_count()
+    launches0 = engine.kernel_launches
+    start = torch.cuda.Event(enable_timing=True)
+    stop = torch.cuda.Event(enable_timing=True)
+    if dist is not None:
+        dist.barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clocks:
+        start.record(stream)
+        for _ in range(args.steps):
+            step()
+        stop.record(stream)
+        torch.cuda.synchronize()
+    ms = start.elapsed_time(stop)
+    launches = engine.kernel_launches - launches0
+    t = torch.tensor([ms], dtype=torch.float64, device="cuda")
+    if dist is not None:
+        dist.barrier()
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_max = float(t.item())
+    value = GLOBAL_BATCH * args.steps / (ms_max / 1000.0)
+    mallocs = device_malloc_count() - mallocs0
+
+    # e2e through the host-buffer public API (inputs/outputs in host memory)
+    out = np.empty_like(noise)
+    engine.sample_diffusion_batch(cond, noise, STEPS, "ddim", SEED)  # warm the host-API path
+    if dist is not None:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e2e_steps = max(1, min(args.steps, 3))
+    t0 = time.perf_counter()
+    for _ in range(e2e_steps):
+        out[:] = engine.sample_diffusion_batch(cond, noise, STEPS, "ddim", SEED)
+    e2e_s = time.perf_counter() - t0
+    te = torch.tensor([e2e_s], dtype=torch.float64, device="cuda")
+    if dist is not None:
+        dist.all_reduce(te, op=dist.ReduceOp.MAX)
+    e2e_value = GLOBAL_BATCH * e2e_steps / float(te.item())
+
+    # dominant kernel: the tcgen05 conv GEMMs of one denoise forward
+    prof = engine.profile_diffusion(shard)
+    peak, peak_kind = _peaks()
+    achieved = prof["conv_flops"] / (prof["conv_ms"] / 1000.0) / 1e12
+    line = None
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": max(args.warmup, 3), "ms_per_step": ms_max / args.steps, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": "C4 bimanual U-Net (A14 H64 cond284, dims 512/1024/2048) DDIM-10, bf16 weights "
+                                   "fp32 accumulate", "global_batch": GLOBAL_BATCH, "per_gpu_batch": shard,
+                       "horizon": spec.horizon, "action_dim": spec.action_dim, "parallelism": f"batch shards x{world}",
+                       "l2": "working set above L2 (each activation tensor 268 MB at b=4096, weights 0.5 GB)"},
+            "clocks": clocks.summary(),
+            "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": int(cond.nbytes + noise.nbytes),
+                    "d2h_bytes_per_step": int(out.nbytes)},
+            "gpu_launches": int(launches),
+            "device_mallocs_in_timed_region": int(mallocs),
+            "roofline": {"bound": "tensor", "kernel": "tc_gemm_kernel (conv GEMMs of one denoise)",
+                         "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
+                         "peak_kind": peak_kind, "traffic": None,
+                         "conv_share_of_forward": prof["conv_ms"] / prof["forward_ms"],
+                         "conv_launches_per_forward": prof["conv_launches"]},
+        }
+    if world == 1 and not args.no_cpu_baseline:
+        threads = os.cpu_count() or 1
+        cpu_value, secs = _reference_throughput(path, spec, threads, threads)
+        line["cpu_baseline"] = {"value": cpu_value, "unit": UNIT, "cores": threads, "kind": "reference",
+                                "sample": f"{threads} chunks (one per host thread, {secs:.1f} s)"}
+    engine.close()
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+    if line is not None:
+        print(json.dumps(line), flush=True)
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    ap.add_argument("--workdir", default=os.environ.get("FLOWEDGE_BENCH_DIR", "/tmp/flowedge_bench"))
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    Path(args.workdir).mkdir(parents=True, exist_ok=True)
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_ours(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -81,6 +81,8 @@ class UnetDevice {
                             int scheduler, std::uint64_t seed, float* action, void* stream,
                             std::string& err) noexcept = 0;
   [[nodiscard]] virtual std::uint64_t kernel_launches() const noexcept = 0;
+  // One forward with CUDA events around each tensor-core conv (see unet.cu).
+  virtual int profile(std::size_t batch, double* metrics, std::string& err) noexcept = 0;
 };
 
 std::unique_ptr<UnetDevice> make_unet_device(const TensorTable& tensors, std::shared_ptr<DeviceContext> ctx,

@@ -1132,6 +1132,22 @@ int fe_engine_smolvla_sample(fe_engine* engine, const float* initial_noise, size
 uint64_t fe_device_malloc_count(void) { return feb::device_malloc_count(); }
 uint64_t fe_host_malloc_count(void) { return feb::host_malloc_count(); }
 
+int fe_engine_profile_diffusion(fe_engine* engine, size_t batch, double* metrics) {
+  clear_error();
+  if (engine == nullptr || metrics == nullptr || batch == 0) {
+    set_error("Invalid arguments to fe_engine_profile_diffusion");
+    return FE_STATUS_INVALID_ARGUMENT;
+  }
+  if (!engine->unet) {
+    set_error("Model has no Diffusion Policy head");
+    return FE_STATUS_UNSUPPORTED_MODEL;
+  }
+  std::string err;
+  const int rc = engine->unet->profile(batch, metrics, err);
+  if (rc != 0) set_error("Diffusion profiling failed: " + err);
+  return rc;
+}
+
 int fe_engine_synchronize(fe_engine* engine) {
   clear_error();
   if (engine == nullptr) {

@@ -171,7 +171,9 @@ class Flow final : public FlowDevice {
                     float* out, void* stream, std::string& err) noexcept override;
 
  private:
-  bool use_tc(std::size_t batch) const { return prec_ == Precision::kBF16 && static_cast<int>(batch) >= kTcMinRows; }
+  bool use_tc(std::size_t batch) const {
+    return tc_ok_ && prec_ == Precision::kBF16 && static_cast<int>(batch) >= kTcMinRows;
+  }
   bool gemm(const Mat& m, const void* in, int in_ld, std::size_t batch, float* out_f32, void* out_bf16, int out_ld,
             const float* add_vec, const float* add_tok, int act, bool tc, cudaStream_t st, std::string& err);
   bool record_step(std::size_t batch, int method, bool tc, cudaStream_t st, std::string& err);
@@ -182,6 +184,7 @@ class Flow final : public FlowDevice {
   Precision prec_;
   FlowConfig cfg_{};
   int a_pad_ = 0, c_pad_ = 0;
+  bool tc_ok_ = false;
   DeviceArena wts_;
   Mat in_, cond_, out_;
   std::vector<Mat> layers_;
@@ -234,10 +237,11 @@ bool Flow::load(const TensorTable& t, std::string& err) {
   const int H = static_cast<int>(cfg_.hidden);
   a_pad_ = static_cast<int>((cfg_.action_dim + 63) / 64 * 64);
   c_pad_ = static_cast<int>((cfg_.cond_dim + 63) / 64 * 64);
-  if (H % 64 != 0) {
-    err = "flow hidden width must be a multiple of 64";
+  if (H % 8 != 0) {
+    err = "flow hidden width must be a multiple of 8";
     return false;
   }
+  tc_ok_ = H % 64 == 0;
   const bool bf = prec_ == Precision::kBF16;
   ArenaPlan plan;
   auto plan_mat = [&](int rows, int cols) {
@@ -291,6 +295,10 @@ bool Flow::load(const TensorTable& t, std::string& err) {
   for (std::size_t j = 0; j < half; ++j)
     f[j] = std::pow(10000.0f, -static_cast<float>(j) / static_cast<float>(half));
   freqs_ = wts_.take_n<float>(half);
+  if (wts_.overflowed()) {
+    err = "internal error: flow weight arena too small";
+    return false;
+  }
   cudaMemcpy(freqs_, f.data(), half * 4, cudaMemcpyHostToDevice);
   if (cudaDeviceSynchronize() != cudaSuccess) {
     err = "flow weight upload failed";
@@ -337,6 +345,11 @@ int Flow::reserve(std::size_t batch, std::string& err) noexcept {
   h1_ = ws_.take(rows * H * 4);
   cin_ = ws_.take(rows * c_pad_ * 4);
   step_ = ws_.take_n<int>(4);
+  if (ws_.overflowed()) {
+    err = "internal error: flow workspace arena too small";
+    cap_ = 0;
+    return 2;
+  }
   cudaMemset(x_, 0, ws_.used());
   if (pinned_ != nullptr) cudaFreeHost(pinned_);
   pinned_ = nullptr;

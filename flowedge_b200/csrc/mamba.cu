@@ -362,6 +362,10 @@ bool Mamba::load(const TensorTable& t, std::string& err) {
     if (!get(i, "mixer.out_proj.weight", {dm, di}, true, v)) return false;
     put_mat(v, static_cast<int>(dm), static_cast<int>(di), L.out_proj);
   }
+  if (wts_.overflowed()) {
+    err = "internal error: Mamba weight arena too small";
+    return false;
+  }
   cudaFuncSetAttribute(scan_kernel<16, 32>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
   cudaFuncSetAttribute(scan_kernel<8, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
   cudaFuncSetAttribute(scan_kernel<4, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
@@ -426,6 +430,11 @@ int Mamba::reserve(std::size_t batch, std::size_t max_len, std::string& err) noe
   yb_ = ws_.take_n<__nv_bfloat16>(rows * di);
   state_ = ws_.take_n<float>(state_floats());
   dh_ = ws_.take_n<float>(dm + 2 * di + di + wd + di + di + dm + 64);
+  if (ws_.overflowed()) {
+    err = "internal error: Mamba workspace arena too small";
+    cap_tokens_ = 0;
+    return 2;
+  }
   cudaMemset(tokens_, 0, ws_.used());
   if (!saved.empty()) cudaMemcpy(state_, saved.data(), saved.size() * 4, cudaMemcpyHostToDevice);
   const std::size_t need = tokens * (dm + 1) + state_floats();

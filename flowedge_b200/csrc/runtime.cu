@@ -157,12 +157,16 @@ bool DeviceArena::init(std::size_t bytes, std::string& err) {
   }
   size_ = bytes;
   used_ = 0;
+  overflowed_ = false;
   return true;
 }
 
 void* DeviceArena::take(std::size_t bytes) {
   const std::size_t aligned = (bytes + 255) & ~std::size_t(255);
-  if (base_ == nullptr || used_ + aligned > size_) return nullptr;
+  if (base_ == nullptr || used_ + aligned > size_) {
+    overflowed_ = true;
+    return nullptr;
+  }
   void* p = base_ + used_;
   used_ += aligned;
   return p;

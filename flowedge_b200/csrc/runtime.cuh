@@ -42,6 +42,9 @@ class DeviceArena {
   }
   [[nodiscard]] std::size_t used() const noexcept { return used_; }
   [[nodiscard]] std::size_t size() const noexcept { return size_; }
+  // True once a take() did not fit (it returned null); callers check this
+  // before launching anything on the carved buffers.
+  [[nodiscard]] bool overflowed() const noexcept { return overflowed_; }
   void reset() noexcept { used_ = 0; }
   void release() noexcept;
 
@@ -49,9 +52,12 @@ class DeviceArena {
   char* base_ = nullptr;
   std::size_t size_ = 0;
   std::size_t used_ = 0;
+  bool overflowed_ = false;
 };
 
-// Sizing pass: the same sequence of take() calls against a counting arena.
+// Sizing pass for a DeviceArena.  Every add() rounds up like take(); the
+// total carries 64 KiB of slack for the rounding of takes that a plan lumps
+// into one add().
 class ArenaPlan {
  public:
   void add(std::size_t bytes) { total_ += (bytes + 255) & ~std::size_t(255); }
@@ -59,7 +65,7 @@ class ArenaPlan {
   void add_n(std::size_t n) {
     add(n * sizeof(T));
   }
-  [[nodiscard]] std::size_t total() const noexcept { return total_; }
+  [[nodiscard]] std::size_t total() const noexcept { return total_ + (std::size_t(1) << 16); }
 
  private:
   std::size_t total_ = 0;

@@ -30,6 +30,9 @@ namespace {
 
 constexpr int kSliceCh = 256;
 constexpr long long kTcMinTokens = 512;
+// The weight-streaming path runs the batch in chunks of at most this many
+// tokens (its split-K partial buffers scale with the chunk, not the batch).
+constexpr std::size_t kSimtChunkTokens = 1024;
 constexpr std::size_t kFinalNormGroups = 8;
 
 std::uint16_t bf16_bits(float v) {
@@ -218,6 +221,14 @@ class Unet final : public UnetDevice {
     k<<<grid, block, smem, st>>>(args...);
     ++recorded_;
   }
+  // fp32 pointer to sample b0_ of a [samples][per_sample] buffer (the
+  // weight-streaming path processes the batch chunk by chunk; b0_ = 0 on the
+  // tensor path)
+  float* at_sample(void* base, std::size_t per_sample) const { return static_cast<float*>(base) + b0_ * per_sample; }
+  std::size_t chunk_samples(std::size_t batch, bool tc) const {
+    return tc ? batch : std::max<std::size_t>(1, kSimtChunkTokens / cfg_.horizon);
+  }
+  bool record_update(std::size_t nb, bool tc, const StepScalars* step, float* eps_out, cudaStream_t st);
 
   std::shared_ptr<DeviceContext> ctx_;
   Precision prec_;
@@ -274,6 +285,13 @@ class Unet final : public UnetDevice {
   std::map<std::tuple<std::size_t, std::size_t, int, bool>, Graph> graphs_;
   std::uint64_t launches_ = 0;
   std::uint64_t recorded_ = 0;
+  std::size_t b0_ = 0;
+  // profiling (fe_engine_profile_diffusion): events around each tensor-core conv
+  bool profiling_ = false;
+  std::vector<std::pair<cudaEvent_t, cudaEvent_t>> prof_events_;
+  double prof_flops_ = 0;
+ public:
+  int profile(std::size_t batch, double* metrics, std::string& err) noexcept override;
 };
 
 bool Unet::load(const TensorTable& t, std::string& err) {
@@ -584,6 +602,10 @@ bool Unet::load(const TensorTable& t, std::string& err) {
   for (std::size_t i = 0; i < T; ++i) ts[i] = static_cast<float>(i);
   float* d_ts = put(ts);
   float* d_tm = wts_.take_n<float>(T * static_cast<std::size_t>(td));
+  if (wts_.overflowed()) {
+    err = "internal error: U-Net weight arena too small";
+    return false;
+  }
   temb_kernel<<<static_cast<unsigned>(T), 128, static_cast<std::size_t>(5 * td) * sizeof(float), st>>>(
       d_ts, static_cast<int>(T), td, te1_w_, te1_b_, te2_w_, te2_b_, d_tm);
   film_time_kernel<<<ew_grid(static_cast<long long>(T) * F_, 256, *ctx_), 256, 0, st>>>(d_tm, static_cast<int>(T), td,
@@ -611,10 +633,12 @@ int Unet::reserve(std::size_t batch, std::string& err) noexcept {
     per_sample = std::max(per_sample, cfg_.dims[s] * (H >> s));
   }
   act_elems_ = per_sample * cap_tc;
-  // split-K partials: nslices * n_tokens * M for the largest conv
+  // split-K partials: nslices * n_tokens * M for the largest conv, for one
+  // chunk of the weight-streaming path
   std::size_t part = 0;
+  const std::size_t simt_batch = std::min(batch, chunk_samples(batch, false));
   auto pc = [&](const ConvDev& c, std::size_t L) {
-    part = std::max(part, static_cast<std::size_t>(c.nslices) * batch * L * static_cast<std::size_t>(c.oc));
+    part = std::max(part, static_cast<std::size_t>(c.nslices) * simt_batch * L * static_cast<std::size_t>(c.oc));
   };
   for (std::size_t s = 0; s < cfg_.stages; ++s) {
     const std::size_t L = H >> s;
@@ -685,6 +709,11 @@ int Unet::reserve(std::size_t batch, std::string& err) noexcept {
   p2_ = ws_.take_n<float>(part_elems_);
   p3_ = ws_.take_n<float>(part_elems_);
   stats_ = ws_.take_n<double>(cap_tc * 8 * 2 * 2 + 64);
+  if (ws_.overflowed()) {
+    err = "internal error: U-Net workspace arena too small";
+    cap_ = 0;
+    return 2;
+  }
   // zero everything once so padded channels / padded samples read as zeros
   cudaMemsetAsync(in_cond_, 0, ws_.used(), ctx_->stream);
   // pinned staging for host calls
@@ -782,7 +811,7 @@ void Unet::simt_gn(const ConvDev& c, const float* partial, std::size_t batch, in
   p.groups = groups;
   p.mish = 1;
   if (film_block != nullptr) {
-    p.film_cond = film_cond_;
+    p.film_cond = film_cond_ + b0_ * static_cast<std::size_t>(F_);
     p.film_time = film_time_row;
     p.film_F = F_;
     p.film_off = film_block->film_off;
@@ -831,7 +860,20 @@ bool Unet::tc_conv(const ConvDev& c, const std::vector<Act>& srcs, int L_out, st
     l.group_ch = c.oc / groups;
   }
   ++recorded_;
-  return tc_gemm(l, *ctx_, st, err) == cudaSuccess;
+  if (!profiling_) return tc_gemm(l, *ctx_, st, err) == cudaSuccess;
+  // algorithmic FLOPs: 2 * out channels * (taps * real input channels) * tokens
+  int ic_real = 0;
+  for (const tc::Seg& sg : c.segs) ic_real += sg.kblocks * 64;
+  if (c.kind == ConvKind::kSame && c.ic_total == cin_pad_) ic_real = static_cast<int>(cfg_.action_dim) * c.taps;
+  prof_flops_ += 2.0 * c.oc * ic_real * static_cast<double>(batch) * L_out;
+  cudaEvent_t a, b;
+  cudaEventCreate(&a);
+  cudaEventCreate(&b);
+  cudaEventRecord(a, st);
+  const bool ok = tc_gemm(l, *ctx_, st, err) == cudaSuccess;
+  cudaEventRecord(b, st);
+  prof_events_.emplace_back(a, b);
+  return ok;
 }
 
 void Unet::tc_gn(const Act& y, std::size_t batch, int groups, int parts, const float* gamma, const float* beta,
@@ -861,7 +903,7 @@ bool Unet::block(const BlockDev& blk, const std::vector<Act>& in, int L, std::si
                  const float* film_time_row, Act out, cudaStream_t st, std::string& err) {
   const int G = static_cast<int>(cfg_.groups);
   const int oc = blk.oc;
-  Act h1{h1_, oc, L};
+  Act h1{at_sample(h1_, static_cast<std::size_t>(oc) * L), oc, L};
   if (!tc) {
     if (!simt_conv(blk.c1, in, L, batch, p1_, st, err)) return false;
     simt_gn(blk.c1, p1_, batch, L, blk.g1, blk.b1, G, &blk, film_time_row, nullptr, nullptr, nullptr, h1, st);
@@ -892,12 +934,12 @@ bool Unet::block(const BlockDev& blk, const std::vector<Act>& in, int L, std::si
 
 bool Unet::record_film_cond(std::size_t batch, bool tc, cudaStream_t st, std::string& err) {
   launch(prep_cond_kernel, dim3(ew_grid(static_cast<long long>(batch) * cond_pad_, 256, *ctx_)), dim3(256), 0, st,
-         static_cast<const float*>(in_cond_), static_cast<int>(batch), static_cast<int>(cfg_.condition_dim), mcond_,
-         cond_pad_, tc ? 1 : 0);
-  Act mc{mcond_, cond_pad_, 1};
+         static_cast<const float*>(in_cond_ + b0_ * cfg_.condition_dim), static_cast<int>(batch),
+         static_cast<int>(cfg_.condition_dim), static_cast<void*>(at_sample(mcond_, cond_pad_)), cond_pad_, tc ? 1 : 0);
+  Act mc{at_sample(mcond_, cond_pad_), cond_pad_, 1};
   if (tc) return tc_conv(film_, {mc}, 1, batch, film_cond_, F_, 1, 1, 0, false, 0, true, st, err);
   if (!simt_conv(film_, {mc}, 1, batch, p1_, st, err)) return false;
-  simt_reduce(film_, p1_, batch, 1, Act{film_cond_, F_, 1}, 1, 1, 0, st);
+  simt_reduce(film_, p1_, batch, 1, Act{film_cond_ + b0_ * static_cast<std::size_t>(F_), F_, 1}, 1, 1, 0, st);
   return true;
 }
 
@@ -905,18 +947,20 @@ bool Unet::record_forward(std::size_t batch, bool tc, const float* ft_row, cudaS
   const std::size_t S = cfg_.stages;
   const int H = static_cast<int>(cfg_.horizon);
   std::size_t li = 0;
-  Act x{x_in_, cin_pad_, H};
+  Act x{at_sample(x_in_, static_cast<std::size_t>(cin_pad_) * H), cin_pad_, H};
   std::vector<Act> skips(S);
   int L = H;
   for (std::size_t s = 0; s < S; ++s) {
     const int oc = static_cast<int>(cfg_.dims[s]);
-    Act o0{acts_[li++], oc, L}, o1{acts_[li++], oc, L};
+    const std::size_t per = static_cast<std::size_t>(oc) * L;
+    Act o0{at_sample(acts_[li], per), oc, L}, o1{at_sample(acts_[li + 1], per), oc, L};
+    li += 2;
     if (!block(down_[s][0], {x}, L, batch, tc, ft_row, o0, st, err)) return false;
     if (!block(down_[s][1], {o0}, L, batch, tc, ft_row, o1, st, err)) return false;
     skips[s] = o1;
     x = o1;
     if (s + 1 < S) {
-      Act d{acts_[li++], oc, L / 2};
+      Act d{at_sample(acts_[li++], per / 2), oc, L / 2};
       if (tc) {
         if (!tc_conv(ds_[s], {x}, L / 2, batch, d.p, oc, L / 2, 1, 0, false, 0, false, st, err)) return false;
       } else {
@@ -930,17 +974,19 @@ bool Unet::record_forward(std::size_t batch, bool tc, const float* ft_row, cudaS
     }
   }
   for (int m = 0; m < 2; ++m) {
-    Act o{acts_[li++], x.C, L};
+    Act o{at_sample(acts_[li++], static_cast<std::size_t>(x.C) * L), x.C, L};
     if (!block(mid_[m], {x}, L, batch, tc, ft_row, o, st, err)) return false;
     x = o;
   }
   for (std::size_t s = 0; s + 1 < S; ++s) {
     const Act skip = skips[S - 1 - s];
     const int low = static_cast<int>(cfg_.dims[S - 2 - s]);
-    Act o0{acts_[li++], low, L}, o1{acts_[li++], low, L};
+    const std::size_t per = static_cast<std::size_t>(low) * L;
+    Act o0{at_sample(acts_[li], per), low, L}, o1{at_sample(acts_[li + 1], per), low, L};
+    li += 2;
     if (!block(up_[s][0], {x, skip}, L, batch, tc, ft_row, o0, st, err)) return false;
     if (!block(up_[s][1], {o0}, L, batch, tc, ft_row, o1, st, err)) return false;
-    Act u{acts_[li++], low, 2 * L};
+    Act u{at_sample(acts_[li++], 2 * per), low, 2 * L};
     for (int ph = 0; ph < 2; ++ph) {
       if (tc) {
         if (!tc_conv(us_[s][ph], {o1}, L, batch, u.p, low, 2 * L, 2, ph, false, 0, false, st, err)) return false;
@@ -954,7 +1000,7 @@ bool Unet::record_forward(std::size_t batch, bool tc, const float* ft_row, cudaS
   }
   // final conv -> GN(8) + Mish -> z in h1_
   const int c0 = static_cast<int>(cfg_.dims[0]);
-  Act z{h1_, c0, H};
+  Act z{at_sample(h1_, static_cast<std::size_t>(c0) * H), c0, H};
   if (tc) {
     if (!tc_conv(fc_, {x}, H, batch, y1_, c0, H, 1, 0, true, static_cast<int>(kFinalNormGroups), false, st, err))
       return false;
@@ -1005,38 +1051,64 @@ __global__ void seeds_kernel(const std::uint64_t* seed0, std::uint64_t* seeds, i
   if (i < n) seeds[i] = *seed0 + static_cast<std::uint64_t>(i);
 }
 
+bool Unet::record_update(std::size_t nb, bool tc, const StepScalars* step, float* eps_out, cudaStream_t st) {
+  const int H = static_cast<int>(cfg_.horizon), A = static_cast<int>(cfg_.action_dim);
+  const int c0 = static_cast<int>(cfg_.dims[0]);
+  const int n_tokens = static_cast<int>(nb) * H;
+  const unsigned blocks = static_cast<unsigned>((n_tokens * 32 + 255) / 256);
+  const std::size_t xa = b0_ * static_cast<std::size_t>(H * A);
+  auto fill = [&](auto& p) {
+    p.C = c0, p.A = A, p.H = H, p.n_tokens = n_tokens;
+    p.W = fo_w_, p.bias = fo_b_, p.x_master = x_master_ + xa;
+    p.eps_out = eps_out != nullptr ? eps_out + xa : nullptr;
+    p.update = step != nullptr ? 1 : 0;
+    if (step != nullptr) p.step = *step;
+    p.seeds = seeds_ + b0_;
+    p.Cin = cin_pad_;
+  };
+  if (tc) {
+    OutParams<__nv_bfloat16> p{};
+    fill(p);
+    p.z = static_cast<const __nv_bfloat16*>(h1_);
+    p.x_in = x_in_;
+    p.x_in_bf16 = 1;
+    if (A <= 16) launch(out_update_kernel<__nv_bfloat16, 16>, dim3(blocks), dim3(256), 0, st, p);
+    else launch(out_update_kernel<__nv_bfloat16, 64>, dim3(blocks), dim3(256), 0, st, p);
+  } else {
+    OutParams<float> p{};
+    fill(p);
+    p.z = at_sample(h1_, static_cast<std::size_t>(c0) * H);
+    p.x_in = at_sample(x_in_, static_cast<std::size_t>(cin_pad_) * H);
+    p.x_in_bf16 = 0;
+    if (A <= 16) launch(out_update_kernel<float, 16>, dim3(blocks), dim3(256), 0, st, p);
+    else launch(out_update_kernel<float, 64>, dim3(blocks), dim3(256), 0, st, p);
+  }
+  return cudaPeekAtLastError() == cudaSuccess;
+}
+
 bool Unet::record_sample(std::size_t batch, const std::vector<StepPlan>& plan, cudaStream_t st, std::string& err) {
   const bool tc = use_tc(batch);
   const int H = static_cast<int>(cfg_.horizon), A = static_cast<int>(cfg_.action_dim);
   const int n_tokens = static_cast<int>(batch) * H;
+  const std::size_t chunk = chunk_samples(batch, tc);
+  b0_ = 0;
   launch(seeds_kernel, dim3((static_cast<unsigned>(batch) + 255) / 256), dim3(256), 0, st,
          static_cast<const std::uint64_t*>(seed0_), seeds_, static_cast<int>(batch));
   launch(prep_sample_kernel, dim3(ew_grid(static_cast<long long>(n_tokens) * cin_pad_, 256, *ctx_)), dim3(256), 0, st,
          static_cast<const float*>(in_noise_), n_tokens, A, x_master_, x_in_, cin_pad_, tc ? 1 : 0);
-  if (!record_film_cond(batch, tc, st, err)) return false;
-  const int c0 = static_cast<int>(cfg_.dims[0]);
+  for (b0_ = 0; b0_ < batch; b0_ += chunk)
+    if (!record_film_cond(std::min(chunk, batch - b0_), tc, st, err)) return false;
   for (const StepPlan& sp : plan) {
     const float* ft_row = film_time_ + static_cast<std::size_t>(sp.timestep) * static_cast<std::size_t>(F_);
-    if (!record_forward(batch, tc, ft_row, st, err)) return false;
-    const unsigned blocks = static_cast<unsigned>((n_tokens * 32 + 255) / 256);
-    if (tc) {
-      OutParams<__nv_bfloat16> p{};
-      p.z = static_cast<const __nv_bfloat16*>(h1_);
-      p.C = c0, p.A = A, p.H = H, p.n_tokens = n_tokens;
-      p.W = fo_w_, p.bias = fo_b_, p.x_master = x_master_, p.eps_out = nullptr, p.update = 1;
-      p.step = sp.scalars, p.seeds = seeds_, p.x_in = x_in_, p.Cin = cin_pad_, p.x_in_bf16 = 1;
-      if (A <= 16) launch(out_update_kernel<__nv_bfloat16, 16>, dim3(blocks), dim3(256), 0, st, p);
-      else launch(out_update_kernel<__nv_bfloat16, 64>, dim3(blocks), dim3(256), 0, st, p);
-    } else {
-      OutParams<float> p{};
-      p.z = static_cast<const float*>(h1_);
-      p.C = c0, p.A = A, p.H = H, p.n_tokens = n_tokens;
-      p.W = fo_w_, p.bias = fo_b_, p.x_master = x_master_, p.eps_out = nullptr, p.update = 1;
-      p.step = sp.scalars, p.seeds = seeds_, p.x_in = x_in_, p.Cin = cin_pad_, p.x_in_bf16 = 0;
-      if (A <= 16) launch(out_update_kernel<float, 16>, dim3(blocks), dim3(256), 0, st, p);
-      else launch(out_update_kernel<float, 64>, dim3(blocks), dim3(256), 0, st, p);
+    for (b0_ = 0; b0_ < batch; b0_ += chunk) {
+      const std::size_t nb = std::min(chunk, batch - b0_);
+      if (!record_forward(nb, tc, ft_row, st, err) || !record_update(nb, tc, &sp.scalars, nullptr, st)) {
+        b0_ = 0;
+        return false;
+      }
     }
   }
+  b0_ = 0;
   launch(unnormalize_kernel, dim3(ew_grid(static_cast<long long>(n_tokens) * A, 256, *ctx_)), dim3(256), 0, st,
          static_cast<const float*>(x_master_), n_tokens, A, static_cast<const float*>(amin_),
          static_cast<const float*>(amax_), out_action_);
@@ -1149,9 +1221,14 @@ int Unet::denoise(const float* condition, const float* sample, float timestep, f
   cudaStream_t st = ctx_->stream;
   const std::size_t H = cfg_.horizon, A = cfg_.action_dim, Cd = cfg_.condition_dim;
   const bool tc = use_tc(batch);
+  const std::size_t chunk = chunk_samples(batch, tc);
   const int n_tokens = static_cast<int>(batch * H);
-  cudaMemcpyAsync(in_cond_, condition, batch * Cd * sizeof(float), cudaMemcpyHostToDevice, st);
-  cudaMemcpyAsync(in_noise_, sample, batch * H * A * sizeof(float), cudaMemcpyHostToDevice, st);
+  float* pc = pinned_;
+  float* pn = pinned_ + batch * Cd;
+  std::memcpy(pc, condition, batch * Cd * sizeof(float));
+  std::memcpy(pn, sample, batch * H * A * sizeof(float));
+  cudaMemcpyAsync(in_cond_, pc, batch * Cd * sizeof(float), cudaMemcpyHostToDevice, st);
+  cudaMemcpyAsync(in_noise_, pn, batch * H * A * sizeof(float), cudaMemcpyHostToDevice, st);
   cudaMemcpyAsync(tstep_, &timestep, sizeof(float), cudaMemcpyHostToDevice, st);
   const int td = static_cast<int>(cfg_.timestep_dim);
   temb_kernel<<<1, 128, static_cast<std::size_t>(5 * td) * sizeof(float), st>>>(tstep_, 1, td, te1_w_, te1_b_,
@@ -1159,24 +1236,14 @@ int Unet::denoise(const float* condition, const float* sample, float timestep, f
   film_time_kernel<<<ew_grid(F_, 256, *ctx_), 256, 0, st>>>(tm_row_, 1, td, wt_, F_, ft_row_);
   prep_sample_kernel<<<ew_grid(static_cast<long long>(n_tokens) * cin_pad_, 256, *ctx_), 256, 0, st>>>(
       in_noise_, n_tokens, static_cast<int>(A), x_master_, x_in_, cin_pad_, tc ? 1 : 0);
-  if (!record_film_cond(batch, tc, st, err) || !record_forward(batch, tc, ft_row_, st, err)) return 2;
-  const unsigned blocks = static_cast<unsigned>((n_tokens * 32 + 255) / 256);
-  const int c0 = static_cast<int>(cfg_.dims[0]);
-  if (tc) {
-    OutParams<__nv_bfloat16> p{};
-    p.z = static_cast<const __nv_bfloat16*>(h1_);
-    p.C = c0, p.A = static_cast<int>(A), p.H = static_cast<int>(H), p.n_tokens = n_tokens;
-    p.W = fo_w_, p.bias = fo_b_, p.x_master = x_master_, p.eps_out = eps_, p.update = 0;
-    if (A <= 16) out_update_kernel<__nv_bfloat16, 16><<<blocks, 256, 0, st>>>(p);
-    else out_update_kernel<__nv_bfloat16, 64><<<blocks, 256, 0, st>>>(p);
-  } else {
-    OutParams<float> p{};
-    p.z = static_cast<const float*>(h1_);
-    p.C = c0, p.A = static_cast<int>(A), p.H = static_cast<int>(H), p.n_tokens = n_tokens;
-    p.W = fo_w_, p.bias = fo_b_, p.x_master = x_master_, p.eps_out = eps_, p.update = 0;
-    if (A <= 16) out_update_kernel<float, 16><<<blocks, 256, 0, st>>>(p);
-    else out_update_kernel<float, 64><<<blocks, 256, 0, st>>>(p);
+  bool ok = true;
+  for (b0_ = 0; ok && b0_ < batch; b0_ += chunk) {
+    const std::size_t nb = std::min(chunk, batch - b0_);
+    ok = record_film_cond(nb, tc, st, err) && record_forward(nb, tc, ft_row_, st, err) &&
+         record_update(nb, tc, nullptr, eps_, st);
   }
+  b0_ = 0;
+  if (!ok) return 2;
   float* pe = pinned_;
   cudaMemcpyAsync(pe, eps_, batch * H * A * sizeof(float), cudaMemcpyDeviceToHost, st);
   if (cudaStreamSynchronize(st) != cudaSuccess) {
@@ -1189,6 +1256,55 @@ int Unet::denoise(const float* condition, const float* sample, float timestep, f
   }
   std::memcpy(eps, pe, batch * H * A * sizeof(float));
   return 0;
+}
+
+// One forward of `batch` samples (timestep 0 row of the FiLM table), run
+// directly on the engine stream with a CUDA event pair around every
+// tensor-core convolution.  metrics[0] = summed conv kernel ms, [1] = conv
+// launches, [2] = algorithmic conv FLOPs, [3] = whole-forward ms.
+int Unet::profile(std::size_t batch, double* metrics, std::string& err) noexcept {
+  if (!use_tc(batch)) {
+    err = "profiling covers the tensor-core path (bf16 mode, batch * horizon >= 512)";
+    return 1;
+  }
+  if (batch > cap_) {
+    err = "batch exceeds the reserved capacity";
+    return 2;
+  }
+  cudaSetDevice(ctx_->device);
+  cudaStream_t st = ctx_->stream;
+  prof_events_.clear();
+  prof_flops_ = 0;
+  profiling_ = true;
+  cudaEvent_t all0, all1;
+  cudaEventCreate(&all0);
+  cudaEventCreate(&all1);
+  cudaEventRecord(all0, st);
+  const bool ok = record_forward(batch, true, film_time_, st, err);
+  cudaEventRecord(all1, st);
+  profiling_ = false;
+  if (!ok || cudaStreamSynchronize(st) != cudaSuccess) {
+    if (err.empty()) err = "profiling forward failed";
+    return 2;
+  }
+  double conv_ms = 0;
+  for (auto& [a, b] : prof_events_) {
+    float ms = 0;
+    cudaEventElapsedTime(&ms, a, b);
+    conv_ms += ms;
+    cudaEventDestroy(a);
+    cudaEventDestroy(b);
+  }
+  float all_ms = 0;
+  cudaEventElapsedTime(&all_ms, all0, all1);
+  cudaEventDestroy(all0);
+  cudaEventDestroy(all1);
+  metrics[0] = conv_ms;
+  metrics[1] = static_cast<double>(prof_events_.size());
+  metrics[2] = prof_flops_;
+  metrics[3] = all_ms;
+  prof_events_.clear();
+  return take_device_error(*ctx_, st) == 0 ? 0 : 2;
 }
 
 }  // namespace

@@ -129,6 +129,7 @@ SIGNATURES = {
     "fe_engine_sample_batch": (C.c_int, [C.c_void_p, _i32p, C.c_size_t, C.c_size_t, _f32p, C.c_size_t, C.c_int,
                                          _f32p]),
     "fe_engine_synchronize": (C.c_int, [C.c_void_p]),
+    "fe_engine_profile_diffusion": (C.c_int, [C.c_void_p, C.c_size_t, C.POINTER(C.c_double)]),
     "fe_device_malloc_count": (C.c_uint64, []),
     "fe_host_malloc_count": (C.c_uint64, []),
     "fe_engine_kernel_launches": (C.c_uint64, [C.c_void_p]),
@@ -293,6 +294,11 @@ class Engine:
 
     def reserve_batch(self, max_batch: int):
         self._check(self.lib.fe_engine_reserve_batch(self.handle, max_batch))
+
+    def profile_diffusion(self, batch: int) -> dict:
+        m = (C.c_double * 4)()
+        self._check(self.lib.fe_engine_profile_diffusion(self.handle, batch, m))
+        return {"conv_ms": m[0], "conv_launches": int(m[1]), "conv_flops": m[2], "forward_ms": m[3]}
 
     def synchronize(self):
         self._check(self.lib.fe_engine_synchronize(self.handle))

@@ -312,6 +312,13 @@ int fe_engine_sample_batch(fe_engine* engine, const int32_t* tokens, size_t batc
 /* Wait for all work enqueued by this engine. */
 int fe_engine_synchronize(fe_engine* engine);
 
+/* Profile one U-Net forward of `batch` samples on the tensor-core path with
+ * CUDA events around every convolution GEMM: metrics[0] = summed GEMM kernel
+ * milliseconds, [1] = GEMM launches, [2] = algorithmic GEMM FLOPs,
+ * [3] = whole forward milliseconds.  The batch must be within the reserved
+ * capacity and use the tensor-core path (bf16 mode). */
+int fe_engine_profile_diffusion(fe_engine* engine, size_t batch, double* metrics);
+
 /* Process-wide counts of device / pinned-host allocations made by this library. */
 uint64_t fe_device_malloc_count(void);
 uint64_t fe_host_malloc_count(void);

@@ -53,6 +53,11 @@ def lib():
         handle.fe_engine_load_with_threads.restype = C.c_void_p
         handle.fe_engine_load_with_threads.argtypes = [C.c_char_p, C.c_uint]
         handle.fe_engine_free.argtypes = [C.c_void_p]
+        handle.fe_weights_load.restype = C.c_void_p
+        handle.fe_weights_load.argtypes = [C.c_char_p]
+        handle.fe_weights_free.argtypes = [C.c_void_p]
+        handle.fe_engine_create_from_weights.restype = C.c_void_p
+        handle.fe_engine_create_from_weights.argtypes = [C.c_void_p, C.c_uint]
         handle.fe_engine_last_error.restype = C.c_char_p
         handle.fe_engine_sample_diffusion.argtypes = [C.c_void_p, _f32p, _f32p, C.c_size_t,
                                                       C.c_int, C.c_uint64, _f32p]
@@ -96,6 +101,16 @@ class ReferenceEngine:
         self.handle = self.lib.fe_engine_load_with_threads(str(path).encode(), threads)
         if not self.handle:
             raise RuntimeError(self.lib.fe_engine_last_error().decode())
+
+    @classmethod
+    def from_weights(cls, weights, threads: int = 0):
+        """Engine over a shared fe_weights store (fe_engine_create_from_weights)."""
+        self = cls.__new__(cls)
+        self.lib = lib()
+        self.handle = self.lib.fe_engine_create_from_weights(weights, threads)
+        if not self.handle:
+            raise RuntimeError(self.lib.fe_engine_last_error().decode())
+        return self
 
     def close(self):
         if self.handle:
