@@ -38,7 +38,7 @@ from flowedge_b200 import checkpoint as ck  # noqa: E402
 
 METRIC = "DDIM action chunks/s at b=4096 (bimanual U-Net, 10-step DDIM)"
 UNIT = "chunks/s"
-GLOBAL_BATCH = 4096
+GLOBAL_BATCH = int(os.environ.get("FLOWEDGE_BENCH_BATCH", "4096"))
 STEPS = 10
 SEED = 0
 
@@ -231,7 +231,10 @@ def run_ours(args):
     cond, noise = _inputs(spec, shard, offset=rank * shard)
     engine = Engine(path, threads=0, device=local, precision="bf16", max_batch=shard)
 
-    stream = torch.cuda.current_stream()
+    # a dedicated (non-default) stream: the engine enqueues on it and the
+    # CUDA events are recorded on it
+    stream = torch.cuda.Stream()
+    torch.cuda.set_stream(stream)
     d_cond = torch.from_numpy(cond).cuda()
     d_noise = torch.from_numpy(noise).cuda()
     d_action = torch.empty((shard, spec.horizon, spec.action_dim), dtype=torch.float32, device="cuda")

@@ -5,6 +5,7 @@
 
 #include <cuda.h>
 #include <cuda_bf16.h>
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -165,6 +166,13 @@ __host__ __device__ constexpr uint32_t idesc_bf16_f32(int m, int n) {
          | (static_cast<uint32_t>(m >> 4) << 24);  // M / 16
 }
 
+// Instruction descriptor: F16 x F16 -> F32, both operands K-major.
+__host__ __device__ constexpr uint32_t idesc_f16_f32(int m, int n) {
+  return (1u << 4)                                 // D = F32
+         | (static_cast<uint32_t>(n >> 3) << 17)   // N / 8
+         | (static_cast<uint32_t>(m >> 4) << 24);  // M / 16
+}
+
 // 32 lanes x 32 columns of 32-bit TMEM data into registers (one row per lane).
 __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
   uint32_t r[32];
@@ -206,8 +214,23 @@ __device__ __forceinline__ float silu_f(float x) { return x / (1.0f + expf(-x));
 
 __device__ __forceinline__ float softplus_f(float x) { return fmaxf(x, 0.0f) + log1pf(expf(-fabsf(x))); }
 
+__device__ __forceinline__ float half_lo(uint32_t packed) {
+  return __half2float(__ushort_as_half(static_cast<unsigned short>(packed & 0xFFFFu)));
+}
+__device__ __forceinline__ float half_hi(uint32_t packed) {
+  return __half2float(__ushort_as_half(static_cast<unsigned short>(packed >> 16)));
+}
+
 __device__ __forceinline__ float bf16_lo(uint32_t packed) { return __uint_as_float(packed << 16); }
 __device__ __forceinline__ float bf16_hi(uint32_t packed) { return __uint_as_float(packed & 0xFFFF0000u); }
+
+// fp16 operand storage saturates at the largest finite value (never inf)
+__device__ __forceinline__ __half to_half_sat(float v) { return __float2half_rn(fminf(fmaxf(v, -65504.0f), 65504.0f)); }
+
+__device__ __forceinline__ uint32_t pack_half(float lo, float hi) {
+  __half2 v = __halves2half2(to_half_sat(lo), to_half_sat(hi));
+  return *reinterpret_cast<uint32_t*>(&v);
+}
 
 __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
   __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);

@@ -25,13 +25,6 @@ namespace {
 
 constexpr int kTcMinRows = 128;
 
-std::uint16_t to_bf16(float v) {
-  std::uint32_t u;
-  std::memcpy(&u, &v, 4);
-  if ((u & 0x7FFFFFFFu) > 0x7F800000u) return 0x7FC0;
-  u += 0x7FFFu + ((u >> 16) & 1u);
-  return static_cast<std::uint16_t>(u >> 16);
-}
 
 struct Mat {
   int rows = 0, rows_pad = 0, cols = 0, cols_pad = 0;
@@ -82,7 +75,7 @@ struct OdeParams {
   const float* k[4];
   void* next_in;
   int ld_in;
-  int next_bf16;
+  int next_half;
 };
 
 __global__ void ode_stage_kernel(const OdeParams p) {
@@ -123,14 +116,14 @@ __global__ void ode_stage_kernel(const OdeParams p) {
       }
     }
     const long long ii = static_cast<long long>(b) * p.ld_in + a;
-    if (p.next_bf16) static_cast<__nv_bfloat16*>(p.next_in)[ii] = __float2bfloat16_rn(nxt);
+    if (p.next_half) static_cast<__half*>(p.next_in)[ii] = to_half_sat(nxt);
     else static_cast<float*>(p.next_in)[ii] = nxt;
   }
   if (p.step_out != nullptr && p.stage == last && blockIdx.x == 0 && threadIdx.x == 0) *p.step_out = *p.step_idx + 1;
 }
 
 // fp32 [B][A] (dense) -> padded fp32 state and padded next-input buffer
-__global__ void load_rows_kernel(const float* src, int B, int A, float* dst, int ld, void* in, int ld_in, int in_bf16) {
+__global__ void load_rows_kernel(const float* src, int B, int A, float* dst, int ld, void* in, int ld_in, int in_half) {
   const long long total = static_cast<long long>(B) * ld_in;
   for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
        i += static_cast<long long>(gridDim.x) * blockDim.x) {
@@ -138,7 +131,7 @@ __global__ void load_rows_kernel(const float* src, int B, int A, float* dst, int
     const int a = static_cast<int>(i - static_cast<long long>(b) * ld_in);
     const float v = a < A ? src[static_cast<long long>(b) * A + a] : 0.0f;
     if (dst != nullptr && a < ld) dst[static_cast<long long>(b) * ld + a] = v;
-    if (in_bf16) static_cast<__nv_bfloat16*>(in)[i] = __float2bfloat16_rn(v);
+    if (in_half) static_cast<__half*>(in)[i] = to_half_sat(v);
     else static_cast<float*>(in)[i] = v;
   }
 }
@@ -174,7 +167,7 @@ class Flow final : public FlowDevice {
   bool use_tc(std::size_t batch) const {
     return tc_ok_ && prec_ == Precision::kBF16 && static_cast<int>(batch) >= kTcMinRows;
   }
-  bool gemm(const Mat& m, const void* in, int in_ld, std::size_t batch, float* out_f32, void* out_bf16, int out_ld,
+  bool gemm(const Mat& m, const void* in, int in_ld, std::size_t batch, float* out_f32, void* out_half, int out_ld,
             const float* add_vec, const float* add_tok, int act, bool tc, cudaStream_t st, std::string& err);
   bool record_step(std::size_t batch, int method, bool tc, cudaStream_t st, std::string& err);
   bool prepare(const float* condition, const float* x0, std::size_t batch, bool cond_device, bool x_device,
@@ -268,7 +261,7 @@ bool Flow::load(const TensorTable& t, std::string& err) {
                   static_cast<std::size_t>(m.cols) * 4);
     if (bf) {
       std::vector<std::uint16_t> h(padded.size());
-      for (std::size_t i = 0; i < h.size(); ++i) h[i] = to_bf16(padded[i]);
+      for (std::size_t i = 0; i < h.size(); ++i) h[i] = fp16_bits_of_bf16_rounded(padded[i]);
       m.w = wts_.take(h.size() * 2);
       cudaMemcpy(m.w, h.data(), h.size() * 2, cudaMemcpyHostToDevice);
     } else {
@@ -363,10 +356,11 @@ int Flow::reserve(std::size_t batch, std::string& err) noexcept {
   return cudaDeviceSynchronize() == cudaSuccess ? 0 : 2;
 }
 
-bool Flow::gemm(const Mat& m, const void* in, int in_ld, std::size_t batch, float* out_f32, void* out_bf16, int out_ld,
+bool Flow::gemm(const Mat& m, const void* in, int in_ld, std::size_t batch, float* out_f32, void* out_half, int out_ld,
                 const float* add_vec, const float* add_tok, int act, bool tc, cudaStream_t st, std::string& err) {
   if (tc) {
     TcLaunch l;
+    l.fp16 = true;
     l.A = m.w;
     l.M_rows = m.rows_pad;
     l.K = m.cols_pad;
@@ -380,7 +374,7 @@ bool Flow::gemm(const Mat& m, const void* in, int in_ld, std::size_t batch, floa
     l.add_ld = static_cast<int>(cfg_.hidden);
     l.act = act;
     l.out_f32 = out_f32 != nullptr;
-    l.out = out_f32 != nullptr ? static_cast<void*>(out_f32) : out_bf16;
+    l.out = out_f32 != nullptr ? static_cast<void*>(out_f32) : out_half;
     l.out_ld = out_ld;
     return tc_gemm(l, *ctx_, st, err) == cudaSuccess;
   }
@@ -409,7 +403,7 @@ bool Flow::gemm(const Mat& m, const void* in, int in_ld, std::size_t batch, floa
   r.add_vec = add_vec;
   r.add_tok = add_tok;
   r.act = act;
-  r.out = out_f32 != nullptr ? out_f32 : static_cast<float*>(out_bf16);
+  r.out = out_f32 != nullptr ? out_f32 : static_cast<float*>(out_half);
   r.out_ld = out_ld;
   reduce_partials_kernel<<<ew_grid(static_cast<long long>(batch) * m.rows, 256, *ctx_), 256, 0, st>>>(r);
   return cudaGetLastError() == cudaSuccess;
@@ -450,7 +444,7 @@ bool Flow::record_step(std::size_t batch, int method, bool tc, cudaStream_t st, 
     for (int i = 0; i < 4; ++i) p.k[i] = k_[i];
     p.next_in = xin_;
     p.ld_in = a_pad_;
-    p.next_bf16 = tc ? 1 : 0;
+    p.next_half = tc ? 1 : 0;
     ode_stage_kernel<<<ew_grid(static_cast<long long>(batch) * A, 256, *ctx_), 256, 0, st>>>(p);
   }
   // step_[0] <- step_[1] (next step index) for the next replay

@@ -55,7 +55,7 @@ struct Layer {
 
 // one warp per row; RMSNorm with eps 1e-5 (kernels_scalar.cc:48-60); optional
 // bf16 copy for the tensor-core GEMM
-__global__ void rmsnorm_kernel(const float* in, const float* w, int rows, int dim, float* out, __nv_bfloat16* out_bf) {
+__global__ void rmsnorm_kernel(const float* in, const float* w, int rows, int dim, float* out, __half* out_bf) {
   const int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (row >= rows) return;
@@ -67,14 +67,14 @@ __global__ void rmsnorm_kernel(const float* in, const float* w, int rows, int di
   for (int i = lane; i < dim; i += 32) {
     const float v = x[i] * scale * w[i];
     if (out != nullptr) out[static_cast<long long>(row) * dim + i] = v;
-    if (out_bf != nullptr) out_bf[static_cast<long long>(row) * dim + i] = __float2bfloat16_rn(v);
+    if (out_bf != nullptr) out_bf[static_cast<long long>(row) * dim + i] = to_half_sat(v);
   }
 }
 
 // u[b][t][c] = SiLU(bias[c] + sum_k w[c][k] * x[b][t - (dc-1) + k][c]), x is the
 // first di columns of xz (row stride 2*di) (kernels_scalar.cc:10-27)
 __global__ void causal_conv_kernel(const float* xz, int B, int L, int di, int dc, const float* w, const float* bias,
-                                   float* u, __nv_bfloat16* u_bf) {
+                                   float* u, __half* u_bf) {
   const long long total = static_cast<long long>(B) * L * di;
   for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
        i += static_cast<long long>(gridDim.x) * blockDim.x) {
@@ -88,7 +88,7 @@ __global__ void causal_conv_kernel(const float* xz, int B, int L, int di, int dc
     }
     const float v = silu_f(acc);
     u[i] = v;
-    if (u_bf != nullptr) u_bf[i] = __float2bfloat16_rn(v);
+    if (u_bf != nullptr) u_bf[i] = to_half_sat(v);
   }
 }
 
@@ -100,7 +100,7 @@ __global__ void causal_conv_kernel(const float* xz, int B, int L, int di, int dc
 template <int DS, int DR>
 __global__ void __launch_bounds__(256) scan_kernel(const float* dbl, int wd, const float* u, const float* xz, int L,
                                                    int di, const float* dt_w, const float* dt_b, const float* a_neg,
-                                                   const float* dsk, float* state, float* y, __nv_bfloat16* y_bf) {
+                                                   const float* dsk, float* state, float* y, __half* y_bf) {
   extern __shared__ float sdbl[];  // [L][wd]
   const int b = blockIdx.y;
   const int c = blockIdx.x * blockDim.x + threadIdx.x;
@@ -136,7 +136,7 @@ __global__ void __launch_bounds__(256) scan_kernel(const float* dbl, int wd, con
     const float zv = xz[tok * 2 * di + di + c];
     const float out = yv * (zv / (1.0f + expf(-zv)));
     y[tok * di + c] = out;
-    if (y_bf != nullptr) y_bf[tok * di + c] = __float2bfloat16_rn(out);
+    if (y_bf != nullptr) y_bf[tok * di + c] = to_half_sat(out);
   }
   if (state != nullptr)
 #pragma unroll
@@ -218,7 +218,7 @@ class Mamba final : public MambaDevice {
   float *hidden_ = nullptr, *xz_ = nullptr, *u_ = nullptr, *dbl_ = nullptr, *y_ = nullptr, *part_ = nullptr;
   float* last_ = nullptr;
   float* out_ = nullptr;
-  __nv_bfloat16 *nb_ = nullptr, *ub_ = nullptr, *yb_ = nullptr;
+  __half *nb_ = nullptr, *ub_ = nullptr, *yb_ = nullptr;
   float* state_ = nullptr;  // decode state (snapshot layout)
   float* dh_ = nullptr;     // decode scratch
   std::size_t part_elems_ = 0;
@@ -307,7 +307,7 @@ bool Mamba::load(const TensorTable& t, std::string& err) {
                   static_cast<std::size_t>(cols) * 4);
     if (bf) {
       std::vector<std::uint16_t> hb(padded.size());
-      for (std::size_t i = 0; i < hb.size(); ++i) hb[i] = bf16_of(padded[i]);
+      for (std::size_t i = 0; i < hb.size(); ++i) hb[i] = fp16_bits_of_bf16_rounded(padded[i]);
       m.w = wts_.take(hb.size() * 2);
       cudaMemcpy(m.w, hb.data(), hb.size() * 2, cudaMemcpyHostToDevice);
     } else {
@@ -400,9 +400,9 @@ int Mamba::reserve(std::size_t batch, std::size_t max_len, std::string& err) noe
   plan.add_n<float>(part_elems_);
   plan.add_n<float>(batch * dm);      // last
   plan.add_n<float>(rows * dm);       // out
-  plan.add_n<__nv_bfloat16>(rows * dm);
-  plan.add_n<__nv_bfloat16>(rows * di);
-  plan.add_n<__nv_bfloat16>(rows * di);
+  plan.add_n<__half>(rows * dm);
+  plan.add_n<__half>(rows * di);
+  plan.add_n<__half>(rows * di);
   plan.add_n<float>(state_floats());
   plan.add_n<float>(dm + 2 * di + di + wd + di + di + dm + 64);
   // keep the decode state across a re-reserve
@@ -425,9 +425,9 @@ int Mamba::reserve(std::size_t batch, std::size_t max_len, std::string& err) noe
   part_ = ws_.take_n<float>(part_elems_);
   last_ = ws_.take_n<float>(batch * dm);
   out_ = ws_.take_n<float>(rows * dm);
-  nb_ = ws_.take_n<__nv_bfloat16>(rows * dm);
-  ub_ = ws_.take_n<__nv_bfloat16>(rows * di);
-  yb_ = ws_.take_n<__nv_bfloat16>(rows * di);
+  nb_ = ws_.take_n<__half>(rows * dm);
+  ub_ = ws_.take_n<__half>(rows * di);
+  yb_ = ws_.take_n<__half>(rows * di);
   state_ = ws_.take_n<float>(state_floats());
   dh_ = ws_.take_n<float>(dm + 2 * di + di + wd + di + di + dm + 64);
   if (ws_.overflowed()) {
@@ -457,6 +457,7 @@ bool Mamba::gemm(const Mat& m, const void* in, int in_ld, long long n_tok, float
                  bool tc, cudaStream_t st, std::string& err) {
   if (tc) {
     TcLaunch l;
+    l.fp16 = true;
     l.A = m.w;
     l.M_rows = m.rows_pad;
     l.K = m.cols_pad;

@@ -26,12 +26,12 @@ EncodeTiled encode_fn() {
 }
 
 bool encode_2d(CUtensorMap* map, const void* ptr, std::uint64_t inner, std::uint64_t outer, std::uint32_t box_inner,
-               std::uint32_t box_outer, std::string& err) {
+               std::uint32_t box_outer, CUtensorMapDataType dtype, std::string& err) {
   const cuuint64_t dims[2] = {inner, outer};
   const cuuint64_t strides[1] = {inner * 2};
   const cuuint32_t box[2] = {box_inner, box_outer};
   const cuuint32_t estr[2] = {1, 1};
-  const CUresult rc = encode_fn()(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides,
+  const CUresult rc = encode_fn()(map, dtype, 2, const_cast<void*>(ptr), dims, strides,
                                   box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (rc != CUDA_SUCCESS) {
@@ -41,14 +41,15 @@ bool encode_2d(CUtensorMap* map, const void* ptr, std::uint64_t inner, std::uint
   return true;
 }
 
-bool encode_3d(CUtensorMap* map, const TcSource& s, std::uint32_t box_l, std::uint32_t box_s, std::string& err) {
+bool encode_3d(CUtensorMap* map, const TcSource& s, std::uint32_t box_l, std::uint32_t box_s, CUtensorMapDataType dtype,
+               std::string& err) {
   const cuuint64_t dims[3] = {static_cast<cuuint64_t>(s.channels), static_cast<cuuint64_t>(s.length),
                               static_cast<cuuint64_t>(s.samples)};
   const cuuint64_t strides[2] = {static_cast<cuuint64_t>(s.channels) * 2,
                                  static_cast<cuuint64_t>(s.channels) * s.length * 2};
   const cuuint32_t box[3] = {64, box_l, box_s};
   const cuuint32_t estr[3] = {1, 1, 1};
-  const CUresult rc = encode_fn()(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(s.ptr), dims, strides,
+  const CUresult rc = encode_fn()(map, dtype, 3, const_cast<void*>(s.ptr), dims, strides,
                                   box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (rc != CUDA_SUCCESS) {
@@ -192,6 +193,19 @@ std::vector<float> widen_f32(const HostTensor& t) {
   return out;
 }
 
+std::uint16_t fp16_bits_of_bf16_rounded(float v) {
+  std::uint32_t u;
+  std::memcpy(&u, &v, 4);
+  if ((u & 0x7FFFFFFFu) <= 0x7F800000u) {
+    u += 0x7FFFu + ((u >> 16) & 1u);
+    u &= 0xFFFF0000u;
+  }
+  float r;
+  std::memcpy(&r, &u, 4);
+  const __half h = __float2half_rn(r);
+  return __half_as_ushort(h);
+}
+
 cudaError_t tc_gemm(const TcLaunch& l, DeviceContext& ctx, cudaStream_t stream, std::string& err) {
   if (l.M_rows % tc::BM != 0 || l.K % tc::BK != 0 || l.L < 1 || l.L > tc::BN || (l.L & (l.L - 1)) != 0 ||
       l.segs.empty() || static_cast<int>(l.segs.size()) > tc::MAX_SEGS) {
@@ -200,6 +214,10 @@ cudaError_t tc_gemm(const TcLaunch& l, DeviceContext& ctx, cudaStream_t stream, 
   }
   tc::Params p{};
   p.L = l.L;
+  p.L_shift = 0;
+  while ((1 << p.L_shift) < l.L) ++p.L_shift;
+  p.fp16 = l.fp16 ? 1 : 0;
+  const CUtensorMapDataType dtype = l.fp16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
   p.tile_samples = tc::BN / l.L;
   if (l.stats != nullptr && (p.tile_samples > tc::MAX_TILE_SAMPLES || l.group_ch % 32 != 0 ||
                              (l.group_ch > tc::BM && l.group_ch % tc::BM != 0) ||
@@ -243,11 +261,12 @@ cudaError_t tc_gemm(const TcLaunch& l, DeviceContext& ctx, cudaStream_t stream, 
   p.err = ctx.d_err;
 
   CUtensorMap ta{}, tb[3]{};
-  if (!encode_2d(&ta, l.A, static_cast<std::uint64_t>(l.K), static_cast<std::uint64_t>(l.M_rows), 64, tc::BM, err))
+  if (!encode_2d(&ta, l.A, static_cast<std::uint64_t>(l.K), static_cast<std::uint64_t>(l.M_rows), 64, tc::BM, dtype,
+                 err))
     return cudaErrorInvalidValue;
   for (int i = 0; i < 3; ++i) {
     const TcSource& s = l.src[i].ptr != nullptr ? l.src[i] : l.src[0];
-    if (!encode_3d(&tb[i], s, static_cast<std::uint32_t>(l.L), static_cast<std::uint32_t>(p.tile_samples), err))
+    if (!encode_3d(&tb[i], s, static_cast<std::uint32_t>(l.L), static_cast<std::uint32_t>(p.tile_samples), dtype, err))
       return cudaErrorInvalidValue;
   }
   const int grid = p.total_tiles < ctx.sm_count ? p.total_tiles : ctx.sm_count;

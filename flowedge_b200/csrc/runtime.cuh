@@ -81,7 +81,8 @@ struct TcSource {
 };
 
 struct TcLaunch {
-  const void* A = nullptr;  // bf16 [M_rows][K], M_rows multiple of 128, K multiple of 64
+  bool fp16 = false;        // operand format of A, B and 16-bit outputs: fp16 (true) or bf16
+  const void* A = nullptr;  // [M_rows][K] 16-bit, M_rows multiple of 128, K multiple of 64
   int M_rows = 0;
   int K = 0;
   TcSource src[3];
@@ -118,5 +119,12 @@ inline int ew_grid(long long total, int threads, const DeviceContext& ctx) {
 int take_device_error(DeviceContext& ctx, cudaStream_t stream);
 
 std::vector<float> widen_f32(const HostTensor& t);
+
+// bf16 mode: a weight is rounded to bf16 (nearest even) and stored on the
+// device as fp16, which holds every bf16 value of magnitude >= 2^-17 exactly
+// (smaller ones round to the fp16 subnormal grid, error < 2^-25).  fp16
+// operands let the activations keep 3 more mantissa bits at the same tensor
+// throughput.
+std::uint16_t fp16_bits_of_bf16_rounded(float v);
 
 }  // namespace feb

@@ -33,7 +33,7 @@ struct SimtSource {
 };
 
 struct SimtConvParams {
-  const void* W;  // [M][K] fp32 or bf16
+  const void* W;  // [M][K] fp32 or fp16
   int M, K;
   SimtSource src[3];
   int stride;     // input time = t * stride + t_off
@@ -43,7 +43,7 @@ struct SimtConvParams {
   float* partial; // [nslices][n_tokens][M]
 };
 
-template <int NT, bool BF16>
+template <int NT, bool HALF>
 static __global__ void __launch_bounds__(128) simt_conv_kernel(const SimtConvParams p) {
   __shared__ __align__(16) float xs[256 * NT];
   const SimtSlice sl = p.slices[blockIdx.x];
@@ -70,15 +70,15 @@ static __global__ void __launch_bounds__(128) simt_conv_kernel(const SimtConvPar
   float acc[NT];
 #pragma unroll
   for (int n = 0; n < NT; ++n) acc[n] = 0.0f;
-  if constexpr (BF16) {
-    const uint4* wrow = reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(p.W) +
+  if constexpr (HALF) {
+    const uint4* wrow = reinterpret_cast<const uint4*>(static_cast<const __half*>(p.W) +
                                                        static_cast<long long>(m) * p.K + sl.k_begin);
     uint4 wnext = __ldg(wrow);
     for (int c = 0; c < sl.nch; c += 8) {
       const uint4 wv = wnext;
       if (c + 8 < sl.nch) wnext = __ldg(wrow + (c + 8) / 8);
-      const float w[8] = {bf16_lo(wv.x), bf16_hi(wv.x), bf16_lo(wv.y), bf16_hi(wv.y),
-                          bf16_lo(wv.z), bf16_hi(wv.z), bf16_lo(wv.w), bf16_hi(wv.w)};
+      const float w[8] = {half_lo(wv.x), half_hi(wv.x), half_lo(wv.y), half_hi(wv.y),
+                          half_lo(wv.z), half_hi(wv.z), half_lo(wv.w), half_hi(wv.w)};
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
         const float4* xr = reinterpret_cast<const float4*>(xs + (c + i) * NT);
@@ -237,12 +237,14 @@ static __global__ void __launch_bounds__(256) gn_partials_kernel(const GnParams 
 }
 
 // ---------------------------------------------------------------------------
-// bf16 token-major GroupNorm application after the tensor-core conv, whose
-// epilogue produced y (bf16, bias included) and per-(sample, group, part)
-// partial sums.  8 channels (16 B) per thread.
+// GroupNorm application after the tensor-core conv, whose epilogue produced
+// y (fp32, bias included) and per-(sample, group, part) partial sums.
+// z = mish(GN(y)) then FiLM, or + residual (fp32 residual stream, or bf16 when
+// no fp32 copy exists).  Writes the bf16 GEMM operand and, optionally, the
+// fp32 residual-stream copy.  8 channels per thread.
 
-struct GnBf16Params {
-  const __nv_bfloat16* y;
+struct GnTcParams {
+  const float* y;
   long long n_tokens;
   int C, L, groups, parts;
   const double* stats;
@@ -251,11 +253,13 @@ struct GnBf16Params {
   const float* film_cond;
   const float* film_time;
   int film_F, film_off;
-  const __nv_bfloat16* res;  // [n][C] or null
-  __nv_bfloat16* out;
+  const float* res_f32;           // [n][C] or null
+  const __half* res_half;  // [n][C] or null
+  __half* out;             // [n][C]
+  float* out_f32;                 // [n][C] or null
 };
 
-static __global__ void __launch_bounds__(256) gn_bf16_kernel(const GnBf16Params p) {
+static __global__ void __launch_bounds__(256) gn_tc_kernel(const GnTcParams p) {
   const int vec_per_tok = p.C / 8;
   const long long total = p.n_tokens * vec_per_tok;
   const int cpg = p.C / p.groups;
@@ -276,14 +280,18 @@ static __global__ void __launch_bounds__(256) gn_bf16_kernel(const GnBf16Params 
     const double var = fmax(0.0, s2 / count - mean * mean);
     const float inv = static_cast<float>(1.0 / sqrt(var + 1e-5));
     const float mean_f = static_cast<float>(mean);
-    const uint4 yv = *reinterpret_cast<const uint4*>(p.y + n * p.C + c0);
-    float v[8] = {bf16_lo(yv.x), bf16_hi(yv.x), bf16_lo(yv.y), bf16_hi(yv.y),
-                  bf16_lo(yv.z), bf16_hi(yv.z), bf16_lo(yv.w), bf16_hi(yv.w)};
+    const float4 ya = *reinterpret_cast<const float4*>(p.y + n * p.C + c0);
+    const float4 yb = *reinterpret_cast<const float4*>(p.y + n * p.C + c0 + 4);
+    float v[8] = {ya.x, ya.y, ya.z, ya.w, yb.x, yb.y, yb.z, yb.w};
     float r[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-    if (p.res != nullptr) {
-      const uint4 rv = *reinterpret_cast<const uint4*>(p.res + n * p.C + c0);
-      r[0] = bf16_lo(rv.x); r[1] = bf16_hi(rv.x); r[2] = bf16_lo(rv.y); r[3] = bf16_hi(rv.y);
-      r[4] = bf16_lo(rv.z); r[5] = bf16_hi(rv.z); r[6] = bf16_lo(rv.w); r[7] = bf16_hi(rv.w);
+    if (p.res_f32 != nullptr) {
+      const float4 ra = *reinterpret_cast<const float4*>(p.res_f32 + n * p.C + c0);
+      const float4 rb = *reinterpret_cast<const float4*>(p.res_f32 + n * p.C + c0 + 4);
+      r[0] = ra.x; r[1] = ra.y; r[2] = ra.z; r[3] = ra.w; r[4] = rb.x; r[5] = rb.y; r[6] = rb.z; r[7] = rb.w;
+    } else if (p.res_half != nullptr) {
+      const uint4 rv = *reinterpret_cast<const uint4*>(p.res_half + n * p.C + c0);
+      r[0] = half_lo(rv.x); r[1] = half_hi(rv.x); r[2] = half_lo(rv.y); r[3] = half_hi(rv.y);
+      r[4] = half_lo(rv.z); r[5] = half_hi(rv.z); r[6] = half_lo(rv.w); r[7] = half_hi(rv.w);
     }
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
@@ -297,11 +305,15 @@ static __global__ void __launch_bounds__(256) gn_bf16_kernel(const GnBf16Params 
       v[j] = z + r[j];
     }
     uint4 o;
-    o.x = pack_bf16(v[0], v[1]);
-    o.y = pack_bf16(v[2], v[3]);
-    o.z = pack_bf16(v[4], v[5]);
-    o.w = pack_bf16(v[6], v[7]);
+    o.x = pack_half(v[0], v[1]);
+    o.y = pack_half(v[2], v[3]);
+    o.z = pack_half(v[4], v[5]);
+    o.w = pack_half(v[6], v[7]);
     *reinterpret_cast<uint4*>(p.out + n * p.C + c0) = o;
+    if (p.out_f32 != nullptr) {
+      *reinterpret_cast<float4*>(p.out_f32 + n * p.C + c0) = make_float4(v[0], v[1], v[2], v[3]);
+      *reinterpret_cast<float4*>(p.out_f32 + n * p.C + c0 + 4) = make_float4(v[4], v[5], v[6], v[7]);
+    }
   }
 }
 
@@ -375,9 +387,9 @@ struct OutParams {
   int update;           // 0: only write eps
   StepScalars step;
   const uint64_t* seeds;  // per-sample seeds (DDPM)
-  void* x_in;           // [n][Cin] next input (fp32 or bf16 per x_in_bf16)
+  void* x_in;           // [n][Cin] next input (fp32 or bf16 per x_in_half)
   int Cin;
-  int x_in_bf16;
+  int x_in_half;
 };
 
 template <typename ZT>
@@ -385,8 +397,8 @@ __device__ __forceinline__ float load_act(const ZT* p, long long i);
 template <>
 __device__ __forceinline__ float load_act<float>(const float* p, long long i) { return p[i]; }
 template <>
-__device__ __forceinline__ float load_act<__nv_bfloat16>(const __nv_bfloat16* p, long long i) {
-  return __bfloat162float(p[i]);
+__device__ __forceinline__ float load_act<__half>(const __half* p, long long i) {
+  return __half2float(p[i]);
 }
 
 template <typename ZT, int MAXA>
@@ -420,14 +432,14 @@ static __global__ void __launch_bounds__(256) out_update_kernel(const OutParams<
                                      static_cast<uint64_t>(t) * p.A + a, p.H * p.A);
     p.x_master[xi] = x;
     const long long ii = static_cast<long long>(n) * p.Cin + a;
-    if (p.x_in_bf16) static_cast<__nv_bfloat16*>(p.x_in)[ii] = __float2bfloat16_rn(x);
+    if (p.x_in_half) static_cast<__half*>(p.x_in)[ii] = to_half_sat(x);
     else static_cast<float*>(p.x_in)[ii] = x;
   }
 }
 
 // noise [n][A] -> x_master [n][A] and x_in [n][Cin] (zero padded)
 static __global__ void prep_sample_kernel(const float* noise, int n_tokens, int A, float* x_master, void* x_in, int Cin,
-                                   int x_in_bf16) {
+                                   int x_in_half) {
   const long long total = static_cast<long long>(n_tokens) * Cin;
   for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
        i += static_cast<long long>(gridDim.x) * blockDim.x) {
@@ -438,20 +450,20 @@ static __global__ void prep_sample_kernel(const float* noise, int n_tokens, int 
       v = noise[n * A + c];
       if (x_master != nullptr) x_master[n * A + c] = v;
     }
-    if (x_in_bf16) static_cast<__nv_bfloat16*>(x_in)[i] = __float2bfloat16_rn(v);
+    if (x_in_half) static_cast<__half*>(x_in)[i] = to_half_sat(v);
     else static_cast<float*>(x_in)[i] = v;
   }
 }
 
 // mish(cond) [B][Cpad] (zero padded) in fp32 or bf16
-static __global__ void prep_cond_kernel(const float* cond, int B, int Cd, void* out, int Cpad, int out_bf16) {
+static __global__ void prep_cond_kernel(const float* cond, int B, int Cd, void* out, int Cpad, int out_half) {
   const long long total = static_cast<long long>(B) * Cpad;
   for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
        i += static_cast<long long>(gridDim.x) * blockDim.x) {
     const long long b = i / Cpad;
     const int c = static_cast<int>(i - b * Cpad);
     const float v = c < Cd ? mish_f(cond[b * Cd + c]) : 0.0f;
-    if (out_bf16) static_cast<__nv_bfloat16*>(out)[i] = __float2bfloat16_rn(v);
+    if (out_half) static_cast<__half*>(out)[i] = to_half_sat(v);
     else static_cast<float*>(out)[i] = v;
   }
 }

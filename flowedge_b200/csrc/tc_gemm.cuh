@@ -2,8 +2,9 @@
 //
 //   out[token][m] = epilogue( sum_seg sum_c A[m][seg.a_k + c] * B_seg[token](c) )
 //
-// A is a K-major bf16 weight matrix [M_total][K_total].  B is gathered per
-// "segment": a TMA box of 64 channels from a bf16 activation tensor laid out
+// A is a K-major 16-bit weight matrix [M_total][K_total] (bf16 or fp16, the
+// same format as B).  B is gathered per "segment": a TMA box of 64 channels
+// from a 16-bit activation tensor laid out
 // [samples][length][channels], read at a time offset `t_off` and channel
 // offset `ch_off`.  A 1-D convolution with k taps is k segments (one per tap,
 // t_off = tap - pad); a channel concatenation is one segment per source; a
@@ -15,8 +16,9 @@
 // accumulators double-buffered in TMEM (2 x 256 columns).  Warp roles:
 //   warp 0: TMA producer (one lane)
 //   warp 1: TMEM allocator + MMA issuer (one lane)
-//   warps 2-5: epilogue (TMEM -> registers -> global), one accumulator row
-//              (= one output channel) per thread.
+//   warps 2-9: epilogue (TMEM -> registers -> global), one accumulator row
+//              (= one output channel) per thread; two warps per TMEM lane
+//              quadrant, each taking half of the tile's 256 columns.
 // Every mbarrier wait is bounded; a timeout sets an error code, raises a
 // shared abort flag, drains in-flight copies/MMAs with bounded waits, frees
 // TMEM and returns.
@@ -36,7 +38,9 @@ constexpr int B_BYTES = BN * BK * 2;
 constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
 constexpr int MAX_SEGS = 12;
 constexpr int MAX_TILE_SAMPLES = 64;  // samples per N tile when GN statistics are gathered
-constexpr int THREADS = 192;
+constexpr int EPI_WARPS = 8;
+constexpr int EPI_THREADS = EPI_WARPS * 32;
+constexpr int THREADS = 64 + EPI_THREADS;
 constexpr int TMEM_COLS = 512;
 constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + 256 + 4 * MAX_TILE_SAMPLES * 16;
 
@@ -52,7 +56,8 @@ struct Seg {
 
 struct Params {
   int n_tiles_m, n_tiles_n, total_tiles;
-  int L;            // tokens per sample inside an N tile (TMA box length)
+  int L;            // tokens per sample inside an N tile (TMA box length, power of 2)
+  int L_shift;      // log2(L)
   int tile_samples; // BN / L
   int n_samples;    // valid samples (tokens of samples >= this are skipped)
   int m_valid;      // rows >= m_valid are not stored
@@ -64,7 +69,8 @@ struct Params {
   const float* add_tok;   // [row][add_ld] fp32 or null (indexed like the output row)
   int add_ld;
   int act;
-  int out_f32;            // 1: fp32 output, 0: bf16
+  int fp16;               // operand format (and 16-bit output format): 1 fp16, 0 bf16
+  int out_f32;            // 1: fp32 output, 0: 16-bit
   int out_accumulate;     // fp32 output only: out += value
   void* out;
   long long out_ld;       // elements per output row
@@ -86,6 +92,8 @@ __device__ __forceinline__ void epilogue_store(const Params& p, int tok_b, int t
     float* out = static_cast<float*>(p.out);
     if (p.out_accumulate) v += out[idx];
     out[idx] = v;
+  } else if (p.fp16) {
+    static_cast<__half*>(p.out)[idx] = __float2half_rn(fminf(fmaxf(v, -65504.0f), 65504.0f));
   } else {
     static_cast<__nv_bfloat16*>(p.out)[idx] = __float2bfloat16_rn(v);
   }
@@ -116,7 +124,7 @@ static __global__ void __launch_bounds__(THREADS, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull[a], 1);
-      mbar_init(&tempty[a], 128);
+      mbar_init(&tempty[a], EPI_THREADS);
     }
     mbar_init(drain, 1);
     *abort_flag = 0;
@@ -185,7 +193,7 @@ static __global__ void __launch_bounds__(THREADS, 1)
   } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
     if (lane == 0) {
-      constexpr uint32_t idesc = idesc_bf16_f32(BM, BN);
+      const uint32_t idesc = p.fp16 ? idesc_f16_f32(BM, BN) : idesc_bf16_f32(BM, BN);
       uint32_t kb_iter = 0;
       uint32_t acc_iter = 0;
       bool ok = true;
@@ -228,11 +236,13 @@ static __global__ void __launch_bounds__(THREADS, 1)
       }
     }
   } else {
-    // ---------------- epilogue (warps 2..5) ----------------
-    const int q = warp & 3;  // TMEM lane quadrant this warp may access
+    // ---------------- epilogue (warps 2..9) ----------------
+    const int q = warp & 3;                // TMEM lane quadrant this warp may access
+    const int half = (warp - 2) >> 2;      // which 128 columns of the tile
     const int row = q * 32 + lane;
     uint32_t acc_iter = 0;
     const bool gather_stats = p.stats != nullptr;
+    const int lmask = p.L - 1;
     for (int tile = blockIdx.x; tile < p.total_tiles; tile += gridDim.x, ++acc_iter) {
       const int m_blk = tile % p.n_tiles_m;
       const int n_blk = tile / p.n_tiles_m;
@@ -250,14 +260,14 @@ static __global__ void __launch_bounds__(THREADS, 1)
       const float addv = (p.add_vec != nullptr && m_ok) ? p.add_vec[m] : 0.0f;
       const int sample0 = n_blk * p.tile_samples;
       float s1 = 0.0f, s2 = 0.0f;
-      for (int chunk = 0; chunk < BN / 32; ++chunk) {
+      for (int chunk = half * (BN / 64); chunk < (half + 1) * (BN / 64); ++chunk) {
         float v[32];
         tmem_ld32(tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * BN + chunk * 32, v);
 #pragma unroll 4
         for (int j = 0; j < 32; ++j) {
           const int n = chunk * 32 + j;
-          const int ls = n / p.L;
-          const int t = n - ls * p.L;
+          const int ls = n >> p.L_shift;
+          const int t = n & lmask;
           const int b = sample0 + ls;
           float y = v[j] + bias + addv;
           if (p.add_tok != nullptr && m_ok && b < p.n_samples) {
@@ -270,7 +280,7 @@ static __global__ void __launch_bounds__(THREADS, 1)
           if (gather_stats) {
             s1 += y;
             s2 += y * y;
-            if (t == p.L - 1) {
+            if (t == lmask) {
               double d1 = s1, d2 = s2;
 #pragma unroll
               for (int off = 16; off > 0; off >>= 1) {
@@ -288,13 +298,13 @@ static __global__ void __launch_bounds__(THREADS, 1)
       tc_fence_before();
       mbar_arrive(&tempty[acc]);
       if (gather_stats) {
-        named_barrier(1, 128);
-        // combine the 4 warps' partials into (sample, group) sums
+        named_barrier(1, EPI_THREADS);
+        // combine the 4 quadrants' partials into (sample, group) sums
         const int tid = threadIdx.x - 64;
         const int warps_per_group = p.group_ch >= BM ? 4 : p.group_ch / 32;
         const int groups_in_tile = BM / (warps_per_group * 32);
         const int items = p.tile_samples * groups_in_tile;
-        for (int it = tid; it < items; it += 128) {
+        for (int it = tid; it < items; it += EPI_THREADS) {
           const int ls = it / groups_in_tile;
           const int gl = it - ls * groups_in_tile;
           const int b = sample0 + ls;
@@ -312,7 +322,7 @@ static __global__ void __launch_bounds__(THREADS, 1)
           dst[0] = d1;
           dst[1] = d2;
         }
-        named_barrier(1, 128);
+        named_barrier(1, EPI_THREADS);
       }
     }
   }

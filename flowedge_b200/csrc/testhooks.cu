@@ -17,7 +17,7 @@ int fail(void* a, void* b, void* c) {
 
 }  // namespace
 
-extern "C" int febtest_gemm_bf16(const uint16_t* A, int M, int K, const uint16_t* B, int N, float* C) {
+extern "C" int febtest_gemm_16(const uint16_t* A, int M, int K, const uint16_t* B, int N, float* C, int fp16) {
   std::string err;
   auto ctx = feb::make_device_context(0, err);
   if (!ctx) return 1;
@@ -32,6 +32,7 @@ extern "C" int febtest_gemm_bf16(const uint16_t* A, int M, int K, const uint16_t
   cudaMemcpy(da, a.data(), a.size() * 2, cudaMemcpyHostToDevice);
   cudaMemcpy(db, b.data(), b.size() * 2, cudaMemcpyHostToDevice);
   feb::TcLaunch l;
+  l.fp16 = fp16 != 0;
   l.A = da;
   l.M_rows = Mp;
   l.K = Kp;
@@ -53,8 +54,8 @@ extern "C" int febtest_gemm_bf16(const uint16_t* A, int M, int K, const uint16_t
   return dev_err == 0 ? 0 : 3;
 }
 
-extern "C" int febtest_conv_bf16(const uint16_t* x, int B, int L, int C, const uint16_t* W, const float* bias, int OC,
-                                 int k, int group_ch, float* y, double* stats) {
+extern "C" int febtest_conv_16(const uint16_t* x, int B, int L, int C, const uint16_t* W, const float* bias, int OC,
+                               int k, int group_ch, float* y, double* stats, int fp16) {
   std::string err;
   auto ctx = feb::make_device_context(0, err);
   if (!ctx) return 1;
@@ -81,6 +82,7 @@ extern "C" int febtest_conv_bf16(const uint16_t* x, int B, int L, int C, const u
   cudaMemcpy(dx, x, static_cast<size_t>(B) * L * C * 2, cudaMemcpyHostToDevice);
   cudaMemcpy(dbias, bias, static_cast<size_t>(OC) * 4, cudaMemcpyHostToDevice);
   feb::TcLaunch l;
+  l.fp16 = fp16 != 0;
   l.A = da;
   l.M_rows = OCp;
   l.K = K;
@@ -106,8 +108,12 @@ extern "C" int febtest_conv_bf16(const uint16_t* x, int B, int L, int C, const u
     std::vector<uint16_t> yb(static_cast<size_t>(B) * L * OC);
     cudaMemcpy(yb.data(), dy, yb.size() * 2, cudaMemcpyDeviceToHost);
     for (size_t i = 0; i < yb.size(); ++i) {
-      const uint32_t bits = static_cast<uint32_t>(yb[i]) << 16;
-      std::memcpy(&y[i], &bits, 4);
+      if (fp16) {
+        y[i] = __half2float(__ushort_as_half(yb[i]));
+      } else {
+        const uint32_t bits = static_cast<uint32_t>(yb[i]) << 16;
+        std::memcpy(&y[i], &bits, 4);
+      }
     }
     if (groups > 0 && stats != nullptr) {
       std::vector<double> s(static_cast<size_t>(B) * groups * parts * 2);

@@ -35,13 +35,6 @@ constexpr long long kTcMinTokens = 512;
 constexpr std::size_t kSimtChunkTokens = 1024;
 constexpr std::size_t kFinalNormGroups = 8;
 
-std::uint16_t bf16_bits(float v) {
-  std::uint32_t u;
-  std::memcpy(&u, &v, 4);
-  if ((u & 0x7FFFFFFFu) > 0x7F800000u) return 0x7FC0;
-  u += 0x7FFFu + ((u >> 16) & 1u);
-  return static_cast<std::uint16_t>(u >> 16);
-}
 
 struct Part {
   int channels;  // actual input channels of this concatenated part
@@ -213,9 +206,13 @@ class Unet final : public UnetDevice {
                long long out_ld, int rps, int tmul, int tadd, bool stats, int groups, bool out_f32, cudaStream_t st,
                std::string& err);
   void tc_gn(const Act& y, std::size_t batch, int groups, int parts, const float* gamma, const float* beta,
-             const BlockDev* film_block, const float* film_time_row, const void* res, Act out, cudaStream_t st);
+             const BlockDev* film_block, const float* film_time_row, const float* res_f32, const void* res_half,
+             Act out, float* out_f32, cudaStream_t st);
+  // `in_f32` / `out_f32`: fp32 residual-stream copies of the block input /
+  // output on the tensor path (null when absent)
   bool block(const BlockDev& blk, const std::vector<Act>& in, int L, std::size_t batch, bool tc,
-             const float* film_time_row, Act out, cudaStream_t st, std::string& err);
+             const float* film_time_row, Act out, cudaStream_t st, std::string& err, const float* in_f32 = nullptr,
+             float* out_f32 = nullptr);
   template <typename Kernel, typename... Args>
   void launch(Kernel k, dim3 grid, dim3 block, std::size_t smem, cudaStream_t st, Args... args) {
     k<<<grid, block, smem, st>>>(args...);
@@ -267,7 +264,8 @@ class Unet final : public UnetDevice {
   void* mcond_ = nullptr;
   float* film_cond_ = nullptr;
   void* x_in_ = nullptr;
-  std::vector<void*> acts_;  // per-layer outputs
+  std::vector<void*> acts_;    // per-layer outputs
+  std::vector<float*> acts32_;  // fp32 residual-stream copies (tensor path)
   void* h1_ = nullptr;
   void* y1_ = nullptr;
   void* y2_ = nullptr;
@@ -556,7 +554,7 @@ bool Unet::load(const TensorTable& t, std::string& err) {
   auto put_conv = [&](ConvDev& c) {
     if (bf16_weights()) {
       bf_stage.resize(c.host_w.size());
-      for (std::size_t i = 0; i < c.host_w.size(); ++i) bf_stage[i] = bf16_bits(c.host_w[i]);
+      for (std::size_t i = 0; i < c.host_w.size(); ++i) bf_stage[i] = fp16_bits_of_bf16_rounded(c.host_w[i]);
       c.w = wts_.take(bf_stage.size() * 2);
       cudaMemcpy(c.w, bf_stage.data(), bf_stage.size() * 2, cudaMemcpyHostToDevice);
     } else {
@@ -678,7 +676,8 @@ int Unet::reserve(std::size_t batch, std::string& err) noexcept {
   plan.add(cap_tc * static_cast<std::size_t>(cond_pad_) * ebytes);
   plan.add_n<float>(batch * static_cast<std::size_t>(F_));
   plan.add(cap_tc * H * static_cast<std::size_t>(cin_pad_) * ebytes);
-  for (std::size_t i = 0; i < n_layers + 4; ++i) plan.add(act_elems_ * ebytes);
+  const bool twins = prec_ == Precision::kBF16 && tc_ok_;
+  for (std::size_t i = 0; i < n_layers + 4 + (twins ? n_layers : 0); ++i) plan.add(act_elems_ * ebytes);
   for (int i = 0; i < 3; ++i) plan.add_n<float>(part_elems_);
   plan.add_n<double>(cap_tc * 8 * 2 * 2 + 64);
   ws_.release();
@@ -701,6 +700,9 @@ int Unet::reserve(std::size_t batch, std::string& err) noexcept {
   x_in_ = ws_.take(cap_tc * H * static_cast<std::size_t>(cin_pad_) * ebytes);
   acts_.clear();
   for (std::size_t i = 0; i < n_layers; ++i) acts_.push_back(ws_.take(act_elems_ * ebytes));
+  acts32_.assign(n_layers, nullptr);
+  if (twins)
+    for (std::size_t i = 0; i < n_layers; ++i) acts32_[i] = ws_.take_n<float>(act_elems_);
   h1_ = ws_.take(act_elems_ * ebytes);
   y1_ = ws_.take(act_elems_ * ebytes);
   y2_ = ws_.take(act_elems_ * ebytes);
@@ -830,6 +832,7 @@ bool Unet::tc_conv(const ConvDev& c, const std::vector<Act>& srcs, int L_out, st
                    long long out_ld, int rps, int tmul, int tadd, bool stats, int groups, bool out_f32,
                    cudaStream_t st, std::string& err) {
   TcLaunch l;
+  l.fp16 = true;
   l.A = c.w;
   l.M_rows = c.oc_rows;
   l.K = c.K;
@@ -877,9 +880,10 @@ bool Unet::tc_conv(const ConvDev& c, const std::vector<Act>& srcs, int L_out, st
 }
 
 void Unet::tc_gn(const Act& y, std::size_t batch, int groups, int parts, const float* gamma, const float* beta,
-                 const BlockDev* film_block, const float* film_time_row, const void* res, Act out, cudaStream_t st) {
-  GnBf16Params p{};
-  p.y = static_cast<const __nv_bfloat16*>(y.p);
+                 const BlockDev* film_block, const float* film_time_row, const float* res_f32, const void* res_half,
+                 Act out, float* out_f32, cudaStream_t st) {
+  GnTcParams p{};
+  p.y = static_cast<const float*>(y.p);
   p.n_tokens = static_cast<long long>(batch) * y.L;
   p.C = y.C;
   p.L = y.L;
@@ -894,13 +898,16 @@ void Unet::tc_gn(const Act& y, std::size_t batch, int groups, int parts, const f
     p.film_F = F_;
     p.film_off = film_block->film_off;
   }
-  p.res = static_cast<const __nv_bfloat16*>(res);
-  p.out = static_cast<__nv_bfloat16*>(out.p);
-  launch(gn_bf16_kernel, dim3(ew_grid(p.n_tokens * (p.C / 8), 256, *ctx_)), dim3(256), 0, st, p);
+  p.res_f32 = res_f32;
+  p.res_half = res_f32 == nullptr ? static_cast<const __half*>(res_half) : nullptr;
+  p.out = static_cast<__half*>(out.p);
+  p.out_f32 = out_f32;
+  launch(gn_tc_kernel, dim3(ew_grid(p.n_tokens * (p.C / 8), 256, *ctx_)), dim3(256), 0, st, p);
 }
 
 bool Unet::block(const BlockDev& blk, const std::vector<Act>& in, int L, std::size_t batch, bool tc,
-                 const float* film_time_row, Act out, cudaStream_t st, std::string& err) {
+                 const float* film_time_row, Act out, cudaStream_t st, std::string& err, const float* in_f32,
+                 float* out_f32) {
   const int G = static_cast<int>(cfg_.groups);
   const int oc = blk.oc;
   Act h1{at_sample(h1_, static_cast<std::size_t>(oc) * L), oc, L};
@@ -917,18 +924,19 @@ bool Unet::block(const BlockDev& blk, const std::vector<Act>& in, int L, std::si
     }
     return true;
   }
+  // conv outputs (pre-norm y, 1x1 residual) stay fp32; only GEMM operands are bf16
   const int parts = (oc / G) > 128 ? (oc / G) / 128 : 1;
-  Act y1{y1_, oc, L}, y2{y2_, oc, L}, yr{yr_, oc, L};
-  if (!tc_conv(blk.c1, in, L, batch, y1_, oc, L, 1, 0, true, G, false, st, err)) return false;
-  tc_gn(y1, batch, G, parts, blk.g1, blk.b1, &blk, film_time_row, nullptr, h1, st);
-  if (!tc_conv(blk.c2, {h1}, L, batch, y2_, oc, L, 1, 0, true, G, false, st, err)) return false;
-  const void* res = in[0].p;
+  Act y1{y1_, oc, L}, y2{y2_, oc, L};
+  if (!tc_conv(blk.c1, in, L, batch, y1_, oc, L, 1, 0, true, G, true, st, err)) return false;
+  tc_gn(y1, batch, G, parts, blk.g1, blk.b1, &blk, film_time_row, nullptr, nullptr, h1, nullptr, st);
+  if (!tc_conv(blk.c2, {h1}, L, batch, y2_, oc, L, 1, 0, true, G, true, st, err)) return false;
+  const float* res_f32 = in_f32;
+  const void* res_half = in[0].p;
   if (blk.has_res) {
-    if (!tc_conv(blk.res, in, L, batch, yr_, oc, L, 1, 0, false, 0, false, st, err)) return false;
-    res = yr_;
+    if (!tc_conv(blk.res, in, L, batch, yr_, oc, L, 1, 0, false, 0, true, st, err)) return false;
+    res_f32 = static_cast<const float*>(yr_);
   }
-  tc_gn(y2, batch, G, parts, blk.g2, blk.b2, nullptr, nullptr, res, out, st);
-  (void)yr;
+  tc_gn(y2, batch, G, parts, blk.g2, blk.b2, nullptr, nullptr, res_f32, res_half, out, out_f32, st);
   return true;
 }
 
@@ -948,15 +956,19 @@ bool Unet::record_forward(std::size_t batch, bool tc, const float* ft_row, cudaS
   const int H = static_cast<int>(cfg_.horizon);
   std::size_t li = 0;
   Act x{at_sample(x_in_, static_cast<std::size_t>(cin_pad_) * H), cin_pad_, H};
+  float* x_f32 = nullptr;  // fp32 residual-stream copy of x (tensor path)
   std::vector<Act> skips(S);
   int L = H;
   for (std::size_t s = 0; s < S; ++s) {
     const int oc = static_cast<int>(cfg_.dims[s]);
     const std::size_t per = static_cast<std::size_t>(oc) * L;
     Act o0{at_sample(acts_[li], per), oc, L}, o1{at_sample(acts_[li + 1], per), oc, L};
+    float* t0 = tc ? acts32_[li] : nullptr;
+    float* t1 = tc ? acts32_[li + 1] : nullptr;
     li += 2;
-    if (!block(down_[s][0], {x}, L, batch, tc, ft_row, o0, st, err)) return false;
-    if (!block(down_[s][1], {o0}, L, batch, tc, ft_row, o1, st, err)) return false;
+    if (!block(down_[s][0], {x}, L, batch, tc, ft_row, o0, st, err, nullptr, t0)) return false;
+    if (!block(down_[s][1], {o0}, L, batch, tc, ft_row, o1, st, err, t0, t1)) return false;
+    x_f32 = t1;
     skips[s] = o1;
     x = o1;
     if (s + 1 < S) {
@@ -968,24 +980,28 @@ bool Unet::record_forward(std::size_t batch, bool tc, const float* ft_row, cudaS
         simt_reduce(ds_[s], p1_, batch, L / 2, d, L / 2, 1, 0, st);
       }
       x = d;
+      x_f32 = nullptr;
       L /= 2;
     } else {
       ++li;
     }
   }
   for (int m = 0; m < 2; ++m) {
+    float* tm = tc ? acts32_[li] : nullptr;
     Act o{at_sample(acts_[li++], static_cast<std::size_t>(x.C) * L), x.C, L};
-    if (!block(mid_[m], {x}, L, batch, tc, ft_row, o, st, err)) return false;
+    if (!block(mid_[m], {x}, L, batch, tc, ft_row, o, st, err, x_f32, tm)) return false;
     x = o;
+    x_f32 = tm;
   }
   for (std::size_t s = 0; s + 1 < S; ++s) {
     const Act skip = skips[S - 1 - s];
     const int low = static_cast<int>(cfg_.dims[S - 2 - s]);
     const std::size_t per = static_cast<std::size_t>(low) * L;
     Act o0{at_sample(acts_[li], per), low, L}, o1{at_sample(acts_[li + 1], per), low, L};
+    float* t0 = tc ? acts32_[li] : nullptr;
     li += 2;
-    if (!block(up_[s][0], {x, skip}, L, batch, tc, ft_row, o0, st, err)) return false;
-    if (!block(up_[s][1], {o0}, L, batch, tc, ft_row, o1, st, err)) return false;
+    if (!block(up_[s][0], {x, skip}, L, batch, tc, ft_row, o0, st, err, nullptr, t0)) return false;
+    if (!block(up_[s][1], {o0}, L, batch, tc, ft_row, o1, st, err, t0, nullptr)) return false;
     Act u{at_sample(acts_[li++], 2 * per), low, 2 * L};
     for (int ph = 0; ph < 2; ++ph) {
       if (tc) {
@@ -1002,9 +1018,10 @@ bool Unet::record_forward(std::size_t batch, bool tc, const float* ft_row, cudaS
   const int c0 = static_cast<int>(cfg_.dims[0]);
   Act z{at_sample(h1_, static_cast<std::size_t>(c0) * H), c0, H};
   if (tc) {
-    if (!tc_conv(fc_, {x}, H, batch, y1_, c0, H, 1, 0, true, static_cast<int>(kFinalNormGroups), false, st, err))
+    if (!tc_conv(fc_, {x}, H, batch, y1_, c0, H, 1, 0, true, static_cast<int>(kFinalNormGroups), true, st, err))
       return false;
-    tc_gn(Act{y1_, c0, H}, batch, static_cast<int>(kFinalNormGroups), 1, fn_g_, fn_b_, nullptr, nullptr, nullptr, z, st);
+    tc_gn(Act{y1_, c0, H}, batch, static_cast<int>(kFinalNormGroups), 1, fn_g_, fn_b_, nullptr, nullptr, nullptr,
+          nullptr, z, nullptr, st);
   } else {
     if (!simt_conv(fc_, {x}, H, batch, p1_, st, err)) return false;
     simt_gn(fc_, p1_, batch, H, fn_g_, fn_b_, static_cast<int>(kFinalNormGroups), nullptr, nullptr, nullptr, nullptr,
@@ -1067,19 +1084,19 @@ bool Unet::record_update(std::size_t nb, bool tc, const StepScalars* step, float
     p.Cin = cin_pad_;
   };
   if (tc) {
-    OutParams<__nv_bfloat16> p{};
+    OutParams<__half> p{};
     fill(p);
-    p.z = static_cast<const __nv_bfloat16*>(h1_);
+    p.z = static_cast<const __half*>(h1_);
     p.x_in = x_in_;
-    p.x_in_bf16 = 1;
-    if (A <= 16) launch(out_update_kernel<__nv_bfloat16, 16>, dim3(blocks), dim3(256), 0, st, p);
-    else launch(out_update_kernel<__nv_bfloat16, 64>, dim3(blocks), dim3(256), 0, st, p);
+    p.x_in_half = 1;
+    if (A <= 16) launch(out_update_kernel<__half, 16>, dim3(blocks), dim3(256), 0, st, p);
+    else launch(out_update_kernel<__half, 64>, dim3(blocks), dim3(256), 0, st, p);
   } else {
     OutParams<float> p{};
     fill(p);
     p.z = at_sample(h1_, static_cast<std::size_t>(c0) * H);
     p.x_in = at_sample(x_in_, static_cast<std::size_t>(cin_pad_) * H);
-    p.x_in_bf16 = 0;
+    p.x_in_half = 0;
     if (A <= 16) launch(out_update_kernel<float, 16>, dim3(blocks), dim3(256), 0, st, p);
     else launch(out_update_kernel<float, 64>, dim3(blocks), dim3(256), 0, st, p);
   }

@@ -17,17 +17,20 @@ extern "C" {
 #pragma GCC visibility push(default)
 #endif
 
-/* C[N][M] = A[M][K] . B[N][K]^T with bf16 operands (raw bits) and fp32 output,
- * on the tcgen05 GEMM.  M, K any positive size (padded internally). */
-int febtest_gemm_bf16(const uint16_t* A, int M, int K, const uint16_t* B, int N, float* C);
+/* C[N][M] = A[M][K] . B[N][K]^T with 16-bit operands (raw bits; fp16 when
+ * `fp16` != 0, else bf16) and fp32 output, on the tcgen05 GEMM.  M, K any
+ * positive size (padded internally). */
+int febtest_gemm_16(const uint16_t* A, int M, int K, const uint16_t* B, int N, float* C, int fp16);
 
 /* y[b][t][o] = bias[o] + sum_{c,j} W[o][c][j] * x[b][t + j - k/2][c] (zero
- * padded), bf16 x / W, fp32 y, on the tcgen05 implicit-GEMM convolution.
+ * padded), 16-bit x / W (fp16 when `fp16` != 0, else bf16), y rounded to the
+ * same 16-bit format and returned as fp32, on the tcgen05 implicit-GEMM
+ * convolution.
  * Also returns the per-(sample, group) GroupNorm sums the epilogue gathers
  * in stats[b][g][2] (sum, sum of squares of the fp32 outputs before their
  * bf16 rounding), groups = OC / group_ch (group_ch = 0: no statistics). */
-int febtest_conv_bf16(const uint16_t* x, int B, int L, int C, const uint16_t* W, const float* bias, int OC, int k,
-                      int group_ch, float* y, double* stats);
+int febtest_conv_16(const uint16_t* x, int B, int L, int C, const uint16_t* W, const float* bias, int OC, int k,
+                    int group_ch, float* y, double* stats, int fp16);
 
 #if defined(__GNUC__)
 #pragma GCC visibility pop
