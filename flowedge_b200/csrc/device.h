@@ -105,6 +105,10 @@ class FlowDevice {
   virtual int advance(std::size_t first, std::size_t count, float* out, std::string& err) noexcept = 0;
   virtual int sample_device(const float* condition, const float* x0, std::size_t batch, std::size_t steps,
                             int method, float* out, void* stream, std::string& err) noexcept = 0;
+  // As sample_device, but every scratch buffer lives in a fixed static
+  // device array (no allocation, no use of the reserved workspace).
+  virtual int sample_static(const float* condition, const float* x0, std::size_t batch, std::size_t steps, int method,
+                            float* out, void* stream, std::string& err) noexcept = 0;
 };
 
 std::unique_ptr<FlowDevice> make_flow_device(const TensorTable& tensors, std::shared_ptr<DeviceContext> ctx,

@@ -703,6 +703,28 @@ int fe_engine_sample_condition_device(fe_engine* engine, const float* condition,
   return rc;
 }
 
+int fe_engine_sample_condition_static(fe_engine* engine, const float* condition, const float* noise, size_t batch,
+                                      size_t steps, int method, float* action, void* stream) {
+  clear_error();
+  if (engine == nullptr || condition == nullptr || noise == nullptr || action == nullptr || steps == 0 ||
+      batch == 0) {
+    set_error("Invalid arguments to fe_engine_sample_condition_static");
+    return FE_STATUS_INVALID_ARGUMENT;
+  }
+  if (!valid_solver(method)) {
+    set_error("Invalid solver method");
+    return FE_STATUS_INVALID_SOLVER;
+  }
+  if (!engine->flow) {
+    set_error("Model has no flow head to sample from");
+    return FE_STATUS_UNSUPPORTED_MODEL;
+  }
+  std::string err;
+  const int rc = engine->flow->sample_static(condition, noise, batch, steps, method, action, stream, err);
+  if (rc != 0) set_error("Static-scratch flow sampling failed: " + err);
+  return rc;
+}
+
 int fe_engine_flow_begin(fe_engine* engine, const float* condition, const float* noise, size_t steps, int method) {
   clear_error();
   if (engine == nullptr || condition == nullptr || noise == nullptr || steps == 0) {

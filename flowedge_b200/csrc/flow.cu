@@ -15,6 +15,7 @@
 #include <cmath>
 #include <cstring>
 #include <map>
+#include <mutex>
 #include <tuple>
 
 #include "runtime.cuh"
@@ -161,6 +162,8 @@ class Flow final : public FlowDevice {
             bool condition_on_device, std::string& err) noexcept override;
   int advance(std::size_t first, std::size_t count, float* out, std::string& err) noexcept override;
   int sample_device(const float* condition, const float* x0, std::size_t batch, std::size_t steps, int method,
+                    float* out, void* stream, std::string& err) noexcept override;
+  int sample_static(const float* condition, const float* x0, std::size_t batch, std::size_t steps, int method,
                     float* out, void* stream, std::string& err) noexcept override;
 
  private:
@@ -603,6 +606,173 @@ int Flow::sample_device(const float* condition, const float* x0, std::size_t bat
   store_rows_kernel<<<ew_grid(static_cast<long long>(batch) * cfg_.action_dim, 256, *ctx_), 256, 0, st>>>(
       x_, static_cast<int>(batch), static_cast<int>(cfg_.action_dim), a_pad_, out);
   return cudaGetLastError() == cudaSuccess ? 0 : 2;
+}
+
+// ---------------------------------------------------------------------------
+// Allocation-free flow solve (fe_engine_sample_condition_static).
+//
+// Some callers cannot call cudaMalloc when they sample: a host application
+// that captures its control step into its own CUDA graph (allocation is not
+// permitted while a stream is being captured), or a real-time loop whose
+// device memory is pre-budgeted by another runtime.  The resident-engine
+// entry points grow the engine's workspace with cudaMalloc when a batch
+// exceeds the reserved capacity; this variant never allocates: its scratch
+// (solver state, stage slopes, hidden activations, split-K partial sums) is
+// the file-scope array below, which every GPU that loads this library holds
+// for the life of the process.
+//
+// * Limit: kStaticScratchBytes (4 MiB); a request whose scratch would not fit
+//   is rejected with FE_STATUS_RESOURCE_EXHAUSTED and a message naming it.
+// * The first call on a device looks up the array's device address with
+//   cudaGetSymbolAddress while that device is current; make that first call
+//   before capturing any stream.
+// * Every call shares the array and it keeps the last call's contents: the
+//   padded columns are rewritten by every call, the step counter is cleared
+//   by every call.  Calls that overlap on the GPU (different streams, or
+//   engines on the same device used concurrently) race on the array.
+// * It always runs the weight-streaming CUDA-core kernels (the same kernels,
+//   in the same order, as the engine's small-batch path).
+constexpr std::size_t kStaticScratchBytes = std::size_t(4) << 20;
+static __device__ __align__(256) unsigned char g_flow_static_scratch[kStaticScratchBytes];
+
+void* static_scratch_address(int device, std::string& err) {
+  static std::mutex mu;
+  static void* addr[64] = {};
+  if (device < 0 || device >= 64) {
+    err = "device index out of range for the static scratch table";
+    return nullptr;
+  }
+  std::lock_guard<std::mutex> lock(mu);
+  if (addr[device] == nullptr) {
+    void* p = nullptr;
+    const cudaError_t rc = cudaGetSymbolAddress(&p, g_flow_static_scratch);
+    if (rc != cudaSuccess || p == nullptr) {
+      err = std::string("cudaGetSymbolAddress(static scratch) failed: ") + cudaGetErrorString(rc);
+      return nullptr;
+    }
+    addr[device] = p;
+  }
+  return addr[device];
+}
+
+int Flow::sample_static(const float* condition, const float* x0, std::size_t batch, std::size_t steps, int method,
+                        float* out, void* stream, std::string& err) noexcept {
+  if (batch == 0 || steps == 0 || method < 0 || method > 2 || condition == nullptr || x0 == nullptr ||
+      out == nullptr) {
+    err = "invalid flow arguments";
+    return 1;
+  }
+  const int H = static_cast<int>(cfg_.hidden), A = static_cast<int>(cfg_.action_dim);
+  const int C = static_cast<int>(cfg_.cond_dim), half = static_cast<int>(cfg_.time_dim / 2);
+  const std::size_t rows = batch;
+  const std::size_t nsl = static_cast<std::size_t>(std::max({in_.nslices, cond_.nslices, out_.nslices,
+                                                             layers_.empty() ? 1 : layers_[0].nslices}));
+  // carve the static array (256-byte aligned pieces) and check it fits
+  std::size_t need = 0;
+  auto piece = [&](std::size_t floats) {
+    const std::size_t off = need;
+    need += (floats * 4 + 255) & ~std::size_t(255);
+    return off;
+  };
+  const std::size_t o_x = piece(rows * a_pad_), o_probe = piece(rows * a_pad_);
+  std::size_t o_k[4];
+  for (auto& o : o_k) o = piece(rows * a_pad_);
+  const std::size_t o_cemb = piece(rows * H), o_tp = piece(H);
+  const std::size_t o_part = piece(nsl * rows * std::max<std::size_t>(H, static_cast<std::size_t>(out_.rows_pad)));
+  const std::size_t o_cin = piece(rows * c_pad_), o_xin = piece(rows * a_pad_);
+  const std::size_t o_h0 = piece(rows * H), o_h1 = piece(rows * H), o_step = piece(4);
+  if (need > kStaticScratchBytes) {
+    err = "request needs " + std::to_string(need) + " bytes of scratch, above the " +
+          std::to_string(kStaticScratchBytes) + "-byte static array (use fewer rows)";
+    return 2;
+  }
+  cudaSetDevice(ctx_->device);
+  auto* base = static_cast<unsigned char*>(static_scratch_address(ctx_->device, err));
+  if (base == nullptr) return 2;
+  auto F = [&](std::size_t off) { return reinterpret_cast<float*>(base + off); };
+  float *x = F(o_x), *probe = F(o_probe), *cemb = F(o_cemb), *tp = F(o_tp), *part = F(o_part);
+  float *cin = F(o_cin), *xin = F(o_xin), *h0 = F(o_h0), *h1 = F(o_h1);
+  float* k[4] = {F(o_k[0]), F(o_k[1]), F(o_k[2]), F(o_k[3])};
+  int* step = reinterpret_cast<int*>(base + o_step);
+  cudaStream_t st = stream != nullptr ? static_cast<cudaStream_t>(stream) : ctx_->stream;
+  const bool bf = prec_ == Precision::kBF16;
+  auto linear = [&](const Mat& m, const float* in, int in_ld, float* dst, int dst_ld, const float* add_vec,
+                    const float* add_tok, int act) {
+    SimtConvParams p{};
+    p.W = m.w;
+    p.M = m.rows;
+    p.K = m.cols_pad;
+    p.src[0] = SimtSource{in, in_ld, 1};
+    p.stride = 1;
+    p.L_out = 1;
+    p.n_tokens = static_cast<int>(rows);
+    p.slices = m.slices;
+    p.partial = part;
+    const int nt = p.n_tokens >= 16 ? 16 : (p.n_tokens >= 8 ? 8 : 4);
+    const dim3 grid(static_cast<unsigned>(m.nslices), static_cast<unsigned>((m.rows + 127) / 128),
+                    static_cast<unsigned>((p.n_tokens + nt - 1) / nt));
+    if (nt == 16) bf ? simt_conv_kernel<16, true><<<grid, 128, 0, st>>>(p) : simt_conv_kernel<16, false><<<grid, 128, 0, st>>>(p);
+    else if (nt == 8) bf ? simt_conv_kernel<8, true><<<grid, 128, 0, st>>>(p) : simt_conv_kernel<8, false><<<grid, 128, 0, st>>>(p);
+    else bf ? simt_conv_kernel<4, true><<<grid, 128, 0, st>>>(p) : simt_conv_kernel<4, false><<<grid, 128, 0, st>>>(p);
+    ReduceParams r{};
+    r.partial = part;
+    r.nslices = m.nslices;
+    r.n_tokens = static_cast<int>(rows);
+    r.M = m.rows;
+    r.add_vec = add_vec;
+    r.add_tok = add_tok;
+    r.act = act;
+    r.out = dst;
+    r.out_ld = dst_ld;
+    reduce_partials_kernel<<<ew_grid(static_cast<long long>(rows) * m.rows, 256, *ctx_), 256, 0, st>>>(r);
+  };
+  // c_emb = W_c cond; x = x0 (padded copies rewrite every padding column)
+  load_rows_kernel<<<ew_grid(static_cast<long long>(rows) * c_pad_, 256, *ctx_), 256, 0, st>>>(
+      condition, static_cast<int>(rows), C, nullptr, 0, cin, c_pad_, 0);
+  linear(cond_, cin, c_pad_, cemb, H, nullptr, nullptr, tc::kActNone);
+  load_rows_kernel<<<ew_grid(static_cast<long long>(rows) * a_pad_, 256, *ctx_), 256, 0, st>>>(
+      x0, static_cast<int>(rows), A, x, a_pad_, xin, a_pad_, 0);
+  cudaMemsetAsync(step, 0, 2 * sizeof(int), st);
+  const int stages = method == 0 ? 1 : (method == 1 ? 2 : 4);
+  for (std::size_t i = 0; i < steps; ++i) {
+    for (int s = 0; s < stages; ++s) {
+      time_proj_kernel<<<(H + 255) / 256, 256, static_cast<std::size_t>(2 * half) * 4, st>>>(
+          step, static_cast<int>(steps), method, s, freqs_, half, wt_, H, tp);
+      float* hin = h0;
+      float* hout = h1;
+      linear(in_, xin, a_pad_, hin, H, tp, cemb, tc::kActSilu);
+      for (const Mat& l : layers_) {
+        linear(l, hin, H, hout, H, nullptr, nullptr, tc::kActSilu);
+        std::swap(hin, hout);
+      }
+      linear(out_, hin, H, k[s], a_pad_, nullptr, nullptr, tc::kActNone);
+      OdeParams p{};
+      p.B = static_cast<int>(rows);
+      p.A = A;
+      p.ld = a_pad_;
+      p.method = method;
+      p.stage = s;
+      p.steps = static_cast<int>(steps);
+      p.step_idx = step;
+      p.step_out = s == stages - 1 ? step + 1 : nullptr;
+      p.x = x;
+      p.probe = probe;
+      for (int j = 0; j < 4; ++j) p.k[j] = k[j];
+      p.next_in = xin;
+      p.ld_in = a_pad_;
+      p.next_half = 0;
+      ode_stage_kernel<<<ew_grid(static_cast<long long>(rows) * A, 256, *ctx_), 256, 0, st>>>(p);
+    }
+    cudaMemcpyAsync(step, step + 1, sizeof(int), cudaMemcpyDeviceToDevice, st);
+  }
+  store_rows_kernel<<<ew_grid(static_cast<long long>(rows) * A, 256, *ctx_), 256, 0, st>>>(
+      x, static_cast<int>(rows), A, a_pad_, out);
+  const cudaError_t rc = cudaGetLastError();
+  if (rc != cudaSuccess) {
+    err = std::string("static flow solve launch failed: ") + cudaGetErrorString(rc);
+    return 2;
+  }
+  return 0;
 }
 
 }  // namespace

@@ -125,6 +125,8 @@ SIGNATURES = {
                                                    _f32p]),
     "fe_engine_sample_condition_device": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_size_t, C.c_size_t,
                                                     C.c_int, C.c_void_p, C.c_void_p]),
+    "fe_engine_sample_condition_static": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_size_t, C.c_size_t,
+                                                    C.c_int, C.c_void_p, C.c_void_p]),
     "fe_engine_run_batch": (C.c_int, [C.c_void_p, _i32p, C.c_size_t, C.c_size_t, _f32p]),
     "fe_engine_sample_batch": (C.c_int, [C.c_void_p, _i32p, C.c_size_t, C.c_size_t, _f32p, C.c_size_t, C.c_int,
                                          _f32p]),

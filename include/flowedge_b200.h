@@ -304,6 +304,19 @@ int fe_engine_sample_condition_batch(fe_engine* engine, const float* condition, 
 /* Device-pointer variant of fe_engine_sample_condition_batch. */
 int fe_engine_sample_condition_device(fe_engine* engine, const float* condition, const float* noise, size_t batch,
                                       size_t steps, int method, float* action, void* stream);
+/* Allocation-free variant of fe_engine_sample_condition_device (no
+ * counterpart in the reference ABI).  For callers that cannot call cudaMalloc
+ * while they sample - a host application capturing its control step into its
+ * own CUDA graph, or a loop whose device memory another runtime pre-budgets -
+ * it runs the flow ODE solve on caller device buffers (condition [batch][C],
+ * noise / action [batch][A], enqueued on `stream`) with its scratch in a
+ * fixed 4 MiB static device array that every GPU loading the library holds
+ * until exit, never touching the engine's reserved workspace.  Requests whose
+ * scratch exceeds 4 MiB are rejected with FE_STATUS_RESOURCE_EXHAUSTED.  The
+ * first call on a device looks up the array's address; make it before any
+ * stream capture.  Calls share the array: calls that overlap on the GPU race. */
+int fe_engine_sample_condition_static(fe_engine* engine, const float* condition, const float* noise, size_t batch,
+                                      size_t steps, int method, float* action, void* stream);
 /* Batched Mamba prefill: tokens [batch][seq_len], out [batch][seq_len][d_model]. */
 int fe_engine_run_batch(fe_engine* engine, const int32_t* tokens, size_t batch, size_t seq_len, float* out);
 /* Batched fe_engine_sample: tokens [batch][seq_len], noise/action [batch][A]. */
