@@ -190,6 +190,17 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
   for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+// 32 lanes x 8 columns (one row per lane).
+__device__ __forceinline__ void tmem_ld8(uint32_t taddr, float (&v)[8]) {
+  uint32_t r[8];
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+               : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 8; ++i) v[i] = __uint_as_float(r[i]);
+}
+
 __device__ __forceinline__ void named_barrier(int id, int threads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
 }
@@ -208,6 +219,15 @@ __device__ __forceinline__ float mish_f(float x) {
   const float e = expf(x);
   const float n = e * (e + 2.0f);
   return x * (n / (n + 2.0f));
+}
+
+// Mish with the fast exponential and division, for values rounded to fp16
+// right afterwards (relative error ~1e-6, far below the fp16 step of 2^-11).
+__device__ __forceinline__ float mish_fast(float x) {
+  if (x > 20.0f) return x;
+  const float e = __expf(x);
+  const float n = e * (e + 2.0f);
+  return x * __fdividef(n, n + 2.0f);
 }
 
 __device__ __forceinline__ float silu_f(float x) { return x / (1.0f + expf(-x)); }

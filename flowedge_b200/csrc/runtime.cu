@@ -121,8 +121,12 @@ std::shared_ptr<DeviceContext> make_device_context(int device, std::string& err)
     err = "device allocation failed";
     return nullptr;
   }
-  if (cudaFuncSetAttribute(tc::tc_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, tc::SMEM_BYTES) !=
-      cudaSuccess) {
+  if (cudaFuncSetAttribute(tc::tc_gemm_kernel<tc::kEpiPlain>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           tc::SMEM_BYTES) != cudaSuccess ||
+      cudaFuncSetAttribute(tc::tc_gemm_kernel<tc::kEpiStats>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           tc::SMEM_BYTES) != cudaSuccess ||
+      cudaFuncSetAttribute(tc::tc_gemm_kernel<tc::kEpiFused>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           tc::SMEM_BYTES) != cudaSuccess) {
     err = "cannot enable the tensor-core kernel's shared memory";
     return nullptr;
   }
@@ -259,6 +263,26 @@ cudaError_t tc_gemm(const TcLaunch& l, DeviceContext& ctx, cudaStream_t stream, 
   p.groups = l.groups;
   p.parts = l.group_ch > tc::BM ? l.group_ch / tc::BM : 1;
   p.err = ctx.d_err;
+  if (l.gn_fuse) {
+    if (l.stats != nullptr || l.out_f32 || l.group_ch < 32 || l.group_ch > tc::BM || tc::BM % l.group_ch != 0 ||
+        tc::BM / l.group_ch > tc::MAX_TILE_GROUPS || p.tile_samples > tc::MAX_TILE_SAMPLES || l.gamma == nullptr ||
+        l.beta == nullptr || l.act != tc::kActNone || l.add_tok != nullptr || !l.fp16) {
+      err = "tc_gemm: unsupported fused GroupNorm geometry";
+      return cudaErrorInvalidValue;
+    }
+    p.gn_fuse = 1;
+    p.group_ch = l.group_ch;
+    p.gamma = l.gamma;
+    p.beta = l.beta;
+    p.film_cond = l.film_cond;
+    p.film_time = l.film_time;
+    p.film_F = l.film_F;
+    p.film_off = l.film_off;
+    p.film_C = l.film_C;
+    p.res_f32 = l.res_f32;
+    p.res16 = l.res16;
+    p.out_twin = l.out_twin;
+  }
 
   CUtensorMap ta{}, tb[3]{};
   if (!encode_2d(&ta, l.A, static_cast<std::uint64_t>(l.K), static_cast<std::uint64_t>(l.M_rows), 64, tc::BM, dtype,
@@ -270,7 +294,12 @@ cudaError_t tc_gemm(const TcLaunch& l, DeviceContext& ctx, cudaStream_t stream, 
       return cudaErrorInvalidValue;
   }
   const int grid = p.total_tiles < ctx.sm_count ? p.total_tiles : ctx.sm_count;
-  tc::tc_gemm_kernel<<<grid, tc::THREADS, tc::SMEM_BYTES, stream>>>(ta, tb[0], tb[1], tb[2], p);
+  if (p.gn_fuse)
+    tc::tc_gemm_kernel<tc::kEpiFused><<<grid, tc::THREADS, tc::SMEM_BYTES, stream>>>(ta, tb[0], tb[1], tb[2], p);
+  else if (p.stats != nullptr)
+    tc::tc_gemm_kernel<tc::kEpiStats><<<grid, tc::THREADS, tc::SMEM_BYTES, stream>>>(ta, tb[0], tb[1], tb[2], p);
+  else
+    tc::tc_gemm_kernel<tc::kEpiPlain><<<grid, tc::THREADS, tc::SMEM_BYTES, stream>>>(ta, tb[0], tb[1], tb[2], p);
   const cudaError_t rc = cudaGetLastError();
   if (rc != cudaSuccess) err = std::string("tc_gemm launch: ") + cudaGetErrorString(rc);
   return rc;

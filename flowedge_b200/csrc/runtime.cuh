@@ -102,6 +102,17 @@ struct TcLaunch {
   int out_rps = 1, out_tmul = 1, out_tadd = 0, out_ch_off = 0;
   double* stats = nullptr;
   int group_ch = 0, groups = 0;
+  // GroupNorm + Mish (+ FiLM or residual) applied in the epilogue; `out` is
+  // then the 16-bit normalised activation (see tc::Params::gn_fuse)
+  bool gn_fuse = false;
+  const float* gamma = nullptr;
+  const float* beta = nullptr;
+  const float* film_cond = nullptr;
+  const float* film_time = nullptr;
+  int film_F = 0, film_off = 0, film_C = 0;
+  const float* res_f32 = nullptr;
+  const void* res16 = nullptr;
+  float* out_twin = nullptr;
 };
 
 cudaError_t tc_gemm(const TcLaunch& launch, DeviceContext& ctx, cudaStream_t stream, std::string& err);

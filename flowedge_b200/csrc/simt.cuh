@@ -293,15 +293,28 @@ static __global__ void __launch_bounds__(256) gn_tc_kernel(const GnTcParams p) {
       r[0] = half_lo(rv.x); r[1] = half_hi(rv.x); r[2] = half_lo(rv.y); r[3] = half_hi(rv.y);
       r[4] = half_lo(rv.z); r[5] = half_hi(rv.z); r[6] = half_lo(rv.w); r[7] = half_hi(rv.w);
     }
+    float gam[8], bet[8], fsc[8], fsh[8];
+    {
+      const float4 g0 = *reinterpret_cast<const float4*>(p.gamma + c0);
+      const float4 g1 = *reinterpret_cast<const float4*>(p.gamma + c0 + 4);
+      const float4 b0 = *reinterpret_cast<const float4*>(p.beta + c0);
+      const float4 b1 = *reinterpret_cast<const float4*>(p.beta + c0 + 4);
+      gam[0] = g0.x; gam[1] = g0.y; gam[2] = g0.z; gam[3] = g0.w; gam[4] = g1.x; gam[5] = g1.y; gam[6] = g1.z; gam[7] = g1.w;
+      bet[0] = b0.x; bet[1] = b0.y; bet[2] = b0.z; bet[3] = b0.w; bet[4] = b1.x; bet[5] = b1.y; bet[6] = b1.z; bet[7] = b1.w;
+    }
+    if (p.film_cond != nullptr) {
+      const float* fc = p.film_cond + static_cast<long long>(b) * p.film_F + p.film_off + c0;
+      const float* ft = p.film_time + p.film_off + c0;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        fsc[j] = fc[j] + ft[j];
+        fsh[j] = fc[p.C + j] + ft[p.C + j];
+      }
+    }
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
-      const int c = c0 + j;
-      float z = mish_f((v[j] - mean_f) * (inv * p.gamma[c]) + p.beta[c]);
-      if (p.film_cond != nullptr) {
-        const float* fc = p.film_cond + static_cast<long long>(b) * p.film_F + p.film_off;
-        const float* ft = p.film_time + p.film_off;
-        z = (fc[c] + ft[c]) * z + (fc[p.C + c] + ft[p.C + c]);
-      }
+      float z = mish_fast((v[j] - mean_f) * (inv * gam[j]) + bet[j]);
+      if (p.film_cond != nullptr) z = fsc[j] * z + fsh[j];
       v[j] = z + r[j];
     }
     uint4 o;

@@ -42,7 +42,9 @@ constexpr int EPI_WARPS = 8;
 constexpr int EPI_THREADS = EPI_WARPS * 32;
 constexpr int THREADS = 64 + EPI_THREADS;
 constexpr int TMEM_COLS = 512;
-constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + 256 + 4 * MAX_TILE_SAMPLES * 16;
+constexpr int MAX_TILE_GROUPS = 4;   // groups of >= 32 channels inside a 128-row tile
+constexpr int SMEM_BYTES =
+    1024 + STAGES * STAGE_BYTES + 256 + 4 * MAX_TILE_SAMPLES * 16 + MAX_TILE_SAMPLES * MAX_TILE_GROUPS * 8;
 
 enum Act : int { kActNone = 0, kActSilu = 1, kActSoftplus = 2 };
 
@@ -82,8 +84,24 @@ struct Params {
   int group_ch;           // channels per group (multiple of 32)
   int groups;             // groups of the layer
   int parts;              // max(1, group_ch / 128)
+  // GroupNorm applied in the epilogue (groups of <= 128 channels lie inside
+  // one tile): z = mish(GN(y)) then FiLM, or + residual; z goes to `out`
+  // (16-bit) and optionally to the fp32 copy `out_twin`.
+  int gn_fuse;
+  const float* gamma;
+  const float* beta;
+  const float* film_cond;  // [sample][film_F]: scale at film_off + m, shift at film_off + film_C + m
+  const float* film_time;  // [film_F] time part, added to both
+  int film_F, film_off, film_C;
+  const float* res_f32;    // residual rows laid out like the output, or null
+  const void* res16;       // 16-bit residual (used when res_f32 is null), or null
+  float* out_twin;         // fp32 copy of z, or null
   int* err;
 };
+
+__device__ __forceinline__ long long out_row(const Params& p, int b, int t) {
+  return static_cast<long long>(b) * p.out_rps + t * p.out_tmul + p.out_tadd;
+}
 
 __device__ __forceinline__ void epilogue_store(const Params& p, int tok_b, int tok_t, int m, float v) {
   const long long row = static_cast<long long>(tok_b) * p.out_rps + tok_t * p.out_tmul + p.out_tadd;
@@ -99,6 +117,14 @@ __device__ __forceinline__ void epilogue_store(const Params& p, int tok_b, int t
   }
 }
 
+// Epilogue modes (one kernel instantiation each, so each carries only its
+// own code):
+//   kEpiPlain: bias (+ add terms, activation), fp32 or 16-bit store
+//   kEpiStats: as plain, plus GroupNorm partial sums to p.stats
+//   kEpiFused: GroupNorm + Mish (+ FiLM / residual) applied in the epilogue
+enum EpiMode : int { kEpiPlain = 0, kEpiStats = 1, kEpiFused = 2 };
+
+template <int MODE>
 static __global__ void __launch_bounds__(THREADS, 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB0,
                    const __grid_constant__ CUtensorMap tmB1, const __grid_constant__ CUtensorMap tmB2,
@@ -155,8 +181,7 @@ static __global__ void __launch_bounds__(THREADS, 1)
     // ---------------- TMA producer ----------------
     if (lane == 0) {
       uint32_t kb_iter = 0;
-      int armed[STAGES];
-      for (int s = 0; s < STAGES; ++s) armed[s] = -1;
+      uint32_t armed = 0, armed_phase = 0;  // per-stage bits: armed at least once / parity of its last arm
       bool ok = true;
       for (int tile = blockIdx.x; tile < p.total_tiles && ok; tile += gridDim.x) {
         const int m_blk = tile % p.n_tiles_m;
@@ -174,7 +199,8 @@ static __global__ void __launch_bounds__(THREADS, 1)
             uint8_t* a_dst = smem + stage * STAGE_BYTES;
             uint8_t* b_dst = a_dst + A_BYTES;
             mbar_arrive_expect_tx(&full[stage], STAGE_BYTES);
-            armed[stage] = static_cast<int>(phase);
+            armed |= 1u << stage;
+            armed_phase = (armed_phase & ~(1u << stage)) | (phase << stage);
             tma_load_2d(a_dst, &tmA, sg.a_k + kb * BK, m_blk * BM, &full[stage]);
             tma_load_3d(b_dst, mapB, sg.ch_off + kb * BK, sg.t_off, n_blk * p.tile_samples, &full[stage]);
           }
@@ -184,8 +210,9 @@ static __global__ void __launch_bounds__(THREADS, 1)
         atomicCAS(p.err, 0, kErrWaitTimeoutProducer);
         *abort_flag = 1;
         for (int s = 0; s < STAGES; ++s)
-          if (armed[s] >= 0) {
-            for (uint32_t spin = 0; spin < kSpinLimit && !mbar_try_wait(&full[s], armed[s]); ++spin) {
+          if (armed & (1u << s)) {
+            const uint32_t ph = (armed_phase >> s) & 1u;
+            for (uint32_t spin = 0; spin < kSpinLimit && !mbar_try_wait(&full[s], ph); ++spin) {
             }
           }
       }
@@ -237,12 +264,15 @@ static __global__ void __launch_bounds__(THREADS, 1)
     }
   } else {
     // ---------------- epilogue (warps 2..9) ----------------
+    constexpr bool kStats = MODE != kEpiPlain;
     const int q = warp & 3;                // TMEM lane quadrant this warp may access
     const int half = (warp - 2) >> 2;      // which 128 columns of the tile
     const int row = q * 32 + lane;
+    float2* stat = reinterpret_cast<float2*>(red + 4 * MAX_TILE_SAMPLES);  // [sample][group] (mean, inv)
     uint32_t acc_iter = 0;
-    const bool gather_stats = p.stats != nullptr;
     const int lmask = p.L - 1;
+    const uint32_t lane_base = static_cast<uint32_t>(q * 32) << 16;
+    const int col0 = half * (BN / 2);
     for (int tile = blockIdx.x; tile < p.total_tiles; tile += gridDim.x, ++acc_iter) {
       const int m_blk = tile % p.n_tiles_m;
       const int n_blk = tile / p.n_tiles_m;
@@ -259,25 +289,28 @@ static __global__ void __launch_bounds__(THREADS, 1)
       const float bias = (p.bias != nullptr && m_ok) ? p.bias[m] : 0.0f;
       const float addv = (p.add_vec != nullptr && m_ok) ? p.add_vec[m] : 0.0f;
       const int sample0 = n_blk * p.tile_samples;
+      const uint32_t tbase = tmem_base + lane_base + acc * BN;
+      // pass 1: bias / activation / store (plain and stats modes) and statistics
       float s1 = 0.0f, s2 = 0.0f;
-      for (int chunk = half * (BN / 64); chunk < (half + 1) * (BN / 64); ++chunk) {
-        float v[32];
-        tmem_ld32(tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * BN + chunk * 32, v);
-#pragma unroll 4
-        for (int j = 0; j < 32; ++j) {
-          const int n = chunk * 32 + j;
+#pragma unroll 1
+      for (int c8 = 0; c8 < BN / 2; c8 += 8) {
+        float v[8];
+        tmem_ld8(tbase + col0 + c8, v);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const int n = col0 + c8 + j;
           const int ls = n >> p.L_shift;
           const int t = n & lmask;
           const int b = sample0 + ls;
           float y = v[j] + bias + addv;
-          if (p.add_tok != nullptr && m_ok && b < p.n_samples) {
-            const long long arow = static_cast<long long>(b) * p.out_rps + t * p.out_tmul + p.out_tadd;
-            y += p.add_tok[arow * p.add_ld + m];
+          if constexpr (MODE != kEpiFused) {
+            if (p.add_tok != nullptr && m_ok && b < p.n_samples)
+              y += p.add_tok[out_row(p, b, t) * p.add_ld + m];
+            if (p.act == kActSilu) y = silu_f(y);
+            else if (p.act == kActSoftplus) y = softplus_f(y);
+            if (m_ok && b < p.n_samples) epilogue_store(p, b, t, m, y);
           }
-          if (p.act == kActSilu) y = silu_f(y);
-          else if (p.act == kActSoftplus) y = softplus_f(y);
-          if (m_ok && b < p.n_samples) epilogue_store(p, b, t, m, y);
-          if (gather_stats) {
+          if constexpr (kStats) {
             s1 += y;
             s2 += y * y;
             if (t == lmask) {
@@ -294,10 +327,12 @@ static __global__ void __launch_bounds__(THREADS, 1)
           }
         }
       }
-      // TMEM buffer may be overwritten by the next tile's MMAs from here on.
-      tc_fence_before();
-      mbar_arrive(&tempty[acc]);
-      if (gather_stats) {
+      if constexpr (MODE != kEpiFused) {
+        // TMEM buffer may be overwritten by the next tile's MMAs from here on.
+        tc_fence_before();
+        mbar_arrive(&tempty[acc]);
+      }
+      if constexpr (kStats) {
         named_barrier(1, EPI_THREADS);
         // combine the 4 quadrants' partials into (sample, group) sums
         const int tid = threadIdx.x - 64;
@@ -308,21 +343,96 @@ static __global__ void __launch_bounds__(THREADS, 1)
           const int ls = it / groups_in_tile;
           const int gl = it - ls * groups_in_tile;
           const int b = sample0 + ls;
-          if (b >= p.n_samples) continue;
           double d1 = 0.0, d2 = 0.0;
           for (int w = 0; w < warps_per_group; ++w) {
             const double2 r = red[(gl * warps_per_group + w) * MAX_TILE_SAMPLES + ls];
             d1 += r.x;
             d2 += r.y;
           }
-          const int row0 = m_blk * BM + gl * warps_per_group * 32;
-          const int g = row0 / p.group_ch;
-          const int part = (row0 % p.group_ch) / BM;
-          double* dst = p.stats + (((static_cast<long long>(b) * p.groups + g) * p.parts + part) * 2);
-          dst[0] = d1;
-          dst[1] = d2;
+          if constexpr (MODE == kEpiFused) {
+            // biased variance E[y^2] - E[y]^2 clamped at 0, eps 1e-5, in double
+            const double cnt = static_cast<double>(p.group_ch) * p.L;
+            const double mean = d1 / cnt;
+            const double var = fmax(0.0, d2 / cnt - mean * mean);
+            stat[ls * MAX_TILE_GROUPS + gl] =
+                make_float2(static_cast<float>(mean), static_cast<float>(1.0 / sqrt(var + 1e-5)));
+          } else {
+            if (b < p.n_samples) {
+              const int row0 = m_blk * BM + gl * warps_per_group * 32;
+              const int g = row0 / p.group_ch;
+              const int part = (row0 % p.group_ch) / BM;
+              double* dst = p.stats + (((static_cast<long long>(b) * p.groups + g) * p.parts + part) * 2);
+              dst[0] = d1;
+              dst[1] = d2;
+            }
+          }
         }
         named_barrier(1, EPI_THREADS);
+      }
+      if constexpr (MODE == kEpiFused) {
+        // pass 2: z = mish((y - mean) * inv * gamma + beta), FiLM or + residual
+        const int gl = row / p.group_ch;
+        const float gam = m_ok ? p.gamma[m] : 0.0f;
+        const float bet = m_ok ? p.beta[m] : 0.0f;
+        const bool film = p.film_cond != nullptr;
+        const float ft_s = (film && m_ok) ? p.film_time[p.film_off + m] : 0.0f;
+        const float ft_h = (film && m_ok) ? p.film_time[p.film_off + p.film_C + m] : 0.0f;
+        float fs = 1.0f, fh = 0.0f, mean = 0.0f, scale = 0.0f;
+        int cur_b = -1;
+        __half* out16 = static_cast<__half*>(p.out);
+        const bool has_res = p.res_f32 != nullptr || p.res16 != nullptr;
+#pragma unroll 1
+        for (int c32 = 0; c32 < BN / 2; c32 += 32) {
+          // issue the 32 residual loads of this slice before any math so they
+          // overlap (one load per column, coalesced across the warp's channels)
+          float r[32];
+          if (has_res) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              const int n = col0 + c32 + j;
+              const int b = sample0 + (n >> p.L_shift);
+              r[j] = 0.0f;
+              if (m_ok && b < p.n_samples) {
+                const long long o = out_row(p, b, n & lmask) * p.out_ld + p.out_ch_off + m;
+                r[j] = p.res_f32 != nullptr ? p.res_f32[o]
+                                            : __half2float(static_cast<const __half*>(p.res16)[o]);
+              }
+            }
+          }
+#pragma unroll
+          for (int c8 = 0; c8 < 32; c8 += 8) {
+            float v[8];
+            tmem_ld8(tbase + col0 + c32 + c8, v);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              const int n = col0 + c32 + c8 + j;
+              const int ls = n >> p.L_shift;
+              const int t = n & lmask;
+              const int b = sample0 + ls;
+              if (b != cur_b) {
+                cur_b = b;
+                const float2 st = stat[ls * MAX_TILE_GROUPS + gl];
+                mean = st.x;
+                scale = st.y * gam;
+                if (film && m_ok && b < p.n_samples) {
+                  const float* fc = p.film_cond + static_cast<long long>(b) * p.film_F + p.film_off;
+                  fs = fc[m] + ft_s;
+                  fh = fc[p.film_C + m] + ft_h;
+                }
+              }
+              if (m_ok && b < p.n_samples) {
+                float z = mish_fast((v[j] + bias - mean) * scale + bet);
+                if (film) z = fs * z + fh;
+                if (has_res) z += r[c8 + j];
+                const long long o = out_row(p, b, t) * p.out_ld + p.out_ch_off + m;
+                out16[o] = to_half_sat(z);
+                if (p.out_twin != nullptr) p.out_twin[o] = z;
+              }
+            }
+          }
+        }
+        tc_fence_before();
+        mbar_arrive(&tempty[acc]);
       }
     }
   }

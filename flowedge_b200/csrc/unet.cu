@@ -202,9 +202,24 @@ class Unet final : public UnetDevice {
   void simt_gn(const ConvDev& c, const float* partial, std::size_t batch, int L, const float* gamma,
                const float* beta, int groups, const BlockDev* film_block, const float* film_time_row,
                const float* res_tensor, const ConvDev* res_conv, const float* res_partial, Act out, cudaStream_t st);
+  // GroupNorm + Mish (+ FiLM / residual) fused into a conv's epilogue
+  struct Fuse {
+    const float* gamma = nullptr;
+    const float* beta = nullptr;
+    const BlockDev* film_block = nullptr;
+    const float* film_time_row = nullptr;
+    const float* res_f32 = nullptr;
+    const void* res16 = nullptr;
+    float* out_twin = nullptr;
+    int groups = 0;
+  };
   bool tc_conv(const ConvDev& c, const std::vector<Act>& srcs, int L_out, std::size_t batch, void* out,
                long long out_ld, int rps, int tmul, int tadd, bool stats, int groups, bool out_f32, cudaStream_t st,
-               std::string& err);
+               std::string& err, const Fuse* fuse = nullptr);
+  bool fusable(int channels, int groups) const {
+    const int gc = channels / groups;
+    return gc >= 32 && gc <= 128 && 128 % gc == 0;
+  }
   void tc_gn(const Act& y, std::size_t batch, int groups, int parts, const float* gamma, const float* beta,
              const BlockDev* film_block, const float* film_time_row, const float* res_f32, const void* res_half,
              Act out, float* out_f32, cudaStream_t st);
@@ -830,7 +845,7 @@ void Unet::simt_gn(const ConvDev& c, const float* partial, std::size_t batch, in
 
 bool Unet::tc_conv(const ConvDev& c, const std::vector<Act>& srcs, int L_out, std::size_t batch, void* out,
                    long long out_ld, int rps, int tmul, int tadd, bool stats, int groups, bool out_f32,
-                   cudaStream_t st, std::string& err) {
+                   cudaStream_t st, std::string& err, const Fuse* fuse) {
   TcLaunch l;
   l.fp16 = true;
   l.A = c.w;
@@ -861,6 +876,23 @@ bool Unet::tc_conv(const ConvDev& c, const std::vector<Act>& srcs, int L_out, st
     l.stats = stats_;
     l.groups = groups;
     l.group_ch = c.oc / groups;
+  }
+  if (fuse != nullptr) {
+    l.gn_fuse = true;
+    l.groups = fuse->groups;
+    l.group_ch = c.oc / fuse->groups;
+    l.gamma = fuse->gamma;
+    l.beta = fuse->beta;
+    if (fuse->film_block != nullptr) {
+      l.film_cond = film_cond_;
+      l.film_time = fuse->film_time_row;
+      l.film_F = F_;
+      l.film_off = fuse->film_block->film_off;
+      l.film_C = c.oc;
+    }
+    l.res_f32 = fuse->res_f32;
+    l.res16 = fuse->res16;
+    l.out_twin = fuse->out_twin;
   }
   ++recorded_;
   if (!profiling_) return tc_gemm(l, *ctx_, st, err) == cudaSuccess;
@@ -924,7 +956,30 @@ bool Unet::block(const BlockDev& blk, const std::vector<Act>& in, int L, std::si
     }
     return true;
   }
-  // conv outputs (pre-norm y, 1x1 residual) stay fp32; only GEMM operands are bf16
+  if (fusable(oc, G)) {
+    // GroupNorm + Mish + FiLM / residual in the conv epilogues
+    Fuse f1;
+    f1.gamma = blk.g1;
+    f1.beta = blk.b1;
+    f1.film_block = &blk;
+    f1.film_time_row = film_time_row;
+    f1.groups = G;
+    if (!tc_conv(blk.c1, in, L, batch, h1.p, oc, L, 1, 0, false, 0, false, st, err, &f1)) return false;
+    Fuse f2;
+    f2.gamma = blk.g2;
+    f2.beta = blk.b2;
+    f2.groups = G;
+    f2.out_twin = out_f32;
+    if (blk.has_res) {
+      if (!tc_conv(blk.res, in, L, batch, yr_, oc, L, 1, 0, false, 0, true, st, err)) return false;
+      f2.res_f32 = static_cast<const float*>(yr_);
+    } else {
+      f2.res_f32 = in_f32;
+      f2.res16 = in_f32 == nullptr ? in[0].p : nullptr;
+    }
+    return tc_conv(blk.c2, {h1}, L, batch, out.p, oc, L, 1, 0, false, 0, false, st, err, &f2);
+  }
+  // conv outputs (pre-norm y, 1x1 residual) stay fp32; only GEMM operands are 16-bit
   const int parts = (oc / G) > 128 ? (oc / G) / 128 : 1;
   Act y1{y1_, oc, L}, y2{y2_, oc, L};
   if (!tc_conv(blk.c1, in, L, batch, y1_, oc, L, 1, 0, true, G, true, st, err)) return false;
@@ -1018,10 +1073,18 @@ bool Unet::record_forward(std::size_t batch, bool tc, const float* ft_row, cudaS
   const int c0 = static_cast<int>(cfg_.dims[0]);
   Act z{at_sample(h1_, static_cast<std::size_t>(c0) * H), c0, H};
   if (tc) {
-    if (!tc_conv(fc_, {x}, H, batch, y1_, c0, H, 1, 0, true, static_cast<int>(kFinalNormGroups), true, st, err))
-      return false;
-    tc_gn(Act{y1_, c0, H}, batch, static_cast<int>(kFinalNormGroups), 1, fn_g_, fn_b_, nullptr, nullptr, nullptr,
-          nullptr, z, nullptr, st);
+    if (fusable(c0, static_cast<int>(kFinalNormGroups))) {
+      Fuse f;
+      f.gamma = fn_g_;
+      f.beta = fn_b_;
+      f.groups = static_cast<int>(kFinalNormGroups);
+      if (!tc_conv(fc_, {x}, H, batch, z.p, c0, H, 1, 0, false, 0, false, st, err, &f)) return false;
+    } else {
+      if (!tc_conv(fc_, {x}, H, batch, y1_, c0, H, 1, 0, true, static_cast<int>(kFinalNormGroups), true, st, err))
+        return false;
+      tc_gn(Act{y1_, c0, H}, batch, static_cast<int>(kFinalNormGroups), 1, fn_g_, fn_b_, nullptr, nullptr, nullptr,
+            nullptr, z, nullptr, st);
+    }
   } else {
     if (!simt_conv(fc_, {x}, H, batch, p1_, st, err)) return false;
     simt_gn(fc_, p1_, batch, H, fn_g_, fn_b_, static_cast<int>(kFinalNormGroups), nullptr, nullptr, nullptr, nullptr,

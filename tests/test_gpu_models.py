@@ -222,3 +222,107 @@ def test_pusht_bf16_paths_match_reference_on_same_weights(tmp_path):
     print(f"PushT bf16 weights: streaming path max-abs {err_small:.3g}, tensor path max-abs {err_big:.3g}")
     assert err_small <= 1e-3
     assert err_big <= 2e-2
+
+
+def _round_bf16(tensors):
+    return {k: (ck.bf16_bits_to_f32(ck.to_bf16_bits(v)) if v.ndim >= 2 and "embeddings" not in k
+                and not k.endswith("A_log") else v) for k, v in tensors.items()}
+
+
+def test_flow_c2_fp32_matches_reference_core(tmp_path):
+    """BASELINE config 2 (flow head 350 / 1024 x 3 / cond 512), fp32, batch 1:
+    Euler-10 and RK4-4 against the compiled reference core (bar 1e-3)."""
+    _needs_reference()
+    from oracle import reference
+
+    path = tmp_path / "flow_c2.safetensors"
+    ck.write_checkpoint(path, ck.flow_tensors(ck.FLOW_C2, seed=2))
+    rng = np.random.default_rng(2)
+    cond = rng.standard_normal(512).astype(np.float32)
+    x0 = rng.standard_normal(350).astype(np.float32)
+    ref = reference.ReferenceEngine(path, threads=8)
+    e = Engine(path, threads=0, device=0, precision="fp32")
+    for solver, steps in (("euler", 10), ("rk4", 4), ("heun", 5)):
+        expected = ref.sample_condition(cond, x0, steps, solver)
+        got = e.sample_condition(cond, x0, steps=steps, method=solver)
+        err = float(np.abs(got - expected).max())
+        print(f"C2 flow fp32 {solver}-{steps} max-abs vs reference: {err:.3g}")
+        assert err <= 1e-3
+    ref.close()
+    e.close()
+
+
+def test_flow_c2_bf16_batched_tensor_path(tmp_path):
+    """C2 at batch 256 in bf16 mode (tcgen05 GEMMs, fp16 operands) against the
+    restatement on the same bf16-rounded weights (bar 2e-2)."""
+    tensors = _round_bf16(ck.flow_tensors(ck.FLOW_C2, seed=3))
+    path = tmp_path / "flow_c2_bf16w.safetensors"
+    ck.write_checkpoint(path, tensors)
+    rng = np.random.default_rng(3)
+    cond = rng.standard_normal((256, 512)).astype(np.float32)
+    x0 = rng.standard_normal((256, 350)).astype(np.float32)
+    flow = restate.FlowModel(tensors)
+    e = Engine(path, threads=0, device=0, precision="bf16", max_batch=256)
+    for solver, steps in (("euler", 10), ("rk4", 4)):
+        got = e.sample_condition_batch(cond, x0, steps=steps, method=solver)
+        expected = flow.sample(cond, x0, steps, solver)
+        err = float(np.abs(got - expected).max())
+        print(f"C2 flow bf16 batch-256 {solver}-{steps} max-abs vs restatement: {err:.3g}")
+        assert err <= 2e-2
+    # the small-batch (weight-streaming) path on the same engine
+    got1 = e.sample_condition(cond[0], x0[0], steps=10, method="euler")
+    assert np.abs(got1 - flow.sample(cond[:1], x0[:1], 10, "euler")[0]).max() <= 1e-3
+    e.close()
+
+
+def _mamba_flow_c3(seed):
+    t = ck.mamba_tensors(ck.MAMBA_C3, seed=seed)
+    t.update(ck.flow_tensors(ck.FLOW_C2, seed=seed + 1))
+    return t
+
+
+def test_mamba_c3_fp32_matches_reference_core(tmp_path):
+    """BASELINE config 3 (Mamba 8 x 512, di 1024, ds 16, L = 128) feeding the
+    C2 flow head, fp32 batch 1, against the compiled reference core."""
+    _needs_reference()
+    from oracle import reference
+
+    path = tmp_path / "mamba_c3.safetensors"
+    ck.write_checkpoint(path, _mamba_flow_c3(4))
+    tokens = np.arange(128, dtype=np.int32)
+    rng = np.random.default_rng(4)
+    x0 = rng.standard_normal(350).astype(np.float32)
+    ref = reference.ReferenceEngine(path, threads=8)
+    e = Engine(path, threads=0, device=0, precision="fp32")
+    hidden = e.run(tokens)
+    expected = ref.run(tokens, 512)
+    err_h = float(np.abs(hidden - expected).max())
+    act = e.sample(tokens, x0, 10, "euler")
+    err_a = float(np.abs(act - ref.sample(tokens, x0, 10, "euler")).max())
+    print(f"C3 Mamba fp32 hidden max-abs {err_h:.3g}, Mamba->flow Euler-10 action max-abs {err_a:.3g}")
+    assert err_h <= 1e-3 and err_a <= 1e-3
+    ref.close()
+    e.close()
+
+
+def test_mamba_c3_bf16_batched_tensor_path(tmp_path):
+    """C3 at batch 4 x 128 tokens in bf16 mode (tcgen05 projections) against the
+    restatement on the same bf16-rounded weights."""
+    tensors = _round_bf16(_mamba_flow_c3(5))
+    path = tmp_path / "mamba_c3_bf16w.safetensors"
+    ck.write_checkpoint(path, tensors)
+    rng = np.random.default_rng(5)
+    tokens = rng.integers(0, 128, size=(4, 128)).astype(np.int32)
+    model = restate.MambaModel(tensors)
+    e = Engine(path, threads=0, device=0, precision="bf16", max_batch=4)
+    hidden = e.run_batch(tokens)
+    expected = np.stack([model.run(tokens[i]) for i in range(4)])
+    err = float(np.abs(hidden - expected).max())
+    print(f"C3 Mamba bf16 batch-4 hidden max-abs vs restatement: {err:.3g}")
+    assert err <= 2e-2
+    x0 = rng.standard_normal((4, 350)).astype(np.float32)
+    act = e.sample_batch(tokens, x0, 10, "euler")
+    flow = restate.FlowModel(tensors)
+    expected_act = np.stack([flow.sample(expected[i, -1], x0[i], 10, "euler") for i in range(4)])
+    assert np.abs(act - expected_act).max() <= 2e-2
+    e.close()
