@@ -310,6 +310,8 @@ def run_ours(args):
                          "conv_share_of_forward": prof["conv_ms"] / prof["forward_ms"],
                          "conv_launches_per_forward": prof["conv_launches"]},
         }
+    if world == 1 and not args.no_extras:
+        line["extra"] = _extras(Path(args.workdir), local)
     if world == 1 and not args.no_cpu_baseline:
         threads = os.cpu_count() or 1
         cpu_value, secs = _reference_throughput(path, spec, threads, threads)
@@ -324,6 +326,86 @@ def run_ours(args):
     return 0
 
 
+def _latency(fn, iters):
+    import torch
+
+    for _ in range(3):
+        fn()
+    torch.cuda.synchronize()
+    times = []
+    for _ in range(iters):
+        t0 = time.perf_counter()
+        fn()
+        times.append((time.perf_counter() - t0) * 1000.0)
+    times.sort()
+    return {"p50_ms": times[len(times) // 2], "p99_ms": times[min(len(times) - 1, int(len(times) * 0.99))],
+            "iters": iters}
+
+
+def _extras(workdir: Path, device: int):
+    """The other BASELINE configurations, through the public host-buffer API
+    (synchronous calls: host->device inputs and device->host outputs included)."""
+    import torch
+
+    from flowedge_b200 import Engine
+
+    out = {}
+    rng = np.random.default_rng(7)
+    # C1: PushT U-Net, batch 1, DDIM-10 (fp32 weights; and the bf16-weight mode)
+    pusht = _checkpoint(workdir / "bench_c1_pusht.safetensors", ck.PUSHT, False)
+    cond = rng.standard_normal(132).astype(np.float32)
+    noise = rng.standard_normal((16, 2)).astype(np.float32)
+    for prec in ("fp32", "bf16"):
+        e = Engine(pusht, threads=0, device=device, precision=prec)
+        out[f"c1_pusht_b1_ddim10_{prec}"] = _latency(lambda: e.sample_diffusion(cond, noise, 10), 200)
+        e.close()
+    # C2: flow head 350 / 1024 x 3 / 512, Euler-10 and RK4-4
+    flow = workdir / "bench_c2_flow.safetensors"
+    if not flow.exists():
+        ck.write_checkpoint(flow, ck.flow_tensors(ck.FLOW_C2, seed=SEED))
+    c = rng.standard_normal(512).astype(np.float32)
+    x0 = rng.standard_normal(350).astype(np.float32)
+    for prec in ("fp32", "bf16"):
+        e = Engine(flow, threads=0, device=device, precision=prec, max_batch=4096)
+        out[f"c2_flow_b1_euler10_{prec}"] = _latency(lambda: e.sample_condition(c, x0, steps=10, method="euler"), 200)
+        out[f"c2_flow_b1_rk4_4_{prec}"] = _latency(lambda: e.sample_condition(c, x0, steps=4, method="rk4"), 200)
+        cb = torch.from_numpy(rng.standard_normal((4096, 512)).astype(np.float32)).cuda()
+        xb = torch.from_numpy(rng.standard_normal((4096, 350)).astype(np.float32)).cuda()
+        ob = torch.empty_like(xb)
+        st = torch.cuda.Stream()
+        run = lambda: e.sample_condition_device(cb.data_ptr(), xb.data_ptr(), 4096, ob.data_ptr(), 10, "euler",
+                                                st.cuda_stream)
+        for _ in range(3):
+            run()
+        st.synchronize()
+        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        ev0.record(st)
+        for _ in range(5):
+            run()
+        ev1.record(st)
+        st.synchronize()
+        out[f"c2_flow_b4096_euler10_{prec}_actions_per_s"] = 4096 * 5 / (ev0.elapsed_time(ev1) / 1000.0)
+        e.close()
+    # C3: Mamba 8 x 512 (L = 128) -> C2 flow head
+    mamba = workdir / "bench_c3_mamba_flow.safetensors"
+    if not mamba.exists():
+        t = ck.mamba_tensors(ck.MAMBA_C3, seed=SEED)
+        t.update(ck.flow_tensors(ck.FLOW_C2, seed=SEED + 1))
+        ck.write_checkpoint(mamba, t)
+    tokens = np.arange(128, dtype=np.int32)
+    for prec in ("fp32", "bf16"):
+        e = Engine(mamba, threads=0, device=device, precision=prec, max_batch=1024)
+        out[f"c3_mamba_b1_prefill128_{prec}"] = _latency(lambda: e.run(tokens), 100)
+        out[f"c3_mamba_flow_b1_sample_euler10_{prec}"] = _latency(lambda: e.sample(tokens, x0, 10, "euler"), 100)
+        tb = np.ascontiguousarray(np.tile(tokens, (1024, 1)))
+        e.run_batch(tb[:2])
+        t0 = time.perf_counter()
+        e.run_batch(tb)
+        out[f"c3_mamba_b1024_prefill128_{prec}_seq_per_s"] = 1024 / (time.perf_counter() - t0)
+        e.close()
+    return out
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
@@ -332,6 +414,7 @@ def main():
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--workdir", default=os.environ.get("FLOWEDGE_BENCH_DIR", "/tmp/flowedge_bench"))
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-extras", action="store_true", help="skip the C1/C2/C3 latency and throughput extras")
     args = ap.parse_args()
     Path(args.workdir).mkdir(parents=True, exist_ok=True)
     if args.impl == "reference":
