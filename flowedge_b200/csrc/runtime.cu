@@ -245,19 +245,31 @@ cudaError_t tc_gemm(const TcLaunch& l, DeviceContext& ctx, cudaStream_t stream, 
       return cudaErrorInvalidValue;
     }
   }
+  // Output row of token (b, t) is b * rps + t * tmul + tadd; the epilogue
+  // needs it affine in the global token b * L + t, i.e. rps == L * tmul.
+  const long long cs = static_cast<long long>(l.out_tmul) * l.out_ld;
+  const long long acs = static_cast<long long>(l.out_tmul) * l.add_ld;
+  if (l.out_rps != l.L * l.out_tmul || l.out_tmul < 1 || l.out_tadd < 0 || l.out_tadd >= l.out_tmul ||
+      cs * tc::BN >= (1LL << 31) || acs * tc::BN >= (1LL << 31)) {
+    err = "tc_gemm: unsupported output row mapping";
+    return cudaErrorInvalidValue;
+  }
+  if (l.stats != nullptr && (l.act != tc::kActNone || l.add_tok != nullptr)) {
+    err = "tc_gemm: GroupNorm statistics need a linear epilogue";
+    return cudaErrorInvalidValue;
+  }
   p.bias = l.bias;
   p.add_vec = l.add_vec;
   p.add_tok = l.add_tok;
-  p.add_ld = l.add_ld;
+  p.add_cs = static_cast<int>(acs);
+  p.add_base = static_cast<long long>(l.out_tadd) * l.add_ld;
   p.act = l.act;
   p.out_f32 = l.out_f32 ? 1 : 0;
   p.out_accumulate = l.out_accumulate ? 1 : 0;
   p.out = l.out;
-  p.out_ld = l.out_ld;
-  p.out_rps = l.out_rps;
-  p.out_tmul = l.out_tmul;
-  p.out_tadd = l.out_tadd;
-  p.out_ch_off = l.out_ch_off;
+  p.out_cs = static_cast<int>(cs);
+  p.out_base = static_cast<long long>(l.out_tadd) * l.out_ld + l.out_ch_off;
+  p.n_tokens = l.n_samples * l.L;
   p.stats = l.stats;
   p.group_ch = l.group_ch;
   p.groups = l.groups;
@@ -265,7 +277,8 @@ cudaError_t tc_gemm(const TcLaunch& l, DeviceContext& ctx, cudaStream_t stream, 
   p.err = ctx.d_err;
   if (l.gn_fuse) {
     if (l.stats != nullptr || l.out_f32 || l.group_ch < 32 || l.group_ch > tc::BM || tc::BM % l.group_ch != 0 ||
-        tc::BM / l.group_ch > tc::MAX_TILE_GROUPS || p.tile_samples > tc::MAX_TILE_SAMPLES || l.gamma == nullptr ||
+        tc::BM / l.group_ch > tc::MAX_TILE_GROUPS || p.tile_samples > tc::MAX_TILE_SAMPLES || l.L < 8 ||
+        l.gamma == nullptr ||
         l.beta == nullptr || l.act != tc::kActNone || l.add_tok != nullptr || !l.fp16) {
       err = "tc_gemm: unsupported fused GroupNorm geometry";
       return cudaErrorInvalidValue;

@@ -16,9 +16,9 @@
 // accumulators double-buffered in TMEM (2 x 256 columns).  Warp roles:
 //   warp 0: TMA producer (one lane)
 //   warp 1: TMEM allocator + MMA issuer (one lane)
-//   warps 2-9: epilogue (TMEM -> registers -> global), one accumulator row
-//              (= one output channel) per thread; two warps per TMEM lane
-//              quadrant, each taking half of the tile's 256 columns.
+//   warps 2..: epilogue (TMEM -> registers -> global), one accumulator row
+//              (= one output channel) per thread; EPI_PARTS warps per TMEM
+//              lane quadrant, each taking EPI_COLS of the tile's 256 columns.
 // Every mbarrier wait is bounded; a timeout sets an error code, raises a
 // shared abort flag, drains in-flight copies/MMAs with bounded waits, frees
 // TMEM and returns.
@@ -40,11 +40,14 @@ constexpr int MAX_SEGS = 12;
 constexpr int MAX_TILE_SAMPLES = 64;  // samples per N tile when GN statistics are gathered
 constexpr int EPI_WARPS = 8;
 constexpr int EPI_THREADS = EPI_WARPS * 32;
+constexpr int EPI_PARTS = EPI_WARPS / 4;    // epilogue warps per TMEM lane quadrant
+constexpr int EPI_COLS = BN / EPI_PARTS;    // tile columns per epilogue warp
 constexpr int THREADS = 64 + EPI_THREADS;
 constexpr int TMEM_COLS = 512;
 constexpr int MAX_TILE_GROUPS = 4;   // groups of >= 32 channels inside a 128-row tile
-constexpr int SMEM_BYTES =
-    1024 + STAGES * STAGE_BYTES + 256 + 4 * MAX_TILE_SAMPLES * 16 + MAX_TILE_SAMPLES * MAX_TILE_GROUPS * 8;
+constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + 256 + 4 * EPI_PARTS * MAX_TILE_SAMPLES * 16 +
+                           MAX_TILE_SAMPLES * MAX_TILE_GROUPS * 8;
+static_assert(SMEM_BYTES <= 232448, "shared memory above the 227 KB per-CTA limit");
 
 enum Act : int { kActNone = 0, kActSilu = 1, kActSoftplus = 2 };
 
@@ -68,17 +71,17 @@ struct Params {
   // epilogue
   const float* bias;      // [m] or null
   const float* add_vec;   // [m] or null
-  const float* add_tok;   // [row][add_ld] fp32 or null (indexed like the output row)
-  int add_ld;
+  const float* add_tok;   // fp32 or null: element add_base + token * add_cs + m
+  long long add_base;
+  int add_cs;
   int act;
   int fp16;               // operand format (and 16-bit output format): 1 fp16, 0 bf16
   int out_f32;            // 1: fp32 output, 0: 16-bit
   int out_accumulate;     // fp32 output only: out += value
-  void* out;
-  long long out_ld;       // elements per output row
-  int out_rps;            // output rows per sample
-  int out_tmul, out_tadd; // output row within sample = t * tmul + tadd
-  int out_ch_off;
+  void* out;              // element out_base + token * out_cs + m, token = sample * L + t
+  long long out_base;
+  int out_cs;
+  int n_tokens;           // n_samples * L
   // GroupNorm partial statistics (sum, sum of squares) per (sample, group, part)
   double* stats;          // null: no statistics
   int group_ch;           // channels per group (multiple of 32)
@@ -98,24 +101,6 @@ struct Params {
   float* out_twin;         // fp32 copy of z, or null
   int* err;
 };
-
-__device__ __forceinline__ long long out_row(const Params& p, int b, int t) {
-  return static_cast<long long>(b) * p.out_rps + t * p.out_tmul + p.out_tadd;
-}
-
-__device__ __forceinline__ void epilogue_store(const Params& p, int tok_b, int tok_t, int m, float v) {
-  const long long row = static_cast<long long>(tok_b) * p.out_rps + tok_t * p.out_tmul + p.out_tadd;
-  const long long idx = row * p.out_ld + p.out_ch_off + m;
-  if (p.out_f32) {
-    float* out = static_cast<float*>(p.out);
-    if (p.out_accumulate) v += out[idx];
-    out[idx] = v;
-  } else if (p.fp16) {
-    static_cast<__half*>(p.out)[idx] = __float2half_rn(fminf(fmaxf(v, -65504.0f), 65504.0f));
-  } else {
-    static_cast<__nv_bfloat16*>(p.out)[idx] = __float2bfloat16_rn(v);
-  }
-}
 
 // Epilogue modes (one kernel instantiation each, so each carries only its
 // own code):
@@ -263,16 +248,24 @@ static __global__ void __launch_bounds__(THREADS, 1)
       }
     }
   } else {
-    // ---------------- epilogue (warps 2..9) ----------------
+    // ---------------- epilogue (warps 2 .. 2 + EPI_WARPS - 1) ----------------
+    // Thread (quadrant q, lane) owns accumulator row q*32 + lane (one output
+    // channel) and COLS consecutive tile columns (tokens).  A tile covers BN
+    // consecutive global tokens, and output rows are affine in the global
+    // token, so column c of this warp lives at element o0 + c * out_cs.  Each
+    // TMEM load brings CH columns; all per-element work is branch-free and
+    // the only branches are per chunk and uniform across the warp.
     constexpr bool kStats = MODE != kEpiPlain;
-    const int q = warp & 3;                // TMEM lane quadrant this warp may access
-    const int half = (warp - 2) >> 2;      // which 128 columns of the tile
+    constexpr int CH = 16;
+    const int q = warp & 3;                    // TMEM lane quadrant this warp may access
+    const int part = (warp - 2) >> 2;          // which COLS-wide slice of the tile's columns
     const int row = q * 32 + lane;
-    float2* stat = reinterpret_cast<float2*>(red + 4 * MAX_TILE_SAMPLES);  // [sample][group] (mean, inv)
-    uint32_t acc_iter = 0;
-    const int lmask = p.L - 1;
+    const int col0 = part * EPI_COLS;
+    float2* stat = reinterpret_cast<float2*>(red + 4 * EPI_PARTS * MAX_TILE_SAMPLES);  // [sample][group] (mean, inv)
     const uint32_t lane_base = static_cast<uint32_t>(q * 32) << 16;
-    const int col0 = half * (BN / 2);
+    const int lmask = p.L - 1;
+    const int cs = p.out_cs;
+    uint32_t acc_iter = 0;
     for (int tile = blockIdx.x; tile < p.total_tiles; tile += gridDim.x, ++acc_iter) {
       const int m_blk = tile % p.n_tiles_m;
       const int n_blk = tile / p.n_tiles_m;
@@ -286,44 +279,86 @@ static __global__ void __launch_bounds__(THREADS, 1)
       tc_fence_after();
       const int m = m_blk * BM + row;
       const bool m_ok = m < p.m_valid;
-      const float bias = (p.bias != nullptr && m_ok) ? p.bias[m] : 0.0f;
-      const float addv = (p.add_vec != nullptr && m_ok) ? p.add_vec[m] : 0.0f;
+      const int mm = m_ok ? m : 0;  // in-range index for per-channel loads
+      const float bb = m_ok ? ((p.bias != nullptr ? p.bias[m] : 0.0f) + (p.add_vec != nullptr ? p.add_vec[m] : 0.0f))
+                            : 0.0f;
+      const int tok0 = n_blk * BN + col0;  // global token of this warp's first column
+      // columns [0, lim) of this warp are stored (0 for padding rows)
+      const int lim = m_ok ? min(max(p.n_tokens - tok0, 0), EPI_COLS) : 0;
+      const long long o0 = static_cast<long long>(tok0) * cs + p.out_base + m;
       const int sample0 = n_blk * p.tile_samples;
-      const uint32_t tbase = tmem_base + lane_base + acc * BN;
-      // pass 1: bias / activation / store (plain and stats modes) and statistics
+      const uint32_t tbase = tmem_base + lane_base + acc * BN + col0;
+
+      // pass 1: GroupNorm partial sums (stats / fused) and the plain store
       float s1 = 0.0f, s2 = 0.0f;
 #pragma unroll 1
-      for (int c8 = 0; c8 < BN / 2; c8 += 8) {
-        float v[8];
-        tmem_ld8(tbase + col0 + c8, v);
+      for (int c = 0; c < EPI_COLS; c += CH) {
+        float v[CH];
+        tmem_ld16(tbase + c, v);
+        if constexpr (kStats) {
+          // sums of v per row; the bias is folded in once per run of columns
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          const int n = col0 + c8 + j;
-          const int ls = n >> p.L_shift;
-          const int t = n & lmask;
-          const int b = sample0 + ls;
-          float y = v[j] + bias + addv;
-          if constexpr (MODE != kEpiFused) {
-            if (p.add_tok != nullptr && m_ok && b < p.n_samples)
-              y += p.add_tok[out_row(p, b, t) * p.add_ld + m];
-            if (p.act == kActSilu) y = silu_f(y);
-            else if (p.act == kActSoftplus) y = softplus_f(y);
-            if (m_ok && b < p.n_samples) epilogue_store(p, b, t, m, y);
-          }
-          if constexpr (kStats) {
-            s1 += y;
-            s2 += y * y;
-            if (t == lmask) {
-              double d1 = s1, d2 = s2;
+          for (int j = 0; j < CH; ++j) {
+            s1 += v[j];
+            s2 = fmaf(v[j], v[j], s2);
+            if ((j & 3) == 3) {  // samples span >= 4 columns, so runs end only here
+              const int col = col0 + c + j;
+              if (((col + 1) & lmask) == 0 || col + 1 == col0 + EPI_COLS) {
+                const double n = static_cast<double>(min(p.L, EPI_COLS));
+                const double db = bb;
+                double d1 = static_cast<double>(s1) + n * db;
+                double d2 = static_cast<double>(s2) + 2.0 * db * static_cast<double>(s1) + n * db * db;
 #pragma unroll
-              for (int off = 16; off > 0; off >>= 1) {
-                d1 += __shfl_xor_sync(0xffffffffu, d1, off);
-                d2 += __shfl_xor_sync(0xffffffffu, d2, off);
+                for (int off = 16; off > 0; off >>= 1) {
+                  d1 += __shfl_xor_sync(0xffffffffu, d1, off);
+                  d2 += __shfl_xor_sync(0xffffffffu, d2, off);
+                }
+                if (lane == 0) red[(q * EPI_PARTS + part) * MAX_TILE_SAMPLES + (col >> p.L_shift)] = make_double2(d1, d2);
+                s1 = 0.0f;
+                s2 = 0.0f;
               }
-              if (lane == 0) red[q * MAX_TILE_SAMPLES + ls] = make_double2(d1, d2);
-              s1 = 0.0f;
-              s2 = 0.0f;
             }
+          }
+        }
+        if constexpr (MODE != kEpiFused) {
+          float y[CH];
+#pragma unroll
+          for (int j = 0; j < CH; ++j) y[j] = v[j] + bb;
+          if (p.add_tok != nullptr) {
+            const float* a = p.add_tok + (static_cast<long long>(tok0 + c) * p.add_cs + p.add_base + mm);
+#pragma unroll
+            for (int j = 0; j < CH; ++j)
+              if (c + j < lim) y[j] += a[j * p.add_cs];
+          }
+          if (p.act == kActSilu) {
+#pragma unroll
+            for (int j = 0; j < CH; ++j) y[j] = silu_f(y[j]);
+          } else if (p.act == kActSoftplus) {
+#pragma unroll
+            for (int j = 0; j < CH; ++j) y[j] = softplus_f(y[j]);
+          }
+          const long long oc = o0 + static_cast<long long>(c) * cs;
+          if (p.out_f32) {
+            float* o = static_cast<float*>(p.out) + oc;
+            if (p.out_accumulate) {
+#pragma unroll
+              for (int j = 0; j < CH; ++j)
+                if (c + j < lim) o[j * cs] += y[j];
+            } else {
+#pragma unroll
+              for (int j = 0; j < CH; ++j)
+                if (c + j < lim) o[j * cs] = y[j];
+            }
+          } else if (p.fp16) {
+            __half* o = static_cast<__half*>(p.out) + oc;
+#pragma unroll
+            for (int j = 0; j < CH; ++j)
+              if (c + j < lim) o[j * cs] = to_half_sat(y[j]);
+          } else {
+            __nv_bfloat16* o = static_cast<__nv_bfloat16*>(p.out) + oc;
+#pragma unroll
+            for (int j = 0; j < CH; ++j)
+              if (c + j < lim) o[j * cs] = __float2bfloat16_rn(y[j]);
           }
         }
       }
@@ -334,7 +369,8 @@ static __global__ void __launch_bounds__(THREADS, 1)
       }
       if constexpr (kStats) {
         named_barrier(1, EPI_THREADS);
-        // combine the 4 quadrants' partials into (sample, group) sums
+        // combine the partials of the quadrants (and column slices) of each
+        // (sample, group) of the tile
         const int tid = threadIdx.x - 64;
         const int warps_per_group = p.group_ch >= BM ? 4 : p.group_ch / 32;
         const int groups_in_tile = BM / (warps_per_group * 32);
@@ -343,12 +379,15 @@ static __global__ void __launch_bounds__(THREADS, 1)
           const int ls = it / groups_in_tile;
           const int gl = it - ls * groups_in_tile;
           const int b = sample0 + ls;
+          const int p_lo = (ls * p.L) / EPI_COLS;
+          const int p_hi = ((ls + 1) * p.L - 1) / EPI_COLS;
           double d1 = 0.0, d2 = 0.0;
-          for (int w = 0; w < warps_per_group; ++w) {
-            const double2 r = red[(gl * warps_per_group + w) * MAX_TILE_SAMPLES + ls];
-            d1 += r.x;
-            d2 += r.y;
-          }
+          for (int w = 0; w < warps_per_group; ++w)
+            for (int pp = p_lo; pp <= p_hi; ++pp) {
+              const double2 r = red[((gl * warps_per_group + w) * EPI_PARTS + pp) * MAX_TILE_SAMPLES + ls];
+              d1 += r.x;
+              d2 += r.y;
+            }
           if constexpr (MODE == kEpiFused) {
             // biased variance E[y^2] - E[y]^2 clamped at 0, eps 1e-5, in double
             const double cnt = static_cast<double>(p.group_ch) * p.L;
@@ -360,8 +399,8 @@ static __global__ void __launch_bounds__(THREADS, 1)
             if (b < p.n_samples) {
               const int row0 = m_blk * BM + gl * warps_per_group * 32;
               const int g = row0 / p.group_ch;
-              const int part = (row0 % p.group_ch) / BM;
-              double* dst = p.stats + (((static_cast<long long>(b) * p.groups + g) * p.parts + part) * 2);
+              const int gpart = (row0 % p.group_ch) / BM;
+              double* dst = p.stats + (((static_cast<long long>(b) * p.groups + g) * p.parts + gpart) * 2);
               dst[0] = d1;
               dst[1] = d2;
             }
@@ -370,65 +409,61 @@ static __global__ void __launch_bounds__(THREADS, 1)
         named_barrier(1, EPI_THREADS);
       }
       if constexpr (MODE == kEpiFused) {
-        // pass 2: z = mish((y - mean) * inv * gamma + beta), FiLM or + residual
+        // pass 2: z = mish((y - mean) * inv * gamma + beta), then FiLM or + residual.
+        // Samples span >= 8 columns, so each 8-column half chunk has one sample.
         const int gl = row / p.group_ch;
         const float gam = m_ok ? p.gamma[m] : 0.0f;
         const float bet = m_ok ? p.beta[m] : 0.0f;
         const bool film = p.film_cond != nullptr;
-        const float ft_s = (film && m_ok) ? p.film_time[p.film_off + m] : 0.0f;
-        const float ft_h = (film && m_ok) ? p.film_time[p.film_off + p.film_C + m] : 0.0f;
-        float fs = 1.0f, fh = 0.0f, mean = 0.0f, scale = 0.0f;
-        int cur_b = -1;
-        __half* out16 = static_cast<__half*>(p.out);
-        const bool has_res = p.res_f32 != nullptr || p.res16 != nullptr;
+        const float ft_s = film ? p.film_time[p.film_off + mm] : 0.0f;
+        const float ft_h = film ? p.film_time[p.film_off + p.film_C + mm] : 0.0f;
+        const float* rf = p.res_f32 != nullptr ? p.res_f32 + o0 : nullptr;
+        const __half* rh = (rf == nullptr && p.res16 != nullptr) ? static_cast<const __half*>(p.res16) + o0 : nullptr;
+        __half* o16 = static_cast<__half*>(p.out) + o0;
+        float* tw = p.out_twin != nullptr ? p.out_twin + o0 : nullptr;
 #pragma unroll 1
-        for (int c32 = 0; c32 < BN / 2; c32 += 32) {
-          // issue the 32 residual loads of this slice before any math so they
-          // overlap (one load per column, coalesced across the warp's channels)
-          float r[32];
-          if (has_res) {
+        for (int c = 0; c < EPI_COLS; c += CH) {
+          // residual loads first, so they are in flight during the TMEM load and the math
+          float r[CH];
+          if (rf != nullptr) {
 #pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              const int n = col0 + c32 + j;
-              const int b = sample0 + (n >> p.L_shift);
-              r[j] = 0.0f;
-              if (m_ok && b < p.n_samples) {
-                const long long o = out_row(p, b, n & lmask) * p.out_ld + p.out_ch_off + m;
-                r[j] = p.res_f32 != nullptr ? p.res_f32[o]
-                                            : __half2float(static_cast<const __half*>(p.res16)[o]);
-              }
-            }
+            for (int j = 0; j < CH; ++j) r[j] = c + j < lim ? rf[static_cast<long long>(c + j) * cs] : 0.0f;
+          } else if (rh != nullptr) {
+#pragma unroll
+            for (int j = 0; j < CH; ++j)
+              r[j] = c + j < lim ? __half2float(rh[static_cast<long long>(c + j) * cs]) : 0.0f;
+          } else {
+#pragma unroll
+            for (int j = 0; j < CH; ++j) r[j] = 0.0f;
           }
+          float v[CH];
+          tmem_ld16(tbase + c, v);
+          float z[CH];
 #pragma unroll
-          for (int c8 = 0; c8 < 32; c8 += 8) {
-            float v[8];
-            tmem_ld8(tbase + col0 + c32 + c8, v);
-#pragma unroll
-            for (int j = 0; j < 8; ++j) {
-              const int n = col0 + c32 + c8 + j;
-              const int ls = n >> p.L_shift;
-              const int t = n & lmask;
-              const int b = sample0 + ls;
-              if (b != cur_b) {
-                cur_b = b;
-                const float2 st = stat[ls * MAX_TILE_GROUPS + gl];
-                mean = st.x;
-                scale = st.y * gam;
-                if (film && m_ok && b < p.n_samples) {
-                  const float* fc = p.film_cond + static_cast<long long>(b) * p.film_F + p.film_off;
-                  fs = fc[m] + ft_s;
-                  fh = fc[p.film_C + m] + ft_h;
-                }
-              }
-              if (m_ok && b < p.n_samples) {
-                float z = mish_fast((v[j] + bias - mean) * scale + bet);
-                if (film) z = fs * z + fh;
-                if (has_res) z += r[c8 + j];
-                const long long o = out_row(p, b, t) * p.out_ld + p.out_ch_off + m;
-                out16[o] = to_half_sat(z);
-                if (p.out_twin != nullptr) p.out_twin[o] = z;
-              }
+          for (int h = 0; h < CH / 8; ++h) {
+            const int ls = (col0 + c + 8 * h) >> p.L_shift;
+            const float2 st = stat[ls * MAX_TILE_GROUPS + gl];
+            const float sc = st.y * gam;
+            const float of = fmaf(bb - st.x, sc, bet);
+            float fs = 1.0f, fh = 0.0f;
+            if (film) {
+              const int b = min(sample0 + ls, p.n_samples - 1);
+              const float* fc = p.film_cond + (static_cast<long long>(b) * p.film_F + p.film_off + mm);
+              fs = fc[0] + ft_s;
+              fh = fc[p.film_C] + ft_h;
             }
+#pragma unroll
+            for (int j = 0; j < 8; ++j) z[8 * h + j] = fmaf(fs, mish_sel(fmaf(v[8 * h + j], sc, of)), fh) + r[8 * h + j];
+          }
+          __half* o = o16 + static_cast<long long>(c) * cs;
+#pragma unroll
+          for (int j = 0; j < CH; ++j)
+            if (c + j < lim) o[j * cs] = to_half_sat(z[j]);
+          if (tw != nullptr) {
+            float* t = tw + static_cast<long long>(c) * cs;
+#pragma unroll
+            for (int j = 0; j < CH; ++j)
+              if (c + j < lim) t[j * cs] = z[j];
           }
         }
         tc_fence_before();

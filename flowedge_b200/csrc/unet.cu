@@ -216,9 +216,11 @@ class Unet final : public UnetDevice {
   bool tc_conv(const ConvDev& c, const std::vector<Act>& srcs, int L_out, std::size_t batch, void* out,
                long long out_ld, int rps, int tmul, int tadd, bool stats, int groups, bool out_f32, cudaStream_t st,
                std::string& err, const Fuse* fuse = nullptr);
-  bool fusable(int channels, int groups) const {
+  // GroupNorm fits the conv epilogue: groups of 32..128 channels inside one
+  // 128-row tile, and samples of at least 8 tokens
+  bool fusable(int channels, int groups, int L) const {
     const int gc = channels / groups;
-    return gc >= 32 && gc <= 128 && 128 % gc == 0;
+    return gc >= 32 && gc <= 128 && 128 % gc == 0 && L >= 8;
   }
   void tc_gn(const Act& y, std::size_t batch, int groups, int parts, const float* gamma, const float* beta,
              const BlockDev* film_block, const float* film_time_row, const float* res_f32, const void* res_half,
@@ -956,7 +958,7 @@ bool Unet::block(const BlockDev& blk, const std::vector<Act>& in, int L, std::si
     }
     return true;
   }
-  if (fusable(oc, G)) {
+  if (fusable(oc, G, L)) {
     // GroupNorm + Mish + FiLM / residual in the conv epilogues
     Fuse f1;
     f1.gamma = blk.g1;
@@ -1073,7 +1075,7 @@ bool Unet::record_forward(std::size_t batch, bool tc, const float* ft_row, cudaS
   const int c0 = static_cast<int>(cfg_.dims[0]);
   Act z{at_sample(h1_, static_cast<std::size_t>(c0) * H), c0, H};
   if (tc) {
-    if (fusable(c0, static_cast<int>(kFinalNormGroups))) {
+    if (fusable(c0, static_cast<int>(kFinalNormGroups), H)) {
       Fuse f;
       f.gamma = fn_g_;
       f.beta = fn_b_;
