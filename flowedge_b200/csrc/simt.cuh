@@ -450,6 +450,42 @@ static __global__ void __launch_bounds__(256) out_update_kernel(const OutParams<
   }
 }
 
+// Scheduler update after the output 1x1 conv ran on the tensor cores.  The
+// conv's weights were split into fp16 high and low rows, so the conv wrote
+// 2A values per token: eps[a] = t[n][a] + t[n][A + a].  Elementwise over the
+// tokens' A values; writes x_master, the next input x_in (fp16, padded to Cin
+// channels) and optionally the raw epsilon.
+struct EpsUpdateParams {
+  const float* t;       // [n][2A]
+  int A, H, n_tokens;
+  float* x_master;      // [n][A]
+  float* eps_out;       // [n][A] or null
+  int update;           // 0: only write eps
+  StepScalars step;
+  const uint64_t* seeds;
+  __half* x_in;         // [n][Cin]
+  int Cin;
+};
+
+static __global__ void __launch_bounds__(256) eps_update_kernel(const EpsUpdateParams p) {
+  const long long total = static_cast<long long>(p.n_tokens) * p.A;
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const int n = static_cast<int>(i / p.A);
+    const int a = static_cast<int>(i - static_cast<long long>(n) * p.A);
+    const float* tr = p.t + static_cast<long long>(n) * 2 * p.A;
+    const float eps = tr[a] + tr[p.A + a];
+    if (p.eps_out != nullptr) p.eps_out[i] = eps;
+    if (!p.update) continue;
+    const int b = n / p.H;
+    const int t = n - b * p.H;
+    const float x = scheduler_update(p.step, p.x_master[i], eps, p.seeds != nullptr ? p.seeds[b] : 0,
+                                     static_cast<uint64_t>(t) * p.A + a, p.H * p.A);
+    p.x_master[i] = x;
+    p.x_in[static_cast<long long>(n) * p.Cin + a] = to_half_sat(x);
+  }
+}
+
 // noise [n][A] -> x_master [n][A] and x_in [n][Cin] (zero padded)
 static __global__ void prep_sample_kernel(const float* noise, int n_tokens, int A, float* x_master, void* x_in, int Cin,
                                    int x_in_half) {

@@ -38,7 +38,7 @@ constexpr int B_BYTES = BN * BK * 2;
 constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
 constexpr int MAX_SEGS = 12;
 constexpr int MAX_TILE_SAMPLES = 64;  // samples per N tile when GN statistics are gathered
-constexpr int EPI_WARPS = 8;
+constexpr int EPI_WARPS = 16;
 constexpr int EPI_THREADS = EPI_WARPS * 32;
 constexpr int EPI_PARTS = EPI_WARPS / 4;    // epilogue warps per TMEM lane quadrant
 constexpr int EPI_COLS = BN / EPI_PARTS;    // tile columns per epilogue warp
@@ -421,10 +421,20 @@ static __global__ void __launch_bounds__(THREADS, 1)
         const __half* rh = (rf == nullptr && p.res16 != nullptr) ? static_cast<const __half*>(p.res16) + o0 : nullptr;
         __half* o16 = static_cast<__half*>(p.out) + o0;
         float* tw = p.out_twin != nullptr ? p.out_twin + o0 : nullptr;
-#pragma unroll 1
-        for (int c = 0; c < EPI_COLS; c += CH) {
-          // residual loads first, so they are in flight during the TMEM load and the math
-          float r[CH];
+        // FiLM (scale, shift) of each 8-column half chunk and the residual run
+        // one chunk ahead of their use, so their latency overlaps the math
+        auto load_film = [&](int c, float2 (&f)[CH / 8]) {
+#pragma unroll
+          for (int h = 0; h < CH / 8; ++h) {
+            f[h] = make_float2(1.0f, 0.0f);
+            if (film) {
+              const int b = min(sample0 + ((col0 + c + 8 * h) >> p.L_shift), p.n_samples - 1);
+              const float* fc = p.film_cond + (static_cast<long long>(b) * p.film_F + p.film_off + mm);
+              f[h] = make_float2(fc[0] + ft_s, fc[p.film_C] + ft_h);
+            }
+          }
+        };
+        auto load_res = [&](int c, float (&r)[CH]) {
           if (rf != nullptr) {
 #pragma unroll
             for (int j = 0; j < CH; ++j) r[j] = c + j < lim ? rf[static_cast<long long>(c + j) * cs] : 0.0f;
@@ -436,6 +446,16 @@ static __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll
             for (int j = 0; j < CH; ++j) r[j] = 0.0f;
           }
+        };
+        float2 f_cur[CH / 8], f_nxt[CH / 8];
+        float r_cur[CH], r_nxt[CH];
+        load_film(0, f_cur);
+        load_res(0, r_cur);
+#pragma unroll 1
+        for (int c = 0; c < EPI_COLS; c += CH) {
+          const int cn = c + CH < EPI_COLS ? c + CH : c;  // the last chunk re-reads its own values
+          load_film(cn, f_nxt);
+          load_res(cn, r_nxt);
           float v[CH];
           tmem_ld16(tbase + c, v);
           float z[CH];
@@ -445,15 +465,9 @@ static __global__ void __launch_bounds__(THREADS, 1)
             const float2 st = stat[ls * MAX_TILE_GROUPS + gl];
             const float sc = st.y * gam;
             const float of = fmaf(bb - st.x, sc, bet);
-            float fs = 1.0f, fh = 0.0f;
-            if (film) {
-              const int b = min(sample0 + ls, p.n_samples - 1);
-              const float* fc = p.film_cond + (static_cast<long long>(b) * p.film_F + p.film_off + mm);
-              fs = fc[0] + ft_s;
-              fh = fc[p.film_C] + ft_h;
-            }
 #pragma unroll
-            for (int j = 0; j < 8; ++j) z[8 * h + j] = fmaf(fs, mish_sel(fmaf(v[8 * h + j], sc, of)), fh) + r[8 * h + j];
+            for (int j = 0; j < 8; ++j)
+              z[8 * h + j] = fmaf(f_cur[h].x, mish_sel(fmaf(v[8 * h + j], sc, of)), f_cur[h].y) + r_cur[8 * h + j];
           }
           __half* o = o16 + static_cast<long long>(c) * cs;
 #pragma unroll
@@ -465,6 +479,10 @@ static __global__ void __launch_bounds__(THREADS, 1)
             for (int j = 0; j < CH; ++j)
               if (c + j < lim) t[j * cs] = z[j];
           }
+#pragma unroll
+          for (int h = 0; h < CH / 8; ++h) f_cur[h] = f_nxt[h];
+#pragma unroll
+          for (int j = 0; j < CH; ++j) r_cur[j] = r_nxt[j];
         }
         tc_fence_before();
         mbar_arrive(&tempty[acc]);

@@ -259,6 +259,10 @@ class Unet final : public UnetDevice {
   std::vector<std::array<ConvDev, 2>> us_;
   ConvDev fc_;
   float *fn_g_ = nullptr, *fn_b_ = nullptr, *fo_w_ = nullptr, *fo_b_ = nullptr;
+  // output 1x1 conv for the tensor path: fp16 rows [hi(w) | lo(w)] padded to
+  // 128 rows, and the bias of the high rows
+  void* fo16_ = nullptr;
+  float* fo_b128_ = nullptr;
   std::vector<float> h_fn_g_, h_fn_b_, h_fo_w_, h_fo_b_;
   ConvDev film_;  // W_c of every block's FiLM, [F][cond_pad]
   float* film_time_ = nullptr;  // [T][F]
@@ -529,7 +533,7 @@ bool Unet::load(const TensorTable& t, std::string& err) {
     const std::size_t gc = d / cfg_.groups;
     if (d % 128 != 0 || gc % 32 != 0 || (gc < 128 && 128 % gc != 0) || (gc > 128 && gc % 128 != 0)) tc_ok_ = false;
   }
-  if ((cfg_.dims[0] / kFinalNormGroups) % 32 != 0 || cfg_.horizon > 256 ||
+  if ((cfg_.dims[0] / kFinalNormGroups) % 32 != 0 || cfg_.horizon > 256 || 2 * cfg_.action_dim > tc::BM ||
       (cfg_.horizon & (cfg_.horizon - 1)) != 0 || (cfg_.horizon >> (cfg_.stages - 1)) < 4)
     tc_ok_ = false;
 
@@ -556,6 +560,8 @@ bool Unet::load(const TensorTable& t, std::string& err) {
   plan_conv(fc_);
   plan_conv(film_);
   plan.add_n<float>(2 * c0 + A * c0 + A + 2 * A);
+  plan.add(static_cast<std::size_t>(tc::BM) * c0 * 2);
+  plan.add_n<float>(tc::BM);
   plan.add_n<float>(T * static_cast<std::size_t>(F_));
   plan.add_n<float>(te1w.size() + te1b.size() + te2w.size() + te2b.size() + wt_all.size());
   plan.add_n<float>(T + T * td);
@@ -605,6 +611,25 @@ bool Unet::load(const TensorTable& t, std::string& err) {
   fn_b_ = put(h_fn_b_);
   fo_w_ = put(h_fo_w_);
   fo_b_ = put(h_fo_b_);
+  if (tc_ok_) {
+    // w = hi + lo with hi = fp16(w), lo = fp16(w - hi): the pair carries the
+    // fp32 weight to about 2^-22 relative, and the tensor cores accumulate in fp32
+    std::vector<std::uint16_t> w16(static_cast<std::size_t>(tc::BM) * c0, 0);
+    std::vector<float> b128(tc::BM, 0.0f);
+    for (int a = 0; a < A; ++a) {
+      for (int c = 0; c < c0; ++c) {
+        const float w = h_fo_w_[static_cast<std::size_t>(a) * c0 + c];
+        const __half hi = __float2half_rn(w);
+        const __half lo = __float2half_rn(w - __half2float(hi));
+        w16[static_cast<std::size_t>(a) * c0 + c] = __half_as_ushort(hi);
+        w16[static_cast<std::size_t>(A + a) * c0 + c] = __half_as_ushort(lo);
+      }
+      b128[static_cast<std::size_t>(a)] = h_fo_b_[static_cast<std::size_t>(a)];
+    }
+    fo16_ = wts_.take(w16.size() * 2);
+    if (fo16_ != nullptr) cudaMemcpy(fo16_, w16.data(), w16.size() * 2, cudaMemcpyHostToDevice);
+    fo_b128_ = put(b128);
+  }
   amin_ = put(amin);
   amax_ = put(amax);
   film_time_ = wts_.take_n<float>(T * static_cast<std::size_t>(F_));
@@ -1149,13 +1174,36 @@ bool Unet::record_update(std::size_t nb, bool tc, const StepScalars* step, float
     p.Cin = cin_pad_;
   };
   if (tc) {
-    OutParams<__half> p{};
-    fill(p);
-    p.z = static_cast<const __half*>(h1_);
-    p.x_in = x_in_;
-    p.x_in_half = 1;
-    if (A <= 16) launch(out_update_kernel<__half, 16>, dim3(blocks), dim3(256), 0, st, p);
-    else launch(out_update_kernel<__half, 64>, dim3(blocks), dim3(256), 0, st, p);
+    // eps pairs [token][2A] on the tensor cores, then the elementwise update
+    TcLaunch l;
+    l.fp16 = true;
+    l.A = fo16_;
+    l.M_rows = tc::BM;
+    l.K = c0;
+    l.src[0] = TcSource{h1_, c0, H, static_cast<int>(cap_tc_)};
+    l.L = H;
+    l.n_samples = static_cast<int>(nb);
+    l.m_valid = 2 * A;
+    l.segs = {tc::Seg{0, 0, 0, c0 / 64, 0}};
+    l.bias = fo_b128_;
+    l.out = yr_;
+    l.out_ld = 2 * A;
+    l.out_rps = H;
+    l.out_f32 = true;
+    std::string err;
+    ++recorded_;
+    if (tc_gemm(l, *ctx_, st, err) != cudaSuccess) return false;
+    EpsUpdateParams p{};
+    p.t = static_cast<const float*>(yr_);
+    p.A = A, p.H = H, p.n_tokens = n_tokens;
+    p.x_master = x_master_ + xa;
+    p.eps_out = eps_out != nullptr ? eps_out + xa : nullptr;
+    p.update = step != nullptr ? 1 : 0;
+    if (step != nullptr) p.step = *step;
+    p.seeds = seeds_ + b0_;
+    p.x_in = static_cast<__half*>(x_in_);
+    p.Cin = cin_pad_;
+    launch(eps_update_kernel, dim3(ew_grid(static_cast<long long>(n_tokens) * A, 256, *ctx_)), dim3(256), 0, st, p);
   } else {
     OutParams<float> p{};
     fill(p);
