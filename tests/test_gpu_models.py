@@ -224,6 +224,34 @@ def test_pusht_bf16_paths_match_reference_on_same_weights(tmp_path):
     assert err_big <= 2e-2
 
 
+def test_bimanual_c4_bf16_tensor_path_matches_reference_on_same_weights(tmp_path):
+    """BASELINE config 4 (the bench's bimanual U-Net: A14, H64, dims
+    512/1024/2048, 8 groups) in bf16 mode, on bf16-representable weights,
+    against the reference core on the same weights: DDIM-10 actions within
+    max-abs 2e-2.  Batch 8 x horizon 64 takes the tensor path, where every
+    GroupNorm is applied in the conv epilogues: groups of 64 and 128 channels
+    in 128-row tiles, the 256-channel groups of the 2048-channel stage in
+    256-row tiles."""
+    _needs_reference()
+    from oracle import reference
+
+    tensors, meta = ck.diffusion_tensors(ck.BIMANUAL, seed=3)
+    path = tmp_path / "bimanual_bf16w.safetensors"
+    ck.write_checkpoint(path, _round_bf16(tensors), metadata=meta)
+    rng = np.random.default_rng(4)
+    cond = rng.standard_normal((8, 284)).astype(np.float32)
+    noise = rng.standard_normal((8, 64, 14)).astype(np.float32)
+    ref = reference.ReferenceEngine(path, threads=8)
+    expected = np.stack([ref.sample_diffusion(cond[i], noise[i], 10) for i in range(8)])
+    ref.close()
+    e = Engine(path, threads=0, device=0, precision="bf16", max_batch=8)
+    got = e.sample_diffusion_batch(cond, noise, 10)
+    e.close()
+    err = float(np.abs(got - expected).max())
+    print(f"C4 bimanual bf16 tensor path DDIM-10 max-abs vs reference: {err:.3g}")
+    assert err <= 2e-2
+
+
 def _round_bf16(tensors):
     return {k: (ck.bf16_bits_to_f32(ck.to_bf16_bits(v)) if v.ndim >= 2 and "embeddings" not in k
                 and not k.endswith("A_log") else v) for k, v in tensors.items()}
