@@ -130,6 +130,28 @@ std::shared_ptr<DeviceContext> make_device_context(int device, std::string& err)
     err = "cannot enable the tensor-core kernel's shared memory";
     return nullptr;
   }
+  // 2-CTA clusters for GroupNorm groups that span two 128-row tiles: launch
+  // only as many clusters as can be resident at once (the kernel is persistent)
+  {
+    cudaLaunchAttribute attr{};
+    attr.id = cudaLaunchAttributeClusterDimension;
+    attr.val.clusterDim.x = 2;
+    attr.val.clusterDim.y = 1;
+    attr.val.clusterDim.z = 1;
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(static_cast<unsigned>(ctx->sm_count & ~1));
+    cfg.blockDim = dim3(tc::THREADS);
+    cfg.dynamicSmemBytes = tc::SMEM_BYTES;
+    cfg.attrs = &attr;
+    cfg.numAttrs = 1;
+    int clusters = 0;
+    if (cudaFuncSetAttribute(tc::tc_gemm_kernel<tc::kEpiFused, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             tc::SMEM_BYTES) == cudaSuccess &&
+        cudaOccupancyMaxActiveClusters(&clusters, tc::tc_gemm_kernel<tc::kEpiFused, true>, &cfg) == cudaSuccess)
+      ctx->pair_clusters = clusters;
+    else
+      cudaGetLastError();
+  }
   return ctx;
 }
 
@@ -276,8 +298,10 @@ cudaError_t tc_gemm(const TcLaunch& l, DeviceContext& ctx, cudaStream_t stream, 
   p.parts = l.group_ch > tc::BM ? l.group_ch / tc::BM : 1;
   p.err = ctx.d_err;
   if (l.gn_fuse) {
-    if (l.stats != nullptr || l.out_f32 || l.group_ch < 32 || l.group_ch > tc::BM || tc::BM % l.group_ch != 0 ||
-        tc::BM / l.group_ch > tc::MAX_TILE_GROUPS || p.tile_samples > tc::MAX_TILE_SAMPLES || l.L < 8 ||
+    const bool in_tile = l.group_ch >= 32 && l.group_ch <= tc::BM && tc::BM % l.group_ch == 0 &&
+                         tc::BM / l.group_ch <= tc::MAX_TILE_GROUPS;
+    const bool paired = l.group_ch == 2 * tc::BM && p.n_tiles_m % 2 == 0 && ctx.pair_clusters > 0;
+    if (l.stats != nullptr || l.out_f32 || !(in_tile || paired) || p.tile_samples > tc::MAX_TILE_SAMPLES || l.L < 8 ||
         l.gamma == nullptr ||
         l.beta == nullptr || l.act != tc::kActNone || l.add_tok != nullptr || !l.fp16) {
       err = "tc_gemm: unsupported fused GroupNorm geometry";
@@ -305,6 +329,24 @@ cudaError_t tc_gemm(const TcLaunch& l, DeviceContext& ctx, cudaStream_t stream, 
     const TcSource& s = l.src[i].ptr != nullptr ? l.src[i] : l.src[0];
     if (!encode_3d(&tb[i], s, static_cast<std::uint32_t>(l.L), static_cast<std::uint32_t>(p.tile_samples), dtype, err))
       return cudaErrorInvalidValue;
+  }
+  if (p.gn_fuse && l.group_ch == 2 * tc::BM) {
+    cudaLaunchAttribute attr{};
+    attr.id = cudaLaunchAttributeClusterDimension;
+    attr.val.clusterDim.x = 2;
+    attr.val.clusterDim.y = 1;
+    attr.val.clusterDim.z = 1;
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(static_cast<unsigned>(2 * std::min(p.total_tiles / 2, ctx.pair_clusters)));
+    cfg.blockDim = dim3(tc::THREADS);
+    cfg.dynamicSmemBytes = tc::SMEM_BYTES;
+    cfg.stream = stream;
+    cfg.attrs = &attr;
+    cfg.numAttrs = 1;
+    const cudaError_t rc =
+        cudaLaunchKernelEx(&cfg, tc::tc_gemm_kernel<tc::kEpiFused, true>, ta, tb[0], tb[1], tb[2], p);
+    if (rc != cudaSuccess) err = std::string("tc_gemm cluster launch: ") + cudaGetErrorString(rc);
+    return rc;
   }
   const int grid = p.total_tiles < ctx.sm_count ? p.total_tiles : ctx.sm_count;
   if (p.gn_fuse)

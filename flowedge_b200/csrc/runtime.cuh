@@ -20,6 +20,7 @@ struct DeviceContext {
   cudaStream_t stream = nullptr;
   int sm_count = 0;
   int* d_err = nullptr;  // device error word written by kernels (never trapped)
+  int pair_clusters = 0;  // co-resident 2-CTA clusters of the paired GroupNorm GEMM (0: unavailable)
   ~DeviceContext();
 };
 

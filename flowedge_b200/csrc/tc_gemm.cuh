@@ -46,7 +46,7 @@ constexpr int THREADS = 64 + EPI_THREADS;
 constexpr int TMEM_COLS = 512;
 constexpr int MAX_TILE_GROUPS = 4;   // groups of >= 32 channels inside a 128-row tile
 constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + 256 + 4 * EPI_PARTS * MAX_TILE_SAMPLES * 16 +
-                           MAX_TILE_SAMPLES * MAX_TILE_GROUPS * 8;
+                           MAX_TILE_SAMPLES * MAX_TILE_GROUPS * 8 + 3 * MAX_TILE_SAMPLES * 16;
 static_assert(SMEM_BYTES <= 232448, "shared memory above the 227 KB per-CTA limit");
 
 enum Act : int { kActNone = 0, kActSilu = 1, kActSoftplus = 2 };
@@ -109,7 +109,14 @@ struct Params {
 //   kEpiFused: GroupNorm + Mish (+ FiLM / residual) applied in the epilogue
 enum EpiMode : int { kEpiPlain = 0, kEpiStats = 1, kEpiFused = 2 };
 
-template <int MODE>
+// PAIR (fused mode, GroupNorm groups of 256 channels): the kernel runs as
+// clusters of 2 CTAs.  Both CTAs of a cluster walk the same sequence of tile
+// pairs; CTA rank r takes the 128-row tile 2*i + r of a 256-row group, so a
+// group's two halves are computed side by side.  After pass 1 each CTA stores
+// its per-sample partial sums into the other's shared memory and arrives on
+// the other's mbarrier (release, cluster scope); each then waits (bounded) for
+// the other's partials and normalises with the whole group's statistics.
+template <int MODE, bool PAIR = false>
 static __global__ void __launch_bounds__(THREADS, 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB0,
                    const __grid_constant__ CUtensorMap tmB1, const __grid_constant__ CUtensorMap tmB2,
@@ -121,7 +128,8 @@ static __global__ void __launch_bounds__(THREADS, 1)
   uint64_t* tfull = empty + STAGES;
   uint64_t* tempty = tfull + 2;
   uint64_t* drain = tempty + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  uint64_t* xfull = drain + 1;  // [2]: the other CTA's GroupNorm partials arrived (PAIR)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(xfull + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   double2* red = reinterpret_cast<double2*>(smem + STAGES * STAGE_BYTES + 256);
 
@@ -138,6 +146,8 @@ static __global__ void __launch_bounds__(THREADS, 1)
       mbar_init(&tempty[a], EPI_THREADS);
     }
     mbar_init(drain, 1);
+    mbar_init(&xfull[0], 1);
+    mbar_init(&xfull[1], 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -155,6 +165,26 @@ static __global__ void __launch_bounds__(THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  // the other CTA's barriers are initialised before anyone arrives on them
+  if constexpr (PAIR) cluster_sync_all();
+
+  // Tile walk.  Plain: tiles blockIdx.x, +gridDim.x, ...  PAIR: tile pairs
+  // (cluster index, +clusters, ...), of which this CTA takes row block
+  // 2 * (pair % (n_tiles_m / 2)) + rank.
+  const int rank = PAIR ? static_cast<int>(cluster_rank()) : 0;
+  const int walk_first = PAIR ? static_cast<int>(cluster_index()) : static_cast<int>(blockIdx.x);
+  const int walk_stride = PAIR ? static_cast<int>(cluster_count()) : static_cast<int>(gridDim.x);
+  const int walk_count = PAIR ? p.total_tiles / 2 : p.total_tiles;
+  auto tile_mn = [&](int t, int& m_blk, int& n_blk) {
+    if constexpr (PAIR) {
+      const int npm = p.n_tiles_m >> 1;
+      m_blk = (t % npm) * 2 + rank;
+      n_blk = t / npm;
+    } else {
+      m_blk = t % p.n_tiles_m;
+      n_blk = t / p.n_tiles_m;
+    }
+  };
 
   const int total_kb = [&] {
     int n = 0;
@@ -168,9 +198,9 @@ static __global__ void __launch_bounds__(THREADS, 1)
       uint32_t kb_iter = 0;
       uint32_t armed = 0, armed_phase = 0;  // per-stage bits: armed at least once / parity of its last arm
       bool ok = true;
-      for (int tile = blockIdx.x; tile < p.total_tiles && ok; tile += gridDim.x) {
-        const int m_blk = tile % p.n_tiles_m;
-        const int n_blk = tile / p.n_tiles_m;
+      for (int tile = walk_first; tile < walk_count && ok; tile += walk_stride) {
+        int m_blk, n_blk;
+        tile_mn(tile, m_blk, n_blk);
         for (int s = 0; s < p.nseg && ok; ++s) {
           const Seg sg = p.seg[s];
           const CUtensorMap* mapB = sg.src == 0 ? &tmB0 : (sg.src == 1 ? &tmB1 : &tmB2);
@@ -209,7 +239,7 @@ static __global__ void __launch_bounds__(THREADS, 1)
       uint32_t kb_iter = 0;
       uint32_t acc_iter = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; tile < p.total_tiles && ok; tile += gridDim.x, ++acc_iter) {
+      for (int tile = walk_first; tile < walk_count && ok; tile += walk_stride, ++acc_iter) {
         const int acc = acc_iter & 1;
         const uint32_t acc_phase = (acc_iter >> 1) & 1;
         if (!mbar_wait(&tempty[acc], acc_phase ^ 1, abort_flag)) {
@@ -262,16 +292,23 @@ static __global__ void __launch_bounds__(THREADS, 1)
     const int row = q * 32 + lane;
     const int col0 = part * EPI_COLS;
     float2* stat = reinterpret_cast<float2*>(red + 4 * EPI_PARTS * MAX_TILE_SAMPLES);  // [sample][group] (mean, inv)
+    // PAIR: [2][sample] partials written by the other CTA (by accumulator
+    // parity), then [sample] this CTA's own
+    double2* xbuf = reinterpret_cast<double2*>(stat + MAX_TILE_SAMPLES * MAX_TILE_GROUPS);
+    double2* xbuf_own = xbuf + 2 * MAX_TILE_SAMPLES;
     const uint32_t lane_base = static_cast<uint32_t>(q * 32) << 16;
     const int lmask = p.L - 1;
     const int cs = p.out_cs;
     uint32_t acc_iter = 0;
-    for (int tile = blockIdx.x; tile < p.total_tiles; tile += gridDim.x, ++acc_iter) {
-      const int m_blk = tile % p.n_tiles_m;
-      const int n_blk = tile / p.n_tiles_m;
+    for (int tile = walk_first; tile < walk_count; tile += walk_stride, ++acc_iter) {
+      int m_blk, n_blk;
+      tile_mn(tile, m_blk, n_blk);
       const int acc = acc_iter & 1;
       const uint32_t acc_phase = (acc_iter >> 1) & 1;
-      if (!mbar_wait(&tfull[acc], acc_phase, abort_flag)) {
+      bool waited = mbar_wait(&tfull[acc], acc_phase, abort_flag);
+      // modes with named barriers below take the same decision in every thread
+      if constexpr (kStats) waited = bar_and(2, EPI_THREADS, waited);
+      if (!waited) {
         atomicCAS(p.err, 0, kErrWaitTimeoutEpilogue);
         *abort_flag = 1;
         break;
@@ -388,7 +425,11 @@ static __global__ void __launch_bounds__(THREADS, 1)
               d1 += r.x;
               d2 += r.y;
             }
-          if constexpr (MODE == kEpiFused) {
+          if constexpr (PAIR) {
+            // this CTA's half of the group: keep it, and send it to the other CTA
+            xbuf_own[ls] = make_double2(d1, d2);
+            st_cluster_f64x2(cluster_map(smem_u32(&xbuf[acc * MAX_TILE_SAMPLES + ls]), rank ^ 1), d1, d2);
+          } else if constexpr (MODE == kEpiFused) {
             // biased variance E[y^2] - E[y]^2 clamped at 0, eps 1e-5, in double
             const double cnt = static_cast<double>(p.group_ch) * p.L;
             const double mean = d1 / cnt;
@@ -407,6 +448,27 @@ static __global__ void __launch_bounds__(THREADS, 1)
           }
         }
         named_barrier(1, EPI_THREADS);
+        if constexpr (PAIR) {
+          if (tid == 0) {
+            fence_acq_rel_cluster();
+            mbar_arrive_cluster(cluster_map(smem_u32(&xfull[acc]), rank ^ 1));
+          }
+          const bool got = bar_and(2, EPI_THREADS, mbar_wait_cluster(&xfull[acc], acc_phase, abort_flag));
+          if (!got) {
+            atomicCAS(p.err, 0, kErrWaitTimeoutEpilogue);
+            *abort_flag = 1;
+            break;
+          }
+          for (int ls = tid; ls < p.tile_samples; ls += EPI_THREADS) {
+            const double2 a = xbuf_own[ls];
+            const double2 o = xbuf[acc * MAX_TILE_SAMPLES + ls];
+            const double cnt = static_cast<double>(p.group_ch) * p.L;
+            const double mean = (a.x + o.x) / cnt;
+            const double var = fmax(0.0, (a.y + o.y) / cnt - mean * mean);
+            stat[ls * MAX_TILE_GROUPS] = make_float2(static_cast<float>(mean), static_cast<float>(1.0 / sqrt(var + 1e-5)));
+          }
+          named_barrier(1, EPI_THREADS);
+        }
       }
       if constexpr (MODE == kEpiFused) {
         // pass 2: z = mish((y - mean) * inv * gamma + beta), then FiLM or + residual.
@@ -494,6 +556,8 @@ static __global__ void __launch_bounds__(THREADS, 1)
   __syncthreads();
   tc_fence_after();
   if (warp == 1) tmem_dealloc(tmem_base, TMEM_COLS);
+  // no CTA leaves while the other may still write into its shared memory
+  if constexpr (PAIR) cluster_sync_all();
 }
 
 }  // namespace tc

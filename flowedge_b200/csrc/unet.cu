@@ -216,11 +216,14 @@ class Unet final : public UnetDevice {
   bool tc_conv(const ConvDev& c, const std::vector<Act>& srcs, int L_out, std::size_t batch, void* out,
                long long out_ld, int rps, int tmul, int tadd, bool stats, int groups, bool out_f32, cudaStream_t st,
                std::string& err, const Fuse* fuse = nullptr);
-  // GroupNorm fits the conv epilogue: groups of 32..128 channels inside one
-  // 128-row tile, and samples of at least 8 tokens
+  // GroupNorm fits the conv epilogue: samples of at least 8 tokens, and
+  // groups of 32..128 channels inside one 128-row tile, or groups of 256
+  // channels over the two tiles of a 2-CTA cluster
   bool fusable(int channels, int groups, int L) const {
     const int gc = channels / groups;
-    return gc >= 32 && gc <= 128 && 128 % gc == 0 && L >= 8;
+    if (gc < 32 || L < 8) return false;
+    if (gc <= 128) return 128 % gc == 0;
+    return gc == 256 && channels % 256 == 0 && ctx_->pair_clusters > 0;
   }
   void tc_gn(const Act& y, std::size_t batch, int groups, int parts, const float* gamma, const float* beta,
              const BlockDev* film_block, const float* film_time_row, const float* res_f32, const void* res_half,
