@@ -20,6 +20,8 @@ enum DeviceError : int {
   kErrWaitTimeoutMma = 2,
   kErrWaitTimeoutEpilogue = 3,
   kErrTmemAlloc = 4,
+  kErrGridBarrierTimeout = 5,
+  kErrProgramLayout = 6,
 };
 
 // Every mbarrier wait gives up after kWaitNs of wall time (read from the

@@ -163,6 +163,18 @@ int synchronize_context(DeviceContext& ctx) noexcept {
   return take_device_error(ctx, ctx.stream) == 0 ? 0 : 2;
 }
 
+const char* device_error_text(int code) noexcept {
+  switch (code) {
+    case kErrWaitTimeoutProducer: return "a device pipeline wait timed out (copy producer)";
+    case kErrWaitTimeoutMma: return "a device pipeline wait timed out (tensor-core consumer)";
+    case kErrWaitTimeoutEpilogue: return "a device pipeline wait timed out (epilogue)";
+    case kErrTmemAlloc: return "tensor memory allocation failed";
+    case kErrGridBarrierTimeout: return "a device grid barrier timed out";
+    case kErrProgramLayout: return "internal error: small-batch program layout check failed";
+    default: return "a device pipeline wait timed out";
+  }
+}
+
 int take_device_error(DeviceContext& ctx, cudaStream_t stream) {
   int host = 0;
   if (cudaMemcpyAsync(&host, ctx.d_err, sizeof(int), cudaMemcpyDeviceToHost, stream) != cudaSuccess) return -1;

@@ -129,6 +129,8 @@ inline int ew_grid(long long total, int threads, const DeviceContext& ctx) {
 // Reads and clears the device error word; non-zero means a bounded wait in a
 // kernel gave up.
 int take_device_error(DeviceContext& ctx, cudaStream_t stream);
+// Message for a device error word value.
+const char* device_error_text(int code) noexcept;
 
 std::vector<float> widen_f32(const HostTensor& t);
 

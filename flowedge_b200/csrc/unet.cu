@@ -17,6 +17,8 @@
 // captured as one CUDA graph per (batch, steps, scheduler).
 #include <algorithm>
 #include <cmath>
+#include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <map>
 #include <numbers>
@@ -24,6 +26,7 @@
 
 #include "runtime.cuh"
 #include "simt.cuh"
+#include "stream.cuh"
 
 namespace feb {
 namespace {
@@ -52,6 +55,10 @@ struct ConvDev {
   int nslices = 0;
   std::vector<tc::Seg> segs;
   int stride = 1;
+  std::vector<int> tap_off;  // input time offset of each tap
+  // small-batch program: rows in mma.sync fragment order (see stream_pack)
+  void* sw = nullptr;
+  int s_rbs = 0, s_ks = 0;
   // host staging before upload
   std::vector<float> host_w;
   std::vector<float> host_b;
@@ -124,6 +131,8 @@ void pack_conv(ConvDev& c, ConvKind kind, const std::vector<float>& w, const std
     }
   c.host_b = b;
   c.stride = kind == ConvKind::kDown ? 2 : 1;
+  c.tap_off.clear();
+  for (const auto& tp : taps) c.tap_off.push_back(tp.second);
   // weight-streaming slices and tensor-core segments
   for (int j = 0; j < c.taps; ++j) {
     const int t_off = taps[static_cast<std::size_t>(j)].second;
@@ -146,6 +155,43 @@ void pack_conv(ConvDev& c, ConvKind kind, const std::vector<float>& w, const std
   c.nslices = static_cast<int>(c.host_slices.size());
 }
 
+// Rows of a [rows][K] weight matrix in the order the small-batch program's
+// mma.sync m16n8k16 A fragments are loaded: for row block rb and K step k,
+// plane p, lane l = 4g + t holds the 32-bit pairs
+//   {W[16rb+g][16k+2t..+1], W[16rb+g+8][16k+2t..+1], W[16rb+g][16k+2t+8..+9], W[16rb+g+8][16k+2t+8..+9]}
+// (lower column in the low half).  bf16 weights: one plane, the bf16-rounded
+// value as fp16.  fp32 weights: planes hi = fp16(w) and lo = fp16(w - hi).
+int stream_planes(bool bf16) { return bf16 ? 1 : 2; }
+
+std::size_t stream_bytes(int rows, int K, bool bf16) {
+  return static_cast<std::size_t>((rows + 15) / 16) * static_cast<std::size_t>(K / 16) *
+         static_cast<std::size_t>(stream_planes(bf16)) * 512;
+}
+
+void stream_pack(const float* w, int rows, int K, bool bf16, std::vector<std::uint32_t>& out) {
+  const int rbs = (rows + 15) / 16, ks = K / 16, planes = stream_planes(bf16);
+  out.assign(static_cast<std::size_t>(rbs) * ks * planes * 128, 0u);
+  auto bits = [&](int r, int k, int plane) -> std::uint32_t {
+    if (r >= rows) return 0u;
+    const float v = w[static_cast<std::size_t>(r) * K + k];
+    if (bf16) return fp16_bits_of_bf16_rounded(v);
+    const __half hi = __float2half_rn(v);
+    return plane == 0 ? __half_as_ushort(hi) : __half_as_ushort(__float2half_rn(v - __half2float(hi)));
+  };
+  auto pair = [&](int r, int k, int plane) { return bits(r, k, plane) | (bits(r, k + 1, plane) << 16); };
+  std::size_t i = 0;
+  for (int rb = 0; rb < rbs; ++rb)
+    for (int k = 0; k < ks; ++k)
+      for (int pl = 0; pl < planes; ++pl)
+        for (int lane = 0; lane < 32; ++lane) {
+          const int r0 = rb * 16 + (lane >> 2), c0 = k * 16 + 2 * (lane & 3);
+          out[i++] = pair(r0, c0, pl);
+          out[i++] = pair(r0 + 8, c0, pl);
+          out[i++] = pair(r0, c0 + 8, pl);
+          out[i++] = pair(r0 + 8, c0 + 8, pl);
+        }
+}
+
 struct Act {
   void* p = nullptr;
   int C = 0;
@@ -162,9 +208,13 @@ class Unet final : public UnetDevice {
  public:
   Unet(std::shared_ptr<DeviceContext> ctx, Precision prec) : ctx_(std::move(ctx)), prec_(prec) {}
   ~Unet() override {
+    write_trace();
+    if (trace_ != nullptr) cudaFreeHost(trace_);
     for (auto& [key, g] : graphs_) {
       cudaGraphExecDestroy(g.exec);
+      if (g.tables != nullptr) cudaFree(g.tables);
     }
+    drop_streams();
     if (pinned_ != nullptr) cudaFreeHost(pinned_);
   }
 
@@ -262,6 +312,7 @@ class Unet final : public UnetDevice {
   std::vector<std::array<ConvDev, 2>> us_;
   ConvDev fc_;
   float *fn_g_ = nullptr, *fn_b_ = nullptr, *fo_w_ = nullptr, *fo_b_ = nullptr;
+  ConvDev fo_s_;  // output 1x1 conv in the small-batch program's layout
   // output 1x1 conv for the tensor path: fp16 rows [hi(w) | lo(w)] padded to
   // 128 rows, and the bias of the high rows
   void* fo16_ = nullptr;
@@ -303,7 +354,27 @@ class Unet final : public UnetDevice {
   struct Graph {
     cudaGraphExec_t exec = nullptr;
     std::uint64_t launches = 0;
+    void* tables = nullptr;  // small-batch program: per-step timestep and scheduler scalars
   };
+  // small-batch persistent program (stream.cuh), one per batch size
+  struct StreamProg {
+    void* dev = nullptr;  // ops, partial-sum buffers, segment tables, barrier words
+    const sp::Op* ops = nullptr;
+    unsigned* sync = nullptr;
+    int n_pre = 0, n_step = 0;
+    std::size_t smem = 0;
+    bool ok = false;
+  };
+  std::map<std::size_t, StreamProg> progs_;
+  // FLOWEDGE_PROGRAM_TRACE=<file>: op timeline of the last program call
+  // (mapped host memory, CTA 0's global-timer stamps), written at close
+  unsigned long long* trace_ = nullptr;
+  std::vector<int> trace_kinds_;
+  void write_trace() noexcept;
+  bool use_stream(std::size_t batch);
+  bool build_stream(std::size_t batch, StreamProg& out);
+  bool record_stream(std::size_t batch, std::size_t steps, const void* tables, cudaStream_t st, std::string& err);
+  void drop_streams() noexcept;
   std::map<std::tuple<std::size_t, std::size_t, int, bool>, Graph> graphs_;
   std::uint64_t launches_ = 0;
   std::uint64_t recorded_ = 0;
@@ -512,6 +583,7 @@ bool Unet::load(const TensorTable& t, std::string& err) {
     film_.host_slices.push_back(SimtSlice{0, 0, ch, std::min(kSliceCh, cond_pad_ - ch), ch});
   film_.nslices = static_cast<int>(film_.host_slices.size());
   film_.segs.push_back(tc::Seg{0, 0, 0, cond_pad_ / 64, 0});
+  film_.tap_off = {0};
 
   // alphas_cumprod: squaredcos_cap_v2 betas in double, cumulative product in
   // float (diffusion.cc:186-191, 529-541)
@@ -545,6 +617,7 @@ bool Unet::load(const TensorTable& t, std::string& err) {
   const std::size_t wbytes = bf16_weights() ? 2 : 4;
   auto plan_conv = [&](const ConvDev& c) {
     plan.add(c.host_w.size() * wbytes);
+    plan.add(stream_bytes(c.oc, c.K, bf16_weights()));
     plan.add_n<float>(c.host_b.size());
     plan.add_n<SimtSlice>(c.host_slices.size());
   };
@@ -565,6 +638,7 @@ bool Unet::load(const TensorTable& t, std::string& err) {
   plan.add_n<float>(2 * c0 + A * c0 + A + 2 * A);
   plan.add(static_cast<std::size_t>(tc::BM) * c0 * 2);
   plan.add_n<float>(tc::BM);
+  plan.add(stream_bytes(A, c0, bf16_weights()));
   plan.add_n<float>(T * static_cast<std::size_t>(F_));
   plan.add_n<float>(te1w.size() + te1b.size() + te2w.size() + te2b.size() + wt_all.size());
   plan.add_n<float>(T + T * td);
@@ -577,7 +651,16 @@ bool Unet::load(const TensorTable& t, std::string& err) {
     return d;
   };
   std::vector<std::uint16_t> bf_stage;
+  std::vector<std::uint32_t> sw_stage;
+  auto put_stream = [&](ConvDev& c, const float* w, int rows) {
+    stream_pack(w, rows, c.K, bf16_weights(), sw_stage);
+    c.sw = wts_.take(sw_stage.size() * 4);
+    if (c.sw != nullptr) cudaMemcpy(c.sw, sw_stage.data(), sw_stage.size() * 4, cudaMemcpyHostToDevice);
+    c.s_rbs = (rows + 15) / 16;
+    c.s_ks = c.K / 16;
+  };
   auto put_conv = [&](ConvDev& c) {
+    put_stream(c, c.host_w.data(), c.oc);
     if (bf16_weights()) {
       bf_stage.resize(c.host_w.size());
       for (std::size_t i = 0; i < c.host_w.size(); ++i) bf_stage[i] = fp16_bits_of_bf16_rounded(c.host_w[i]);
@@ -614,6 +697,15 @@ bool Unet::load(const TensorTable& t, std::string& err) {
   fn_b_ = put(h_fn_b_);
   fo_w_ = put(h_fo_w_);
   fo_b_ = put(h_fo_b_);
+  // output 1x1 conv as a program conv (A rows x c0)
+  fo_s_.kind = ConvKind::kPoint;
+  fo_s_.oc = A;
+  fo_s_.K = c0;
+  fo_s_.ic_total = c0;
+  fo_s_.taps = 1;
+  fo_s_.tap_off = {0};
+  fo_s_.bias = fo_b_;
+  put_stream(fo_s_, h_fo_w_.data(), A);
   if (tc_ok_) {
     // w = hi + lo with hi = fp16(w), lo = fp16(w - hi): the pair carries the
     // fp32 weight to about 2^-22 relative, and the tensor cores accumulate in fp32
@@ -663,9 +755,13 @@ bool Unet::load(const TensorTable& t, std::string& err) {
 int Unet::reserve(std::size_t batch, std::string& err) noexcept {
   if (batch == 0) batch = 1;
   if (batch <= cap_) return 0;
-  // drop graphs recorded against the old workspace
-  for (auto& [key, g] : graphs_) cudaGraphExecDestroy(g.exec);
+  // drop graphs and programs recorded against the old workspace
+  for (auto& [key, g] : graphs_) {
+    cudaGraphExecDestroy(g.exec);
+    if (g.tables != nullptr) cudaFree(g.tables);
+  }
   graphs_.clear();
+  drop_streams();
   const std::size_t H = cfg_.horizon, A = cfg_.action_dim;
   const std::size_t cap_tc = (batch + 255) / 256 * 256;
   std::size_t max_c = 0;
@@ -1248,6 +1344,396 @@ bool Unet::record_sample(std::size_t batch, const std::vector<StepPlan>& plan, c
   return true;
 }
 
+// ---------------------------------------------------------------------------
+// small-batch persistent program (stream.cuh)
+
+namespace {
+// per-step tables of a recorded program: int timestep[steps], then StepScalars[steps]
+std::size_t stream_table_off(std::size_t steps) { return (steps * sizeof(int) + 255) & ~std::size_t(255); }
+
+// CTA whose unit range [U c / NC, U (c + 1) / NC) holds unit u (host twin of sp::cta_of)
+int cta_of_host(long long u, long long U, int NC) {
+  int c = static_cast<int>((u * NC) / U);
+  while (c + 1 < NC && (U * (c + 1)) / NC <= u) ++c;
+  while (c > 0 && (U * c) / NC > u) --c;
+  return c;
+}
+}  // namespace
+
+void Unet::write_trace() noexcept {
+  const char* path = std::getenv("FLOWEDGE_PROGRAM_TRACE");
+  if (trace_ == nullptr || path == nullptr) return;
+  if (std::FILE* f = std::fopen(path, "w")) {
+    for (std::size_t i = 0; i + 1 < trace_kinds_.size() + 1 && trace_[i + 1] != 0; ++i)
+      std::fprintf(f, "%zu %d %llu\n", i, trace_kinds_[i % trace_kinds_.size()], trace_[i + 1] - trace_[i]);
+    std::fclose(f);
+  }
+}
+
+void Unet::drop_streams() noexcept {
+  for (auto& [b, pg] : progs_)
+    if (pg.dev != nullptr) cudaFree(pg.dev);
+  progs_.clear();
+}
+
+bool Unet::use_stream(std::size_t batch) {
+  if (use_tc(batch) || batch * cfg_.horizon > static_cast<std::size_t>(sp::kMaxTok) || fo_s_.sw == nullptr)
+    return false;
+  auto it = progs_.find(batch);
+  if (it == progs_.end()) {
+    StreamProg pg;
+    if (!build_stream(batch, pg)) {
+      if (pg.dev != nullptr) cudaFree(pg.dev);
+      pg = StreamProg{};
+    }
+    it = progs_.emplace(batch, pg).first;
+  }
+  return it->second.ok;
+}
+
+// Builds the op list of one sampling call for `batch` samples: it mirrors the
+// weight-streaming forward op by op (same buffers, fp32 activations).  Two
+// passes over the same emission code: the first sizes the device buffer, the
+// second fills in its addresses.
+bool Unet::build_stream(std::size_t batch, StreamProg& out) {
+  const int NC = ctx_->sm_count;
+  const int planes = stream_planes(bf16_weights());
+  const int S = static_cast<int>(cfg_.stages);
+  const int H = static_cast<int>(cfg_.horizon), A = static_cast<int>(cfg_.action_dim);
+  const int G = static_cast<int>(cfg_.groups);
+  const int B = static_cast<int>(batch);
+  int dev_smem_max = 0;
+  cudaDeviceGetAttribute(&dev_smem_max, cudaDevAttrMaxSharedMemoryPerBlockOptin, ctx_->device);
+  std::size_t total = 0;
+  for (int pass = 0; pass < 2; ++pass) {
+    const std::uintptr_t base = reinterpret_cast<std::uintptr_t>(out.dev);
+    std::size_t used = 0;
+    bool fits = true;
+    std::size_t smem = 0;
+    std::vector<std::pair<std::size_t, std::vector<int>>> tables;
+    auto take = [&](std::size_t bytes) {
+      used = (used + 255) & ~std::size_t(255);
+      const std::size_t off = used;
+      used += bytes;
+      return off;
+    };
+    auto at = [&](std::size_t off) { return base + off; };
+    std::vector<sp::Op> pre, step;
+    std::vector<sp::Op>* cur = &pre;
+
+    auto conv = [&](const ConvDev& c, const std::vector<Act>& srcs, int L_in, int L_out, bool barrier) {
+      sp::Op op{};
+      op.kind = sp::kOpConv;
+      op.barrier_after = barrier ? 1 : 0;
+      sp::ConvOp& o = op.conv;
+      o.w = static_cast<const uint4*>(c.sw);
+      o.planes = planes;
+      o.rbs = c.s_rbs;
+      o.ks = c.s_ks;
+      o.ic_pad = c.ic_total;
+      o.src0 = static_cast<const float*>(srcs[0].p);
+      o.c0 = srcs[0].C;
+      if (srcs.size() > 1) {
+        o.src1 = static_cast<const float*>(srcs[1].p);
+        o.c1 = srcs[1].C;
+      }
+      if (o.c0 + o.c1 != o.ic_pad || c.tap_off.empty() || c.tap_off.size() > static_cast<std::size_t>(sp::kMaxTaps) ||
+          o.ic_pad % 16 != 0 || o.ks < 1 || o.rbs < 1 || c.sw == nullptr) {
+        fits = false;
+        return sp::YSrc{};
+      }
+      o.samples = B;
+      o.L_in = L_in;
+      o.L_out = L_out;
+      o.stride = c.stride;
+      o.ntaps = static_cast<int>(c.tap_off.size());
+      int lo = 0, hi = 0;
+      for (int j = 0; j < o.ntaps && j < sp::kMaxTaps; ++j) {
+        o.tap_off[j] = c.tap_off[static_cast<std::size_t>(j)];
+        lo = std::min(lo, o.tap_off[j]);
+        hi = std::max(hi, o.tap_off[j]);
+      }
+      o.halo_lo = -lo;
+      o.rows = L_in + o.halo_lo + std::max(0, (L_out - 1) * o.stride + hi - (L_in - 1));
+      o.T = B * L_out;
+      if (o.T > sp::kMaxTok) fits = false;
+      const long long U = static_cast<long long>(o.rbs) * o.ks;
+      // CTAs the units are split over: all of them, unless a row block would
+      // then meet more than kMaxSeg CTAs (tiny convs with few row blocks)
+      const int nct = static_cast<int>(
+          std::max<long long>(1, std::min<long long>(NC, static_cast<long long>(o.rbs) * (sp::kMaxSeg - 1))));
+      o.nct = nct;
+      std::vector<int> nseg(static_cast<std::size_t>(o.rbs));
+      int seg_max = 1;
+      for (int rb = 0; rb < o.rbs; ++rb) {
+        const long long u0 = static_cast<long long>(rb) * o.ks;
+        nseg[static_cast<std::size_t>(rb)] = cta_of_host(u0 + o.ks - 1, U, nct) - cta_of_host(u0, U, nct) + 1;
+        seg_max = std::max(seg_max, nseg[static_cast<std::size_t>(rb)]);
+      }
+      // row blocks one CTA's units meet (a slot per compute warp each)
+      int nslots = 1;
+      for (int ci = 0; ci < nct; ++ci) {
+        const long long a = (U * ci) / nct, b = (U * (ci + 1)) / nct;
+        if (b > a) nslots = std::max(nslots, static_cast<int>((b - 1) / o.ks - a / o.ks + 1));
+      }
+      if (nslots > sp::kMaxSlots) fits = false;
+      o.nslots = nslots;
+      if (seg_max > sp::kMaxSeg) fits = false;
+      o.seg_max = seg_max;
+      const std::size_t poff = take(static_cast<std::size_t>(o.rbs) * seg_max * o.T * 16 * sizeof(float));
+      const std::size_t noff = take(static_cast<std::size_t>(o.rbs) * sizeof(int));
+      tables.emplace_back(noff, std::move(nseg));
+      o.P = reinterpret_cast<float*>(at(poff));
+      // shared memory: staged input (fp16 hi / lo), per-warp slots, then the weight ring
+      const std::size_t head = static_cast<std::size_t>(2) * (B * o.rows + 1) * (o.ic_pad + sp::kRowPad) * 2 +
+                               static_cast<std::size_t>(sp::kComputeWarps) * nslots * 16 * o.T * sizeof(float) +
+                               static_cast<std::size_t>(sp::kWarps) * nslots * sizeof(int);
+      o.ring_off = static_cast<int>((head + 127) & ~std::size_t(127));
+      smem = std::max(smem, static_cast<std::size_t>(o.ring_off) + sp::kMinStages * sp::kChunk);
+      // as many stages as the launch's shared memory (sized in the first pass) leaves
+      o.stages = pass == 0 ? sp::kMinStages
+                           : static_cast<int>(std::min<std::size_t>(sp::kMaxStages, (out.smem - o.ring_off) / sp::kChunk));
+      cur->push_back(op);
+      sp::YSrc y{};
+      y.P = o.P;
+      y.nseg = reinterpret_cast<const int*>(at(noff));
+      y.bias = c.bias;
+      y.ks = o.ks;
+      y.units = U;
+      y.seg_max = seg_max;
+      y.T = o.T;
+      return y;
+    };
+    auto gn = [&](const sp::YSrc& y, int C, int groups, int L, const float* gamma, const float* beta,
+                  const BlockDev* film_blk, int res_mode, const sp::YSrc* res, const void* res_tensor, void* dst) {
+      if ((C / groups) * L > sp::kGnPerThread * sp::kThreads) fits = false;
+      sp::Op op{};
+      op.kind = sp::kOpGn;
+      op.barrier_after = 1;
+      sp::GnOp& o = op.gn;
+      o.y = y;
+      o.C = C;
+      o.groups = groups;
+      o.samples = B;
+      o.L = L;
+      o.gamma = gamma;
+      o.beta = beta;
+      if (film_blk != nullptr) {
+        o.film = 1;
+        o.film_cond = film_cond_;
+        o.film_time = film_time_;
+        o.film_F = F_;
+        o.film_off = film_blk->film_off;
+      }
+      o.res_mode = res_mode;
+      if (res != nullptr) o.res = *res;
+      o.res_tensor = static_cast<const float*>(res_tensor);
+      o.out = static_cast<float*>(dst);
+      cur->push_back(op);
+    };
+    auto reduce = [&](const sp::YSrc& y, int M, int L, int tmul, int tadd, void* dst, bool barrier) {
+      sp::Op op{};
+      op.kind = sp::kOpReduce;
+      op.barrier_after = barrier ? 1 : 0;
+      op.reduce.y = y;
+      op.reduce.M = M;
+      op.reduce.L = L;
+      op.reduce.tmul = tmul;
+      op.reduce.tadd = tadd;
+      op.reduce.out = static_cast<float*>(dst);
+      cur->push_back(op);
+    };
+    auto block = [&](const BlockDev& blk, const std::vector<Act>& in, int L, Act o) {
+      const int oc = blk.oc;
+      const sp::YSrc y1 = conv(blk.c1, in, L, L, true);
+      gn(y1, oc, G, L, blk.g1, blk.b1, &blk, 0, nullptr, nullptr, h1_);
+      sp::YSrc yr{};
+      if (blk.has_res) yr = conv(blk.res, in, L, L, false);
+      const sp::YSrc y2 = conv(blk.c2, {Act{h1_, oc, L}}, L, L, true);
+      if (blk.has_res) gn(y2, oc, G, L, blk.g2, blk.b2, nullptr, 1, &yr, nullptr, o.p);
+      else gn(y2, oc, G, L, blk.g2, blk.b2, nullptr, 2, nullptr, in[0].p, o.p);
+    };
+
+    // once per call: FiLM condition part W_c * mish(cond) + b -> film_cond_
+    const sp::YSrc yf = conv(film_, {Act{mcond_, cond_pad_, 1}}, 1, 1, true);
+    reduce(yf, F_, 1, 1, 0, film_cond_, true);
+    // every step: the forward and the update
+    cur = &step;
+    std::size_t li = 0;
+    int L = H;
+    Act x{x_in_, cin_pad_, H};
+    std::vector<Act> skips(static_cast<std::size_t>(S));
+    for (int st = 0; st < S; ++st) {
+      const int oc = static_cast<int>(cfg_.dims[static_cast<std::size_t>(st)]);
+      const Act o0{acts_[li], oc, L}, o1{acts_[li + 1], oc, L};
+      li += 2;
+      block(down_[static_cast<std::size_t>(st)][0], {x}, L, o0);
+      block(down_[static_cast<std::size_t>(st)][1], {o0}, L, o1);
+      skips[static_cast<std::size_t>(st)] = o1;
+      x = o1;
+      if (st + 1 < S) {
+        const Act d{acts_[li++], oc, L / 2};
+        const sp::YSrc yd = conv(ds_[static_cast<std::size_t>(st)], {x}, L, L / 2, true);
+        reduce(yd, oc, L / 2, 1, 0, d.p, true);
+        x = d;
+        L /= 2;
+      } else {
+        ++li;
+      }
+    }
+    for (int m = 0; m < 2; ++m) {
+      const Act o{acts_[li++], x.C, L};
+      block(mid_[static_cast<std::size_t>(m)], {x}, L, o);
+      x = o;
+    }
+    for (int st = 0; st + 1 < S; ++st) {
+      const Act skip = skips[static_cast<std::size_t>(S - 1 - st)];
+      const int low = static_cast<int>(cfg_.dims[static_cast<std::size_t>(S - 2 - st)]);
+      const Act o0{acts_[li], low, L}, o1{acts_[li + 1], low, L};
+      li += 2;
+      block(up_[static_cast<std::size_t>(st)][0], {x, skip}, L, o0);
+      block(up_[static_cast<std::size_t>(st)][1], {o0}, L, o1);
+      const Act u{acts_[li++], low, 2 * L};
+      const sp::YSrc y0 = conv(us_[static_cast<std::size_t>(st)][0], {o1}, L, L, false);
+      const sp::YSrc y1 = conv(us_[static_cast<std::size_t>(st)][1], {o1}, L, L, true);
+      reduce(y0, low, L, 2, 0, u.p, false);
+      reduce(y1, low, L, 2, 1, u.p, true);
+      x = u;
+      L *= 2;
+    }
+    const int c0 = static_cast<int>(cfg_.dims[0]);
+    const sp::YSrc yc = conv(fc_, {x}, H, H, true);
+    gn(yc, c0, static_cast<int>(kFinalNormGroups), H, fn_g_, fn_b_, nullptr, 0, nullptr, nullptr, h1_);
+    const sp::YSrc ye = conv(fo_s_, {Act{h1_, c0, H}}, H, H, true);
+    {
+      sp::Op op{};
+      op.kind = sp::kOpUpdate;
+      op.barrier_after = 1;
+      op.update.y = ye;
+      op.update.A = A;
+      op.update.H = H;
+      op.update.Cin = cin_pad_;
+      op.update.samples = B;
+      op.update.x_master = x_master_;
+      op.update.x_in = static_cast<float*>(x_in_);
+      op.update.seeds = seeds_;
+      step.push_back(op);
+    }
+    // L2 prefetch chain: each conv names the next conv's weights (the last
+    // conv of a step names the first conv of the next step)
+    std::vector<sp::ConvOp*> convs;
+    for (auto& op : pre)
+      if (op.kind == sp::kOpConv) convs.push_back(&op.conv);
+    const std::size_t first_step = convs.size();
+    for (auto& op : step)
+      if (op.kind == sp::kOpConv) convs.push_back(&op.conv);
+    for (std::size_t i = 0; i < convs.size(); ++i) {
+      const sp::ConvOp* nx = convs[i + 1 < convs.size() ? i + 1 : first_step];
+      convs[i]->next_w = nx->w;
+      convs[i]->next_units = static_cast<long long>(nx->rbs) * nx->ks;
+      convs[i]->next_planes = nx->planes;
+    }
+    const std::size_t n_ops = pre.size() + step.size();
+    const std::size_t ops_off = take(n_ops * sizeof(sp::Op));
+    const std::size_t sync_off = take(4 * sizeof(unsigned));
+    if (pass == 0) {
+      // use all the shared memory a CTA may have: deeper rings for the smaller convs
+      if (!fits || smem > static_cast<std::size_t>(dev_smem_max) - 1024) return false;
+      smem = std::max(smem, static_cast<std::size_t>(dev_smem_max) - 1024);
+      total = used;
+      if (counted_malloc(&out.dev, total) != cudaSuccess) {
+        cudaGetLastError();
+        out.dev = nullptr;
+        return false;
+      }
+      cudaMemset(out.dev, 0, total);
+      out.smem = smem;
+      continue;
+    }
+    std::vector<sp::Op> all(pre);
+    all.insert(all.end(), step.begin(), step.end());
+    char* dev = static_cast<char*>(out.dev);
+    cudaMemcpy(dev + ops_off, all.data(), n_ops * sizeof(sp::Op), cudaMemcpyHostToDevice);
+    for (const auto& [off, tab] : tables) cudaMemcpy(dev + off, tab.data(), tab.size() * sizeof(int), cudaMemcpyHostToDevice);
+    out.ops = reinterpret_cast<const sp::Op*>(dev + ops_off);
+    if (std::getenv("FLOWEDGE_PROGRAM_TRACE") != nullptr && trace_ == nullptr) {
+      // one stamp per op of a call of up to train_timesteps steps
+      const std::size_t n = 2 + pre.size() + cfg_.train_timesteps * step.size();
+      if (cudaHostAlloc(reinterpret_cast<void**>(&trace_), n * sizeof(unsigned long long), cudaHostAllocMapped) !=
+          cudaSuccess)
+        trace_ = nullptr;
+      else
+        std::memset(trace_, 0, n * sizeof(unsigned long long));
+      trace_kinds_.clear();
+      for (const auto& op : pre) trace_kinds_.push_back(10 + op.kind);
+      for (std::size_t r = 0; r < cfg_.train_timesteps; ++r)
+        for (const auto& op : step) trace_kinds_.push_back(op.kind);
+    }
+    out.sync = reinterpret_cast<unsigned*>(dev + sync_off);
+    out.n_pre = static_cast<int>(pre.size());
+    out.n_step = static_cast<int>(step.size());
+  }
+  // the whole grid must be resident at once (cooperative launch)
+  auto kernel = planes == 1 ? sp::unet_program_kernel<1> : sp::unet_program_kernel<2>;
+  int per_sm = 0;
+  if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(out.smem)) !=
+          cudaSuccess ||
+      cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, sp::kThreads, out.smem) != cudaSuccess ||
+      per_sm < 1 || cudaDeviceSynchronize() != cudaSuccess) {
+    cudaGetLastError();
+    return false;
+  }
+  out.ok = true;
+  return true;
+}
+
+bool Unet::record_stream(std::size_t batch, std::size_t steps, const void* tables, cudaStream_t st,
+                         std::string& err) {
+  const StreamProg& pg = progs_.at(batch);
+  const int H = static_cast<int>(cfg_.horizon), A = static_cast<int>(cfg_.action_dim);
+  const int n_tokens = static_cast<int>(batch) * H;
+  b0_ = 0;
+  launch(seeds_kernel, dim3((static_cast<unsigned>(batch) + 255) / 256), dim3(256), 0, st,
+         static_cast<const std::uint64_t*>(seed0_), seeds_, static_cast<int>(batch));
+  launch(prep_sample_kernel, dim3(ew_grid(static_cast<long long>(n_tokens) * cin_pad_, 256, *ctx_)), dim3(256), 0, st,
+         static_cast<const float*>(in_noise_), n_tokens, A, x_master_, x_in_, cin_pad_, 0);
+  launch(prep_cond_kernel, dim3(ew_grid(static_cast<long long>(batch) * cond_pad_, 256, *ctx_)), dim3(256), 0, st,
+         static_cast<const float*>(in_cond_), static_cast<int>(batch), static_cast<int>(cfg_.condition_dim),
+         mcond_, cond_pad_, 0);
+  cudaMemsetAsync(pg.sync, 0, 4 * sizeof(unsigned), st);
+  sp::Program prog{};
+  prog.ops = pg.ops;
+  prog.n_pre = pg.n_pre;
+  prog.n_step = pg.n_step;
+  prog.steps = static_cast<int>(steps);
+  prog.step_t = static_cast<const int*>(tables);
+  prog.scalars = reinterpret_cast<const StepScalars*>(static_cast<const char*>(tables) + stream_table_off(steps));
+  prog.sync = pg.sync;
+  prog.err = ctx_->d_err;
+  prog.trace = trace_;
+  cudaLaunchAttribute attr{};
+  attr.id = cudaLaunchAttributeCooperative;
+  attr.val.cooperative = 1;
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(static_cast<unsigned>(ctx_->sm_count));
+  cfg.blockDim = dim3(sp::kThreads);
+  cfg.dynamicSmemBytes = pg.smem;
+  cfg.stream = st;
+  cfg.attrs = &attr;
+  cfg.numAttrs = 1;
+  const cudaError_t rc = bf16_weights() ? cudaLaunchKernelEx(&cfg, sp::unet_program_kernel<1>, prog)
+                                        : cudaLaunchKernelEx(&cfg, sp::unet_program_kernel<2>, prog);
+  ++recorded_;
+  if (rc != cudaSuccess) {
+    err = std::string("program launch: ") + cudaGetErrorString(rc);
+    return false;
+  }
+  launch(unnormalize_kernel, dim3(ew_grid(static_cast<long long>(n_tokens) * A, 256, *ctx_)), dim3(256), 0, st,
+         static_cast<const float*>(x_master_), n_tokens, A, static_cast<const float*>(amin_),
+         static_cast<const float*>(amax_), out_action_);
+  return true;
+}
+
 int Unet::sample_device(const float* condition, const float* noise, std::size_t batch, std::size_t steps,
                         int scheduler, std::uint64_t seed, float* action, void* stream, std::string& err) noexcept {
   if (batch == 0 || steps == 0 || steps > cfg_.train_timesteps || (scheduler != 0 && scheduler != 1)) {
@@ -1275,16 +1761,38 @@ int Unet::sample_device(const float* condition, const float* noise, std::size_t 
     cudaStreamSynchronize(st);
     cudaGraph_t graph = nullptr;
     recorded_ = 0;
+    // small batches: one persistent program launch; its per-step tables are
+    // uploaded before the capture
+    const bool stream = use_stream(batch);
+    const std::vector<StepPlan> plan = plan_steps(steps, scheduler);
+    void* tables = nullptr;
+    if (stream) {
+      std::vector<char> host(stream_table_off(steps) + steps * sizeof(StepScalars));
+      for (std::size_t i = 0; i < steps; ++i) {
+        std::memcpy(host.data() + i * sizeof(int), &plan[i].timestep, sizeof(int));
+        std::memcpy(host.data() + stream_table_off(steps) + i * sizeof(StepScalars), &plan[i].scalars,
+                    sizeof(StepScalars));
+      }
+      if (counted_malloc(&tables, host.size()) != cudaSuccess ||
+          cudaMemcpy(tables, host.data(), host.size(), cudaMemcpyHostToDevice) != cudaSuccess) {
+        err = "device allocation of the program tables failed";
+        if (tables != nullptr) cudaFree(tables);
+        cudaStreamDestroy(cap);
+        return 2;
+      }
+    }
     if (cudaStreamBeginCapture(cap, cudaStreamCaptureModeThreadLocal) != cudaSuccess) {
       err = "cudaStreamBeginCapture failed";
+      if (tables != nullptr) cudaFree(tables);
       cudaStreamDestroy(cap);
       return 2;
     }
-    const bool ok = record_sample(batch, plan_steps(steps, scheduler), cap, err);
+    const bool ok = stream ? record_stream(batch, steps, tables, cap, err) : record_sample(batch, plan, cap, err);
     const cudaError_t end = cudaStreamEndCapture(cap, &graph);
     cudaStreamDestroy(cap);
     if (!ok || end != cudaSuccess || graph == nullptr) {
       if (graph != nullptr) cudaGraphDestroy(graph);
+      if (tables != nullptr) cudaFree(tables);
       if (err.empty()) err = std::string("graph capture failed: ") + cudaGetErrorString(end);
       cudaGetLastError();
       return 2;
@@ -1294,9 +1802,11 @@ int Unet::sample_device(const float* condition, const float* noise, std::size_t 
     cudaGraphDestroy(graph);
     if (inst != cudaSuccess) {
       err = std::string("cudaGraphInstantiate failed: ") + cudaGetErrorString(inst);
+      if (tables != nullptr) cudaFree(tables);
       return 2;
     }
     g.launches = recorded_;
+    g.tables = tables;
     it = graphs_.emplace(key, g).first;
   }
   if (cudaGraphLaunch(it->second.exec, st) != cudaSuccess) {
@@ -1332,8 +1842,8 @@ int Unet::sample(const float* condition, const float* noise, std::size_t batch, 
     err = std::string("diffusion sampling failed on the device: ") + cudaGetErrorString(cudaGetLastError());
     return 2;
   }
-  if (take_device_error(*ctx_, st) != 0) {
-    err = "a device pipeline wait timed out";
+  if (const int code = take_device_error(*ctx_, st); code != 0) {
+    err = device_error_text(code);
     return 2;
   }
   std::memcpy(action, pa, batch * H * A * sizeof(float));
@@ -1383,8 +1893,8 @@ int Unet::denoise(const float* condition, const float* sample, float timestep, f
     err = std::string("diffusion denoise failed on the device: ") + cudaGetErrorString(cudaGetLastError());
     return 2;
   }
-  if (take_device_error(*ctx_, st) != 0) {
-    err = "a device pipeline wait timed out";
+  if (const int code = take_device_error(*ctx_, st); code != 0) {
+    err = device_error_text(code);
     return 2;
   }
   std::memcpy(eps, pe, batch * H * A * sizeof(float));

@@ -199,6 +199,7 @@ def test_pusht_bf16_paths_match_reference_on_same_weights(tmp_path):
     """bf16 mode on bf16-representable weights, against the reference core run
     on the very same weights (stored as fp32, which the reference accepts).
 
+    * batch-1 program (fp16 hi/lo activations on mma.sync): max-abs <= 1e-3
     * weight-streaming path (batch 2, fp32 activations): max-abs <= 1e-3
     * tensor-core path (batch 32, bf16 activations, fp32 accumulate): <= 2e-2
     and, for the record, the quantisation error of bf16 weights against the
@@ -214,12 +215,16 @@ def test_pusht_bf16_paths_match_reference_on_same_weights(tmp_path):
     noise = rng.standard_normal((32, 16, 2)).astype(np.float32)
     expected, _ = _reference_run(path, cond, noise)
     e = Engine(path, threads=0, device=0, precision="bf16", max_batch=32)
+    single = e.sample_diffusion(cond[0], noise[0], 10)  # batch 1: the persistent small-batch program
+    err_single = float(np.abs(single - expected[0]).max())
     small = e.sample_diffusion_batch(cond[:2], noise[:2], 10)
     err_small = float(np.abs(small - expected[:2]).max())
     big = e.sample_diffusion_batch(cond, noise, 10)
     err_big = float(np.abs(big - expected).max())
     e.close()
-    print(f"PushT bf16 weights: streaming path max-abs {err_small:.3g}, tensor path max-abs {err_big:.3g}")
+    print(f"PushT bf16 weights: batch-1 program max-abs {err_single:.3g}, streaming path max-abs {err_small:.3g}, "
+          f"tensor path max-abs {err_big:.3g}")
+    assert err_single <= 1e-3
     assert err_small <= 1e-3
     assert err_big <= 2e-2
 
