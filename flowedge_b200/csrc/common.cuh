@@ -100,7 +100,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
 
 // ---------------------------------------------------------------------------
 // thread-block clusters: distributed shared memory between the CTAs of a
-// cluster (plain remote stores and remote mbarrier arrivals, no multicast)
+// cluster (plain remote stores and remote mbarrier arrivals only)
 
 __device__ __forceinline__ uint32_t cluster_rank() {
   uint32_t r;
@@ -174,7 +174,7 @@ __device__ __forceinline__ bool bar_and(int id, int threads, bool pred) {
 }
 
 // ---------------------------------------------------------------------------
-// TMA (no multicast anywhere in this library)
+// TMA: plain tiled loads, each CTA fetching its own tiles
 
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int c0, int c1, uint64_t* bar) {
   asm volatile(
@@ -347,6 +347,11 @@ __device__ __forceinline__ float mish_sel(float x) {
 }
 
 __device__ __forceinline__ float silu_f(float x) { return x / (1.0f + expf(-x)); }
+
+// SiLU with the fast exponential and division, for the tensor path (its
+// outputs are rounded to 16 bits; relative error ~1e-6).  For x < -87 the
+// exponential overflows to inf and the quotient is -0, the limit of silu.
+__device__ __forceinline__ float silu_fast(float x) { return __fdividef(x, 1.0f + __expf(-x)); }
 
 __device__ __forceinline__ float softplus_f(float x) { return fmaxf(x, 0.0f) + log1pf(expf(-fabsf(x))); }
 

@@ -46,7 +46,9 @@ __device__ __forceinline__ float stage_time(int step, int steps, int method, int
   return t;
 }
 
-// tp[h] = sum_j Wt[h][j] * [sin(t f) | cos(t f)]_j
+// tp[h] = sum_j Wt[h][j] * [sin(t f) | cos(t f)]_j; one warp per row h, the
+// lanes stride the row (coalesced) and a shuffle tree adds their sums
+constexpr int kTimeProjRowsPerBlock = 8;
 __global__ void time_proj_kernel(const int* step_idx, int steps, int method, int stage, const float* freqs, int half,
                                  const float* wt, int H, float* tp) {
   extern __shared__ float sinu[];
@@ -56,10 +58,15 @@ __global__ void time_proj_kernel(const int* step_idx, int steps, int method, int
     sinu[half + j] = cosf(t * freqs[j]);
   }
   __syncthreads();
-  for (int h = blockIdx.x * blockDim.x + threadIdx.x; h < H; h += gridDim.x * blockDim.x) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int warps = blockDim.x >> 5;
+  for (int h = blockIdx.x * warps + warp; h < H; h += gridDim.x * warps) {
+    const float* w = wt + static_cast<long long>(h) * 2 * half;
     float acc = 0.0f;
-    for (int j = 0; j < 2 * half; ++j) acc = fmaf(wt[h * 2 * half + j], sinu[j], acc);
-    tp[h] = acc;
+    for (int j = lane; j < 2 * half; j += 32) acc = fmaf(w[j], sinu[j], acc);
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+    if (lane == 0) tp[h] = acc;
   }
 }
 
@@ -418,7 +425,7 @@ bool Flow::record_step(std::size_t batch, int method, bool tc, cudaStream_t st, 
   const int half = static_cast<int>(cfg_.time_dim / 2);
   const int stages = method == 0 ? 1 : (method == 1 ? 2 : 4);
   for (int s = 0; s < stages; ++s) {
-    time_proj_kernel<<<(H + 255) / 256, 256, static_cast<std::size_t>(2 * half) * 4, st>>>(
+    time_proj_kernel<<<(H + kTimeProjRowsPerBlock - 1) / kTimeProjRowsPerBlock, 32 * kTimeProjRowsPerBlock, static_cast<std::size_t>(2 * half) * 4, st>>>(
         step_, static_cast<int>(steps_), method, s, freqs_, half, wt_, H, tp_);
     // h = SiLU(W_in x + tp + c_emb)
     void* hin = h0_;
@@ -736,7 +743,7 @@ int Flow::sample_static(const float* condition, const float* x0, std::size_t bat
   const int stages = method == 0 ? 1 : (method == 1 ? 2 : 4);
   for (std::size_t i = 0; i < steps; ++i) {
     for (int s = 0; s < stages; ++s) {
-      time_proj_kernel<<<(H + 255) / 256, 256, static_cast<std::size_t>(2 * half) * 4, st>>>(
+      time_proj_kernel<<<(H + kTimeProjRowsPerBlock - 1) / kTimeProjRowsPerBlock, 32 * kTimeProjRowsPerBlock, static_cast<std::size_t>(2 * half) * 4, st>>>(
           step, static_cast<int>(steps), method, s, freqs_, half, wt_, H, tp);
       float* hin = h0;
       float* hout = h1;

@@ -369,7 +369,7 @@ static __global__ void __launch_bounds__(THREADS, 1)
           }
           if (p.act == kActSilu) {
 #pragma unroll
-            for (int j = 0; j < CH; ++j) y[j] = silu_f(y[j]);
+            for (int j = 0; j < CH; ++j) y[j] = silu_fast(y[j]);
           } else if (p.act == kActSoftplus) {
 #pragma unroll
             for (int j = 0; j < CH; ++j) y[j] = softplus_f(y[j]);
