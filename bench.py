@@ -285,6 +285,23 @@ def run_ours(args):
         dist.all_reduce(te, op=dist.ReduceOp.MAX)
     e2e_value = GLOBAL_BATCH * e2e_steps / float(te.item())
 
+    # results gathered to every rank after the timed region (timed separately)
+    gather = None
+    if dist is not None:
+        parts = [torch.empty_like(d_action) for _ in range(world)]
+        g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        dist.barrier()
+        torch.cuda.synchronize()
+        g0.record(stream)
+        dist.all_gather(parts, d_action)
+        g1.record(stream)
+        torch.cuda.synchronize()
+        tg = torch.tensor([g0.elapsed_time(g1)], dtype=torch.float64, device="cuda")
+        dist.all_reduce(tg, op=dist.ReduceOp.MAX)
+        gather = {"op": "all_gather of the actions", "bytes": int(d_action.numel() * 4 * world),
+                  "ms": float(tg.item())}
+        del parts
+
     # dominant kernel: the tcgen05 conv GEMMs of one denoise forward
     prof = engine.profile_diffusion(shard)
     peak, peak_kind = _peaks()
@@ -303,6 +320,8 @@ def run_ours(args):
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": int(cond.nbytes + noise.nbytes),
                     "d2h_bytes_per_step": int(out.nbytes)},
             "gpu_launches": int(launches),
+            # conv FLOPs of the chunks processed per second by each GPU, over the measured peak
+            "per_gpu_tensor_frac": value / world * STEPS * prof["conv_flops"] / shard / (peak * 1e12),
             "device_mallocs_in_timed_region": int(mallocs),
             "roofline": {"bound": "tensor", "kernel": "tc_gemm_kernel (conv GEMMs of one denoise)",
                          "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
@@ -310,6 +329,8 @@ def run_ours(args):
                          "conv_share_of_forward": prof["conv_ms"] / prof["forward_ms"],
                          "conv_launches_per_forward": prof["conv_launches"]},
         }
+    if gather is not None and line is not None:
+        line["gather"] = gather
     if world == 1 and not args.no_extras:
         line["extra"] = _extras(Path(args.workdir), local)
     if world == 1 and not args.no_cpu_baseline:
@@ -329,9 +350,12 @@ def run_ours(args):
 def _latency(fn, iters):
     import torch
 
+    from flowedge_b200.engine import device_malloc_count
+
     for _ in range(3):
         fn()
     torch.cuda.synchronize()
+    mallocs0 = device_malloc_count()
     times = []
     for _ in range(iters):
         t0 = time.perf_counter()
@@ -339,7 +363,7 @@ def _latency(fn, iters):
         times.append((time.perf_counter() - t0) * 1000.0)
     times.sort()
     return {"p50_ms": times[len(times) // 2], "p99_ms": times[min(len(times) - 1, int(len(times) * 0.99))],
-            "iters": iters}
+            "iters": iters, "device_mallocs": int(device_malloc_count() - mallocs0)}
 
 
 def _extras(workdir: Path, device: int):
@@ -357,7 +381,7 @@ def _extras(workdir: Path, device: int):
     noise = rng.standard_normal((16, 2)).astype(np.float32)
     for prec in ("fp32", "bf16"):
         e = Engine(pusht, threads=0, device=device, precision=prec)
-        out[f"c1_pusht_b1_ddim10_{prec}"] = _latency(lambda: e.sample_diffusion(cond, noise, 10), 200)
+        out[f"c1_pusht_b1_ddim10_{prec}"] = _latency(lambda: e.sample_diffusion(cond, noise, 10), 1000)
         e.close()
     # C2: flow head 350 / 1024 x 3 / 512, Euler-10 and RK4-4
     flow = workdir / "bench_c2_flow.safetensors"
