@@ -30,6 +30,12 @@ constexpr int kTcMinRows = 128;
 struct Mat {
   int rows = 0, rows_pad = 0, cols = 0, cols_pad = 0;
   void* w = nullptr;  // [rows_pad][cols_pad]
+  // fp32 engines, tensor-core path: fp16 [rows_pad][3 * cols_pad] rows
+  // [hi(W) | hi(W) | lo(W)], lo = W - hi rounded to fp16, so that one GEMM
+  // over the activations split the same way, [hi(x) | lo(x)] against
+  // [hi | hi | lo] with the x segments hi, lo, hi, gives
+  // hi(W) hi(x) + hi(W) lo(x) + lo(W) hi(x), W x to about 2^-21 relative
+  void* w3 = nullptr;
   SimtSlice* slices = nullptr;
   int nslices = 0;
 };
@@ -83,7 +89,7 @@ struct OdeParams {
   const float* k[4];
   void* next_in;
   int ld_in;
-  int next_half;
+  int next_mode;  // 0 fp32, 1 fp16, 2 fp16 hi at a and lo at ld_in + a (row stride 2 ld_in)
 };
 
 __global__ void ode_stage_kernel(const OdeParams p) {
@@ -123,15 +129,23 @@ __global__ void ode_stage_kernel(const OdeParams p) {
         p.x[o] = nxt;
       }
     }
-    const long long ii = static_cast<long long>(b) * p.ld_in + a;
-    if (p.next_half) static_cast<__half*>(p.next_in)[ii] = to_half_sat(nxt);
-    else static_cast<float*>(p.next_in)[ii] = nxt;
+    if (p.next_mode == 2) {
+      const long long ii = static_cast<long long>(b) * 2 * p.ld_in + a;
+      const __half hi = to_half_sat(nxt);
+      static_cast<__half*>(p.next_in)[ii] = hi;
+      static_cast<__half*>(p.next_in)[ii + p.ld_in] = __float2half_rn(nxt - __half2float(hi));
+    } else {
+      const long long ii = static_cast<long long>(b) * p.ld_in + a;
+      if (p.next_mode == 1) static_cast<__half*>(p.next_in)[ii] = to_half_sat(nxt);
+      else static_cast<float*>(p.next_in)[ii] = nxt;
+    }
   }
   if (p.step_out != nullptr && p.stage == last && blockIdx.x == 0 && threadIdx.x == 0) *p.step_out = *p.step_idx + 1;
 }
 
-// fp32 [B][A] (dense) -> padded fp32 state and padded next-input buffer
-__global__ void load_rows_kernel(const float* src, int B, int A, float* dst, int ld, void* in, int ld_in, int in_half) {
+// fp32 [B][A] (dense) -> padded fp32 state and padded next-input buffer;
+// in_mode as OdeParams::next_mode
+__global__ void load_rows_kernel(const float* src, int B, int A, float* dst, int ld, void* in, int ld_in, int in_mode) {
   const long long total = static_cast<long long>(B) * ld_in;
   for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
        i += static_cast<long long>(gridDim.x) * blockDim.x) {
@@ -139,8 +153,16 @@ __global__ void load_rows_kernel(const float* src, int B, int A, float* dst, int
     const int a = static_cast<int>(i - static_cast<long long>(b) * ld_in);
     const float v = a < A ? src[static_cast<long long>(b) * A + a] : 0.0f;
     if (dst != nullptr && a < ld) dst[static_cast<long long>(b) * ld + a] = v;
-    if (in_half) static_cast<__half*>(in)[i] = to_half_sat(v);
-    else static_cast<float*>(in)[i] = v;
+    if (in_mode == 2) {
+      const long long ii = static_cast<long long>(b) * 2 * ld_in + a;
+      const __half hi = to_half_sat(v);
+      static_cast<__half*>(in)[ii] = hi;
+      static_cast<__half*>(in)[ii + ld_in] = __float2half_rn(v - __half2float(hi));
+    } else if (in_mode == 1) {
+      static_cast<__half*>(in)[i] = to_half_sat(v);
+    } else {
+      static_cast<float*>(in)[i] = v;
+    }
   }
 }
 
@@ -174,9 +196,10 @@ class Flow final : public FlowDevice {
                     float* out, void* stream, std::string& err) noexcept override;
 
  private:
-  bool use_tc(std::size_t batch) const {
-    return tc_ok_ && prec_ == Precision::kBF16 && static_cast<int>(batch) >= kTcMinRows;
-  }
+  bool use_tc(std::size_t batch) const { return tc_ok_ && static_cast<int>(batch) >= kTcMinRows; }
+  // fp32 engines run the tensor-core path on hi / lo fp16 splits
+  bool split() const { return prec_ != Precision::kBF16; }
+  int in_mode(bool tc) const { return tc ? (split() ? 2 : 1) : 0; }
   bool gemm(const Mat& m, const void* in, int in_ld, std::size_t batch, float* out_f32, void* out_half, int out_ld,
             const float* add_vec, const float* add_tok, int act, bool tc, cudaStream_t st, std::string& err);
   bool record_step(std::size_t batch, int method, bool tc, cudaStream_t st, std::string& err);
@@ -251,6 +274,7 @@ bool Flow::load(const TensorTable& t, std::string& err) {
     const int rp = (rows + 127) / 128 * 128;
     const int cp2 = (cols + 63) / 64 * 64;
     plan.add(static_cast<std::size_t>(rp) * cp2 * (bf ? 2 : 4));
+    if (!bf && tc_ok_) plan.add(static_cast<std::size_t>(rp) * cp2 * 3 * 2);
     plan.add_n<SimtSlice>(static_cast<std::size_t>((cp2 + 255) / 256));
   };
   plan_mat(H, static_cast<int>(cfg_.action_dim));
@@ -277,6 +301,21 @@ bool Flow::load(const TensorTable& t, std::string& err) {
     } else {
       m.w = wts_.take(padded.size() * 4);
       cudaMemcpy(m.w, padded.data(), padded.size() * 4, cudaMemcpyHostToDevice);
+      if (tc_ok_) {
+        const std::size_t cp = static_cast<std::size_t>(m.cols_pad);
+        std::vector<std::uint16_t> h3(padded.size() * 3);
+        for (int r = 0; r < m.rows_pad; ++r)
+          for (std::size_t c = 0; c < cp; ++c) {
+            const float v = padded[static_cast<std::size_t>(r) * cp + c];
+            const __half hi = __float2half_rn(v);
+            std::uint16_t* row = &h3[static_cast<std::size_t>(r) * 3 * cp];
+            row[c] = __half_as_ushort(hi);
+            row[cp + c] = __half_as_ushort(hi);
+            row[2 * cp + c] = __half_as_ushort(__float2half_rn(v - __half2float(hi)));
+          }
+        m.w3 = wts_.take(h3.size() * 2);
+        cudaMemcpy(m.w3, h3.data(), h3.size() * 2, cudaMemcpyHostToDevice);
+      }
     }
     std::vector<SimtSlice> sl;
     for (int c = 0; c < m.cols_pad; c += 256) sl.push_back(SimtSlice{0, 0, c, std::min(256, m.cols_pad - c), c});
@@ -371,14 +410,26 @@ bool Flow::gemm(const Mat& m, const void* in, int in_ld, std::size_t batch, floa
   if (tc) {
     TcLaunch l;
     l.fp16 = true;
-    l.A = m.w;
     l.M_rows = m.rows_pad;
-    l.K = m.cols_pad;
-    l.src[0] = TcSource{in, in_ld, 1, static_cast<int>(cap_rows_)};
     l.L = 1;
     l.n_samples = static_cast<int>(batch);
     l.m_valid = m.rows;
-    l.segs = {tc::Seg{0, 0, 0, m.cols_pad / 64, 0}};
+    const int kb = m.cols_pad / 64;
+    if (split()) {
+      l.A = m.w3;
+      l.K = 3 * m.cols_pad;
+      l.src[0] = TcSource{in, 2 * in_ld, 1, static_cast<int>(cap_rows_)};
+      l.segs = {tc::Seg{0, 0, 0, kb, 0}, tc::Seg{0, 0, in_ld, kb, m.cols_pad}, tc::Seg{0, 0, 0, kb, 2 * m.cols_pad}};
+      if (out_f32 == nullptr) {
+        l.out_lo_off = out_ld;
+        out_ld *= 2;
+      }
+    } else {
+      l.A = m.w;
+      l.K = m.cols_pad;
+      l.src[0] = TcSource{in, in_ld, 1, static_cast<int>(cap_rows_)};
+      l.segs = {tc::Seg{0, 0, 0, kb, 0}};
+    }
     l.add_vec = add_vec;
     l.add_tok = add_tok;
     l.add_ld = static_cast<int>(cfg_.hidden);
@@ -454,7 +505,7 @@ bool Flow::record_step(std::size_t batch, int method, bool tc, cudaStream_t st, 
     for (int i = 0; i < 4; ++i) p.k[i] = k_[i];
     p.next_in = xin_;
     p.ld_in = a_pad_;
-    p.next_half = tc ? 1 : 0;
+    p.next_mode = in_mode(tc);
     ode_stage_kernel<<<ew_grid(static_cast<long long>(batch) * A, 256, *ctx_), 256, 0, st>>>(p);
   }
   // step_[0] <- step_[1] (next step index) for the next replay
@@ -487,12 +538,12 @@ bool Flow::prepare(const float* condition, const float* x0, std::size_t batch, b
   }
   // condition -> padded input (fp32 or bf16), then c_emb = W_c cond (flow.cc:256)
   load_rows_kernel<<<ew_grid(static_cast<long long>(batch) * c_pad_, 256, *ctx_), 256, 0, st>>>(
-      dcond, static_cast<int>(batch), C, nullptr, 0, tc ? cin_ : static_cast<void*>(in_cond_), c_pad_, tc ? 1 : 0);
+      dcond, static_cast<int>(batch), C, nullptr, 0, tc ? cin_ : static_cast<void*>(in_cond_), c_pad_, in_mode(tc));
   if (!gemm(cond_, tc ? cin_ : static_cast<void*>(in_cond_), c_pad_, batch, cemb_, nullptr,
             static_cast<int>(cfg_.hidden), nullptr, nullptr, tc::kActNone, tc, st, err))
     return false;
   load_rows_kernel<<<ew_grid(static_cast<long long>(batch) * a_pad_, 256, *ctx_), 256, 0, st>>>(
-      dx, static_cast<int>(batch), A, x_, a_pad_, xin_, a_pad_, tc ? 1 : 0);
+      dx, static_cast<int>(batch), A, x_, a_pad_, xin_, a_pad_, in_mode(tc));
   cudaMemsetAsync(step_, 0, 2 * sizeof(int), st);
   return cudaGetLastError() == cudaSuccess;
 }
@@ -767,7 +818,7 @@ int Flow::sample_static(const float* condition, const float* x0, std::size_t bat
       for (int j = 0; j < 4; ++j) p.k[j] = k[j];
       p.next_in = xin;
       p.ld_in = a_pad_;
-      p.next_half = 0;
+      p.next_mode = 0;
       ode_stage_kernel<<<ew_grid(static_cast<long long>(rows) * A, 256, *ctx_), 256, 0, st>>>(p);
     }
     cudaMemcpyAsync(step, step + 1, sizeof(int), cudaMemcpyDeviceToDevice, st);

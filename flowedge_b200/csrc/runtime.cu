@@ -304,6 +304,13 @@ cudaError_t tc_gemm(const TcLaunch& l, DeviceContext& ctx, cudaStream_t stream, 
   p.out_cs = static_cast<int>(cs);
   p.out_base = static_cast<long long>(l.out_tadd) * l.out_ld + l.out_ch_off;
   p.n_tokens = l.n_samples * l.L;
+  if (l.out_lo_off != 0) {
+    if (!l.fp16 || l.out_f32 || l.gn_fuse || l.stats != nullptr) {
+      err = "tc_gemm: a hi/lo output needs a plain fp16 epilogue";
+      return cudaErrorInvalidValue;
+    }
+    p.out_lo_off = static_cast<int>(l.out_lo_off);
+  }
   p.stats = l.stats;
   p.group_ch = l.group_ch;
   p.groups = l.groups;

@@ -101,6 +101,9 @@ struct TcLaunch {
   void* out = nullptr;
   long long out_ld = 0;
   int out_rps = 1, out_tmul = 1, out_tadd = 0, out_ch_off = 0;
+  // fp16 output only, nonzero: the rounding remainder y - half(y) of each
+  // output element is also stored, out_lo_off elements after it
+  long long out_lo_off = 0;
   double* stats = nullptr;
   int group_ch = 0, groups = 0;
   // GroupNorm + Mish (+ FiLM or residual) applied in the epilogue; `out` is

@@ -82,6 +82,8 @@ struct Params {
   long long out_base;
   int out_cs;
   int n_tokens;           // n_samples * L
+  int out_lo_off;         // fp16 16-bit output only, nonzero: also store the rounding
+                          // remainder y - half(y) at element offset out_lo_off
   // GroupNorm partial statistics (sum, sum of squares) per (sample, group, part)
   double* stats;          // null: no statistics
   int group_ch;           // channels per group (multiple of 32)
@@ -388,9 +390,19 @@ static __global__ void __launch_bounds__(THREADS, 1)
             }
           } else if (p.fp16) {
             __half* o = static_cast<__half*>(p.out) + oc;
+            if (p.out_lo_off != 0) {
 #pragma unroll
-            for (int j = 0; j < CH; ++j)
-              if (c + j < lim) o[j * cs] = to_half_sat(y[j]);
+              for (int j = 0; j < CH; ++j)
+                if (c + j < lim) {
+                  const __half hi = to_half_sat(y[j]);
+                  o[j * cs] = hi;
+                  o[j * cs + p.out_lo_off] = __float2half_rn(y[j] - __half2float(hi));
+                }
+            } else {
+#pragma unroll
+              for (int j = 0; j < CH; ++j)
+                if (c + j < lim) o[j * cs] = to_half_sat(y[j]);
+            }
           } else {
             __nv_bfloat16* o = static_cast<__nv_bfloat16*>(p.out) + oc;
 #pragma unroll

@@ -308,6 +308,30 @@ def test_flow_c2_bf16_batched_tensor_path(tmp_path):
     e.close()
 
 
+def test_flow_c2_fp32_batched_split_tensor_path(tmp_path):
+    """C2 at batch 256 in fp32 mode: tcgen05 GEMMs over fp16 hi / lo splits of
+    weights and activations, against the fp32 restatement (bar 1e-3), and a
+    batch-1 call (CUDA-core fp32 path) against the same rows."""
+    tensors = ck.flow_tensors(ck.FLOW_C2, seed=4)
+    path = tmp_path / "flow_c2_fp32.safetensors"
+    ck.write_checkpoint(path, tensors)
+    rng = np.random.default_rng(4)
+    cond = rng.standard_normal((256, 512)).astype(np.float32)
+    x0 = rng.standard_normal((256, 350)).astype(np.float32)
+    flow = restate.FlowModel(tensors)
+    e = Engine(path, threads=0, device=0, precision="fp32", max_batch=256)
+    for solver, steps in (("euler", 10), ("rk4", 4)):
+        got = e.sample_condition_batch(cond, x0, steps=steps, method=solver)
+        expected = flow.sample(cond, x0, steps, solver)
+        err = float(np.abs(got - expected).max())
+        print(f"C2 flow fp32 batch-256 {solver}-{steps} max-abs vs restatement: {err:.3g}")
+        assert err <= 1e-3
+    got1 = e.sample_condition(cond[5], x0[5], steps=10, method="euler")
+    batch = e.sample_condition_batch(cond, x0, steps=10, method="euler")
+    assert np.abs(got1 - batch[5]).max() <= 1e-3
+    e.close()
+
+
 def _mamba_flow_c3(seed):
     t = ck.mamba_tensors(ck.MAMBA_C3, seed=seed)
     t.update(ck.flow_tensors(ck.FLOW_C2, seed=seed + 1))
