@@ -353,6 +353,12 @@ __device__ __forceinline__ float silu_f(float x) { return x / (1.0f + expf(-x));
 // exponential overflows to inf and the quotient is -0, the limit of silu.
 __device__ __forceinline__ float silu_fast(float x) { return __fdividef(x, 1.0f + __expf(-x)); }
 
+// 2^x by the hardware approximation (MUFU.EX2, flush-to-zero)
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
 __device__ __forceinline__ float softplus_f(float x) { return fmaxf(x, 0.0f) + log1pf(expf(-fabsf(x))); }
 
 __device__ __forceinline__ float half_lo(uint32_t packed) {

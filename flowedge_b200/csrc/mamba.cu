@@ -26,6 +26,7 @@ namespace {
 constexpr int kTcMinTokens = 256;
 constexpr int kMaxState = 16;
 constexpr int kMaxRank = 64;
+constexpr int kMaxConv = 8;  // causal conv width limit (register window)
 
 std::uint16_t bf16_of(float v) {
   std::uint32_t u;
@@ -72,9 +73,63 @@ __global__ void rmsnorm_kernel(const float* in, const float* w, int rows, int di
 }
 
 // u[b][t][c] = SiLU(bias[c] + sum_k w[c][k] * x[b][t - (dc-1) + k][c]), x is the
-// first di columns of xz (row stride 2*di) (kernels_scalar.cc:10-27)
+// first di columns of xz (row stride 2*di) (kernels_scalar.cc:10-27).
+//
+// Many sequences: one thread per (sequence, 4 channels) walks t with the last
+// dc inputs in a register window (float4 loads and stores, each input read
+// once).  The window is right-aligned in kMaxConv slots so every index is a
+// compile-time constant; slots before the first step hold zeros, which the
+// taps that reach before t = 0 multiply (the reference skips them: same sum).
 __global__ void causal_conv_kernel(const float* xz, int B, int L, int di, int dc, const float* w, const float* bias,
                                    float* u, __half* u_bf) {
+  const int q = di >> 2;
+  const long long total = static_cast<long long>(B) * q;
+  const int first = kMaxConv - dc;
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const int b = static_cast<int>(i / q);
+    const int c = static_cast<int>(i - static_cast<long long>(b) * q) * 4;
+    float wk[4][kMaxConv];
+#pragma unroll
+    for (int j = 0; j < kMaxConv; ++j)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) wk[e][j] = j >= first ? w[(c + e) * dc + (j - first)] : 0.0f;
+    const float4 bv = *reinterpret_cast<const float4*>(bias + c);
+    float4 win[kMaxConv];
+#pragma unroll
+    for (int j = 0; j < kMaxConv; ++j) win[j] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    const long long tok0 = static_cast<long long>(b) * L;
+    for (int t = 0; t < L; ++t) {
+#pragma unroll
+      for (int j = 0; j + 1 < kMaxConv; ++j) win[j] = win[j + 1];
+      win[kMaxConv - 1] = *reinterpret_cast<const float4*>(xz + (tok0 + t) * 2 * di + c);
+      float a0 = bv.x, a1 = bv.y, a2 = bv.z, a3 = bv.w;
+#pragma unroll
+      for (int j = 0; j < kMaxConv; ++j)
+        if (j >= first) {
+          a0 += wk[0][j] * win[j].x;
+          a1 += wk[1][j] * win[j].y;
+          a2 += wk[2][j] * win[j].z;
+          a3 += wk[3][j] * win[j].w;
+        }
+      const float4 v = make_float4(silu_f(a0), silu_f(a1), silu_f(a2), silu_f(a3));
+      const long long o = (tok0 + t) * di + c;
+      *reinterpret_cast<float4*>(u + o) = v;
+      if (u_bf != nullptr) {
+        const __half2 lo = __halves2half2(to_half_sat(v.x), to_half_sat(v.y));
+        const __half2 hi = __halves2half2(to_half_sat(v.z), to_half_sat(v.w));
+        uint2 packed;
+        packed.x = *reinterpret_cast<const uint32_t*>(&lo);
+        packed.y = *reinterpret_cast<const uint32_t*>(&hi);
+        *reinterpret_cast<uint2*>(u_bf + o) = packed;
+      }
+    }
+  }
+}
+
+// Few sequences: one thread per (token, channel), the dc inputs re-read
+__global__ void causal_conv_tok_kernel(const float* xz, int B, int L, int di, int dc, const float* w,
+                                       const float* bias, float* u, __half* u_bf) {
   const long long total = static_cast<long long>(B) * L * di;
   for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
        i += static_cast<long long>(gridDim.x) * blockDim.x) {
@@ -97,7 +152,10 @@ __global__ void causal_conv_kernel(const float* xz, int B, int L, int di, int dc
 //   dt = softplus(b_dt[c] + sum_r W_dt[c][r] dbl[t][r])
 //   h_n = exp(dt A_n) h_n + dt B_n u ;  y = (D u + sum_n h_n C_n) * SiLU(z)
 // dbl rows of the block's sequence are staged in shared memory.
-template <int DS, int DR>
+// FAST (the bf16-activation path): exp(dt A) as 2^(dt A log2 e) by the
+// hardware ex2 approximation with A pre-scaled, softplus and the SiLU gate
+// through the fast exp / log intrinsics
+template <int DS, int DR, bool FAST>
 __global__ void __launch_bounds__(256) scan_kernel(const float* dbl, int wd, const float* u, const float* xz, int L,
                                                    int di, const float* dt_w, const float* dt_b, const float* a_neg,
                                                    const float* dsk, float* state, float* y, __half* y_bf) {
@@ -113,7 +171,7 @@ __global__ void __launch_bounds__(256) scan_kernel(const float* dbl, int wd, con
   for (int r = 0; r < DR; ++r) wdt[r] = dt_w[c * DR + r];
 #pragma unroll
   for (int n = 0; n < DS; ++n) {
-    an[n] = a_neg[n * di + c];
+    an[n] = FAST ? a_neg[n * di + c] * 1.4426950408889634f : a_neg[n * di + c];
     h[n] = state != nullptr ? state[(static_cast<long long>(b) * DS + n) * di + c] : 0.0f;
   }
   const float bdt = dt_b[c], dk = dsk[c];
@@ -122,19 +180,20 @@ __global__ void __launch_bounds__(256) scan_kernel(const float* dbl, int wd, con
     float acc = 0.0f;
 #pragma unroll
     for (int r = 0; r < DR; ++r) acc += row[r] * wdt[r];
-    const float dt = softplus_f(acc + bdt);
+    const float pre = acc + bdt;
+    const float dt = FAST ? fmaxf(pre, 0.0f) + __logf(1.0f + __expf(-fabsf(pre))) : softplus_f(pre);
     const long long tok = static_cast<long long>(b) * L + t;
     const float uv = u[tok * di + c];
     float yv = dk * uv;
 #pragma unroll
     for (int n = 0; n < DS; ++n) {
-      const float da = expf(dt * an[n]);
+      const float da = FAST ? ex2_approx(dt * an[n]) : expf(dt * an[n]);
       const float dbu = dt * row[DR + n] * uv;
       h[n] = (da * h[n]) + dbu;
       yv += h[n] * row[DR + DS + n];
     }
     const float zv = xz[tok * 2 * di + di + c];
-    const float out = yv * (zv / (1.0f + expf(-zv)));
+    const float out = yv * (FAST ? silu_fast(zv) : (zv / (1.0f + expf(-zv))));
     y[tok * di + c] = out;
     if (y_bf != nullptr) y_bf[tok * di + c] = to_half_sat(out);
   }
@@ -248,8 +307,9 @@ bool Mamba::load(const TensorTable& t, std::string& err) {
   }
   cfg_.dt_rank = xp0->shape[0] - 2 * cfg_.d_state;
   if (cfg_.d_state > static_cast<std::size_t>(kMaxState) || cfg_.dt_rank > static_cast<std::size_t>(kMaxRank) ||
-      cfg_.d_model % 8 != 0 || cfg_.d_inner % 8 != 0) {
-    err = "Mamba dimensions outside this build's limits (d_state <= 16, dt_rank <= 64)";
+      cfg_.d_model % 8 != 0 || cfg_.d_inner % 8 != 0 || cfg_.d_conv < 1 ||
+      cfg_.d_conv > static_cast<std::size_t>(kMaxConv)) {
+    err = "Mamba dimensions outside this build's limits (d_state <= 16, dt_rank <= 64, d_conv <= 8)";
     return false;
   }
   const std::size_t dm = cfg_.d_model, di = cfg_.d_inner, ds = cfg_.d_state, dc = cfg_.d_conv, dr = cfg_.dt_rank;
@@ -366,9 +426,13 @@ bool Mamba::load(const TensorTable& t, std::string& err) {
     err = "internal error: Mamba weight arena too small";
     return false;
   }
-  cudaFuncSetAttribute(scan_kernel<16, 32>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-  cudaFuncSetAttribute(scan_kernel<8, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-  cudaFuncSetAttribute(scan_kernel<4, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+  for (const void* k : {reinterpret_cast<const void*>(scan_kernel<16, 32, false>),
+                        reinterpret_cast<const void*>(scan_kernel<16, 32, true>),
+                        reinterpret_cast<const void*>(scan_kernel<8, 4, false>),
+                        reinterpret_cast<const void*>(scan_kernel<8, 4, true>),
+                        reinterpret_cast<const void*>(scan_kernel<4, 4, false>),
+                        reinterpret_cast<const void*>(scan_kernel<4, 4, true>)})
+    cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
   if (cudaDeviceSynchronize() != cudaSuccess) {
     err = "Mamba weight upload failed";
     return false;
@@ -518,21 +582,26 @@ bool Mamba::run_layers(long long n_tok, int B, int L, bool tc, cudaStream_t st, 
                                                                                       tc ? nb_ : nullptr);
     if (!gemm(Ly.in_proj, tc ? static_cast<const void*>(nb_) : normed, dm, n_tok, xz_, 2 * di, false, tc, st, err))
       return false;
-    causal_conv_kernel<<<ew_grid(n_tok * di, 256, *ctx_), 256, 0, st>>>(xz_, B, L, di, dc, Ly.conv_w, Ly.conv_b, u_,
-                                                                        tc ? ub_ : nullptr);
+    if (static_cast<long long>(B) * (di / 4) >= 32LL * 32 * ctx_->sm_count)
+      causal_conv_kernel<<<ew_grid(static_cast<long long>(B) * (di / 4), 256, *ctx_), 256, 0, st>>>(
+          xz_, B, L, di, dc, Ly.conv_w, Ly.conv_b, u_, tc ? ub_ : nullptr);
+    else
+      causal_conv_tok_kernel<<<ew_grid(n_tok * di, 256, *ctx_), 256, 0, st>>>(xz_, B, L, di, dc, Ly.conv_w, Ly.conv_b,
+                                                                            u_, tc ? ub_ : nullptr);
     if (!gemm(Ly.x_proj, tc ? static_cast<const void*>(ub_) : u_, di, n_tok, dbl_, wd, false, tc, st, err))
       return false;
     const dim3 grid(static_cast<unsigned>((di + 255) / 256), static_cast<unsigned>(B));
     const std::size_t smem = static_cast<std::size_t>(L) * wd * 4;
+    auto scan = [&](auto kernel) {
+      kernel<<<grid, 256, smem, st>>>(dbl_, wd, u_, xz_, L, di, Ly.dt_w, Ly.dt_b, Ly.a_neg, Ly.d, nullptr, y_,
+                                      tc ? yb_ : nullptr);
+    };
     if (ds == 16 && dr == 32)
-      scan_kernel<16, 32><<<grid, 256, smem, st>>>(dbl_, wd, u_, xz_, L, di, Ly.dt_w, Ly.dt_b, Ly.a_neg, Ly.d, nullptr,
-                                                   y_, tc ? yb_ : nullptr);
+      tc ? scan(scan_kernel<16, 32, true>) : scan(scan_kernel<16, 32, false>);
     else if (ds == 4 && dr == 4)
-      scan_kernel<4, 4><<<grid, 256, smem, st>>>(dbl_, wd, u_, xz_, L, di, Ly.dt_w, Ly.dt_b, Ly.a_neg, Ly.d, nullptr, y_,
-                                                 tc ? yb_ : nullptr);
+      tc ? scan(scan_kernel<4, 4, true>) : scan(scan_kernel<4, 4, false>);
     else if (ds == 8 && dr == 4)
-      scan_kernel<8, 4><<<grid, 256, smem, st>>>(dbl_, wd, u_, xz_, L, di, Ly.dt_w, Ly.dt_b, Ly.a_neg, Ly.d, nullptr, y_,
-                                                 tc ? yb_ : nullptr);
+      tc ? scan(scan_kernel<8, 4, true>) : scan(scan_kernel<8, 4, false>);
     else {
       err = "no scan instantiation for this (d_state, dt_rank)";
       return false;
@@ -619,11 +688,11 @@ int Mamba::step(std::int32_t token, float* out, std::string& err) noexcept {
     const dim3 grid(static_cast<unsigned>((di + 255) / 256), 1);
     const std::size_t smem = static_cast<std::size_t>(wd) * 4;
     if (ds == 16 && dr == 32)
-      scan_kernel<16, 32><<<grid, 256, smem, st>>>(dbl, wd, u, xz, 1, di, Ly.dt_w, Ly.dt_b, Ly.a_neg, Ly.d, h, y, nullptr);
+      scan_kernel<16, 32, false><<<grid, 256, smem, st>>>(dbl, wd, u, xz, 1, di, Ly.dt_w, Ly.dt_b, Ly.a_neg, Ly.d, h, y, nullptr);
     else if (ds == 4 && dr == 4)
-      scan_kernel<4, 4><<<grid, 256, smem, st>>>(dbl, wd, u, xz, 1, di, Ly.dt_w, Ly.dt_b, Ly.a_neg, Ly.d, h, y, nullptr);
+      scan_kernel<4, 4, false><<<grid, 256, smem, st>>>(dbl, wd, u, xz, 1, di, Ly.dt_w, Ly.dt_b, Ly.a_neg, Ly.d, h, y, nullptr);
     else if (ds == 8 && dr == 4)
-      scan_kernel<8, 4><<<grid, 256, smem, st>>>(dbl, wd, u, xz, 1, di, Ly.dt_w, Ly.dt_b, Ly.a_neg, Ly.d, h, y, nullptr);
+      scan_kernel<8, 4, false><<<grid, 256, smem, st>>>(dbl, wd, u, xz, 1, di, Ly.dt_w, Ly.dt_b, Ly.a_neg, Ly.d, h, y, nullptr);
     else {
       err = "no scan instantiation for this (d_state, dt_rank)";
       return 2;
