@@ -43,6 +43,11 @@ __all__ = [
     "BIMANUAL",
     "FLOW_C2",
     "MAMBA_C3",
+    "SmolVLASpec",
+    "smolvla_tensors",
+    "smolvla_prefix",
+    "SMOLVLA_C5",
+    "SMOLVLA_REF",
 ]
 
 
@@ -162,6 +167,49 @@ class MambaSpec:
     dt_rank: int = 32
     dt_init: float = 0.01
 
+
+@dataclass(frozen=True)
+class SmolVLASpec:
+    """SmolVLA-shaped flow action expert (the reference's
+    src/core/models/smolvla/smolvla_action_expert.cc:70-208 tensor set).
+
+    `cache_width` is the width of the caller's per-layer prefix K / V cache:
+    cross-attention layers project it (k_proj / v_proj take `cache_width`
+    inputs) and self-attention layers attend over it directly when it equals
+    `kv_heads * head_width` (the reference's layout), else over the action
+    tokens only.
+    """
+
+    expert_width: int = 720
+    layers: int = 16
+    heads: int = 12
+    kv_heads: int = 4
+    head_width: int = 60
+    mlp_width: int = 2048
+    action_dim: int = 32
+    chunk: int = 50
+    state_dim: int = 32
+    vlm_width: int = 960
+    cache_width: int = 960
+    prefix: int = 241
+
+    @property
+    def attention_width(self) -> int:
+        return self.heads * self.head_width
+
+    @property
+    def kv_width(self) -> int:
+        return self.kv_heads * self.head_width
+
+
+# BASELINE config 5: 16 layers, width 720, 12 heads of 60, SwiGLU 2048, 50
+# action tokens of dim 32, a 241-token prefix of width 960 projected per
+# cross-attention layer (3:1 grouped-query attention, 4 K / V heads).
+SMOLVLA_C5 = SmolVLASpec()
+# The shapes the reference's loader accepts (smolvla_action_expert.cc:120-128:
+# attention 960 = 15 x 64, K / V 320 = 5 x 64, MLP 2048, cache width 320).
+SMOLVLA_REF = SmolVLASpec(expert_width=720, layers=4, heads=15, kv_heads=5, head_width=64, mlp_width=2048,
+                          action_dim=32, chunk=10, state_dim=32, vlm_width=960, cache_width=320, prefix=24)
 
 # BASELINE config 1: PushT-shaped U-Net (A 2, H 16, cond 132).
 PUSHT = DiffusionSpec(action_dim=2, horizon=16, condition_dim=132)
@@ -314,6 +362,63 @@ def mamba_tensors(spec: MambaSpec, seed: int = 0) -> dict:
         out[p + "mixer.out_proj.weight"] = init.uniform((dm, di), di)
     out["backbone.norm_f.weight"] = np.ones(dm, np.float32)
     return out
+
+
+def smolvla_tensors(spec: SmolVLASpec, seed: int = 0) -> dict:
+    """Random-init SmolVLA action expert (names and shapes of
+    smolvla_action_expert.cc:70-180; Linear weights and biases PyTorch-default
+    uniform, RMSNorm weights 1).  The matrices are rounded to bf16 values (the
+    expert's source dtype); biases stay f32, as the reference loader requires
+    (smolvla_action_expert.cc:98-105).  `flowedge.smolvla.head_width` records
+    the head width, which the reference fixes at 64 and this build reads."""
+    init = _Init(seed)
+    w, a = spec.expert_width, spec.action_dim
+
+    def lin(rows, cols):
+        return bf16_bits_to_f32(to_bf16_bits(init.uniform((rows, cols), cols)))
+
+    out = {
+        "model.action_in_proj.weight": lin(w, a),
+        "model.action_in_proj.bias": init.uniform((w,), a),
+        "model.action_out_proj.weight": lin(a, w),
+        "model.action_out_proj.bias": init.uniform((a,), w),
+        "model.action_time_mlp_in.weight": lin(w, 2 * w),
+        "model.action_time_mlp_in.bias": init.uniform((w,), 2 * w),
+        "model.action_time_mlp_out.weight": lin(w, w),
+        "model.action_time_mlp_out.bias": init.uniform((w,), w),
+        "model.state_proj.weight": lin(spec.vlm_width, spec.state_dim),
+        "model.state_proj.bias": init.uniform((spec.vlm_width,), spec.state_dim),
+        "model.vlm_with_expert.lm_expert.norm.weight": np.ones(w, np.float32),
+        "flowedge.smolvla.head_width": np.array([spec.head_width], np.float32),
+    }
+    for layer in range(spec.layers):
+        p = f"model.vlm_with_expert.lm_expert.layers.{layer}."
+        kv_in = spec.cache_width if layer % 2 == 1 else w
+        out[p + "input_layernorm.weight"] = np.ones(w, np.float32)
+        out[p + "post_attention_layernorm.weight"] = np.ones(w, np.float32)
+        out[p + "self_attn.q_proj.weight"] = lin(spec.attention_width, w)
+        out[p + "self_attn.k_proj.weight"] = lin(spec.kv_width, kv_in)
+        out[p + "self_attn.v_proj.weight"] = lin(spec.kv_width, kv_in)
+        out[p + "self_attn.o_proj.weight"] = lin(w, spec.attention_width)
+        out[p + "mlp.gate_proj.weight"] = lin(spec.mlp_width, w)
+        out[p + "mlp.up_proj.weight"] = lin(spec.mlp_width, w)
+        out[p + "mlp.down_proj.weight"] = lin(w, spec.mlp_width)
+    return out
+
+
+def smolvla_prefix(spec: SmolVLASpec, seed: int = 0, batch: int | None = None, masked: int = 0):
+    """Synthetic VLM prefix cache: keys and values [layers][prefix][cache_width]
+    (with a leading batch axis when `batch` is given), bf16-valued ~N(0, 1),
+    and a validity mask with the last `masked` slots padded."""
+    rng = np.random.default_rng(seed)
+    lead = () if batch is None else (batch,)
+    shape = lead + (spec.layers, spec.prefix, spec.cache_width)
+    keys = bf16_bits_to_f32(to_bf16_bits(rng.standard_normal(shape, dtype=np.float32)))
+    values = bf16_bits_to_f32(to_bf16_bits(rng.standard_normal(shape, dtype=np.float32)))
+    mask = np.ones(lead + (spec.prefix,), np.uint8)
+    if masked:
+        mask[..., spec.prefix - masked:] = 0
+    return keys, values, mask
 
 
 def cast_tensors(tensors: dict, matrices: str = "f32", convs: str = "f32") -> dict:

@@ -143,4 +143,41 @@ class MambaDevice {
 std::unique_ptr<MambaDevice> make_mamba_device(const TensorTable& tensors, std::shared_ptr<DeviceContext> ctx,
                                                Precision precision, std::string& err);
 
+struct SmolVLAConfig {
+  std::size_t expert_width{}, action_dim{}, vlm_width{}, state_dim{}, layers{};
+  std::size_t heads{}, kv_heads{}, head_width{}, mlp_width{}, cache_width{};
+};
+
+// SmolVLA-shaped flow action expert (smolvla_action_expert.h:31-124).  The
+// batch-one entries mirror the reference's; sample() also takes a batch of
+// independent chunks with per-sample or shared prefix caches.
+class SmolVLADevice {
+ public:
+  virtual ~SmolVLADevice() = default;
+  [[nodiscard]] virtual const SmolVLAConfig& config() const noexcept = 0;
+  // Host buffers, synchronous.  Return 0, or the reference runtime's codes:
+  // 1 for sizes outside the limits, 3 when the expert could not run (an
+  // invalid mask), 2 for device failures.
+  virtual int embed_suffix(const float* noisy, std::size_t chunk, float timestep, float* out,
+                           std::string& err) noexcept = 0;
+  virtual int run_expert(const float* suffix, std::size_t chunk, const float* keys, const float* values,
+                         const std::uint8_t* mask, std::size_t prefix, float* out, std::string& err) noexcept = 0;
+  virtual int project_actions(const float* hidden, std::size_t chunk, float* out, std::string& err) noexcept = 0;
+  virtual int denoise(const float* noisy, std::size_t chunk, float timestep, const float* keys, const float* values,
+                      const std::uint8_t* mask, std::size_t prefix, float* out, std::string& err) noexcept = 0;
+  // noise / out [batch][chunk][action_dim]; keys / values [batch or 1][layers][prefix][cache_width];
+  // mask [batch or 1][prefix] (1 = shared_prefix).  `on_device`: every pointer is a device
+  // pointer and the work is enqueued on `stream` without a final synchronisation.
+  virtual int sample(const float* noise, std::size_t batch, std::size_t chunk, std::size_t steps, const float* keys,
+                     const float* values, const std::uint8_t* mask, std::size_t prefix, bool shared_prefix,
+                     float* out, bool on_device, void* stream, std::string& err) noexcept = 0;
+  // Workspace for `batch` chunks of `chunk` tokens and prefixes of `prefix` slots.
+  virtual int reserve(std::size_t batch, std::size_t chunk, std::size_t prefix, bool shared_prefix,
+                      std::string& err) noexcept = 0;
+  [[nodiscard]] virtual std::uint64_t kernel_launches() const noexcept = 0;
+};
+
+std::unique_ptr<SmolVLADevice> make_smolvla_device(const TensorTable& tensors, std::shared_ptr<DeviceContext> ctx,
+                                                   std::string& err);
+
 }  // namespace feb

@@ -104,6 +104,7 @@ struct FeEngine {
   std::unique_ptr<feb::UnetDevice> unet;
   std::unique_ptr<feb::FlowDevice> flow;
   std::unique_ptr<feb::MambaDevice> mamba;
+  std::unique_ptr<feb::SmolVLADevice> smolvla;
   unsigned threads = 0;
   std::uint32_t architecture = FE_ARCH_UNKNOWN;
   std::uint64_t d_model = 0, n_layers = 0, d_inner = 0, d_state = 0, d_conv = 0;
@@ -178,6 +179,14 @@ fe_engine* create_engine(std::shared_ptr<const feb::ModelWeights> weights, const
         return nullptr;
       }
     }
+    // engine_runtime.cc:76-83: a SmolVLA expert is recognised by its action / state projections
+    if (t.find("model.action_in_proj.weight") != nullptr && t.find("model.state_proj.weight") != nullptr) {
+      engine->smolvla = feb::make_smolvla_device(t, engine->ctx, err);
+      if (!engine->smolvla) {
+        set_error("SmolVLA action expert failed to load: " + err);
+        return nullptr;
+      }
+    }
     if (t.find("backbone.embeddings.weight") != nullptr) {
       engine->mamba = feb::make_mamba_device(t, engine->ctx, precision, err);
       if (!engine->mamba) {
@@ -185,10 +194,11 @@ fe_engine* create_engine(std::shared_ptr<const feb::ModelWeights> weights, const
         return nullptr;
       }
     }
-    // architecture (engine_runtime.cc:167-176, Transformer / SmolVLA not built)
+    // architecture (engine_runtime.cc:167-176, Transformer not built)
     engine->architecture = engine->unet               ? FE_ARCH_DIFFUSION_HEAD
                            : engine->mamba && engine->flow ? FE_ARCH_MAMBA_FLOW
                            : engine->mamba            ? FE_ARCH_MAMBA
+                           : engine->smolvla          ? FE_ARCH_SMOLVLA_ACTION_EXPERT
                            : engine->flow             ? FE_ARCH_FLOW_HEAD
                                                       : FE_ARCH_UNKNOWN;
     if (engine->architecture == FE_ARCH_UNKNOWN) {
@@ -214,6 +224,14 @@ fe_engine* create_engine(std::shared_ptr<const feb::ModelWeights> weights, const
         set_error("Flow workspace: " + err);
         return nullptr;
       }
+    }
+    if (engine->smolvla) {
+      // engine_runtime.cc:192-198
+      const auto& c = engine->smolvla->config();
+      engine->d_model = c.vlm_width;
+      engine->n_layers = c.layers;
+      engine->d_inner = c.expert_width;
+      engine->action_dim = c.action_dim;
     }
     if (engine->unet) {
       engine->action_dim = engine->unet->config().action_dim;
@@ -501,7 +519,8 @@ size_t fe_engine_action_dim(const fe_engine* engine) { return engine != nullptr 
 size_t fe_engine_action_horizon(const fe_engine* engine) {
   if (engine == nullptr) return 0;
   if (engine->unet) return engine->unet->config().horizon;
-  return engine->flow ? 1 : 0;
+  if (engine->flow) return 1;
+  return engine->smolvla ? 50 : 0;  // engine_runtime.cc:322-327
 }
 
 size_t fe_engine_condition_dim(const fe_engine* engine) { return engine != nullptr ? engine->condition_dim : 0; }
@@ -1095,8 +1114,14 @@ int fe_engine_smolvla_embed_suffix(fe_engine* engine, const float* noisy_actions
     set_error("Invalid arguments to fe_engine_smolvla_embed_suffix");
     return FE_STATUS_INVALID_ARGUMENT;
   }
-  set_error("Model has no SmolVLA action-expert projection boundary");
-  return FE_STATUS_UNSUPPORTED_MODEL;
+  if (!engine->smolvla) {
+    set_error("Model has no SmolVLA action-expert projection boundary");
+    return FE_STATUS_UNSUPPORTED_MODEL;
+  }
+  std::string err;
+  const int rc = engine->smolvla->embed_suffix(noisy_actions, chunk_size, timestep, out, err);
+  if (rc != 0) set_error(err);
+  return rc;
 }
 
 int fe_engine_smolvla_run_expert(fe_engine* engine, const float* suffix, size_t chunk_size,
@@ -1108,8 +1133,15 @@ int fe_engine_smolvla_run_expert(fe_engine* engine, const float* suffix, size_t 
     set_error("Invalid arguments to fe_engine_smolvla_run_expert");
     return FE_STATUS_INVALID_ARGUMENT;
   }
-  set_error("Model has no SmolVLA action expert");
-  return FE_STATUS_UNSUPPORTED_MODEL;
+  if (!engine->smolvla) {
+    set_error("Model has no SmolVLA action expert");
+    return FE_STATUS_UNSUPPORTED_MODEL;
+  }
+  std::string err;
+  const int rc = engine->smolvla->run_expert(suffix, chunk_size, prefix_keys, prefix_values, prefix_mask,
+                                             prefix_length, out, err);
+  if (rc != 0) set_error(err);
+  return rc;
 }
 
 int fe_engine_smolvla_project_actions(fe_engine* engine, const float* hidden, size_t chunk_size, float* out) {
@@ -1118,8 +1150,14 @@ int fe_engine_smolvla_project_actions(fe_engine* engine, const float* hidden, si
     set_error("Invalid arguments to fe_engine_smolvla_project_actions");
     return FE_STATUS_INVALID_ARGUMENT;
   }
-  set_error("Model has no SmolVLA action expert");
-  return FE_STATUS_UNSUPPORTED_MODEL;
+  if (!engine->smolvla) {
+    set_error("Model has no SmolVLA action expert");
+    return FE_STATUS_UNSUPPORTED_MODEL;
+  }
+  std::string err;
+  const int rc = engine->smolvla->project_actions(hidden, chunk_size, out, err);
+  if (rc != 0) set_error(err);
+  return rc;
 }
 
 int fe_engine_smolvla_denoise(fe_engine* engine, const float* noisy_actions, size_t chunk_size, float timestep,
@@ -1132,8 +1170,15 @@ int fe_engine_smolvla_denoise(fe_engine* engine, const float* noisy_actions, siz
     set_error("Invalid arguments to fe_engine_smolvla_denoise");
     return FE_STATUS_INVALID_ARGUMENT;
   }
-  set_error("Model has no SmolVLA action expert");
-  return FE_STATUS_UNSUPPORTED_MODEL;
+  if (!engine->smolvla) {
+    set_error("Model has no SmolVLA action expert");
+    return FE_STATUS_UNSUPPORTED_MODEL;
+  }
+  std::string err;
+  const int rc = engine->smolvla->denoise(noisy_actions, chunk_size, timestep, prefix_keys, prefix_values,
+                                          prefix_mask, prefix_length, out, err);
+  if (rc != 0) set_error(err);
+  return rc;
 }
 
 int fe_engine_smolvla_sample(fe_engine* engine, const float* initial_noise, size_t chunk_size, size_t steps,
@@ -1145,8 +1190,78 @@ int fe_engine_smolvla_sample(fe_engine* engine, const float* initial_noise, size
     set_error("Invalid arguments to fe_engine_smolvla_sample");
     return FE_STATUS_INVALID_ARGUMENT;
   }
-  set_error("Model has no SmolVLA action expert");
-  return FE_STATUS_UNSUPPORTED_MODEL;
+  if (!engine->smolvla) {
+    set_error("Model has no SmolVLA action expert");
+    return FE_STATUS_UNSUPPORTED_MODEL;
+  }
+  std::string err;
+  // `out` may alias `initial_noise` (engine.h:187-193): the noise is copied to the device first
+  const int rc = engine->smolvla->sample(initial_noise, 1, chunk_size, steps, prefix_keys, prefix_values,
+                                         prefix_mask, prefix_length, true, out, false, nullptr, err);
+  if (rc != 0) set_error(err);
+  return rc;
+}
+
+int fe_engine_smolvla_sample_batch(fe_engine* engine, const float* initial_noise, size_t batch, size_t chunk_size,
+                                   size_t steps, const float* prefix_keys, const float* prefix_values,
+                                   const uint8_t* prefix_mask, size_t prefix_length, int shared_prefix, float* out) {
+  clear_error();
+  if (engine == nullptr || initial_noise == nullptr || batch == 0 || chunk_size == 0 || steps == 0 ||
+      prefix_keys == nullptr || prefix_values == nullptr || prefix_mask == nullptr || prefix_length == 0 ||
+      out == nullptr) {
+    set_error("Invalid arguments to fe_engine_smolvla_sample_batch");
+    return FE_STATUS_INVALID_ARGUMENT;
+  }
+  if (!engine->smolvla) {
+    set_error("Model has no SmolVLA action expert");
+    return FE_STATUS_UNSUPPORTED_MODEL;
+  }
+  std::string err;
+  const int rc = engine->smolvla->sample(initial_noise, batch, chunk_size, steps, prefix_keys, prefix_values,
+                                         prefix_mask, prefix_length, shared_prefix != 0, out, false, nullptr, err);
+  if (rc != 0) set_error(err);
+  return rc;
+}
+
+int fe_engine_smolvla_sample_device(fe_engine* engine, const float* initial_noise, size_t batch, size_t chunk_size,
+                                    size_t steps, const float* prefix_keys, const float* prefix_values,
+                                    const uint8_t* prefix_mask, size_t prefix_length, int shared_prefix, float* out,
+                                    void* stream) {
+  clear_error();
+  if (engine == nullptr || initial_noise == nullptr || batch == 0 || chunk_size == 0 || steps == 0 ||
+      prefix_keys == nullptr || prefix_values == nullptr || prefix_mask == nullptr || prefix_length == 0 ||
+      out == nullptr) {
+    set_error("Invalid arguments to fe_engine_smolvla_sample_device");
+    return FE_STATUS_INVALID_ARGUMENT;
+  }
+  if (!engine->smolvla) {
+    set_error("Model has no SmolVLA action expert");
+    return FE_STATUS_UNSUPPORTED_MODEL;
+  }
+  std::string err;
+  const int rc = engine->smolvla->sample(initial_noise, batch, chunk_size, steps, prefix_keys, prefix_values,
+                                         prefix_mask, prefix_length, shared_prefix != 0, out, true, stream, err);
+  if (rc != 0) set_error(err);
+  return rc;
+}
+
+int fe_engine_smolvla_reserve(fe_engine* engine, size_t batch, size_t chunk_size, size_t prefix_length,
+                              int shared_prefix) {
+  clear_error();
+  if (engine == nullptr || batch == 0 || chunk_size == 0 || prefix_length == 0) {
+    set_error("Invalid arguments to fe_engine_smolvla_reserve");
+    return FE_STATUS_INVALID_ARGUMENT;
+  }
+  if (!engine->smolvla) {
+    set_error("Model has no SmolVLA action expert");
+    return FE_STATUS_UNSUPPORTED_MODEL;
+  }
+  std::string err;
+  if (engine->smolvla->reserve(batch, chunk_size, prefix_length, shared_prefix != 0, err) != 0) {
+    set_error("SmolVLA workspace: " + err);
+    return FE_STATUS_RESOURCE_EXHAUSTED;
+  }
+  return FE_STATUS_OK;
 }
 
 // ---- counters ---------------------------------------------------------------------
@@ -1184,7 +1299,9 @@ int fe_engine_synchronize(fe_engine* engine) {
 }
 
 uint64_t fe_engine_kernel_launches(const fe_engine* engine) {
-  return engine != nullptr && engine->unet ? engine->unet->kernel_launches() : 0;
+  if (engine == nullptr) return 0;
+  return (engine->unet ? engine->unet->kernel_launches() : 0) +
+         (engine->smolvla ? engine->smolvla->kernel_launches() : 0);
 }
 
 }  // extern "C"

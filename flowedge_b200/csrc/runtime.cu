@@ -311,6 +311,13 @@ cudaError_t tc_gemm(const TcLaunch& l, DeviceContext& ctx, cudaStream_t stream, 
     }
     p.out_lo_off = static_cast<int>(l.out_lo_off);
   }
+  if (l.out_bf16) {
+    if (l.out_f32 || l.gn_fuse || l.stats != nullptr || l.out_lo_off != 0) {
+      err = "tc_gemm: a bf16 output needs a plain 16-bit epilogue";
+      return cudaErrorInvalidValue;
+    }
+    p.out_bf16 = 1;
+  }
   p.stats = l.stats;
   p.group_ch = l.group_ch;
   p.groups = l.groups;

@@ -104,6 +104,8 @@ struct TcLaunch {
   // fp16 output only, nonzero: the rounding remainder y - half(y) of each
   // output element is also stored, out_lo_off elements after it
   long long out_lo_off = 0;
+  // plain epilogue with fp16 operands: store the 16-bit output as bf16
+  bool out_bf16 = false;
   double* stats = nullptr;
   int group_ch = 0, groups = 0;
   // GroupNorm + Mish (+ FiLM or residual) applied in the epilogue; `out` is

@@ -82,6 +82,7 @@ struct Params {
   long long out_base;
   int out_cs;
   int n_tokens;           // n_samples * L
+  int out_bf16;           // 16-bit output as bf16 even with fp16 operands
   int out_lo_off;         // fp16 16-bit output only, nonzero: also store the rounding
                           // remainder y - half(y) at element offset out_lo_off
   // GroupNorm partial statistics (sum, sum of squares) per (sample, group, part)
@@ -388,7 +389,7 @@ static __global__ void __launch_bounds__(THREADS, 1)
               for (int j = 0; j < CH; ++j)
                 if (c + j < lim) o[j * cs] = y[j];
             }
-          } else if (p.fp16) {
+          } else if (p.fp16 && !p.out_bf16) {
             __half* o = static_cast<__half*>(p.out) + oc;
             if (p.out_lo_off != 0) {
 #pragma unroll

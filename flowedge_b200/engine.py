@@ -24,6 +24,7 @@ LIB_PATH = Path(__file__).resolve().parent / "libflowedge_b200.so"
 _f32p = C.POINTER(C.c_float)
 _i32p = C.POINTER(C.c_int32)
 _size_p = C.POINTER(C.c_size_t)
+_u8p = C.POINTER(C.c_uint8)
 
 SOLVERS = {"euler": 0, "heun": 1, "rk4": 2}
 SCHEDULERS = {"ddim": 0, "ddpm": 1}
@@ -112,6 +113,14 @@ SIGNATURES = {
     "fe_engine_export_decode_state": (C.c_int, [C.c_void_p, C.c_void_p, C.c_size_t]),
     "fe_engine_import_decode_state": (C.c_int, [C.c_void_p, C.c_void_p, C.c_size_t]),
     "fe_engine_free": (None, [C.c_void_p]),
+    "fe_engine_smolvla_embed_suffix": (C.c_int, [C.c_void_p, _f32p, C.c_size_t, C.c_float, _f32p]),
+    "fe_engine_smolvla_run_expert": (C.c_int, [C.c_void_p, _f32p, C.c_size_t, _f32p, _f32p, _u8p, C.c_size_t,
+                                               _f32p]),
+    "fe_engine_smolvla_project_actions": (C.c_int, [C.c_void_p, _f32p, C.c_size_t, _f32p]),
+    "fe_engine_smolvla_denoise": (C.c_int, [C.c_void_p, _f32p, C.c_size_t, C.c_float, _f32p, _f32p, _u8p,
+                                            C.c_size_t, _f32p]),
+    "fe_engine_smolvla_sample": (C.c_int, [C.c_void_p, _f32p, C.c_size_t, C.c_size_t, _f32p, _f32p, _u8p,
+                                           C.c_size_t, _f32p]),
     # extensions
     "fe_engine_load_with_options": (C.c_void_p, [C.c_char_p, C.POINTER(EngineOptions)]),
     "fe_engine_create_from_weights_with_options": (C.c_void_p, [C.c_void_p, C.POINTER(EngineOptions)]),
@@ -130,6 +139,12 @@ SIGNATURES = {
     "fe_engine_run_batch": (C.c_int, [C.c_void_p, _i32p, C.c_size_t, C.c_size_t, _f32p]),
     "fe_engine_sample_batch": (C.c_int, [C.c_void_p, _i32p, C.c_size_t, C.c_size_t, _f32p, C.c_size_t, C.c_int,
                                          _f32p]),
+    "fe_engine_smolvla_sample_batch": (C.c_int, [C.c_void_p, _f32p, C.c_size_t, C.c_size_t, C.c_size_t, _f32p,
+                                                 _f32p, _u8p, C.c_size_t, C.c_int, _f32p]),
+    "fe_engine_smolvla_sample_device": (C.c_int, [C.c_void_p, C.c_void_p, C.c_size_t, C.c_size_t, C.c_size_t,
+                                                  C.c_void_p, C.c_void_p, C.c_void_p, C.c_size_t, C.c_int,
+                                                  C.c_void_p, C.c_void_p]),
+    "fe_engine_smolvla_reserve": (C.c_int, [C.c_void_p, C.c_size_t, C.c_size_t, C.c_size_t, C.c_int]),
     "fe_engine_synchronize": (C.c_int, [C.c_void_p]),
     "fe_engine_profile_diffusion": (C.c_int, [C.c_void_p, C.c_size_t, C.POINTER(C.c_double)]),
     "fe_device_malloc_count": (C.c_uint64, []),
@@ -383,6 +398,69 @@ class Engine:
 
     def reset(self):
         self.lib.fe_engine_reset(self.handle)
+
+    # ---- SmolVLA action expert (engine.h:136-196); prefix caches [layers][prefix][cache_width]
+    @staticmethod
+    def _u8(a):
+        return a.ctypes.data_as(_u8p)
+
+    def smolvla_embed_suffix(self, noisy, timestep: float, width: int):
+        x = _f32(noisy)
+        out = np.empty((x.shape[0], width), np.float32)
+        self._check(self.lib.fe_engine_smolvla_embed_suffix(self.handle, _p(x), x.shape[0], float(timestep),
+                                                            _p(out)))
+        return out
+
+    def smolvla_run_expert(self, suffix, keys, values, mask):
+        x, k, v = _f32(suffix), _f32(keys), _f32(values)
+        m = np.ascontiguousarray(mask, np.uint8)
+        out = np.empty_like(x)
+        self._check(self.lib.fe_engine_smolvla_run_expert(self.handle, _p(x), x.shape[0], _p(k), _p(v), self._u8(m),
+                                                          m.size, _p(out)))
+        return out
+
+    def smolvla_project_actions(self, hidden):
+        x = _f32(hidden)
+        out = np.empty((x.shape[0], self.action_dim), np.float32)
+        self._check(self.lib.fe_engine_smolvla_project_actions(self.handle, _p(x), x.shape[0], _p(out)))
+        return out
+
+    def smolvla_denoise(self, noisy, timestep: float, keys, values, mask):
+        x, k, v = _f32(noisy), _f32(keys), _f32(values)
+        m = np.ascontiguousarray(mask, np.uint8)
+        out = np.empty_like(x)
+        self._check(self.lib.fe_engine_smolvla_denoise(self.handle, _p(x), x.shape[0], float(timestep), _p(k), _p(v),
+                                                       self._u8(m), m.size, _p(out)))
+        return out
+
+    def smolvla_sample(self, noise, steps: int, keys, values, mask):
+        x, k, v = _f32(noise), _f32(keys), _f32(values)
+        m = np.ascontiguousarray(mask, np.uint8)
+        out = np.empty_like(x)
+        self._check(self.lib.fe_engine_smolvla_sample(self.handle, _p(x), x.shape[0], steps, _p(k), _p(v),
+                                                      self._u8(m), m.size, _p(out)))
+        return out
+
+    def smolvla_sample_batch(self, noise, steps: int, keys, values, mask, shared_prefix: bool = False):
+        """noise [batch][chunk][A]; keys / values [batch][layers][prefix][cache_width] and mask
+        [batch][prefix], or a single prefix ([layers][prefix][cache_width], [prefix]) when shared."""
+        x, k, v = _f32(noise), _f32(keys), _f32(values)
+        m = np.ascontiguousarray(mask, np.uint8)
+        out = np.empty_like(x)
+        self._check(self.lib.fe_engine_smolvla_sample_batch(self.handle, _p(x), x.shape[0], x.shape[1], steps, _p(k),
+                                                            _p(v), self._u8(m), m.shape[-1], int(shared_prefix),
+                                                            _p(out)))
+        return out
+
+    def smolvla_sample_device(self, noise_ptr: int, batch: int, chunk: int, steps: int, keys_ptr: int,
+                              values_ptr: int, mask_ptr: int, prefix: int, shared_prefix: bool, out_ptr: int,
+                              stream: int = 0):
+        self._check(self.lib.fe_engine_smolvla_sample_device(self.handle, noise_ptr, batch, chunk, steps, keys_ptr,
+                                                             values_ptr, mask_ptr, prefix, int(shared_prefix),
+                                                             out_ptr, stream or None))
+
+    def smolvla_reserve(self, batch: int, chunk: int, prefix: int, shared_prefix: bool = False):
+        self._check(self.lib.fe_engine_smolvla_reserve(self.handle, batch, chunk, prefix, int(shared_prefix)))
 
     def decode_state(self) -> bytes:
         size = self.lib.fe_engine_decode_state_bytes(self.handle)

@@ -189,20 +189,23 @@ int fe_engine_run_embeddings(fe_engine* engine, const float* embeddings, size_t 
 /* engine.h:126-134 (not built: FE_STATUS_UNSUPPORTED_MODEL) */
 int fe_engine_run_embeddings_masked(fe_engine* engine, const float* embeddings, const uint8_t* attention_mask,
                                     size_t seq_len, float* out);
-/* engine.h:136-146 (not built: FE_STATUS_UNSUPPORTED_MODEL) */
+/* engine.h:136-146: SmolVLA suffix embedding, out [chunk_size][expert_width] */
 int fe_engine_smolvla_embed_suffix(fe_engine* engine, const float* noisy_actions, size_t chunk_size,
                                    float timestep, float* out);
-/* engine.h:148-161 (not built: FE_STATUS_UNSUPPORTED_MODEL) */
+/* engine.h:148-161: the expert's layers over a caller-supplied prefix cache
+ * [expert_layers][prefix_length][cache_width] (cache_width = the K / V width in
+ * the reference's layout; this build also accepts a wider cache that the
+ * cross-attention layers project) */
 int fe_engine_smolvla_run_expert(fe_engine* engine, const float* suffix, size_t chunk_size,
                                  const float* prefix_keys, const float* prefix_values, const uint8_t* prefix_mask,
                                  size_t prefix_length, float* out);
-/* engine.h:163-171 (not built: FE_STATUS_UNSUPPORTED_MODEL) */
+/* engine.h:163-171 */
 int fe_engine_smolvla_project_actions(fe_engine* engine, const float* hidden, size_t chunk_size, float* out);
-/* engine.h:173-183 (not built: FE_STATUS_UNSUPPORTED_MODEL) */
+/* engine.h:173-183 */
 int fe_engine_smolvla_denoise(fe_engine* engine, const float* noisy_actions, size_t chunk_size, float timestep,
                               const float* prefix_keys, const float* prefix_values, const uint8_t* prefix_mask,
                               size_t prefix_length, float* out);
-/* engine.h:185-196 (not built: FE_STATUS_UNSUPPORTED_MODEL) */
+/* engine.h:185-196: Euler sample, t = 1 - step / steps */
 int fe_engine_smolvla_sample(fe_engine* engine, const float* initial_noise, size_t chunk_size, size_t steps,
                              const float* prefix_keys, const float* prefix_values, const uint8_t* prefix_mask,
                              size_t prefix_length, float* out);
@@ -322,6 +325,25 @@ int fe_engine_run_batch(fe_engine* engine, const int32_t* tokens, size_t batch, 
 /* Batched fe_engine_sample: tokens [batch][seq_len], noise/action [batch][A]. */
 int fe_engine_sample_batch(fe_engine* engine, const int32_t* tokens, size_t batch, size_t seq_len,
                            const float* noise, size_t steps, int method, float* action);
+/* Batched fe_engine_smolvla_sample: initial_noise / out [batch][chunk_size][max_action_dim];
+ * prefix_keys / prefix_values [batch][expert_layers][prefix_length][cache_width] and
+ * prefix_mask [batch][prefix_length], or one prefix for every sample when
+ * shared_prefix != 0. */
+int fe_engine_smolvla_sample_batch(fe_engine* engine, const float* initial_noise, size_t batch, size_t chunk_size,
+                                   size_t steps, const float* prefix_keys, const float* prefix_values,
+                                   const uint8_t* prefix_mask, size_t prefix_length, int shared_prefix, float* out);
+/* As fe_engine_smolvla_sample_batch with DEVICE pointers, enqueued on `stream`
+ * (NULL = the engine's stream); returns before the work completes.  The mask is
+ * not validated on the host. */
+int fe_engine_smolvla_sample_device(fe_engine* engine, const float* initial_noise, size_t batch, size_t chunk_size,
+                                    size_t steps, const float* prefix_keys, const float* prefix_values,
+                                    const uint8_t* prefix_mask, size_t prefix_length, int shared_prefix, float* out,
+                                    void* stream);
+/* Reserve the SmolVLA workspace for `batch` chunks of `chunk_size` tokens and
+ * prefixes of `prefix_length` slots (the only SmolVLA call besides the first
+ * sample of a larger shape that allocates device memory). */
+int fe_engine_smolvla_reserve(fe_engine* engine, size_t batch, size_t chunk_size, size_t prefix_length,
+                              int shared_prefix);
 /* Wait for all work enqueued by this engine. */
 int fe_engine_synchronize(fe_engine* engine);
 

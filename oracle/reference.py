@@ -82,6 +82,15 @@ def lib():
         handle.fe_engine_flow_begin.argtypes = [C.c_void_p, _f32p, _f32p, C.c_size_t, C.c_int]
         handle.fe_engine_flow_advance.argtypes = [C.c_void_p, C.c_size_t, _f32p,
                                                   C.POINTER(C.c_size_t)]
+        _u8p = C.POINTER(C.c_uint8)
+        handle.fe_engine_smolvla_embed_suffix.argtypes = [C.c_void_p, _f32p, C.c_size_t, C.c_float, _f32p]
+        handle.fe_engine_smolvla_run_expert.argtypes = [C.c_void_p, _f32p, C.c_size_t, _f32p, _f32p, _u8p,
+                                                        C.c_size_t, _f32p]
+        handle.fe_engine_smolvla_project_actions.argtypes = [C.c_void_p, _f32p, C.c_size_t, _f32p]
+        handle.fe_engine_smolvla_denoise.argtypes = [C.c_void_p, _f32p, C.c_size_t, C.c_float, _f32p, _f32p,
+                                                     _u8p, C.c_size_t, _f32p]
+        handle.fe_engine_smolvla_sample.argtypes = [C.c_void_p, _f32p, C.c_size_t, C.c_size_t, _f32p, _f32p,
+                                                    _u8p, C.c_size_t, _f32p]
         _lib = handle
     return _lib
 
@@ -196,3 +205,49 @@ class ReferenceEngine:
         buf = C.create_string_buffer(size)
         self._check(self.lib.fe_engine_export_decode_state(self.handle, buf, size))
         return buf.raw
+
+    # SmolVLA action expert (engine.h:136-196); keys / values [layers][prefix][320]
+
+    @staticmethod
+    def _u8(array):
+        return array.ctypes.data_as(C.POINTER(C.c_uint8))
+
+    def smolvla_embed_suffix(self, noisy, timestep, width):
+        x = np.ascontiguousarray(noisy, np.float32)
+        chunk = x.shape[0]
+        out = np.empty((chunk, width), np.float32)
+        self._check(self.lib.fe_engine_smolvla_embed_suffix(self.handle, _p(x), chunk, float(timestep), _p(out)))
+        return out
+
+    def smolvla_run_expert(self, suffix, keys, values, mask):
+        x = np.ascontiguousarray(suffix, np.float32)
+        k, v = np.ascontiguousarray(keys, np.float32), np.ascontiguousarray(values, np.float32)
+        m = np.ascontiguousarray(mask, np.uint8)
+        out = np.empty_like(x)
+        self._check(self.lib.fe_engine_smolvla_run_expert(self.handle, _p(x), x.shape[0], _p(k), _p(v), self._u8(m),
+                                                          m.size, _p(out)))
+        return out
+
+    def smolvla_project_actions(self, hidden, action_dim):
+        x = np.ascontiguousarray(hidden, np.float32)
+        out = np.empty((x.shape[0], action_dim), np.float32)
+        self._check(self.lib.fe_engine_smolvla_project_actions(self.handle, _p(x), x.shape[0], _p(out)))
+        return out
+
+    def smolvla_denoise(self, noisy, timestep, keys, values, mask):
+        x = np.ascontiguousarray(noisy, np.float32)
+        k, v = np.ascontiguousarray(keys, np.float32), np.ascontiguousarray(values, np.float32)
+        m = np.ascontiguousarray(mask, np.uint8)
+        out = np.empty_like(x)
+        self._check(self.lib.fe_engine_smolvla_denoise(self.handle, _p(x), x.shape[0], float(timestep), _p(k), _p(v),
+                                                       self._u8(m), m.size, _p(out)))
+        return out
+
+    def smolvla_sample(self, noise, steps, keys, values, mask):
+        x = np.ascontiguousarray(noise, np.float32)
+        k, v = np.ascontiguousarray(keys, np.float32), np.ascontiguousarray(values, np.float32)
+        m = np.ascontiguousarray(mask, np.uint8)
+        out = np.empty_like(x)
+        self._check(self.lib.fe_engine_smolvla_sample(self.handle, _p(x), x.shape[0], steps, _p(k), _p(v),
+                                                      self._u8(m), m.size, _p(out)))
+        return out

@@ -443,3 +443,186 @@ class MambaModel:
             y = (y[0] * silu(xz[di:])).astype(F32)
             hidden = (hidden + lw["out_proj"] @ y).astype(F32)
         return rmsnorm(hidden[None, :], self.t["backbone.norm_f.weight"])[0]
+
+
+# --------------------------------------------------------------------------
+# SmolVLA flow action expert (src/core/models/smolvla/smolvla_action_expert.cc)
+
+
+def round_bf16(x):
+    """round_to_bf16 (src/core/kernels/kernels.h:236-244): round to nearest
+    even in the bit pattern, no NaN special case."""
+    bits = np.ascontiguousarray(x, F32).view(np.uint32)
+    bias = ((bits >> np.uint32(16)) & np.uint32(1)) + np.uint32(0x7FFF)
+    return ((bits + bias) & np.uint32(0xFFFF0000)).view(F32)
+
+
+def rmsnorm_bf16(x, weight, eps=1e-5):
+    """kernels.h:246-265: scale in f32, bf16 after the scale and after the weight."""
+    x = np.asarray(x, F32)
+    ss = np.sum(x * x, axis=-1, dtype=F32, keepdims=True)
+    scale = (F32(1) / np.sqrt(ss / F32(x.shape[-1]) + F32(eps))).astype(F32)
+    return round_bf16(round_bf16(x * scale) * np.asarray(weight, F32))
+
+
+def apply_rope(x, head_width, position_base):
+    """Interleaved-halves RoPE on [rows][heads][head_width] (kernels.h:339-362)."""
+    half = head_width // 2
+    c = np.arange(half, dtype=F32)
+    exponent = ((F32(2) * c) / F32(head_width)).astype(F32)
+    denom = np.exp(F32(9.210340371976184) * exponent).astype(F32)
+    pos = (F32(position_base) + np.arange(x.shape[0], dtype=F32)).astype(F32)
+    angle = (pos[:, None] / denom[None, :]).astype(F32)
+    sin, cos = np.sin(angle)[:, None, :], np.cos(angle)[:, None, :]
+    first, second = x[..., :half], x[..., half:]
+    out = np.empty_like(x)
+    out[..., :half] = first * cos - second * sin
+    out[..., half:] = second * cos + first * sin
+    return out.astype(F32)
+
+
+def softmax_rows(s):
+    """kernels.h:181-194 per row: exp(s - max), then times 1 / sum."""
+    m = np.max(s, axis=-1, keepdims=True)
+    e = np.exp((s - m).astype(F32)).astype(F32)
+    inv = (F32(1) / np.sum(e, axis=-1, dtype=F32, keepdims=True)).astype(F32)
+    return (e * inv).astype(F32)
+
+
+class SmolVLAExpert:
+    """Parameterised restatement of SmolVLAActionExpert (smolvla_action_expert.cc:209-477).
+
+    The reference fixes the head width at 64 with 15 query and 5 K / V heads
+    (:120-128); here they come from the checkpoint (`flowedge.smolvla.head_width`,
+    default 64).  Cross-attention layers (odd) project the per-layer prefix
+    cache; self-attention layers (even) attend over [cache ; action tokens]
+    when the cache width equals the K / V width (the reference's layout), else
+    over the action tokens only.  All bf16 rounding points are the reference's.
+    """
+
+    PREFIX = "model.vlm_with_expert.lm_expert."
+
+    def __init__(self, tensors):
+        t = {k: np.asarray(v, F32) for k, v in tensors.items()}
+        self.w_in, self.b_in = t["model.action_in_proj.weight"], t["model.action_in_proj.bias"]
+        self.w_out, self.b_out = t["model.action_out_proj.weight"], t["model.action_out_proj.bias"]
+        self.w_tin, self.b_tin = t["model.action_time_mlp_in.weight"], t["model.action_time_mlp_in.bias"]
+        self.w_tout, self.b_tout = t["model.action_time_mlp_out.weight"], t["model.action_time_mlp_out.bias"]
+        self.final_norm = t[self.PREFIX + "norm.weight"]
+        self.width = self.w_in.shape[0]
+        self.action_dim = self.w_in.shape[1]
+        hw = t.get("flowedge.smolvla.head_width")
+        self.head_width = int(hw[0]) if hw is not None else 64
+        self.layers = []
+        while self.PREFIX + f"layers.{len(self.layers)}.self_attn.q_proj.weight" in t:
+            p = self.PREFIX + f"layers.{len(self.layers)}."
+            self.layers.append({k: t[p + k] for k in (
+                "input_layernorm.weight", "post_attention_layernorm.weight", "self_attn.q_proj.weight",
+                "self_attn.k_proj.weight", "self_attn.v_proj.weight", "self_attn.o_proj.weight",
+                "mlp.gate_proj.weight", "mlp.up_proj.weight", "mlp.down_proj.weight")})
+        self.heads = self.layers[0]["self_attn.q_proj.weight"].shape[0] // self.head_width
+        self.kv_heads = self.layers[0]["self_attn.k_proj.weight"].shape[0] // self.head_width
+        self.kv_width = self.kv_heads * self.head_width
+        self.cache_width = (self.layers[1]["self_attn.k_proj.weight"].shape[1] if len(self.layers) > 1
+                            else self.kv_width)
+
+    def embed_suffix(self, noisy, timestep):
+        """smolvla_action_expert.cc:209-256."""
+        noisy = np.asarray(noisy, F32).reshape(-1, self.action_dim)
+        action = (noisy @ self.w_in.T + self.b_in).astype(F32)
+        half = self.width // 2
+        i = np.arange(half, dtype=F32)
+        fraction = (i / F32(half - 1)).astype(F32)
+        period = (F32(0.004) * np.power(F32(4.0) / F32(0.004), fraction).astype(F32)).astype(F32)
+        angle = ((F32(2.0) * F32(3.14159265358979323846) / period) * F32(timestep)).astype(F32)
+        time = np.concatenate([np.sin(angle), np.cos(angle)]).astype(F32)
+        fused = np.concatenate([action, np.broadcast_to(time, action.shape)], axis=1)
+        h = silu((fused @ self.w_tin.T).astype(F32) + self.b_tin)
+        return ((h @ self.w_tout.T).astype(F32) + self.b_tout).astype(F32)
+
+    def _attention(self, q, k, v, prefix_k, prefix_v, mask, cross):
+        """grouped_query_attention (kernels.h:275-336) on [rows][heads][hw]."""
+        rows, hw = q.shape[0], self.head_width
+        groups = self.heads // self.kv_heads
+        scale = F32(np.sqrt(F32(hw)))
+        out = np.zeros((rows, self.heads, hw), F32)
+        valid = mask.astype(bool)
+        causal = np.tril(np.ones((rows, rows), bool))
+        for h in range(self.heads):
+            kh = h // groups
+            parts, vals = [], []
+            if cross:
+                s = ((q[:, h, :] @ k[:, kh, :].T).astype(F32) / scale).astype(F32)
+                s[:, ~valid] = -np.inf
+                parts.append(s)
+                vals.append(v[:, kh, :])
+            else:
+                if prefix_k is not None:
+                    s = ((q[:, h, :] @ prefix_k[:, kh, :].T).astype(F32) / scale).astype(F32)
+                    s[:, ~valid] = -np.inf
+                    parts.append(s)
+                    vals.append(prefix_v[:, kh, :])
+                s = ((q[:, h, :] @ k[:, kh, :].T).astype(F32) / scale).astype(F32)
+                s[~causal] = -np.inf
+                parts.append(s)
+                vals.append(v[:, kh, :])
+            p = round_bf16(softmax_rows(np.concatenate(parts, axis=1)))
+            out[:, h, :] = p @ np.concatenate(vals, axis=0)
+        return out.reshape(rows, self.heads * hw)
+
+    def run(self, suffix, keys, values, mask):
+        """run_with_prefix_kv (smolvla_action_expert.cc:277-394); keys / values
+        [layers][prefix][cache_width], mask [prefix]."""
+        out = np.asarray(suffix, F32).reshape(-1, self.width).copy()
+        rows, hw = out.shape[0], self.head_width
+        mask = np.asarray(mask, np.uint8)
+        valid = int(mask.sum())
+        for li, L in enumerate(self.layers):
+            cross = li % 2 == 1
+            normed = round_bf16(rmsnorm_bf16(out, L["input_layernorm.weight"]))
+            q = round_bf16(normed @ L["self_attn.q_proj.weight"].T).reshape(rows, self.heads, hw)
+            prefix_k = prefix_v = None
+            if cross:
+                k = round_bf16(keys[li] @ L["self_attn.k_proj.weight"].T).reshape(-1, self.kv_heads, hw)
+                v = round_bf16(values[li] @ L["self_attn.v_proj.weight"].T).reshape(-1, self.kv_heads, hw)
+                q = apply_rope(q, hw, 0)
+            else:
+                k = round_bf16(normed @ L["self_attn.k_proj.weight"].T).reshape(rows, self.kv_heads, hw)
+                v = round_bf16(normed @ L["self_attn.v_proj.weight"].T).reshape(rows, self.kv_heads, hw)
+                q = apply_rope(q, hw, valid)
+                k = round_bf16(apply_rope(k, hw, valid))
+                if self.cache_width == self.kv_width:
+                    prefix_k = np.asarray(keys[li], F32).reshape(-1, self.kv_heads, hw)
+                    prefix_v = np.asarray(values[li], F32).reshape(-1, self.kv_heads, hw)
+            q = round_bf16(q)
+            att = round_bf16(self._attention(q, k, v, prefix_k, prefix_v, mask, cross))
+            proj = round_bf16(att @ L["self_attn.o_proj.weight"].T)
+            out = round_bf16(out + proj)
+            normed = round_bf16(rmsnorm_bf16(out, L["post_attention_layernorm.weight"]))
+            gate = round_bf16(normed @ L["mlp.gate_proj.weight"].T)
+            up = round_bf16(normed @ L["mlp.up_proj.weight"].T)
+            gate = round_bf16(up * silu(gate))
+            proj = round_bf16(gate @ L["mlp.down_proj.weight"].T)
+            out = round_bf16(out + proj)
+        return round_bf16(rmsnorm_bf16(out, self.final_norm))
+
+    def project_actions(self, hidden):
+        """smolvla_action_expert.cc:258-275."""
+        hidden = np.asarray(hidden, F32).reshape(-1, self.width)
+        return ((hidden @ self.w_out.T).astype(F32) + self.b_out).astype(F32)
+
+    def denoise(self, noisy, timestep, keys, values, mask):
+        """denoise_with_prefix_kv (smolvla_action_expert.cc:396-420)."""
+        hidden = self.run(self.embed_suffix(noisy, timestep), keys, values, mask)
+        return self.project_actions(hidden)
+
+    def sample(self, noise, steps, keys, values, mask):
+        """sample_euler_with_prefix_kv (smolvla_action_expert.cc:422-474):
+        t = 1 + step * dt, dt = -1 / steps; noise [chunk][action_dim]."""
+        x = np.asarray(noise, F32).reshape(-1, self.action_dim).copy()
+        dt = F32(-1.0) / F32(steps)
+        for step in range(steps):
+            t = F32(F32(1.0) + F32(step) * dt)
+            v = self.denoise(x, t, keys, values, mask)
+            x = (x + dt * v).astype(F32)
+        return x

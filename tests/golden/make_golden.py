@@ -4,7 +4,7 @@
 Run in a container that has the reference checkout (default /root/reference,
 override with FLOWEDGE_REFERENCE) and PyTorch:
 
-    python tests/golden/make_golden.py
+    python tests/golden/make_golden.py [fixture names]
 
 For each fixture it
   1. builds a small seeded model in the *source* layout the reference converter
@@ -191,12 +191,55 @@ def make_mamba_flow(name, params):
     print(f"{name}: hidden norm {np.linalg.norm(hidden):.4f}")
 
 
+# SmolVLA action expert at the shapes the reference loads (attention 960 = 15 x 64,
+# K / V 320, MLP 2048).  The weights and the prefix cache are regenerated at test
+# time from (spec, seed) by flowedge_b200.checkpoint, so the fixture holds only
+# the inputs the generators do not make and the reference's outputs.
+SMOLVLA_FIXTURES = {
+    "smolvla_ref": dict(layers=4, chunk=10, prefix=24, masked=5, seed=11, timestep=0.7, steps=10),
+    "smolvla_ref16": dict(layers=16, chunk=50, prefix=64, masked=9, seed=12, timestep=0.35, steps=10),
+}
+
+
+def make_smolvla(name, params):
+    import dataclasses
+
+    from flowedge_b200 import checkpoint as ck
+
+    spec = dataclasses.replace(ck.SMOLVLA_REF, layers=params["layers"], chunk=params["chunk"],
+                               prefix=params["prefix"])
+    tensors = ck.smolvla_tensors(spec, params["seed"])
+    keys, values, mask = ck.smolvla_prefix(spec, params["seed"] + 1, masked=params["masked"])
+    rng = np.random.default_rng(params["seed"] + 2)
+    noise = rng.standard_normal((spec.chunk, spec.action_dim), dtype=np.float32)
+    with tempfile.TemporaryDirectory() as tmp:
+        path = Path(tmp) / f"{name}.safetensors"
+        ck.write_checkpoint(path, tensors, matrices="bf16")
+        engine = oracle_ref.ReferenceEngine(path, threads=8)
+        t = np.float32(params["timestep"])
+        embed = engine.smolvla_embed_suffix(noise, t, spec.expert_width)
+        hidden = engine.smolvla_run_expert(embed, keys, values, mask)
+        project = engine.smolvla_project_actions(hidden, spec.action_dim)
+        denoise = engine.smolvla_denoise(noise, t, keys, values, mask)
+        sample = engine.smolvla_sample(noise, params["steps"], keys, values, mask)
+        engine.close()
+    np.savez(HERE / f"{name}.npz", noise=noise, timestep=t, embed=embed, hidden=hidden, project=project,
+             denoise=denoise, sample=sample, params=np.array(json.dumps(params)))
+    print(f"{name}: sample norm {np.linalg.norm(sample):.4f}")
+
+
 def main():
     oracle_ref.build()
+    only = sys.argv[1:]
     for name, params in DIFFUSION_FIXTURES.items():
-        make_diffusion(name, params)
+        if not only or name in only:
+            make_diffusion(name, params)
     for name, params in MAMBA_FLOW_FIXTURES.items():
-        make_mamba_flow(name, params)
+        if not only or name in only:
+            make_mamba_flow(name, params)
+    for name, params in SMOLVLA_FIXTURES.items():
+        if not only or name in only:
+            make_smolvla(name, params)
 
 
 if __name__ == "__main__":

@@ -1,0 +1,128 @@
+"""SmolVLA action expert on the GPU (BASELINE configuration 5 and the
+reference's shapes) through the C ABI.
+
+Parity: against the reference's own outputs (golden fixtures, reference
+shapes) and against the restatement (C5 shapes, which the reference cannot
+load).  The layers round every intermediate to bf16, so results differ from
+any other summation order by the chaos the restatement's pin documents
+(tests/test_smolvla_oracle.py): layer outputs are compared by relative L2
+error (< 3e-2), the Euler-10 actions by the bf16 bar (2e-2 max-abs).
+"""
+
+import dataclasses
+
+import numpy as np
+import pytest
+
+from flowedge_b200 import Engine
+from flowedge_b200 import checkpoint as ck
+from flowedge_b200.engine import FlowEdgeError, device_malloc_count
+from oracle import restate
+from tests.test_smolvla_oracle import rel, smolvla_fixture
+
+pytestmark = pytest.mark.gpu
+
+# C5 with fewer layers keeps the restatement fast; the full 16 layers run in
+# test_smolvla_c5_full_depth_matches_restatement.
+C5_SMALL = dataclasses.replace(ck.SMOLVLA_C5, layers=4)
+
+
+def _engine(tmp_path, spec, seed, name="smolvla"):
+    tensors = ck.smolvla_tensors(spec, seed)
+    path = tmp_path / f"{name}.safetensors"
+    ck.write_checkpoint(path, tensors, matrices="bf16")
+    return tensors, Engine(path, threads=0, device=0)
+
+
+@pytest.mark.parametrize("name", ["smolvla_ref", "smolvla_ref16"])
+def test_smolvla_reference_shapes_match_reference(tmp_path, name):
+    spec, p, tensors, keys, values, mask, g = smolvla_fixture(name)
+    path = tmp_path / f"{name}.safetensors"
+    ck.write_checkpoint(path, tensors, matrices="bf16")
+    e = Engine(path, threads=0, device=0)
+    meta = e.model_metadata
+    assert meta["architecture"] == 7 and meta["d_inner"] == spec.expert_width and e.action_horizon == 50
+    embed = e.smolvla_embed_suffix(g["noise"], float(g["timestep"]), spec.expert_width)
+    print(f"{name} embed max-abs {np.abs(embed - g['embed']).max():.3g}")
+    np.testing.assert_allclose(embed, g["embed"], atol=1e-4)
+    np.testing.assert_allclose(e.smolvla_project_actions(g["hidden"]), g["project"], atol=1e-4)
+    hidden = e.smolvla_run_expert(g["embed"], keys, values, mask)
+    den = e.smolvla_denoise(g["noise"], float(g["timestep"]), keys, values, mask)
+    sample = e.smolvla_sample(g["noise"], p["steps"], keys, values, mask)
+    err = float(np.abs(sample - g["sample"]).max())
+    print(f"{name} hidden rel {rel(hidden, g['hidden']):.3g}, denoise rel {rel(den, g['denoise']):.3g}, "
+          f"Euler-{p['steps']} max-abs vs reference {err:.3g}")
+    assert rel(hidden, g["hidden"]) < 3e-2
+    assert rel(den, g["denoise"]) < 3e-2
+    assert err <= 2e-2
+    e.close()
+
+
+def test_smolvla_c5_batched_matches_restatement(tmp_path):
+    """C5 shapes (12 heads of 60, 4 K / V heads, 960-wide prefix projected by the
+    cross-attention layers), 4 layers: a batch of 3 with per-sample prefixes and
+    masks, a shared-prefix batch, and single calls equal to their batch rows."""
+    spec = C5_SMALL
+    tensors, e = _engine(tmp_path, spec, 21)
+    model = restate.SmolVLAExpert(tensors)
+    keys, values, mask = ck.smolvla_prefix(spec, 22, batch=3)
+    mask[1, -30:] = 0
+    mask[2, :17] = 0
+    rng = np.random.default_rng(23)
+    noise = rng.standard_normal((3, spec.chunk, spec.action_dim), dtype=np.float32)
+    out = e.smolvla_sample_batch(noise, 10, keys, values, mask)
+    for b in range(3):
+        expected = model.sample(noise[b], 10, keys[b], values[b], mask[b])
+        err = float(np.abs(out[b] - expected).max())
+        print(f"C5 (4 layers) sample {b} Euler-10 max-abs vs restatement: {err:.3g}")
+        assert err <= 2e-2
+        single = e.smolvla_sample(noise[b], 10, keys[b], values[b], mask[b])
+        assert float(np.abs(single - out[b]).max()) <= 1e-6
+    shared = e.smolvla_sample_batch(noise[:2], 10, keys[0], values[0], mask[0], shared_prefix=True)
+    assert float(np.abs(shared[0] - out[0]).max()) <= 1e-6
+    assert float(np.abs(shared[1] - model.sample(noise[1], 10, keys[0], values[0], mask[0])).max()) <= 2e-2
+    e.close()
+
+
+def test_smolvla_c5_full_depth_matches_restatement(tmp_path):
+    """BASELINE configuration 5 at full depth (16 layers), batch 1, Euler-10."""
+    spec = ck.SMOLVLA_C5
+    tensors, e = _engine(tmp_path, spec, 31)
+    model = restate.SmolVLAExpert(tensors)
+    keys, values, mask = ck.smolvla_prefix(spec, 32)
+    noise = np.random.default_rng(33).standard_normal((spec.chunk, spec.action_dim), dtype=np.float32)
+    got = e.smolvla_sample(noise, 10, keys, values, mask)
+    expected = model.sample(noise, 10, keys, values, mask)
+    err = float(np.abs(got - expected).max())
+    print(f"C5 full depth Euler-10 max-abs vs restatement: {err:.3g} (rel {rel(got, expected):.3g})")
+    assert err <= 2e-2
+    e.close()
+
+
+def test_smolvla_errors_and_no_allocation(tmp_path):
+    spec = dataclasses.replace(C5_SMALL, layers=2, prefix=32)
+    tensors, e = _engine(tmp_path, spec, 41)
+    keys, values, mask = ck.smolvla_prefix(spec, 42)
+    noise = np.random.default_rng(43).standard_normal((spec.chunk, spec.action_dim), dtype=np.float32)
+    e.smolvla_sample(noise, 10, keys, values, mask)
+    before = device_malloc_count()
+    for _ in range(3):
+        e.smolvla_sample(noise, 10, keys, values, mask)
+    assert device_malloc_count() == before
+    bad = mask.copy()
+    bad[3] = 2
+    with pytest.raises(FlowEdgeError) as info:
+        e.smolvla_sample(noise, 10, keys, values, bad)
+    assert info.value.status == 3
+    with pytest.raises(FlowEdgeError) as info:
+        e.smolvla_sample(noise, 10, keys, values, np.zeros_like(mask))
+    assert info.value.status == 3
+    with pytest.raises(FlowEdgeError) as info:
+        e.smolvla_sample(noise, 101, keys, values, mask)
+    assert info.value.status == 1
+    big = np.ones(513, np.uint8)
+    kb = np.zeros((spec.layers, 513, spec.cache_width), np.float32)
+    with pytest.raises(FlowEdgeError) as info:
+        e.smolvla_sample(noise, 10, kb, kb, big)
+    assert info.value.status == 1
+    e.close()
