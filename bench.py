@@ -338,6 +338,8 @@ def run_ours(args):
         cpu_value, secs = _reference_throughput(path, spec, threads, threads)
         line["cpu_baseline"] = {"value": cpu_value, "unit": UNIT, "cores": threads, "kind": "reference",
                                 "sample": f"{threads} chunks (one per host thread, {secs:.1f} s)"}
+        if not args.no_extras:
+            line["cpu_baseline"]["c5_smolvla"] = _smolvla_cpu_baseline(threads)
     engine.close()
     if dist is not None:
         dist.barrier()
@@ -364,6 +366,21 @@ def _latency(fn, iters):
     times.sort()
     return {"p50_ms": times[len(times) // 2], "p99_ms": times[min(len(times) - 1, int(len(times) * 0.99))],
             "iters": iters, "device_mallocs": int(device_malloc_count() - mallocs0)}
+
+
+def _smolvla_flops(spec) -> float:
+    """Algorithmic FLOPs of one SmolVLA chunk through one Euler step
+    (smolvla_action_expert.cc:209-394): every projection once, attention over
+    the valid keys (cross: the prefix; self: causal over the action tokens)."""
+    w, a, attn, kv, mlp, layers = (spec.expert_width, spec.action_dim, spec.attention_width, spec.kv_width,
+                                   spec.mlp_width, spec.layers)
+    cross = layers // 2
+    self_layers = layers - cross
+    per_token = 2 * (layers * (w * attn + attn * w + 3 * mlp * w) + self_layers * 2 * kv * w)
+    per_token += 2 * (a * w + 2 * w * w + w * w) + 2 * w * a
+    self_keys = spec.chunk + 1 + (spec.prefix if spec.cache_width == kv else 0) * 2
+    per_token += 4 * attn * (cross * spec.prefix + self_layers * self_keys / 2)
+    return float(per_token * spec.chunk)
 
 
 def _extras(workdir: Path, device: int):
@@ -427,7 +444,64 @@ def _extras(workdir: Path, device: int):
         e.run_batch(tb)
         out[f"c3_mamba_b1024_prefill128_{prec}_seq_per_s"] = 1024 / (time.perf_counter() - t0)
         e.close()
+    # C5: SmolVLA-shaped action expert (bf16 by construction), Euler-10, one
+    # fixed 241-slot prefix shared by the batch
+    spec = ck.SMOLVLA_C5
+    sv = workdir / "bench_c5_smolvla.safetensors"
+    if not sv.exists():
+        ck.write_checkpoint(sv, ck.smolvla_tensors(spec, seed=SEED), matrices="bf16")
+    keys, values, mask = ck.smolvla_prefix(spec, SEED + 1)
+    noise1 = rng.standard_normal((spec.chunk, spec.action_dim)).astype(np.float32)
+    e = Engine(sv, threads=0, device=device)
+    out["c5_smolvla_b1_euler10_bf16"] = _latency(lambda: e.smolvla_sample(noise1, 10, keys, values, mask), 100)
+    batch = 512
+    nb = rng.standard_normal((batch, spec.chunk, spec.action_dim)).astype(np.float32)
+    e.smolvla_reserve(batch, spec.chunk, spec.prefix, True)
+    dn, dk, dv = (torch.from_numpy(x).cuda() for x in (nb, keys, values))
+    dm = torch.from_numpy(mask).cuda()
+    do = torch.empty_like(dn)
+    st = torch.cuda.Stream()
+    run = lambda: e.smolvla_sample_device(dn.data_ptr(), batch, spec.chunk, 10, dk.data_ptr(), dv.data_ptr(),
+                                          dm.data_ptr(), spec.prefix, True, do.data_ptr(), st.cuda_stream)
+    for _ in range(2):
+        run()
+    st.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record(st)
+    for _ in range(3):
+        run()
+    ev1.record(st)
+    st.synchronize()
+    sec = ev0.elapsed_time(ev1) / 1000.0 / 3
+    e.smolvla_sample_batch(nb, 10, keys, values, mask, shared_prefix=True)
+    t0 = time.perf_counter()
+    e.smolvla_sample_batch(nb, 10, keys, values, mask, shared_prefix=True)
+    e2e = time.perf_counter() - t0
+    peak, peak_kind = _peaks()
+    tflops = batch * 10 * _smolvla_flops(spec) / sec / 1e12
+    out["c5_smolvla_b512_euler10_bf16"] = {
+        "chunks_per_s": batch / sec, "e2e_chunks_per_s": batch / e2e, "ms_per_call": sec * 1000.0,
+        "tflops": tflops, "frac_of_peak": tflops / peak, "peak_kind": peak_kind,
+        "flops_per_chunk_step": _smolvla_flops(spec)}
+    e.close()
     return out
+
+
+def _smolvla_cpu_baseline(threads: int) -> dict:
+    """The reference cannot load configuration 5's shapes
+    (smolvla_action_expert.cc:120-128), so its CPU figure is the numpy
+    restatement of the same algorithm (oracle/restate.py) on the host cores."""
+    from oracle import restate
+
+    spec = ck.SMOLVLA_C5
+    model = restate.SmolVLAExpert(ck.smolvla_tensors(spec, seed=SEED))
+    keys, values, mask = ck.smolvla_prefix(spec, SEED + 1)
+    noise = np.random.default_rng(SEED).standard_normal((spec.chunk, spec.action_dim)).astype(np.float32)
+    t0 = time.perf_counter()
+    model.sample(noise, 10, keys, values, mask)
+    sec = time.perf_counter() - t0
+    return {"value": 1.0 / sec, "unit": "chunks/s", "cores": threads, "kind": "port",
+            "sample": "1 chunk, Euler-10, numpy restatement (BLAS threads = host cores)"}
 
 
 def main():

@@ -311,6 +311,12 @@ cudaError_t tc_gemm(const TcLaunch& l, DeviceContext& ctx, cudaStream_t stream, 
     }
     p.out_lo_off = static_cast<int>(l.out_lo_off);
   }
+  if (l.act == tc::kActSwiGLU &&
+      (l.out_f32 || (l.fp16 && !l.out_bf16) || l.out_lo_off != 0 || l.gn_fuse || l.stats != nullptr ||
+       l.m_valid % 2 != 0 || l.add_tok != nullptr)) {
+    err = "tc_gemm: the SwiGLU epilogue needs interleaved rows and a plain bf16 output";
+    return cudaErrorInvalidValue;
+  }
   if (l.out_bf16) {
     if (l.out_f32 || l.gn_fuse || l.stats != nullptr || l.out_lo_off != 0) {
       err = "tc_gemm: a bf16 output needs a plain 16-bit epilogue";

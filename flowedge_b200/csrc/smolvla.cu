@@ -10,13 +10,13 @@
 //     projections take bf16 operands: the reference rounds their inputs and
 //     weights to bf16, so the tensor cores see the reference's operand values
 //     and the products are exact; only the fp32 summation order differs.  The
-//     epilogue rounds to bf16 where the reference does (q, k, v, gate, up).
+//     epilogue rounds to bf16 where the reference does (q, k, v, gate, up,
+//     o and down) and applies the SwiGLU gate ([Wgate; Wup] rows interleaved).
 //     The suffix embedding, the action projection and the cross-attention
 //     K / V projections consume fp32 activations (the reference does not round
 //     them): they run on fp16 hi / lo splits of the activations against
 //     [W | W], which keeps ~22 bits of each activation.
-//   * Fused q / k / v rows ([Wq; Wk; Wv], one GEMM) for self-attention layers
-//     and [Wgate; Wup] for the MLP.
+//   * Fused q / k / v rows ([Wq; Wk; Wv], one GEMM) for self-attention layers.
 //   * Attention (grouped-query, RoPE, the reference's softmax order: max,
 //     exp, 1 / sum, bf16 probabilities) runs on mma.sync with bf16 operands,
 //     one CTA per (sample, K / V head) with K and V^T staged in shared memory.
@@ -173,24 +173,6 @@ __global__ void rms_kernel(float* __restrict__ h, int ld_h, const bf16* __restri
   }
 }
 
-// act[r][j] = bf16(up * (gate / (1 + exp(-gate)))) (gate_silu, kernels_scalar.cc:61-67, then
-// bf16 as smolvla_action_expert.cc:370-371); gu rows hold [gate | up] (already bf16).
-__global__ void gate_silu_kernel(const bf16* gu, int ld_gu, int mlp, bf16* act, int ld_act, long long rows) {
-  const int pairs = mlp / 2;
-  const long long total = rows * pairs;
-  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
-       i += static_cast<long long>(gridDim.x) * blockDim.x) {
-    const long long r = i / pairs;
-    const int j = static_cast<int>(i - r * pairs) * 2;
-    const __nv_bfloat162 g2 = *reinterpret_cast<const __nv_bfloat162*>(gu + r * ld_gu + j);
-    const __nv_bfloat162 u2 = *reinterpret_cast<const __nv_bfloat162*>(gu + r * ld_gu + mlp + j);
-    const float g0 = __low2float(g2), g1 = __high2float(g2);
-    const float a0 = __fmul_rn(__low2float(u2), g0 / (1.0f + expf(-g0)));
-    const float a1 = __fmul_rn(__high2float(u2), g1 / (1.0f + expf(-g1)));
-    *reinterpret_cast<__nv_bfloat162*>(act + r * ld_act + j) = __floats2bfloat162_rn(a0, a1);
-  }
-}
-
 // x = x + dt v (smolvla_action_expert.cc:472-473), the next step's fp16 hi / lo
 // input and the step counter.
 __global__ void euler_kernel(const float* v, int ld_v, float* x, int A, long long rows, int steps, __half* x2,
@@ -264,7 +246,7 @@ struct AttnParams {
   long long mask_b;
   const int* valid;
   int valid_b;
-  const float* rope_denom;  // [hw / 2]: exp(ln(1e4) * 2c / hw)
+  const float2* rope;  // [position][hw / 2]: (cos, sin) of position / exp(ln(1e4) * 2c / hw)
   int chunk, chunk_pad, P, heads, kv_heads, hw;
   int cross;
   int S, S_pad, npre;  // keys (prefix part first), padded to 16; npre keys precede the action tokens
@@ -279,11 +261,33 @@ __device__ __forceinline__ void mma_bf16_16816(float (&d)[4], const uint32_t (&a
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
-__device__ __forceinline__ void rope_pair(float first, float second, float pos, float denom, float& o0, float& o1) {
-  float s, c;
-  sincosf(pos / denom, &s, &c);
-  o0 = __fsub_rn(__fmul_rn(first, c), __fmul_rn(second, s));
-  o1 = __fadd_rn(__fmul_rn(second, c), __fmul_rn(first, s));
+// (first, second) rotated by the angle whose (cos, sin) is cs (kernels.h:353-358)
+__device__ __forceinline__ void rope_pair(float first, float second, float2 cs, float& o0, float& o1) {
+  o0 = __fsub_rn(__fmul_rn(first, cs.x), __fmul_rn(second, cs.y));
+  o1 = __fadd_rn(__fmul_rn(second, cs.x), __fmul_rn(first, cs.y));
+}
+
+// table[pos][c] = (cos, sin)(pos / denom[c]), the angles of apply_rope
+// (kernels.h:345-352) for positions 0 .. npos - 1
+__global__ void rope_table_kernel(const float* denom, int half, int npos, float2* table) {
+  const int total = npos * half;
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
+    const int pos = i / half, c = i - pos * half;
+    float sn, cs;
+    sincosf(static_cast<float>(pos) / denom[c], &sn, &cs);
+    table[i] = make_float2(cs, sn);
+  }
+}
+
+__device__ __forceinline__ void ldsm_x4(const void* p, uint32_t (&r)[4]) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(smem_u32(p)));
+}
+__device__ __forceinline__ void ldsm_x4_t(const void* p, uint32_t (&r)[4]) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(smem_u32(p)));
 }
 
 __device__ __forceinline__ uint2 ld_bf16x4(const bf16* p) { return __ldg(reinterpret_cast<const uint2*>(p)); }
@@ -298,40 +302,42 @@ __device__ __forceinline__ uint2 bf16x4_of(const float* p) {
 constexpr int kAttnWarps = kAttnThreads / 32;
 constexpr int kStageBatch = 4;  // independent 8-byte loads in flight per thread while staging
 
-// One CTA per (sample, K / V head, task slice): K and V^T of the head staged
-// once per CTA.  A task is (G query heads of the group, 16 query rows): the G
-// heads share every K / V fragment a warp loads (grouped-query attention), and
-// the CTA's four warps split the task's keys (blocks of 16, round robin):
+// One CTA per (sample, K / V head, task slice): K and V of the head staged
+// once per CTA (row-major, 8-byte copies; RoPE of the action-token keys from a
+// per-call cos / sin table).  A task is (G query heads of the group, 16 query
+// rows): the G heads share every K / V fragment a warp loads (grouped-query
+// attention), and the CTA's four warps split the task's keys (blocks of 16,
+// round robin):
 //   phase 1: scores with an online row max / sum per warp, merged across the
 //            warps in warp order (the rescaled sum equals the reference's sum
 //            of exp(s - max) up to rounding),
 //   phase 2: p = bf16(exp(s - max) / sum) packed as A fragments, O += P V over
 //            the warp's keys; the warps' O partials are summed in warp order.
+// Fragments come from shared memory by ldmatrix (V transposed on the fly).
 // Exponentials are 2^x (ex2.approx) of scores scaled by log2(e) / sqrt(hw).
 // gridDim.z slices the tasks so that small batches still fill the GPU.
 template <int G>
 __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const AttnParams p) {
   extern __shared__ __align__(16) uint8_t smem[];
   bf16* Ks = reinterpret_cast<bf16*>(smem);                  // [S_pad][kKRow]
-  const int vt_ld = p.S_pad + 8;
-  bf16* Vt = Ks + static_cast<long long>(p.S_pad) * kKRow;  // [kHwPad][vt_ld]
-  float* kbias = reinterpret_cast<float*>(Vt + static_cast<long long>(kHwPad) * vt_ld);  // [S_pad]
+  bf16* Vs = Ks + static_cast<long long>(p.S_pad) * kKRow;  // [S_pad][kKRow]
+  float* kbias = reinterpret_cast<float*>(Vs + static_cast<long long>(p.S_pad) * kKRow);  // [S_pad]
   float* red = kbias + p.S_pad;                             // [G][warps][16][max, sum]
   float* opart = red + G * kAttnWarps * 16 * 2;             // [warps][16][kHwPad]
   bf16* Qs = reinterpret_cast<bf16*>(opart + kAttnWarps * 16 * kHwPad);  // [G][16][kKRow]
   const int b = blockIdx.x, kvh = blockIdx.y;
   const int tid = threadIdx.x;
   const int hw = p.hw, half = hw / 2, nq = hw / 4;
-  const float base = p.cross ? 0.0f : static_cast<float>(p.valid[static_cast<long long>(b) * p.valid_b]);
+  const int base = p.cross ? 0 : p.valid[static_cast<long long>(b) * p.valid_b];  // RoPE position of token 0
   const long long tok0 = static_cast<long long>(b) * p.chunk;
   const uint32_t z2 = 0u;
 
   // zero padding (keys >= S, dims >= hw) and the key bias
-  for (int i = tid; i < p.S_pad * kHwPad; i += kAttnThreads) {
-    const int j = i / kHwPad, d = i - j * kHwPad;
-    if (j >= p.S || d >= hw) {
-      Ks[j * kKRow + d] = __float2bfloat16_rn(0.0f);
-      Vt[d * vt_ld + j] = __float2bfloat16_rn(0.0f);
+  for (int i = tid; i < p.S_pad * (kHwPad / 4); i += kAttnThreads) {
+    const int j = i / (kHwPad / 4), q = i - j * (kHwPad / 4);
+    if (j >= p.S || q >= nq) {
+      *reinterpret_cast<uint2*>(Ks + j * kKRow + 4 * q) = make_uint2(z2, z2);
+      *reinterpret_cast<uint2*>(Vs + j * kKRow + 4 * q) = make_uint2(z2, z2);
     }
   }
   for (int i = tid; i < p.S_pad; i += kAttnThreads) {
@@ -340,7 +346,7 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const AttnParam
     else if (i < p.S) bias = 0.0f;
     kbias[i] = bias;
   }
-  // raw K / V rows, 4 dims per item, kStageBatch loads in flight per thread
+  // K / V rows, 4 dims per item, kStageBatch loads in flight per thread
   const int items = p.S * nq;
   for (int i0 = tid; i0 < items; i0 += kAttnThreads * kStageBatch) {
     uint2 kv[kStageBatch], vv[kStageBatch];
@@ -374,9 +380,7 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const AttnParam
       if (i < items) {
         const int j = i / nq, q = i - j * nq;
         *reinterpret_cast<uint2*>(Ks + j * kKRow + 4 * q) = kv[u];
-        const bf16* v4 = reinterpret_cast<const bf16*>(&vv[u]);
-#pragma unroll
-        for (int e = 0; e < 4; ++e) Vt[(4 * q + e) * vt_ld + j] = v4[e];
+        *reinterpret_cast<uint2*>(Vs + j * kKRow + 4 * q) = vv[u];
       }
     }
   }
@@ -388,8 +392,7 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const AttnParam
       const int t = i / half, c = i - t * half;
       bf16* kr = Ks + (p.npre + t) * kKRow;
       float r0, r1;
-      rope_pair(__bfloat162float(kr[c]), __bfloat162float(kr[c + half]), base + static_cast<float>(t), p.rope_denom[c],
-                r0, r1);
+      rope_pair(__bfloat162float(kr[c]), __bfloat162float(kr[c + half]), p.rope[(base + t) * half + c], r0, r1);
       kr[c] = __float2bfloat16_rn(r0);
       kr[c + half] = __float2bfloat16_rn(r1);
     }
@@ -398,6 +401,7 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const AttnParam
 
   const int warp = tid >> 5, lane = tid & 31;
   const int g = lane >> 2, t4 = lane & 3;
+  const int lr = lane & 7, lm = lane >> 3;  // ldmatrix: row within, and index of, the lane's 8x8 matrix
   const int groups = p.heads / p.kv_heads;
   const int hgroups = groups / G;  // tasks per m-tile
   const int n_mt = p.chunk_pad / 16;
@@ -416,8 +420,8 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const AttnParam
   for (int task = t_lo; task < t_hi; ++task) {
     const int hg = task / n_mt, mt = task - hg * n_mt;
     const int h0 = kvh * groups + hg * G;  // first query head of the task
-    // the task's G x 16 query rows: raw, then RoPE in place
-    for (int i = tid; i < G * 16 * kHwPad / 4; i += kAttnThreads) {
+    // the task's G x 16 query rows with RoPE (position base + row)
+    for (int i = tid; i < G * 16 * (kHwPad / 4); i += kAttnThreads) {
       const int gr = i / (kHwPad / 4), q = i - gr * (kHwPad / 4);
       const int gh = gr / 16, r = gr - gh * 16;
       uint2 v = make_uint2(z2, z2);
@@ -431,35 +435,26 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const AttnParam
       const int r = gr & 15;
       float r0, r1;
       rope_pair(__bfloat162float(Qs[gr * kKRow + c]), __bfloat162float(Qs[gr * kKRow + c + half]),
-                base + static_cast<float>(mt * 16 + r), p.rope_denom[c], r0, r1);
+                p.rope[(base + mt * 16 + r) * half + c], r0, r1);
       Qs[gr * kKRow + c] = __float2bfloat16_rn(r0);
       Qs[gr * kKRow + c + half] = __float2bfloat16_rn(r1);
     }
     __syncthreads();
+    // A fragments: matrices (rows 0-7, k lo), (rows 8-15, k lo), (rows 0-7, k hi), (rows 8-15, k hi)
     uint32_t qa[G][kHwPad / 16][4];
 #pragma unroll
     for (int gh = 0; gh < G; ++gh)
 #pragma unroll
-      for (int ks = 0; ks < kHwPad / 16; ++ks) {
-        const bf16* q0 = Qs + (gh * 16 + g) * kKRow + ks * 16 + 2 * t4;
-        const bf16* q1 = q0 + 8 * kKRow;
-        qa[gh][ks][0] = *reinterpret_cast<const uint32_t*>(q0);
-        qa[gh][ks][1] = *reinterpret_cast<const uint32_t*>(q1);
-        qa[gh][ks][2] = *reinterpret_cast<const uint32_t*>(q0 + 8);
-        qa[gh][ks][3] = *reinterpret_cast<const uint32_t*>(q1 + 8);
-      }
+      for (int ks = 0; ks < kHwPad / 16; ++ks)
+        ldsm_x4(Qs + (gh * 16 + (lm & 1) * 8 + lr) * kKRow + ks * 16 + (lm >> 1) * 8, qa[gh][ks]);
     const int row0 = mt * 16 + g, row1 = row0 + 8;
     // scores of the 16 keys of block kk for the G heads (K fragments loaded once)
     auto scores16 = [&](int kk, float (&s)[G][2][4]) {
-      uint32_t kb[2][kHwPad / 16][2];
+      // B fragments: matrices (keys 0-7, k lo), (keys 0-7, k hi), (keys 8-15, k lo), (keys 8-15, k hi)
+      uint32_t kb[kHwPad / 16][4];
 #pragma unroll
-      for (int x = 0; x < 2; ++x)
-#pragma unroll
-        for (int ks = 0; ks < kHwPad / 16; ++ks) {
-          const bf16* kr = Ks + ((2 * kk + x) * 8 + g) * kKRow + ks * 16 + 2 * t4;
-          kb[x][ks][0] = *reinterpret_cast<const uint32_t*>(kr);
-          kb[x][ks][1] = *reinterpret_cast<const uint32_t*>(kr + 8);
-        }
+      for (int ks = 0; ks < kHwPad / 16; ++ks)
+        ldsm_x4(Ks + (kk * 16 + (lm >> 1) * 8 + lr) * kKRow + ks * 16 + (lm & 1) * 8, kb[ks]);
       float acc[G][2][4];
 #pragma unroll
       for (int gh = 0; gh < G; ++gh)
@@ -472,17 +467,28 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const AttnParam
 #pragma unroll
         for (int gh = 0; gh < G; ++gh)
 #pragma unroll
-          for (int x = 0; x < 2; ++x) mma_bf16_16816(acc[gh][x], qa[gh][ks], kb[x][ks][0], kb[x][ks][1]);
+          for (int x = 0; x < 2; ++x) mma_bf16_16816(acc[gh][x], qa[gh][ks], kb[ks][2 * x], kb[ks][2 * x + 1]);
+      float2 bias[2];
 #pragma unroll
-      for (int x = 0; x < 2; ++x)
+      for (int x = 0; x < 2; ++x) bias[x] = *reinterpret_cast<const float2*>(kbias + (2 * kk + x) * 8 + 2 * t4);
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int j = (2 * kk + x) * 8 + 2 * t4 + (e & 1);
-          const float bias = kbias[j];
-          const bool future = !p.cross && j >= p.npre && j - p.npre > (e < 2 ? row0 : row1);  // causal
+      for (int gh = 0; gh < G; ++gh)
 #pragma unroll
-          for (int gh = 0; gh < G; ++gh) s[gh][x][e] = future ? -INFINITY : fmaf(acc[gh][x][e], sc, bias);
-        }
+        for (int x = 0; x < 2; ++x)
+#pragma unroll
+          for (int e = 0; e < 4; ++e) s[gh][x][e] = fmaf(acc[gh][x][e], sc, (e & 1) ? bias[x].y : bias[x].x);
+      // causal action tokens: only blocks reaching past this m-tile's first row
+      if (!p.cross && kk * 16 + 15 - p.npre > mt * 16) {
+#pragma unroll
+        for (int x = 0; x < 2; ++x)
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int j = (2 * kk + x) * 8 + 2 * t4 + (e & 1);
+            if (j >= p.npre && j - p.npre > (e < 2 ? row0 : row1))
+#pragma unroll
+              for (int gh = 0; gh < G; ++gh) s[gh][x][e] = -INFINITY;
+          }
+      }
     };
     // phase 1: this warp's key blocks kk = warp, warp + 4, ...: online max / sum
     float m[G][2], l[G][2];
@@ -554,13 +560,12 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const AttnParam
     for (int kk = warp; kk < nkk; kk += kAttnWarps) {
       float s[G][2][4];
       scores16(kk, s);
-      uint32_t vb[kHwPad / 8][2];
+      // B fragments of V (transposed): matrices (keys lo, dims dn), (keys hi, dims dn),
+      // (keys lo, dims dn + 1), (keys hi, dims dn + 1)
+      uint32_t vb[kHwPad / 16][4];
 #pragma unroll
-      for (int dn = 0; dn < kHwPad / 8; ++dn) {
-        const bf16* vr = Vt + (dn * 8 + g) * vt_ld + kk * 16 + 2 * t4;
-        vb[dn][0] = *reinterpret_cast<const uint32_t*>(vr);
-        vb[dn][1] = *reinterpret_cast<const uint32_t*>(vr + 8);
-      }
+      for (int d2 = 0; d2 < kHwPad / 16; ++d2)
+        ldsm_x4_t(Vs + (kk * 16 + (lm & 1) * 8 + lr) * kKRow + (2 * d2 + (lm >> 1)) * 8, vb[d2]);
 #pragma unroll
       for (int gh = 0; gh < G; ++gh) {
         uint32_t pa[4];
@@ -573,7 +578,10 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const AttnParam
         pa[3] = pack_bf16(ex2_approx(s[gh][1][2] - m[gh][1]) * inv[gh][1],
                           ex2_approx(s[gh][1][3] - m[gh][1]) * inv[gh][1]);
 #pragma unroll
-        for (int dn = 0; dn < kHwPad / 8; ++dn) mma_bf16_16816(o[gh][dn], pa, vb[dn][0], vb[dn][1]);
+        for (int d2 = 0; d2 < kHwPad / 16; ++d2) {
+          mma_bf16_16816(o[gh][2 * d2], pa, vb[d2][0], vb[d2][1]);
+          mma_bf16_16816(o[gh][2 * d2 + 1], pa, vb[d2][2], vb[d2][3]);
+        }
       }
     }
     // partial outputs of the warps, summed in warp order (one head at a time)
@@ -582,12 +590,8 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const AttnParam
 #pragma unroll
       for (int dn = 0; dn < kHwPad / 8; ++dn) {
         const int c = dn * 8 + 2 * t4;
-        float* o0 = opart + (warp * 16 + g) * kHwPad + c;
-        float* o1 = opart + (warp * 16 + g + 8) * kHwPad + c;
-        o0[0] = o[gh][dn][0];
-        o0[1] = o[gh][dn][1];
-        o1[0] = o[gh][dn][2];
-        o1[1] = o[gh][dn][3];
+        *reinterpret_cast<float2*>(opart + (warp * 16 + g) * kHwPad + c) = make_float2(o[gh][dn][0], o[gh][dn][1]);
+        *reinterpret_cast<float2*>(opart + (warp * 16 + g + 8) * kHwPad + c) = make_float2(o[gh][dn][2], o[gh][dn][3]);
       }
       __syncthreads();
       for (int i = tid; i < 16 * (hw / 2); i += kAttnThreads) {
@@ -595,8 +599,9 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const AttnParam
         if (mt * 16 + r < p.chunk) {
           float a0 = 0.0f, a1 = 0.0f;
           for (int w = 0; w < kAttnWarps; ++w) {
-            a0 += opart[(w * 16 + r) * kHwPad + c];
-            a1 += opart[(w * 16 + r) * kHwPad + c + 1];
+            const float2 v = *reinterpret_cast<const float2*>(opart + (w * 16 + r) * kHwPad + c);
+            a0 += v.x;
+            a1 += v.y;
           }
           *reinterpret_cast<__nv_bfloat162*>(p.out + (tok0 + mt * 16 + r) * p.out_ld + (h0 + gh) * hw + c) =
               __floats2bfloat162_rn(a0, a1);
@@ -604,6 +609,259 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const AttnParam
       }
       __syncthreads();
     }
+  }
+}
+
+// Batched variant: one CTA per (sample, K / V head), K and V staged once;
+// each warp owns whole tasks (G query heads x 16 rows over every key), so a
+// task needs no cross-warp merge and no CTA barrier after the staging.  The
+// warp stages its queries with RoPE in its own buffer.  Same arithmetic as
+// attention_kernel (online max / sum over the keys in block order, then
+// bf16 probabilities times V).
+template <int G>
+__global__ void __launch_bounds__(kAttnThreads) attention_rows_kernel(const AttnParams p) {
+  extern __shared__ __align__(16) uint8_t smem[];
+  bf16* Ks = reinterpret_cast<bf16*>(smem);                  // [S_pad][kKRow]
+  bf16* Vs = Ks + static_cast<long long>(p.S_pad) * kKRow;  // [S_pad][kKRow]
+  float* kbias = reinterpret_cast<float*>(Vs + static_cast<long long>(p.S_pad) * kKRow);  // [S_pad]
+  bf16* Qw = reinterpret_cast<bf16*>(kbias + p.S_pad);      // [warps][G][16][kKRow]
+  const int b = blockIdx.x, kvh = blockIdx.y;
+  const int tid = threadIdx.x;
+  const int hw = p.hw, half = hw / 2, nq = hw / 4;
+  const int base = p.cross ? 0 : p.valid[static_cast<long long>(b) * p.valid_b];
+  const long long tok0 = static_cast<long long>(b) * p.chunk;
+  const uint32_t z2 = 0u;
+  for (int i = tid; i < p.S_pad * (kHwPad / 4); i += kAttnThreads) {
+    const int j = i / (kHwPad / 4), q = i - j * (kHwPad / 4);
+    if (j >= p.S || q >= nq) {
+      *reinterpret_cast<uint2*>(Ks + j * kKRow + 4 * q) = make_uint2(z2, z2);
+      *reinterpret_cast<uint2*>(Vs + j * kKRow + 4 * q) = make_uint2(z2, z2);
+    }
+  }
+  for (int i = tid; i < p.S_pad; i += kAttnThreads) {
+    float bias = -INFINITY;
+    if (i < p.npre) bias = p.mask[static_cast<long long>(b) * p.mask_b + i] != 0 ? 0.0f : -INFINITY;
+    else if (i < p.S) bias = 0.0f;
+    kbias[i] = bias;
+  }
+  const int items = p.S * nq;
+  for (int i0 = tid; i0 < items; i0 += kAttnThreads * kStageBatch) {
+    uint2 kv[kStageBatch], vv[kStageBatch];
+#pragma unroll
+    for (int u = 0; u < kStageBatch; ++u) {
+      const int i = i0 + u * kAttnThreads;
+      kv[u] = make_uint2(z2, z2);
+      vv[u] = make_uint2(z2, z2);
+      if (i < items) {
+        const int j = i / nq, q = i - j * nq;
+        const int col = kvh * hw + 4 * q;
+        if (p.cross) {
+          const bf16* row = p.kvp + (static_cast<long long>(b) * p.kvp_b + j) * p.kvp_ld;
+          kv[u] = ld_bf16x4(row + col);
+          vv[u] = ld_bf16x4(row + p.kv_w + col);
+        } else if (j < p.npre) {
+          const long long o = static_cast<long long>(b) * p.p_b * p.p_ld + p.layer_off +
+                              static_cast<long long>(j) * p.p_ld + col;
+          kv[u] = bf16x4_of(p.pk + o);
+          vv[u] = bf16x4_of(p.pv + o);
+        } else {
+          const bf16* row = p.qkv + (tok0 + j - p.npre) * p.qkv_ld;
+          kv[u] = ld_bf16x4(row + p.k_off + col);
+          vv[u] = ld_bf16x4(row + p.v_off + col);
+        }
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < kStageBatch; ++u) {
+      const int i = i0 + u * kAttnThreads;
+      if (i < items) {
+        const int j = i / nq, q = i - j * nq;
+        *reinterpret_cast<uint2*>(Ks + j * kKRow + 4 * q) = kv[u];
+        *reinterpret_cast<uint2*>(Vs + j * kKRow + 4 * q) = vv[u];
+      }
+    }
+  }
+  __syncthreads();
+  if (!p.cross) {
+    const int n = (p.S - p.npre) * half;
+    for (int i = tid; i < n; i += kAttnThreads) {
+      const int t = i / half, c = i - t * half;
+      bf16* kr = Ks + (p.npre + t) * kKRow;
+      float r0, r1;
+      rope_pair(__bfloat162float(kr[c]), __bfloat162float(kr[c + half]), p.rope[(base + t) * half + c], r0, r1);
+      kr[c] = __float2bfloat16_rn(r0);
+      kr[c + half] = __float2bfloat16_rn(r1);
+    }
+    __syncthreads();
+  }
+
+  const int warp = tid >> 5, lane = tid & 31;
+  const int g = lane >> 2, t4 = lane & 3;
+  const int lr = lane & 7, lm = lane >> 3;
+  const int groups = p.heads / p.kv_heads;
+  const int n_mt = p.chunk_pad / 16;
+  const int tasks = (groups / G) * n_mt;
+  const int nkk = p.S_pad / 16;
+  const float sc = 1.4426950408889634f / p.sqrt_hw;
+  bf16* Qs = Qw + warp * G * 16 * kKRow;
+  for (int task = warp; task < tasks; task += kAttnWarps) {
+    const int hg = task / n_mt, mt = task - hg * n_mt;
+    const int h0 = kvh * groups + hg * G;
+    __syncwarp();
+    // raw query rows, then RoPE in place (each lane rotates whole pairs)
+    for (int i = lane; i < G * 16 * (kHwPad / 4); i += 32) {
+      const int gr = i / (kHwPad / 4), q = i - gr * (kHwPad / 4);
+      const int gh = gr / 16, r = gr - gh * 16;
+      uint2 v = make_uint2(z2, z2);
+      if (mt * 16 + r < p.chunk && q < nq)
+        v = ld_bf16x4(p.qkv + (tok0 + mt * 16 + r) * p.qkv_ld + (h0 + gh) * hw + 4 * q);
+      *reinterpret_cast<uint2*>(Qs + gr * kKRow + 4 * q) = v;
+    }
+    __syncwarp();
+    for (int i = lane; i < G * 16 * half; i += 32) {
+      const int gr = i / half, c = i - gr * half;
+      const int r = gr & 15;
+      float r0, r1;
+      rope_pair(__bfloat162float(Qs[gr * kKRow + c]), __bfloat162float(Qs[gr * kKRow + c + half]),
+                p.rope[(base + mt * 16 + r) * half + c], r0, r1);
+      Qs[gr * kKRow + c] = __float2bfloat16_rn(r0);
+      Qs[gr * kKRow + c + half] = __float2bfloat16_rn(r1);
+    }
+    __syncwarp();
+    uint32_t qa[G][kHwPad / 16][4];
+#pragma unroll
+    for (int gh = 0; gh < G; ++gh)
+#pragma unroll
+      for (int ks = 0; ks < kHwPad / 16; ++ks)
+        ldsm_x4(Qs + (gh * 16 + (lm & 1) * 8 + lr) * kKRow + ks * 16 + (lm >> 1) * 8, qa[gh][ks]);
+    const int row0 = mt * 16 + g, row1 = row0 + 8;
+    auto scores16 = [&](int kk, float (&s)[G][2][4]) {
+      uint32_t kb[kHwPad / 16][4];
+#pragma unroll
+      for (int ks = 0; ks < kHwPad / 16; ++ks)
+        ldsm_x4(Ks + (kk * 16 + (lm >> 1) * 8 + lr) * kKRow + ks * 16 + (lm & 1) * 8, kb[ks]);
+      float acc[G][2][4];
+#pragma unroll
+      for (int gh = 0; gh < G; ++gh)
+#pragma unroll
+        for (int x = 0; x < 2; ++x)
+#pragma unroll
+          for (int e = 0; e < 4; ++e) acc[gh][x][e] = 0.0f;
+#pragma unroll
+      for (int ks = 0; ks < kHwPad / 16; ++ks)
+#pragma unroll
+        for (int gh = 0; gh < G; ++gh)
+#pragma unroll
+          for (int x = 0; x < 2; ++x) mma_bf16_16816(acc[gh][x], qa[gh][ks], kb[ks][2 * x], kb[ks][2 * x + 1]);
+      float2 bias[2];
+#pragma unroll
+      for (int x = 0; x < 2; ++x) bias[x] = *reinterpret_cast<const float2*>(kbias + (2 * kk + x) * 8 + 2 * t4);
+#pragma unroll
+      for (int gh = 0; gh < G; ++gh)
+#pragma unroll
+        for (int x = 0; x < 2; ++x)
+#pragma unroll
+          for (int e = 0; e < 4; ++e) s[gh][x][e] = fmaf(acc[gh][x][e], sc, (e & 1) ? bias[x].y : bias[x].x);
+      if (!p.cross && kk * 16 + 15 - p.npre > mt * 16) {
+#pragma unroll
+        for (int x = 0; x < 2; ++x)
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int j = (2 * kk + x) * 8 + 2 * t4 + (e & 1);
+            if (j >= p.npre && j - p.npre > (e < 2 ? row0 : row1))
+#pragma unroll
+              for (int gh = 0; gh < G; ++gh) s[gh][x][e] = -INFINITY;
+          }
+      }
+    };
+    float m[G][2], l[G][2];
+#pragma unroll
+    for (int gh = 0; gh < G; ++gh) {
+      m[gh][0] = m[gh][1] = -INFINITY;
+      l[gh][0] = l[gh][1] = 0.0f;
+    }
+    for (int kk = 0; kk < nkk; ++kk) {
+      float s[G][2][4];
+      scores16(kk, s);
+#pragma unroll
+      for (int gh = 0; gh < G; ++gh)
+#pragma unroll
+        for (int rr = 0; rr < 2; ++rr) {
+          const float tmax = fmaxf(fmaxf(s[gh][0][2 * rr], s[gh][0][2 * rr + 1]),
+                                   fmaxf(s[gh][1][2 * rr], s[gh][1][2 * rr + 1]));
+          const float mn = fmaxf(m[gh][rr], tmax);
+          if (mn != -INFINITY) {
+            l[gh][rr] = (m[gh][rr] == -INFINITY ? 0.0f : l[gh][rr] * ex2_approx(m[gh][rr] - mn)) +
+                        ex2_approx(s[gh][0][2 * rr] - mn) + ex2_approx(s[gh][0][2 * rr + 1] - mn) +
+                        ex2_approx(s[gh][1][2 * rr] - mn) + ex2_approx(s[gh][1][2 * rr + 1] - mn);
+            m[gh][rr] = mn;
+          }
+        }
+    }
+    float inv[G][2];
+#pragma unroll
+    for (int gh = 0; gh < G; ++gh)
+#pragma unroll
+      for (int rr = 0; rr < 2; ++rr) {
+#pragma unroll
+        for (int off = 1; off <= 2; off <<= 1) {
+          const float mo = __shfl_xor_sync(0xffffffffu, m[gh][rr], off);
+          const float lo = __shfl_xor_sync(0xffffffffu, l[gh][rr], off);
+          const float mn = fmaxf(m[gh][rr], mo);
+          if (mn != -INFINITY)
+            l[gh][rr] = (m[gh][rr] == -INFINITY ? 0.0f : l[gh][rr] * ex2_approx(m[gh][rr] - mn)) +
+                        (mo == -INFINITY ? 0.0f : lo * ex2_approx(mo - mn));
+          m[gh][rr] = mn;
+        }
+        inv[gh][rr] = 1.0f / l[gh][rr];
+      }
+    float o[G][kHwPad / 8][4];
+#pragma unroll
+    for (int gh = 0; gh < G; ++gh)
+#pragma unroll
+      for (int dn = 0; dn < kHwPad / 8; ++dn)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) o[gh][dn][e] = 0.0f;
+    for (int kk = 0; kk < nkk; ++kk) {
+      float s[G][2][4];
+      scores16(kk, s);
+      uint32_t vb[kHwPad / 16][4];
+#pragma unroll
+      for (int d2 = 0; d2 < kHwPad / 16; ++d2)
+        ldsm_x4_t(Vs + (kk * 16 + (lm & 1) * 8 + lr) * kKRow + (2 * d2 + (lm >> 1)) * 8, vb[d2]);
+#pragma unroll
+      for (int gh = 0; gh < G; ++gh) {
+        uint32_t pa[4];
+        pa[0] = pack_bf16(ex2_approx(s[gh][0][0] - m[gh][0]) * inv[gh][0],
+                          ex2_approx(s[gh][0][1] - m[gh][0]) * inv[gh][0]);
+        pa[1] = pack_bf16(ex2_approx(s[gh][0][2] - m[gh][1]) * inv[gh][1],
+                          ex2_approx(s[gh][0][3] - m[gh][1]) * inv[gh][1]);
+        pa[2] = pack_bf16(ex2_approx(s[gh][1][0] - m[gh][0]) * inv[gh][0],
+                          ex2_approx(s[gh][1][1] - m[gh][0]) * inv[gh][0]);
+        pa[3] = pack_bf16(ex2_approx(s[gh][1][2] - m[gh][1]) * inv[gh][1],
+                          ex2_approx(s[gh][1][3] - m[gh][1]) * inv[gh][1]);
+#pragma unroll
+        for (int d2 = 0; d2 < kHwPad / 16; ++d2) {
+          mma_bf16_16816(o[gh][2 * d2], pa, vb[d2][0], vb[d2][1]);
+          mma_bf16_16816(o[gh][2 * d2 + 1], pa, vb[d2][2], vb[d2][3]);
+        }
+      }
+    }
+#pragma unroll
+    for (int gh = 0; gh < G; ++gh)
+#pragma unroll
+      for (int dn = 0; dn < kHwPad / 8; ++dn) {
+        const int c = dn * 8 + 2 * t4;
+        if (c < hw) {
+          bf16* orow = p.out + (h0 + gh) * hw + c;
+          if (row0 < p.chunk)
+            *reinterpret_cast<__nv_bfloat162*>(orow + (tok0 + row0) * p.out_ld) =
+                __floats2bfloat162_rn(o[gh][dn][0], o[gh][dn][1]);
+          if (row1 < p.chunk)
+            *reinterpret_cast<__nv_bfloat162*>(orow + (tok0 + row1) * p.out_ld) =
+                __floats2bfloat162_rn(o[gh][dn][2], o[gh][dn][3]);
+        }
+      }
   }
 }
 
@@ -670,9 +928,12 @@ class SmolVLA final : public SmolVLADevice {
                ? 3
                : 1;
   }
+  static std::size_t attn_rows_smem(int S_pad, int G) {
+    return static_cast<std::size_t>(S_pad) * kKRow * 2 * 2 + static_cast<std::size_t>(S_pad) * 4 +
+           static_cast<std::size_t>(kAttnWarps) * G * 16 * kKRow * 2;
+  }
   std::size_t attn_smem(int S_pad, int G) const {
-    return static_cast<std::size_t>(S_pad) * kKRow * 2 + static_cast<std::size_t>(kHwPad) * (S_pad + 8) * 2 +
-           static_cast<std::size_t>(S_pad) * 4 + static_cast<std::size_t>(G) * kAttnWarps * 16 * 2 * 4 +
+    return static_cast<std::size_t>(S_pad) * kKRow * 2 * 2 + static_cast<std::size_t>(S_pad) * 4 + static_cast<std::size_t>(G) * kAttnWarps * 16 * 2 * 4 +
            static_cast<std::size_t>(kAttnWarps) * 16 * kHwPad * 4 + static_cast<std::size_t>(G) * 16 * kKRow * 2;
   }
 
@@ -693,8 +954,9 @@ class SmolVLA final : public SmolVLADevice {
   float *x_ = nullptr, *h_ = nullptr, *v_ = nullptr, *temb_ = nullptr, *tval_ = nullptr;
   bf16* proj_ = nullptr;  // bf16 output projection (o / down), added to h by the next norm
   float *kcache_ = nullptr, *vcache_ = nullptr, *io_ = nullptr;
+  float2* rope_tab_ = nullptr;  // [prefix + chunk][head_width / 2] (cos, sin), rebuilt by every call
   __half *x2_ = nullptr, *a2_ = nullptr, *h12_ = nullptr, *fin2_ = nullptr, *c2_ = nullptr;
-  bf16 *nb_ = nullptr, *qkv_ = nullptr, *att_ = nullptr, *gu_ = nullptr, *act_ = nullptr, *kvp_ = nullptr;
+  bf16 *nb_ = nullptr, *qkv_ = nullptr, *att_ = nullptr, *act_ = nullptr, *kvp_ = nullptr;
   std::uint8_t* mask_ = nullptr;
   int *valid_ = nullptr, *step_ = nullptr;
   std::size_t prefix_ = 0;
@@ -905,7 +1167,13 @@ bool SmolVLA::load(const TensorTable& t, std::string& err) {
       put_mat(L.qkv, {&s.q, &s.k, &s.v}, W_, false);
     }
     put_mat(L.o, {&s.o}, attn_, false);
-    put_mat(L.gu, {&s.g, &s.u}, W_, false);
+    // rows interleaved gate / up (gate f at 2f, up f at 2f + 1) for the SwiGLU epilogue
+    std::vector<float> gu(static_cast<std::size_t>(2) * mlp * W);
+    for (std::size_t f = 0; f < mlp; ++f) {
+      std::memcpy(&gu[(2 * f) * W], &s.g[f * W], W * 4);
+      std::memcpy(&gu[(2 * f + 1) * W], &s.u[f * W], W * 4);
+    }
+    put_mat(L.gu, {&gu}, W_, false);
     put_mat(L.down, {&s.d}, mlp_, false);
     L.in_norm = put_vec(s.in_norm);
     L.post_norm = put_vec(s.post_norm);
@@ -950,6 +1218,8 @@ bool SmolVLA::load(const TensorTable& t, std::string& err) {
   }
   cudaFuncSetAttribute(attention_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
   cudaFuncSetAttribute(attention_kernel<3>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+  cudaFuncSetAttribute(attention_rows_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+  cudaFuncSetAttribute(attention_rows_kernel<3>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
   if (cudaDeviceSynchronize() != cudaSuccess) {
     err = "SmolVLA weight upload failed";
     return false;
@@ -993,9 +1263,9 @@ int SmolVLA::reserve(std::size_t batch, std::size_t chunk, std::size_t prefix, b
   plan.add_n<bf16>(ra * Wp);                         // nb
   plan.add_n<bf16>(ra * qkv_ld_);                    // qkv
   plan.add_n<bf16>(ra * attn_p_);                    // att
-  plan.add_n<bf16>(ra * 2 * mlp_);                   // gu
   plan.add_n<bf16>(ra * mlp_p_);                     // act
   plan.add_n<bf16>(L * prow * kvp_ld_);              // kvp
+  plan.add_n<float2>((Pc + Cc) * cfg_.head_width / 2);
   plan.add_n<std::uint8_t>(Sc * Pc);
   plan.add_n<int>(Sc + 4);
   ws_.release();
@@ -1020,9 +1290,9 @@ int SmolVLA::reserve(std::size_t batch, std::size_t chunk, std::size_t prefix, b
   nb_ = ws_.take_n<bf16>(ra * Wp);
   qkv_ = ws_.take_n<bf16>(ra * qkv_ld_);
   att_ = ws_.take_n<bf16>(ra * attn_p_);
-  gu_ = ws_.take_n<bf16>(ra * 2 * mlp_);
   act_ = ws_.take_n<bf16>(ra * mlp_p_);
   kvp_ = ws_.take_n<bf16>(L * prow * kvp_ld_);
+  rope_tab_ = ws_.take_n<float2>((Pc + Cc) * cfg_.head_width / 2);
   mask_ = ws_.take_n<std::uint8_t>(Sc * Pc);
   valid_ = ws_.take_n<int>(Sc + 4);
   step_ = valid_ + Sc;
@@ -1084,7 +1354,7 @@ int SmolVLA::check_prefix(const std::uint8_t* mask, std::size_t prefix, std::siz
     return 1;
   }
   const int S = static_cast<int>(ref_layout_ ? prefix + chunk : std::max(prefix, chunk));
-  if (attn_smem(pad(S, 16), 3) > 227 * 1024) {
+  if (std::max(attn_smem(pad(S, 16), 3), attn_rows_smem(pad(S, 16), 3)) > 227 * 1024) {
     err = "SmolVLA prefix + chunk exceeds this build's attention tile (shared memory)";
     return 1;
   }
@@ -1115,6 +1385,14 @@ bool SmolVLA::prepare_prefix(const float* keys, const float* values, const std::
   cudaMemcpyAsync(mask_, mask, samples * prefix, kind, st);
   count_valid_kernel<<<static_cast<unsigned>(samples), 256, 0, st>>>(mask_, static_cast<int>(prefix), valid_);
   ++launches_;
+  // RoPE angles of every position a call can reach (valid prefix slots + action tokens)
+  {
+    const int half = static_cast<int>(cfg_.head_width / 2);
+    const int npos = static_cast<int>(prefix + cap_chunk_);
+    rope_table_kernel<<<ew_grid(static_cast<long long>(npos) * half, 256, *ctx_), 256, 0, st>>>(rope_, half, npos,
+                                                                                                rope_tab_);
+    ++launches_;
+  }
   prefix_ = prefix;
   const long long prow = static_cast<long long>(samples * prefix);
   for (std::size_t l = 0; l < L; ++l) {
@@ -1168,7 +1446,7 @@ bool SmolVLA::attention(const Layer& Ly, std::size_t li, std::size_t batch, std:
   p.mask_b = shared ? 0 : P;
   p.valid = valid_;
   p.valid_b = shared ? 0 : 1;
-  p.rope_denom = rope_;
+  p.rope = rope_tab_;
   p.chunk = static_cast<int>(chunk);
   p.chunk_pad = pad(p.chunk, 16);
   p.P = P;
@@ -1183,6 +1461,19 @@ bool SmolVLA::attention(const Layer& Ly, std::size_t li, std::size_t batch, std:
   p.out = att_;
   p.out_ld = attn_p_;
   const int G = attn_g(batch);
+  if (static_cast<long long>(batch) * p.kv_heads >= 2LL * ctx_->sm_count) {
+    // enough (sample, head) CTAs to fill the GPU: warps own whole tasks
+    const dim3 grid(static_cast<unsigned>(batch), static_cast<unsigned>(cfg_.kv_heads));
+    const std::size_t rsmem = attn_rows_smem(p.S_pad, G);
+    if (G == 3) attention_rows_kernel<3><<<grid, kAttnThreads, rsmem, st>>>(p);
+    else attention_rows_kernel<1><<<grid, kAttnThreads, rsmem, st>>>(p);
+    ++launches_;
+    if (cudaGetLastError() != cudaSuccess) {
+      err = "SmolVLA attention launch failed";
+      return false;
+    }
+    return true;
+  }
   const std::size_t smem = attn_smem(p.S_pad, G);
   // tasks of a K / V head: (G query heads of its group, 16 query rows), all
   // four warps on each; one CTA per task while the (sample, head) CTAs alone
@@ -1214,9 +1505,9 @@ bool SmolVLA::record_layers(std::size_t batch, std::size_t chunk, bool shared, i
     if (!gemm(L.o, att_, rows, proj_, Wp_, false, 0, nullptr, nullptr, tc::kActNone, st, err)) return false;
     rms_kernel<<<rgrid, 256, 0, st>>>(h_, Wp_, proj_, Wp_, L.post_norm, W_, rows, 0, nb_, Wp_);
     ++launches_;
-    if (!gemm(L.gu, nb_, rows, gu_, 2 * mlp_, false, 0, nullptr, nullptr, tc::kActNone, st, err)) return false;
-    gate_silu_kernel<<<ew_grid(rows * (mlp_ / 2), 256, *ctx_), 256, 0, st>>>(gu_, 2 * mlp_, mlp_, act_, mlp_p_, rows);
-    ++launches_;
+    // act = bf16(bf16(up) * SiLU(bf16(gate))) straight from the GEMM epilogue
+    // (gate_silu, kernels_scalar.cc:61-67, smolvla_action_expert.cc:366-372)
+    if (!gemm(L.gu, nb_, rows, act_, mlp_p_, false, 0, nullptr, nullptr, tc::kActSwiGLU, st, err)) return false;
     if (!gemm(L.down, act_, rows, proj_, Wp_, false, 0, nullptr, nullptr, tc::kActNone, st, err)) return false;
     pending = proj_;
   }

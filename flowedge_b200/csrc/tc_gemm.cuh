@@ -49,7 +49,10 @@ constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + 256 + 4 * EPI_PARTS * M
                            MAX_TILE_SAMPLES * MAX_TILE_GROUPS * 8 + 3 * MAX_TILE_SAMPLES * 16;
 static_assert(SMEM_BYTES <= 232448, "shared memory above the 227 KB per-CTA limit");
 
-enum Act : int { kActNone = 0, kActSilu = 1, kActSoftplus = 2 };
+// kActSwiGLU: accumulator rows interleave gate (even row 2f) and up (odd row
+// 2f + 1) of feature f; the output holds bf16(bf16(up) * SiLU(bf16(gate))) at
+// channel f (bf16 output, plain epilogue).
+enum Act : int { kActNone = 0, kActSilu = 1, kActSoftplus = 2, kActSwiGLU = 3 };
 
 struct Seg {
   int src;      // which B tensor map (0..2)
@@ -378,7 +381,16 @@ static __global__ void __launch_bounds__(THREADS, 1)
             for (int j = 0; j < CH; ++j) y[j] = softplus_f(y[j]);
           }
           const long long oc = o0 + static_cast<long long>(c) * cs;
-          if (p.out_f32) {
+          if (p.act == kActSwiGLU) {
+            // the gate lane (even row) takes the up value of the next lane
+            __nv_bfloat16* o = static_cast<__nv_bfloat16*>(p.out) + (oc - m + (m >> 1));
+#pragma unroll
+            for (int j = 0; j < CH; ++j) {
+              const float r = __bfloat162float(__float2bfloat16_rn(y[j]));
+              const float up = __shfl_xor_sync(0xffffffffu, r, 1);
+              if ((lane & 1) == 0 && c + j < lim) o[j * cs] = __float2bfloat16_rn(up * (r / (1.0f + expf(-r))));
+            }
+          } else if (p.out_f32) {
             float* o = static_cast<float*>(p.out) + oc;
             if (p.out_accumulate) {
 #pragma unroll

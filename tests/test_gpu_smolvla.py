@@ -84,6 +84,24 @@ def test_smolvla_c5_batched_matches_restatement(tmp_path):
     e.close()
 
 
+def test_smolvla_c5_large_batch_matches_restatement(tmp_path):
+    """A batch large enough for the warp-per-task attention kernel (batch x K/V
+    heads >= 2 x SMs), one shared prefix with masked slots: first and last
+    rows against the restatement."""
+    spec = C5_SMALL
+    tensors, e = _engine(tmp_path, spec, 51)
+    model = restate.SmolVLAExpert(tensors)
+    keys, values, mask = ck.smolvla_prefix(spec, 52, masked=11)
+    rng = np.random.default_rng(53)
+    noise = rng.standard_normal((80, spec.chunk, spec.action_dim), dtype=np.float32)
+    out = e.smolvla_sample_batch(noise, 10, keys, values, mask, shared_prefix=True)
+    for b in (0, 79):
+        err = float(np.abs(out[b] - model.sample(noise[b], 10, keys, values, mask)).max())
+        print(f"C5 (4 layers) batch-80 row {b} Euler-10 max-abs vs restatement: {err:.3g}")
+        assert err <= 2e-2
+    e.close()
+
+
 def test_smolvla_c5_full_depth_matches_restatement(tmp_path):
     """BASELINE configuration 5 at full depth (16 layers), batch 1, Euler-10."""
     spec = ck.SMOLVLA_C5
