@@ -112,63 +112,82 @@ __global__ void time_embed_kernel(const int* step_idx, int steps, const float* t
 //   epilogue already rounded to bf16)
 //   n = bf16(bf16(h * scale) * w), scale = 1 / sqrt(sum(h^2) / W + 1e-5)
 // out_mode 0: n as bf16 [rows][ld_out]; 1: fp16 hi / lo [rows][2 ld_out]; 2: fp32 [rows][ld_out].
-// The row stays in registers (W <= 32 * kRmsPerLane); every load of a row is
-// issued before the first is used.
-constexpr int kRmsPerLane = 32;
+// Lane l holds elements 4 (l + 32 k) .. + 3 (16-byte loads, W a multiple of 4,
+// W <= 128 * kRmsVec); every load of a row is issued before the first use.
+constexpr int kRmsVec = 8;
+__device__ __forceinline__ float4 bf16x4_to_f4(uint2 u) {
+  return make_float4(__uint_as_float(u.x << 16), __uint_as_float(u.x & 0xFFFF0000u), __uint_as_float(u.y << 16),
+                     __uint_as_float(u.y & 0xFFFF0000u));
+}
 __global__ void rms_kernel(float* __restrict__ h, int ld_h, const bf16* __restrict__ proj, int ld_p,
                            const float* __restrict__ w, int W, long long rows, int out_mode, void* out, int ld_out) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const long long r = blockIdx.x * static_cast<long long>(blockDim.x >> 5) + warp;
   if (r >= rows) return;
   float* hr = h + r * ld_h;
-  float v[kRmsPerLane];
+  float4 v[kRmsVec];
 #pragma unroll
-  for (int k = 0; k < kRmsPerLane; ++k) {
-    const int c = lane + 32 * k;
-    v[k] = c < W ? hr[c] : 0.0f;
+  for (int k = 0; k < kRmsVec; ++k) {
+    const int c = 4 * (lane + 32 * k);
+    v[k] = c < W ? *reinterpret_cast<const float4*>(hr + c) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
   }
   if (proj != nullptr) {
-    float pr[kRmsPerLane];
+    uint2 pr[kRmsVec];
 #pragma unroll
-    for (int k = 0; k < kRmsPerLane; ++k) {
-      const int c = lane + 32 * k;
-      pr[k] = c < W ? __bfloat162float(proj[r * ld_p + c]) : 0.0f;
+    for (int k = 0; k < kRmsVec; ++k) {
+      const int c = 4 * (lane + 32 * k);
+      pr[k] = c < W ? __ldg(reinterpret_cast<const uint2*>(proj + r * ld_p + c)) : make_uint2(0u, 0u);
     }
 #pragma unroll
-    for (int k = 0; k < kRmsPerLane; ++k) {
-      const int c = lane + 32 * k;
+    for (int k = 0; k < kRmsVec; ++k) {
+      const int c = 4 * (lane + 32 * k);
       if (c < W) {
-        v[k] = bf16r(__fadd_rn(v[k], pr[k]));
-        hr[c] = v[k];
+        const float4 pf = bf16x4_to_f4(pr[k]);
+        v[k] = make_float4(bf16r(__fadd_rn(v[k].x, pf.x)), bf16r(__fadd_rn(v[k].y, pf.y)),
+                           bf16r(__fadd_rn(v[k].z, pf.z)), bf16r(__fadd_rn(v[k].w, pf.w)));
+        *reinterpret_cast<float4*>(hr + c) = v[k];
       }
     }
   }
   float ss = 0.0f;
 #pragma unroll
-  for (int k = 0; k < kRmsPerLane; ++k) ss = fmaf(v[k], v[k], ss);
+  for (int k = 0; k < kRmsVec; ++k) {
+    ss = fmaf(v[k].x, v[k].x, ss);
+    ss = fmaf(v[k].y, v[k].y, ss);
+    ss = fmaf(v[k].z, v[k].z, ss);
+    ss = fmaf(v[k].w, v[k].w, ss);
+  }
 #pragma unroll
   for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
   const float scale = 1.0f / sqrtf(__fadd_rn(ss / static_cast<float>(W), 1e-5f));
-  float wv[kRmsPerLane];
+  float4 wv[kRmsVec];
 #pragma unroll
-  for (int k = 0; k < kRmsPerLane; ++k) {
-    const int c = lane + 32 * k;
-    wv[k] = c < W ? __ldg(w + c) : 0.0f;
+  for (int k = 0; k < kRmsVec; ++k) {
+    const int c = 4 * (lane + 32 * k);
+    wv[k] = c < W ? __ldg(reinterpret_cast<const float4*>(w + c)) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
   }
+  auto norm = [&](float x, float wx) { return bf16r(__fmul_rn(bf16r(__fmul_rn(x, scale)), wx)); };
 #pragma unroll
-  for (int k = 0; k < kRmsPerLane; ++k) {
-    const int c = lane + 32 * k;
+  for (int k = 0; k < kRmsVec; ++k) {
+    const int c = 4 * (lane + 32 * k);
     if (c >= W) continue;
-    const float n = bf16r(__fmul_rn(bf16r(__fmul_rn(v[k], scale)), wv[k]));
+    const float4 n = make_float4(norm(v[k].x, wv[k].x), norm(v[k].y, wv[k].y), norm(v[k].z, wv[k].z),
+                                 norm(v[k].w, wv[k].w));
     if (out_mode == 0) {
-      static_cast<bf16*>(out)[r * ld_out + c] = __float2bfloat16_rn(n);
+      *reinterpret_cast<uint2*>(static_cast<bf16*>(out) + r * ld_out + c) =
+          make_uint2(pack_bf16(n.x, n.y), pack_bf16(n.z, n.w));
     } else if (out_mode == 1) {
-      __half* o = static_cast<__half*>(out) + r * 2 * ld_out;
-      const __half hi = to_half_sat(n);
-      o[c] = hi;
-      o[ld_out + c] = __float2half_rn(n - __half2float(hi));
+      __half* o = static_cast<__half*>(out) + r * 2 * ld_out + c;
+      const __half h0 = to_half_sat(n.x), h1 = to_half_sat(n.y), h2 = to_half_sat(n.z), h3 = to_half_sat(n.w);
+      const __half2 hi01 = __halves2half2(h0, h1), hi23 = __halves2half2(h2, h3);
+      const __half2 lo01 = __floats2half2_rn(n.x - __half2float(h0), n.y - __half2float(h1));
+      const __half2 lo23 = __floats2half2_rn(n.z - __half2float(h2), n.w - __half2float(h3));
+      *reinterpret_cast<uint2*>(o) = make_uint2(*reinterpret_cast<const uint32_t*>(&hi01),
+                                                *reinterpret_cast<const uint32_t*>(&hi23));
+      *reinterpret_cast<uint2*>(o + ld_out) = make_uint2(*reinterpret_cast<const uint32_t*>(&lo01),
+                                                         *reinterpret_cast<const uint32_t*>(&lo23));
     } else {
-      static_cast<float*>(out)[r * ld_out + c] = n;
+      *reinterpret_cast<float4*>(static_cast<float*>(out) + r * ld_out + c) = n;
     }
   }
 }
@@ -1027,9 +1046,9 @@ bool SmolVLA::load(const TensorTable& t, std::string& err) {
     hw = static_cast<std::size_t>(v[0]);
   }
   if (hw % 4 != 0 || hw > kHwPad || attn % hw != 0 || kvw % hw != 0 || kvw == 0 || (attn / hw) % (kvw / hw) != 0 ||
-      mlp % 2 != 0 || W > 32 * static_cast<std::size_t>(kRmsPerLane)) {
+      mlp % 2 != 0 || W % 4 != 0 || W > 128 * static_cast<std::size_t>(kRmsVec)) {
     err = "SmolVLA geometry unsupported by this build (head width a multiple of 4 and <= 64, query heads a "
-          "multiple of K/V heads, expert width <= 1024)";
+          "multiple of K/V heads, expert width a multiple of 4 and <= 1024)";
     return false;
   }
   std::vector<std::size_t> kv_in;
