@@ -438,6 +438,8 @@ def _extras(workdir: Path, device: int):
         e = Engine(mamba, threads=0, device=device, precision=prec, max_batch=1024)
         out[f"c3_mamba_b1_prefill128_{prec}"] = _latency(lambda: e.run(tokens), 100)
         out[f"c3_mamba_flow_b1_sample_euler10_{prec}"] = _latency(lambda: e.sample(tokens, x0, 10, "euler"), 100)
+        e.reset()
+        out[f"c3_mamba_decode_token_{prec}"] = _latency(lambda: e.step(5), 500)
         tb = np.ascontiguousarray(np.tile(tokens, (1024, 1)))
         e.run_batch(tb[:2])
         t0 = time.perf_counter()

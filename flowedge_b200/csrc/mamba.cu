@@ -237,10 +237,225 @@ __global__ void conv_step_kernel(const float* xz, int di, int dc, float* window,
   u[c] = silu_f(acc);
 }
 
+// ---------------------------------------------------------------------------
+// Fused streaming decode: one cooperative launch per token (mamba.cc:317-382).
+// Every CTA is resident; phases are separated by a bounded grid barrier
+// (monotonic arrival counter, release / acquire at GPU scope).  Per layer:
+//   A. RMSNorm of the residual (each CTA computes the scale itself and stages
+//      the normed row in shared memory); in_proj rows spread over all warps
+//      (one warp per row, lanes stride K); the warp of x row c then steps the
+//      conv window of channel c and writes u[c] = SiLU(conv)       | barrier
+//   B. x_proj rows ([dt_in | B | C])                                 | barrier
+//   C. dt_proj + softplus, selective-scan update and the SiLU(z) gate,
+//      one thread per channel (scan_kernel's expression order)      | barrier
+//   D. out_proj rows added to the residual                          | barrier
+// then the final RMSNorm.  Data written inside the launch is read through L2
+// (ld.global.cg); a channel's conv window and scan state are touched only by
+// the thread that owns the channel.
+
+constexpr int kDecThreads = 512;
+constexpr int kDecWarps = kDecThreads / 32;
+
+struct DecodeLayer {
+  const void* w_in;   // [2 di][ld_in], fp32 or fp16
+  const void* w_x;    // [dr + 2 ds][ld_x]
+  const void* w_out;  // [dm][ld_out]
+  int ld_in, ld_x, ld_out;
+  const float *norm, *conv_w, *conv_b, *dt_w, *dt_b, *a_neg, *d;
+};
+
+struct DecodeParams {
+  const DecodeLayer* layers;
+  int n_layers, dm, di, ds, dc, dr;
+  const int* token;
+  const float* emb;
+  const float* norm_f;
+  float* state;  // [layers][di * (dc + ds)]: window [di][dc], then h [ds][di]
+  float *x, *xz, *u, *dbl, *y, *out;
+  unsigned* sync;  // [0] arrivals, [2] abort
+  int* err;
+};
+
+__device__ bool dec_grid_sync(const DecodeParams& p, unsigned& epoch) {
+  __shared__ int s_ok;
+  __syncthreads();
+  ++epoch;
+  if (threadIdx.x == 0) {
+    volatile unsigned* abort_flag = p.sync + 2;
+    int ok = *abort_flag == 0u;
+    if (ok) {
+      const unsigned target = epoch * gridDim.x;
+      asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(p.sync) : "memory");
+      const uint64_t t0 = global_ns();
+      for (uint32_t spin = 0;; ++spin) {
+        unsigned v;
+        asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p.sync) : "memory");
+        if (v >= target) break;
+        if ((spin & 15u) == 15u) {
+          if (*abort_flag != 0u) {
+            ok = 0;
+            break;
+          }
+          if (global_ns() - t0 > kWaitNs) {
+            atomicCAS(p.err, 0, kErrGridBarrierTimeout);
+            atomicExch(p.sync + 2, 1u);
+            ok = 0;
+            break;
+          }
+        }
+      }
+    }
+    s_ok = ok;
+  }
+  __syncthreads();
+  return s_ok != 0;
+}
+
+// sum over a row of `n` weights times the shared / global vector v (one warp)
+template <bool HALF>
+__device__ __forceinline__ float warp_dot(const void* w, long long row, int ld, int n, const float* v) {
+  float acc = 0.0f;
+  const int lane = threadIdx.x & 31;
+  // lane l takes pairs (k, k + 1), k = 2 l + 64 j; four pairs in flight
+  if constexpr (HALF) {
+    const __half* wr = static_cast<const __half*>(w) + row * ld;
+    for (int k0 = lane * 2; k0 < n; k0 += 256) {
+      __half2 h2[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int k = k0 + 64 * u;
+        h2[u] = k < n ? *reinterpret_cast<const __half2*>(wr + k) : __floats2half2_rn(0.0f, 0.0f);
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int k = k0 + 64 * u;
+        if (k < n) acc = fmaf(__low2float(h2[u]), v[k], acc);
+        if (k + 1 < n) acc = fmaf(__high2float(h2[u]), v[k + 1], acc);
+      }
+    }
+  } else {
+    const float* wr = static_cast<const float*>(w) + row * ld;
+    for (int k0 = lane * 2; k0 < n; k0 += 256) {
+      float2 f2[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int k = k0 + 64 * u;
+        f2[u] = k < n ? *reinterpret_cast<const float2*>(wr + k) : make_float2(0.0f, 0.0f);
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int k = k0 + 64 * u;
+        if (k < n) acc = fmaf(f2[u].x, v[k], acc);
+        if (k + 1 < n) acc = fmaf(f2[u].y, v[k + 1], acc);
+      }
+    }
+  }
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+  return acc;
+}
+
+// RMSNorm scale of the residual (read through L2), every CTA on its own
+__device__ float dec_rms_scale(const float* x, int dm, float* red) {
+  float ss = 0.0f;
+  for (int k = threadIdx.x; k < dm; k += blockDim.x) {
+    const float v = __ldcg(x + k);
+    ss = fmaf(v, v, ss);
+  }
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  float t = 0.0f;
+  for (int w = 0; w < kDecWarps; ++w) t += red[w];
+  __syncthreads();
+  return 1.0f / sqrtf((t / static_cast<float>(dm)) + 1e-5f);
+}
+
+template <bool HALF>
+__global__ void __launch_bounds__(kDecThreads, 1) mamba_decode_kernel(const DecodeParams p) {
+  extern __shared__ float sh[];  // [max(dm, di)] staged input vector
+  __shared__ float red[kDecWarps];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // index i belongs to CTA i % gridDim.x: short loops still spread over every SM
+  const int gwarp = warp * gridDim.x + blockIdx.x, nwarps = gridDim.x * kDecWarps;
+  const int gthread = threadIdx.x * gridDim.x + blockIdx.x, nthreads = gridDim.x * blockDim.x;
+  const int dm = p.dm, di = p.di, ds = p.ds, dc = p.dc, dr = p.dr, wd = dr + 2 * ds;
+  unsigned epoch = 0;
+  const int tok = *p.token;
+  for (int k = gthread; k < dm; k += nthreads) p.x[k] = p.emb[static_cast<long long>(tok) * dm + k];
+  if (!dec_grid_sync(p, epoch)) return;
+  const std::size_t per = static_cast<std::size_t>(di) * (dc + ds);
+  for (int li = 0; li < p.n_layers; ++li) {
+    const DecodeLayer L = p.layers[li];
+    float* window = p.state + li * per;
+    float* h = window + static_cast<std::size_t>(di) * dc;
+    // A. normed row (x * scale * w, kernels_scalar.cc:48-60), in_proj, conv step
+    const float scale = dec_rms_scale(p.x, dm, red);
+    for (int k = threadIdx.x; k < dm; k += blockDim.x) sh[k] = __ldcg(p.x + k) * scale * L.norm[k];
+    __syncthreads();
+    for (int r = gwarp; r < 2 * di; r += nwarps) {
+      const float v = warp_dot<HALF>(L.w_in, r, L.ld_in, dm, sh);
+      if (lane == 0) {
+        p.xz[r] = v;
+        if (r < di) {  // conv_step_kernel: shift, append, conv + bias, SiLU
+          float* wc = window + static_cast<long long>(r) * dc;
+          for (int k = 0; k + 1 < dc; ++k) wc[k] = wc[k + 1];
+          wc[dc - 1] = v;
+          float acc = L.conv_b[r];
+          for (int k = 0; k < dc; ++k) acc += L.conv_w[r * dc + k] * wc[k];
+          p.u[r] = silu_f(acc);
+        }
+      }
+    }
+    if (!dec_grid_sync(p, epoch)) return;
+    // B. x_proj
+    for (int k = threadIdx.x; k < di; k += blockDim.x) sh[k] = __ldcg(p.u + k);
+    __syncthreads();
+    for (int r = gwarp; r < wd; r += nwarps) {
+      const float v = warp_dot<HALF>(L.w_x, r, L.ld_x, di, sh);
+      if (lane == 0) p.dbl[r] = v;
+    }
+    if (!dec_grid_sync(p, epoch)) return;
+    // C. scan step per channel (scan_kernel order, non-FAST)
+    for (int k = threadIdx.x; k < wd; k += blockDim.x) sh[k] = __ldcg(p.dbl + k);
+    __syncthreads();
+    for (int c = gthread; c < di; c += nthreads) {
+      float acc = 0.0f;
+      for (int r = 0; r < dr; ++r) acc += sh[r] * L.dt_w[c * dr + r];
+      const float dt = softplus_f(acc + L.dt_b[c]);
+      const float uv = __ldcg(p.u + c);
+      float yv = L.d[c] * uv;
+      for (int n = 0; n < ds; ++n) {
+        const float da = expf(dt * L.a_neg[n * di + c]);
+        const float dbu = dt * sh[dr + n] * uv;
+        const float hn = (da * h[static_cast<long long>(n) * di + c]) + dbu;
+        h[static_cast<long long>(n) * di + c] = hn;
+        yv += hn * sh[dr + ds + n];
+      }
+      const float zv = __ldcg(p.xz + di + c);
+      p.y[c] = yv * (zv / (1.0f + expf(-zv)));
+    }
+    if (!dec_grid_sync(p, epoch)) return;
+    // D. out_proj added to the residual
+    for (int k = threadIdx.x; k < di; k += blockDim.x) sh[k] = __ldcg(p.y + k);
+    __syncthreads();
+    for (int r = gwarp; r < dm; r += nwarps) {
+      const float v = warp_dot<HALF>(L.w_out, r, L.ld_out, di, sh);
+      if (lane == 0) p.x[r] = __ldcg(p.x + r) + v;
+    }
+    if (!dec_grid_sync(p, epoch)) return;
+  }
+  // final RMSNorm
+  const float scale = dec_rms_scale(p.x, dm, red);
+  for (int k = gthread; k < dm; k += nthreads) p.out[k] = __ldcg(p.x + k) * scale * p.norm_f[k];
+}
+
 class Mamba final : public MambaDevice {
  public:
   Mamba(std::shared_ptr<DeviceContext> ctx, Precision prec) : ctx_(std::move(ctx)), prec_(prec) {}
   ~Mamba() override {
+    if (step_graph_ != nullptr) cudaGraphExecDestroy(step_graph_);
     if (pinned_ != nullptr) cudaFreeHost(pinned_);
   }
   bool load(const TensorTable& t, std::string& err);
@@ -264,6 +479,8 @@ class Mamba final : public MambaDevice {
   bool gemm(const Mat& m, const void* in, int in_ld, long long n_tok, float* out, int out_ld, bool accumulate,
             bool tc, cudaStream_t st, std::string& err);
   bool run_layers(long long n_tok, int B, int L, bool tc, cudaStream_t st, std::string& err);
+  // one decode token: the token from pinned_[0], the normed output to pinned_ + 1
+  bool record_step(cudaStream_t st, std::string& err);
 
   std::shared_ptr<DeviceContext> ctx_;
   Precision prec_;
@@ -283,6 +500,13 @@ class Mamba final : public MambaDevice {
   std::size_t part_elems_ = 0;
   float* pinned_ = nullptr;
   std::size_t pinned_floats_ = 0;
+  // the decode step as one graph (token upload, every layer, output download);
+  // rebuilt after reserve() moves the buffers
+  cudaGraphExec_t step_graph_ = nullptr;
+  // fused decode (one cooperative launch per token) when the whole grid fits
+  DecodeLayer* dec_layers_ = nullptr;
+  unsigned* dec_sync_ = nullptr;
+  bool dec_fused_ = false;
 };
 
 bool Mamba::load(const TensorTable& t, std::string& err) {
@@ -445,6 +669,10 @@ int Mamba::reserve(std::size_t batch, std::size_t max_len, std::string& err) noe
   if (max_len == 0) max_len = 512;
   const std::size_t tokens = batch * max_len;
   if (tokens <= cap_tokens_ && batch <= cap_batch_) return 0;
+  if (step_graph_ != nullptr) {
+    cudaGraphExecDestroy(step_graph_);
+    step_graph_ = nullptr;
+  }
   const std::size_t dm = cfg_.d_model, di = cfg_.d_inner, wd = cfg_.dt_rank + 2 * cfg_.d_state;
   const std::size_t rows = (tokens + 255) / 256 * 256;
   std::size_t nsl = 1;
@@ -469,6 +697,8 @@ int Mamba::reserve(std::size_t batch, std::size_t max_len, std::string& err) noe
   plan.add_n<__half>(rows * di);
   plan.add_n<float>(state_floats());
   plan.add_n<float>(dm + 2 * di + di + wd + di + di + dm + 64);
+  plan.add_n<DecodeLayer>(layers_.size());
+  plan.add_n<unsigned>(4);
   // keep the decode state across a re-reserve
   std::vector<float> saved;
   if (state_ != nullptr) {
@@ -494,12 +724,33 @@ int Mamba::reserve(std::size_t batch, std::size_t max_len, std::string& err) noe
   yb_ = ws_.take_n<__half>(rows * di);
   state_ = ws_.take_n<float>(state_floats());
   dh_ = ws_.take_n<float>(dm + 2 * di + di + wd + di + di + dm + 64);
+  dec_layers_ = ws_.take_n<DecodeLayer>(layers_.size());
+  dec_sync_ = ws_.take_n<unsigned>(4);
   if (ws_.overflowed()) {
     err = "internal error: Mamba workspace arena too small";
     cap_tokens_ = 0;
     return 2;
   }
   cudaMemset(tokens_, 0, ws_.used());
+  {
+    std::vector<DecodeLayer> dl(layers_.size());
+    for (std::size_t i = 0; i < layers_.size(); ++i) {
+      const Layer& Ly = layers_[i];
+      dl[i] = DecodeLayer{Ly.in_proj.w, Ly.x_proj.w, Ly.out_proj.w, Ly.in_proj.cols_pad, Ly.x_proj.cols_pad,
+                          Ly.out_proj.cols_pad, Ly.norm, Ly.conv_w, Ly.conv_b, Ly.dt_w, Ly.dt_b, Ly.a_neg, Ly.d};
+    }
+    cudaMemcpy(dec_layers_, dl.data(), dl.size() * sizeof(DecodeLayer), cudaMemcpyHostToDevice);
+    // the fused decode needs one resident CTA per SM (cooperative launch)
+    const std::size_t smem = std::max({dm, di, wd}) * 4;
+    int per_sm = 0;
+    const bool half = prec_ == Precision::kBF16;
+    const cudaError_t oc = half ? cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, mamba_decode_kernel<true>,
+                                                                               kDecThreads, smem)
+                                : cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, mamba_decode_kernel<false>,
+                                                                               kDecThreads, smem);
+    dec_fused_ = oc == cudaSuccess && per_sm >= 1;
+    cudaGetLastError();
+  }
   if (!saved.empty()) cudaMemcpy(state_, saved.data(), saved.size() * 4, cudaMemcpyHostToDevice);
   const std::size_t need = tokens * (dm + 1) + state_floats();
   if (pinned_floats_ < need) {
@@ -660,10 +911,51 @@ int Mamba::forward(const std::int32_t* tokens, std::size_t batch, std::size_t le
   return 0;
 }
 
-int Mamba::step(std::int32_t token, float* out, std::string& err) noexcept {
-  cudaSetDevice(ctx_->device);
-  cudaStream_t st = ctx_->stream;
+bool Mamba::record_step(cudaStream_t st, std::string& err) {
   const int dm = static_cast<int>(cfg_.d_model), di = static_cast<int>(cfg_.d_inner);
+  if (dec_fused_) {
+    float* x = dh_;
+    DecodeParams p{};
+    p.layers = dec_layers_;
+    p.n_layers = static_cast<int>(layers_.size());
+    p.dm = dm;
+    p.di = di;
+    p.ds = static_cast<int>(cfg_.d_state);
+    p.dc = static_cast<int>(cfg_.d_conv);
+    p.dr = static_cast<int>(cfg_.dt_rank);
+    p.token = tokens_;
+    p.emb = emb_;
+    p.norm_f = norm_f_;
+    p.state = state_;
+    p.x = x;
+    p.xz = x + dm;
+    p.u = p.xz + 2 * di;
+    p.dbl = p.u + di;
+    p.y = p.dbl + (p.dr + 2 * p.ds);
+    p.out = p.y + 2 * di;
+    p.sync = dec_sync_;
+    p.err = ctx_->d_err;
+    cudaMemcpyAsync(tokens_, pinned_, 4, cudaMemcpyHostToDevice, st);
+    cudaMemsetAsync(dec_sync_, 0, 4 * sizeof(unsigned), st);
+    cudaLaunchAttribute attr{};
+    attr.id = cudaLaunchAttributeCooperative;
+    attr.val.cooperative = 1;
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(static_cast<unsigned>(ctx_->sm_count));
+    cfg.blockDim = dim3(kDecThreads);
+    cfg.dynamicSmemBytes = static_cast<std::size_t>(std::max({dm, di, p.dr + 2 * p.ds})) * 4;
+    cfg.stream = st;
+    cfg.attrs = &attr;
+    cfg.numAttrs = 1;
+    const cudaError_t rc = prec_ == Precision::kBF16 ? cudaLaunchKernelEx(&cfg, mamba_decode_kernel<true>, p)
+                                                     : cudaLaunchKernelEx(&cfg, mamba_decode_kernel<false>, p);
+    if (rc != cudaSuccess) {
+      err = std::string("fused decode launch: ") + cudaGetErrorString(rc);
+      return false;
+    }
+    cudaMemcpyAsync(pinned_ + 1, p.out, dm * 4, cudaMemcpyDeviceToHost, st);
+    return cudaGetLastError() == cudaSuccess;
+  }
   const int ds = static_cast<int>(cfg_.d_state), dc = static_cast<int>(cfg_.d_conv);
   const int dr = static_cast<int>(cfg_.dt_rank), wd = dr + 2 * ds;
   float* x = dh_;                // [dm] hidden
@@ -672,9 +964,7 @@ int Mamba::step(std::int32_t token, float* out, std::string& err) noexcept {
   float* dbl = u + di;           // [wd]
   float* y = dbl + wd;           // [di]
   float* normed = y + di + di;   // [dm]
-  auto* tok = reinterpret_cast<int*>(pinned_);
-  *tok = token;
-  cudaMemcpyAsync(tokens_, tok, 4, cudaMemcpyHostToDevice, st);
+  cudaMemcpyAsync(tokens_, pinned_, 4, cudaMemcpyHostToDevice, st);
   embed_kernel<<<1, 256, 0, st>>>(tokens_, 1, emb_, dm, x);
   const std::size_t per = static_cast<std::size_t>(di) * (dc + ds);
   for (std::size_t li = 0; li < layers_.size(); ++li) {
@@ -682,9 +972,9 @@ int Mamba::step(std::int32_t token, float* out, std::string& err) noexcept {
     float* window = state_ + li * per;
     float* h = window + static_cast<std::size_t>(di) * dc;
     rmsnorm_kernel<<<1, 32, 0, st>>>(x, Ly.norm, 1, dm, normed, nullptr);
-    if (!gemm(Ly.in_proj, normed, dm, 1, xz, 2 * di, false, false, st, err)) return 2;
+    if (!gemm(Ly.in_proj, normed, dm, 1, xz, 2 * di, false, false, st, err)) return false;
     conv_step_kernel<<<(di + 255) / 256, 256, 0, st>>>(xz, di, dc, window, Ly.conv_w, Ly.conv_b, u);
-    if (!gemm(Ly.x_proj, u, di, 1, dbl, wd, false, false, st, err)) return 2;
+    if (!gemm(Ly.x_proj, u, di, 1, dbl, wd, false, false, st, err)) return false;
     const dim3 grid(static_cast<unsigned>((di + 255) / 256), 1);
     const std::size_t smem = static_cast<std::size_t>(wd) * 4;
     if (ds == 16 && dr == 32)
@@ -695,18 +985,53 @@ int Mamba::step(std::int32_t token, float* out, std::string& err) noexcept {
       scan_kernel<8, 4, false><<<grid, 256, smem, st>>>(dbl, wd, u, xz, 1, di, Ly.dt_w, Ly.dt_b, Ly.a_neg, Ly.d, h, y, nullptr);
     else {
       err = "no scan instantiation for this (d_state, dt_rank)";
-      return 2;
+      return false;
     }
-    if (!gemm(Ly.out_proj, y, di, 1, x, dm, true, false, st, err)) return 2;
+    if (!gemm(Ly.out_proj, y, di, 1, x, dm, true, false, st, err)) return false;
   }
   rmsnorm_kernel<<<1, 32, 0, st>>>(x, norm_f_, 1, dm, normed, nullptr);
-  float* ph = pinned_ + 1;
-  cudaMemcpyAsync(ph, normed, dm * 4, cudaMemcpyDeviceToHost, st);
-  if (cudaStreamSynchronize(st) != cudaSuccess) {
+  cudaMemcpyAsync(pinned_ + 1, normed, dm * 4, cudaMemcpyDeviceToHost, st);
+  return cudaGetLastError() == cudaSuccess;
+}
+
+// Streaming decode of one token (mamba.cc:317-382): the conv window and scan
+// state stay on the device; the whole step replays as one CUDA graph.
+int Mamba::step(std::int32_t token, float* out, std::string& err) noexcept {
+  cudaSetDevice(ctx_->device);
+  cudaStream_t st = ctx_->stream;
+  if (step_graph_ == nullptr) {
+    cudaStream_t cap = nullptr;
+    cudaStreamCreateWithFlags(&cap, cudaStreamNonBlocking);
+    cudaStreamSynchronize(st);
+    cudaGraph_t graph = nullptr;
+    cudaStreamBeginCapture(cap, cudaStreamCaptureModeThreadLocal);
+    const bool ok = record_step(cap, err);
+    const cudaError_t end = cudaStreamEndCapture(cap, &graph);
+    cudaStreamDestroy(cap);
+    if (!ok || end != cudaSuccess || graph == nullptr) {
+      if (graph != nullptr) cudaGraphDestroy(graph);
+      if (err.empty()) err = "Mamba step graph capture failed";
+      cudaGetLastError();
+      return 2;
+    }
+    const cudaError_t inst = cudaGraphInstantiate(&step_graph_, graph, 0);
+    cudaGraphDestroy(graph);
+    if (inst != cudaSuccess) {
+      step_graph_ = nullptr;
+      err = "Mamba step graph instantiation failed";
+      return 2;
+    }
+  }
+  *reinterpret_cast<int*>(pinned_) = token;
+  if (cudaGraphLaunch(step_graph_, st) != cudaSuccess || cudaStreamSynchronize(st) != cudaSuccess) {
     err = std::string("Mamba step failed: ") + cudaGetErrorString(cudaGetLastError());
     return 2;
   }
-  std::memcpy(out, ph, dm * 4);
+  if (const int code = take_device_error(*ctx_, st); code != 0) {
+    err = device_error_text(code);
+    return 2;
+  }
+  std::memcpy(out, pinned_ + 1, cfg_.d_model * 4);
   return 0;
 }
 
