@@ -885,6 +885,165 @@ __global__ void __launch_bounds__(kAttnThreads) attention_rows_kernel(const Attn
 }
 
 // ---------------------------------------------------------------------------
+// Small-row GEMM (rows <= kSmallRows tokens, e.g. one 50-token chunk): the
+// tcgen05 GEMM would run one 256-row N tile on M / 128 CTAs, so instead the
+// K range is split over many CTAs.  CTA (m16, ks) computes a 16-row block of
+// W times all rows over K slice ks on mma.sync m16n8k16 (A = weights straight
+// from global, B = activations staged in shared memory; bf16 operands, or
+// fp16 W against the fp16 hi and lo planes of split activations); the four
+// warps take alternate 16-wide K steps and add their tiles in warp order.
+// partial[ks][row][m] then goes to small_epilogue_kernel, which adds the
+// slices in slice order and applies the tcgen05 GEMM's epilogue.
+constexpr int kSmallRows = 64;
+constexpr int kSmallK = 128;  // K per CTA
+constexpr int kSmallLd = kSmallK + 8;  // staged row (16-bit elements)
+
+struct SmallGemm {
+  const void* w;       // [M_pad][ld_w]: bf16, or fp16 [W | W] (split)
+  int ld_w, M, kp;     // kp: K (multiple of 64)
+  int split;           // 1: fp16 weights and fp16 hi / lo activations [rows][2 kp]
+  const void* x;       // activations [rows][ld_x] (16-bit)
+  int ld_x, rows;
+  float* partial;      // [nks][rows][M_pad16]
+  int m_pad;           // M rounded up to 16
+};
+
+template <bool SPLIT>
+__global__ void __launch_bounds__(128) small_gemm_kernel(const SmallGemm g) {
+  // [plane][row][k] staged activations; reused as [warp][16][rows] fp32 tiles
+  __shared__ __align__(16) uint16_t xs[2 * kSmallRows * kSmallLd];
+  float* red = reinterpret_cast<float*>(xs);
+  const int mb = blockIdx.x, ks = blockIdx.y;
+  const int k0 = ks * kSmallK;
+  const int kn = min(kSmallK, g.kp - k0);  // multiple of 16
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int g4 = lane >> 2, t4 = lane & 3;
+  // stage x[rows][k0 .. k0 + kn) (both planes when split); rows >= g.rows are zero
+  const int nq = kn / 8;  // 16-byte groups per row and plane
+  for (int i = tid; i < (SPLIT ? 2 : 1) * kSmallRows * nq; i += 128) {
+    const int pl = i / (kSmallRows * nq);
+    const int rem = i - pl * kSmallRows * nq;
+    const int r = rem / nq, q = rem - r * nq;
+    uint4 v = make_uint4(0u, 0u, 0u, 0u);
+    if (r < g.rows)
+      v = __ldg(reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(g.x) + static_cast<long long>(r) * g.ld_x +
+                                               pl * g.kp + k0 + 8 * q));
+    *reinterpret_cast<uint4*>(&xs[(pl * kSmallRows + r) * kSmallLd + 8 * q]) = v;
+  }
+  __syncthreads();
+  const int nt = (g.rows + 7) / 8;  // n-tiles of 8 rows
+  float acc[SPLIT ? 2 : 1][kSmallRows / 8][4];
+#pragma unroll
+  for (int pl = 0; pl < (SPLIT ? 2 : 1); ++pl)
+#pragma unroll
+    for (int n = 0; n < kSmallRows / 8; ++n)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) acc[pl][n][e] = 0.0f;
+  const uint16_t* wrow0 = static_cast<const uint16_t*>(g.w) + static_cast<long long>(mb * 16 + g4) * g.ld_w + k0;
+  const uint16_t* wrow1 = wrow0 + 8LL * g.ld_w;
+  for (int kk = warp * 16; kk < kn; kk += 64) {
+    uint32_t a[4];
+    a[0] = __ldg(reinterpret_cast<const uint32_t*>(wrow0 + kk + 2 * t4));
+    a[1] = __ldg(reinterpret_cast<const uint32_t*>(wrow1 + kk + 2 * t4));
+    a[2] = __ldg(reinterpret_cast<const uint32_t*>(wrow0 + kk + 2 * t4 + 8));
+    a[3] = __ldg(reinterpret_cast<const uint32_t*>(wrow1 + kk + 2 * t4 + 8));
+#pragma unroll
+    for (int n = 0; n < kSmallRows / 8; ++n) {
+      if (n < nt) {
+#pragma unroll
+        for (int pl = 0; pl < (SPLIT ? 2 : 1); ++pl) {
+          const uint16_t* xr = &xs[(pl * kSmallRows + n * 8 + g4) * kSmallLd + kk + 2 * t4];
+          const uint32_t b0 = *reinterpret_cast<const uint32_t*>(xr);
+          const uint32_t b1 = *reinterpret_cast<const uint32_t*>(xr + 8);
+          if constexpr (SPLIT) {
+            asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+                "{%0,%1,%2,%3};"
+                : "+f"(acc[pl][n][0]), "+f"(acc[pl][n][1]), "+f"(acc[pl][n][2]), "+f"(acc[pl][n][3])
+                : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+          } else {
+            mma_bf16_16816(acc[pl][n], a, b0, b1);
+          }
+        }
+      }
+    }
+  }
+  // warp tiles (hi + lo planes) to shared memory, then added in warp order
+  __syncthreads();  // every warp is done with the staged activations
+#pragma unroll
+  for (int n = 0; n < kSmallRows / 8; ++n) {
+    if (n < nt) {
+      float v[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) v[e] = SPLIT ? acc[0][n][e] + acc[SPLIT ? 1 : 0][n][e] : acc[0][n][e];
+      float* rw = red + warp * 16 * kSmallRows;
+      rw[g4 * kSmallRows + n * 8 + 2 * t4] = v[0];
+      rw[g4 * kSmallRows + n * 8 + 2 * t4 + 1] = v[1];
+      rw[(g4 + 8) * kSmallRows + n * 8 + 2 * t4] = v[2];
+      rw[(g4 + 8) * kSmallRows + n * 8 + 2 * t4 + 1] = v[3];
+    }
+  }
+  __syncthreads();
+  for (int i = tid; i < 16 * g.rows; i += 128) {
+    const int r = i / 16, mm = i - r * 16;  // consecutive threads: consecutive output rows m
+    const int o = mm * kSmallRows + r;
+    const float v = red[o] + red[16 * kSmallRows + o] + red[32 * kSmallRows + o] + red[48 * kSmallRows + o];
+    g.partial[(static_cast<long long>(ks) * g.rows + r) * g.m_pad + mb * 16 + mm] = v;
+  }
+}
+
+struct SmallEpilogue {
+  const float* partial;
+  int nks, rows, m_valid, m_pad;
+  const float* bias;
+  const float* add_vec;
+  int act;          // tc::kActNone / kActSilu / kActSwiGLU
+  int out_kind;     // 0 fp32, 1 bf16, 2 fp16, 3 fp16 hi / lo
+  void* out;
+  long long out_ld;
+  long long lo_off;
+  int ch_off;
+};
+
+// y = sum of the K slices in slice order + bias + add_vec, then the act and
+// the store of the tcgen05 epilogue (SwiGLU: rows 2f / 2f + 1 are gate / up)
+__global__ void small_epilogue_kernel(const SmallEpilogue e) {
+  const bool swiglu = e.act == tc::kActSwiGLU;
+  const int cols = swiglu ? e.m_valid / 2 : e.m_valid;
+  const long long total = static_cast<long long>(e.rows) * cols;
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const int r = static_cast<int>(i / cols), c = static_cast<int>(i - static_cast<long long>(r) * cols);
+    auto y_of = [&](int m) {
+      float y = 0.0f;
+      for (int k = 0; k < e.nks; ++k) y += e.partial[(static_cast<long long>(k) * e.rows + r) * e.m_pad + m];
+      if (e.bias != nullptr) y += e.bias[m];
+      if (e.add_vec != nullptr) y += e.add_vec[m];
+      return y;
+    };
+    float y;
+    if (swiglu) {
+      const float gte = bf16r(y_of(2 * c)), up = bf16r(y_of(2 * c + 1));
+      y = up * (gte / (1.0f + expf(-gte)));
+    } else {
+      y = y_of(c);
+      if (e.act == tc::kActSilu) y = silu_fast(y);
+    }
+    const long long o = static_cast<long long>(r) * e.out_ld + e.ch_off + c;
+    if (e.out_kind == 0) {
+      static_cast<float*>(e.out)[o] = y;
+    } else if (e.out_kind == 1) {
+      static_cast<bf16*>(e.out)[o] = __float2bfloat16_rn(y);
+    } else if (e.out_kind == 2) {
+      static_cast<__half*>(e.out)[o] = to_half_sat(y);
+    } else {
+      const __half hi = to_half_sat(y);
+      static_cast<__half*>(e.out)[o] = hi;
+      static_cast<__half*>(e.out)[o + e.lo_off] = __float2half_rn(y - __half2float(hi));
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
 
 struct Mat {
   void* w = nullptr;
@@ -923,6 +1082,12 @@ class SmolVLA final : public SmolVLADevice {
   std::uint64_t kernel_launches() const noexcept override { return launches_; }
 
  private:
+  // largest split-K partial buffer of any small-row GEMM: K slices x rows x M
+  std::size_t small_part_floats() const {
+    const std::size_t kmax = static_cast<std::size_t>(std::max({Wp_, attn_p_, mlp_p_, Cp_, Ap_}));
+    const std::size_t mmax = static_cast<std::size_t>(std::max({qkv_ld_, 2 * mlp_, Wp_, kvp_ld_, Ap_ + 128}));
+    return (kmax + kSmallK - 1) / kSmallK * kSmallRows * mmax;
+  }
   bool gemm(const Mat& m, const void* src, long long rows, void* out, int out_ld, bool out_f32, long long lo_off,
             const float* bias, const float* add_vec, int act, cudaStream_t st, std::string& err,
             long long src_rows = 0, int out_ch_off = 0, bool out_bf16 = false);
@@ -974,6 +1139,7 @@ class SmolVLA final : public SmolVLADevice {
   bf16* proj_ = nullptr;  // bf16 output projection (o / down), added to h by the next norm
   float *kcache_ = nullptr, *vcache_ = nullptr, *io_ = nullptr;
   float2* rope_tab_ = nullptr;  // [prefix + chunk][head_width / 2] (cos, sin), rebuilt by every call
+  float* small_part_ = nullptr;  // split-K partials of the small-row GEMM
   __half *x2_ = nullptr, *a2_ = nullptr, *h12_ = nullptr, *fin2_ = nullptr, *c2_ = nullptr;
   bf16 *nb_ = nullptr, *qkv_ = nullptr, *att_ = nullptr, *act_ = nullptr, *kvp_ = nullptr;
   std::uint8_t* mask_ = nullptr;
@@ -1285,6 +1451,7 @@ int SmolVLA::reserve(std::size_t batch, std::size_t chunk, std::size_t prefix, b
   plan.add_n<bf16>(ra * mlp_p_);                     // act
   plan.add_n<bf16>(L * prow * kvp_ld_);              // kvp
   plan.add_n<float2>((Pc + Cc) * cfg_.head_width / 2);
+  plan.add_n<float>(small_part_floats());
   plan.add_n<std::uint8_t>(Sc * Pc);
   plan.add_n<int>(Sc + 4);
   ws_.release();
@@ -1312,6 +1479,7 @@ int SmolVLA::reserve(std::size_t batch, std::size_t chunk, std::size_t prefix, b
   act_ = ws_.take_n<bf16>(ra * mlp_p_);
   kvp_ = ws_.take_n<bf16>(L * prow * kvp_ld_);
   rope_tab_ = ws_.take_n<float2>((Pc + Cc) * cfg_.head_width / 2);
+  small_part_ = ws_.take_n<float>(small_part_floats());
   mask_ = ws_.take_n<std::uint8_t>(Sc * Pc);
   valid_ = ws_.take_n<int>(Sc + 4);
   step_ = valid_ + Sc;
@@ -1336,6 +1504,42 @@ bool SmolVLA::gemm(const Mat& m, const void* src, long long rows, void* out, int
                    long long lo_off, const float* bias, const float* add_vec, int act, cudaStream_t st,
                    std::string& err, long long src_rows, int out_ch_off, bool out_bf16) {
   if (src_rows == 0) src_rows = rows_alloc_;
+  if (rows <= kSmallRows) {
+    // split-K mma.sync tiles + a fixed-order reduction with the same epilogue
+    SmallGemm g{};
+    g.w = m.w;
+    g.ld_w = m.split ? 2 * m.kp : m.kp;
+    g.M = m.rows;
+    g.kp = m.kp;
+    g.split = m.split ? 1 : 0;
+    g.x = src;
+    g.ld_x = m.split ? 2 * m.kp : m.kp;
+    g.rows = static_cast<int>(rows);
+    g.partial = small_part_;
+    g.m_pad = pad(m.rows, 16);
+    const int nks = (m.kp + kSmallK - 1) / kSmallK;
+    const dim3 grid(static_cast<unsigned>(g.m_pad / 16), static_cast<unsigned>(nks));
+    if (m.split) small_gemm_kernel<true><<<grid, 128, 0, st>>>(g);
+    else small_gemm_kernel<false><<<grid, 128, 0, st>>>(g);
+    SmallEpilogue e{};
+    e.partial = small_part_;
+    e.nks = nks;
+    e.rows = g.rows;
+    e.m_valid = m.rows;
+    e.m_pad = g.m_pad;
+    e.bias = bias;
+    e.add_vec = add_vec;
+    e.act = act;
+    e.out_kind = out_f32 ? 0 : (!m.split || out_bf16) ? 1 : (lo_off != 0 ? 3 : 2);
+    e.out = out;
+    e.out_ld = out_ld;
+    e.lo_off = lo_off;
+    e.ch_off = out_ch_off;
+    const long long cols = act == tc::kActSwiGLU ? m.rows / 2 : m.rows;
+    small_epilogue_kernel<<<ew_grid(rows * cols, 256, *ctx_), 256, 0, st>>>(e);
+    launches_ += 2;
+    return cudaGetLastError() == cudaSuccess;
+  }
   TcLaunch l;
   l.fp16 = m.split;
   l.A = m.w;

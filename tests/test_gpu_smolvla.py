@@ -76,8 +76,11 @@ def test_smolvla_c5_batched_matches_restatement(tmp_path):
         err = float(np.abs(out[b] - expected).max())
         print(f"C5 (4 layers) sample {b} Euler-10 max-abs vs restatement: {err:.3g}")
         assert err <= 2e-2
+        # a single chunk (50 rows) runs the small-row GEMMs, the batch the tcgen05 ones: another
+        # summation order, so the rows agree to the bf16 bar, not bit for bit
         single = e.smolvla_sample(noise[b], 10, keys[b], values[b], mask[b])
-        assert float(np.abs(single - out[b]).max()) <= 1e-6
+        assert float(np.abs(single - out[b]).max()) <= 2e-2
+    # batches on the same (tcgen05) path: rows are bitwise independent of the batch around them
     shared = e.smolvla_sample_batch(noise[:2], 10, keys[0], values[0], mask[0], shared_prefix=True)
     assert float(np.abs(shared[0] - out[0]).max()) <= 1e-6
     assert float(np.abs(shared[1] - model.sample(noise[1], 10, keys[0], values[0], mask[0])).max()) <= 2e-2
