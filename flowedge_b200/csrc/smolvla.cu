@@ -1023,7 +1023,7 @@ __global__ void small_epilogue_kernel(const SmallEpilogue e) {
     float y;
     if (swiglu) {
       const float gte = bf16r(y_of(2 * c)), up = bf16r(y_of(2 * c + 1));
-      y = up * (gte / (1.0f + expf(-gte)));
+      y = up * silu_fast(gte);
     } else {
       y = y_of(c);
       if (e.act == tc::kActSilu) y = silu_fast(y);
