@@ -290,6 +290,7 @@ def run_ours(args):
     if dist is not None:
         parts = [torch.empty_like(d_action) for _ in range(world)]
         g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        dist.all_gather(parts, d_action)  # untimed: the first gather sets up NCCL's channels
         dist.barrier()
         torch.cuda.synchronize()
         g0.record(stream)
