@@ -353,6 +353,48 @@ __device__ __forceinline__ float silu_f(float x) { return x / (1.0f + expf(-x));
 // exponential overflows to inf and the quotient is -0, the limit of silu.
 __device__ __forceinline__ float silu_fast(float x) { return __fdividef(x, 1.0f + __expf(-x)); }
 
+// Grid barrier of a cooperative launch (every CTA resident) on a monotonic
+// arrival counter sync[0]: barrier number `epoch` (from 1) passes once the
+// counter reaches epoch * gridDim.x.  Thread 0 arrives with a GPU-scope
+// release and polls with a GPU-scope acquire, between two CTA barriers.  The
+// wait is bounded: after kWaitNs it records kErrGridBarrierTimeout and sets
+// the abort word sync[2]; every CTA returns false at its next barrier once
+// the abort word is set.  sync[0] and sync[2] start at zero for each launch.
+__device__ inline bool coop_grid_sync(unsigned* sync, int* err, unsigned& epoch) {
+  __shared__ int s_ok;
+  __syncthreads();
+  ++epoch;
+  if (threadIdx.x == 0) {
+    volatile unsigned* abort_flag = sync + 2;
+    int ok = *abort_flag == 0u;
+    if (ok) {
+      const unsigned target = epoch * gridDim.x;
+      asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(sync) : "memory");
+      const uint64_t t0 = global_ns();
+      for (uint32_t spin = 0;; ++spin) {
+        unsigned v;
+        asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(sync) : "memory");
+        if (v >= target) break;
+        if ((spin & 15u) == 15u) {
+          if (*abort_flag != 0u) {
+            ok = 0;
+            break;
+          }
+          if (global_ns() - t0 > kWaitNs) {
+            atomicCAS(err, 0, kErrGridBarrierTimeout);
+            atomicExch(sync + 2, 1u);
+            ok = 0;
+            break;
+          }
+        }
+      }
+    }
+    s_ok = ok;
+  }
+  __syncthreads();
+  return s_ok != 0;
+}
+
 // 2^x by the hardware approximation (MUFU.EX2, flush-to-zero)
 __device__ __forceinline__ float ex2_approx(float x) {
   float y;

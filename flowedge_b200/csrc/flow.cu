@@ -176,6 +176,207 @@ __global__ void store_rows_kernel(const float* src, int B, int A, int ld, float*
   }
 }
 
+// ---------------------------------------------------------------------------
+// Fused small-batch solve: one cooperative launch runs `count` ODE steps
+// (flow.cc:152-184, 210-323).  Every CTA is resident; per velocity evaluation
+//   P1  sinusoid of t (each CTA), then per hidden row h (one warp per row,
+//       lanes stride K): tp = W_t[h] . sinu, h0 = SiLU(W_in[h] . x + tp + c_emb)
+//   P2  hidden layers h = SiLU(W_l h), one phase each
+//   P3  v = W_out h; the warp of output element a then applies the ODE stage
+//       update of ode_stage_kernel to (b, a) and writes the next input
+// separated by bounded grid barriers (coop_grid_sync).  Rows are spread
+// CTA-first so short phases still use every SM; inputs written inside the
+// launch are staged into shared memory through L2 (ld.global.cg).
+constexpr int kFlowThreads = 512;
+constexpr int kFlowWarps = kFlowThreads / 32;
+constexpr int kFuseMaxBatch = 8;
+constexpr int kFuseMaxLayers = 8;
+
+struct FlowFusedParams {
+  int B, A, H, half, layers, steps, method, first, count;
+  const float* freqs;  // [half]
+  const float* wt;     // [H][2 half] fp32
+  const void* w_in;    // [H][ld_in], fp32 or fp16
+  int ld_in;
+  const void* w_l[kFuseMaxLayers];  // [H][ld_l]
+  int ld_l;
+  const void* w_out;  // [A][ld_out]
+  int ld_out;
+  const float* cemb;  // [B][H]
+  float* x;           // [B][ld_a] state
+  float* probe;
+  float* k[4];
+  float* xin;         // [B][ld_a] current evaluation input (fp32)
+  int ld_a;
+  float* h0;
+  float* h1;  // [B][H]
+  unsigned* sync;
+  int* err;
+};
+
+// dot products of one weight row with nb staged vectors (row stride ldv);
+// lane l takes pairs (k, k + 1), k = 2 l + 64 j, and issues up to
+// kFlowPairs of its weight loads before the first multiply
+constexpr int kFlowPairs = 16;
+template <bool HALF>
+__device__ __forceinline__ void flow_dots(const void* w, long long row, int ld, int n, const float* v, int ldv,
+                                          int nb, float (&acc)[kFuseMaxBatch]) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int b = 0; b < kFuseMaxBatch; ++b) acc[b] = 0.0f;
+  for (int k0 = 2 * lane; k0 < n; k0 += 64 * kFlowPairs) {
+    float2 wv[kFlowPairs];
+#pragma unroll
+    for (int u = 0; u < kFlowPairs; ++u) {
+      const int k = k0 + 64 * u;
+      wv[u] = make_float2(0.0f, 0.0f);
+      if (k < n) {
+        if constexpr (HALF) {
+          wv[u] = __half22float2(*reinterpret_cast<const __half2*>(static_cast<const __half*>(w) + row * ld + k));
+        } else {
+          wv[u] = *reinterpret_cast<const float2*>(static_cast<const float*>(w) + row * ld + k);
+        }
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < kFlowPairs; ++u) {
+      const int k = k0 + 64 * u;
+      if (k < n) {
+        const bool two = k + 1 < n;
+#pragma unroll
+        for (int b = 0; b < kFuseMaxBatch; ++b)
+          if (b < nb) {
+            acc[b] = fmaf(wv[u].x, v[b * ldv + k], acc[b]);
+            if (two) acc[b] = fmaf(wv[u].y, v[b * ldv + k + 1], acc[b]);
+          }
+      }
+    }
+  }
+#pragma unroll
+  for (int b = 0; b < kFuseMaxBatch; ++b)
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) acc[b] += __shfl_xor_sync(0xffffffffu, acc[b], off);
+}
+
+template <bool HALF>
+__global__ void __launch_bounds__(kFlowThreads, 1) flow_fused_kernel(const FlowFusedParams p) {
+  extern __shared__ float sv[];  // [B][max(H, ld_a)] staged vectors, then [2 half] sinusoid
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int gwarp = warp * gridDim.x + blockIdx.x, nwarps = gridDim.x * kFlowWarps;
+  const int B = p.B, A = p.A, H = p.H;
+  const int ldv = H > p.ld_a ? H : p.ld_a;
+  float* sinu = sv + B * ldv;
+  const int stages = p.method == 0 ? 1 : (p.method == 1 ? 2 : 4);
+  const int last = stages - 1;
+  const float dt = 1.0f / static_cast<float>(p.steps);
+  unsigned epoch = 0;
+  for (int step = p.first; step < p.first + p.count; ++step) {
+    for (int s = 0; s < stages; ++s) {
+      // P1: time projection and input layer
+      const float t = stage_time(step, p.steps, p.method, s);
+      for (int j = threadIdx.x; j < p.half; j += blockDim.x) {
+        sinu[j] = sinf(t * p.freqs[j]);
+        sinu[p.half + j] = cosf(t * p.freqs[j]);
+      }
+      for (int i = threadIdx.x; i < B * p.ld_a; i += blockDim.x) {
+        const int b = i / p.ld_a, a = i - b * p.ld_a;
+        sv[b * ldv + a] = __ldcg(p.xin + i);
+      }
+      __syncthreads();
+      for (int h = gwarp; h < H; h += nwarps) {
+        const float* w = p.wt + static_cast<long long>(h) * 2 * p.half;
+        float tp = 0.0f;
+        for (int j = lane; j < 2 * p.half; j += 32) tp = fmaf(w[j], sinu[j], tp);
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) tp += __shfl_xor_sync(0xffffffffu, tp, off);
+        float acc[kFuseMaxBatch];
+        flow_dots<HALF>(p.w_in, h, p.ld_in, A, sv, ldv, B, acc);
+        if (lane == 0) {
+#pragma unroll
+          for (int b = 0; b < kFuseMaxBatch; ++b)
+            if (b < B)
+              p.h0[static_cast<long long>(b) * H + h] =
+                  silu_f((acc[b] + tp) + p.cemb[static_cast<long long>(b) * H + h]);
+        }
+      }
+      if (!coop_grid_sync(p.sync, p.err, epoch)) return;
+      // P2: hidden layers
+      float* hin = p.h0;
+      float* hout = p.h1;
+      for (int l = 0; l < p.layers; ++l) {
+        for (int i = threadIdx.x; i < B * H; i += blockDim.x) {
+          const int b = i / H, c = i - b * H;
+          sv[b * ldv + c] = __ldcg(hin + i);
+        }
+        __syncthreads();
+        for (int r = gwarp; r < H; r += nwarps) {
+          float acc[kFuseMaxBatch];
+          flow_dots<HALF>(p.w_l[l], r, p.ld_l, H, sv, ldv, B, acc);
+          if (lane == 0) {
+#pragma unroll
+            for (int b = 0; b < kFuseMaxBatch; ++b)
+              if (b < B) hout[static_cast<long long>(b) * H + r] = silu_f(acc[b]);
+          }
+        }
+        if (!coop_grid_sync(p.sync, p.err, epoch)) return;
+        float* tmp = hin;
+        hin = hout;
+        hout = tmp;
+      }
+      // P3: output layer and the ODE stage update (span_ops.h:33-56 order)
+      for (int i = threadIdx.x; i < B * H; i += blockDim.x) {
+        const int b = i / H, c = i - b * H;
+        sv[b * ldv + c] = __ldcg(hin + i);
+      }
+      __syncthreads();
+      for (int a = gwarp; a < A; a += nwarps) {
+        float acc[kFuseMaxBatch];
+        flow_dots<HALF>(p.w_out, a, p.ld_out, H, sv, ldv, B, acc);
+        if (lane == 0)
+#pragma unroll
+          for (int b = 0; b < kFuseMaxBatch; ++b) {
+            if (b >= B) continue;
+            const long long o = static_cast<long long>(b) * p.ld_a + a;
+            p.k[s][o] = acc[b];
+            const float x = __ldcg(p.x + o);
+            float nxt;
+            if (p.method == 0) {
+              nxt = x + dt * acc[b];
+              p.x[o] = nxt;
+            } else if (p.method == 1) {
+              if (s == 0) {
+                nxt = x + (dt * acc[b]);
+                p.probe[o] = nxt;
+              } else {
+                nxt = x + 0.5f * dt * (__ldcg(p.k[0] + o) + acc[b]);
+                p.x[o] = nxt;
+              }
+            } else {
+              const float hf = 0.5f * dt;
+              if (s == 0) {
+                nxt = x + (hf * acc[b]);
+                p.probe[o] = nxt;
+              } else if (s == 1) {
+                nxt = x + (hf * acc[b]);
+                p.probe[o] = nxt;
+              } else if (s == 2) {
+                nxt = x + (dt * acc[b]);
+                p.probe[o] = nxt;
+              } else {
+                nxt = x + (dt / 6.0f) * (__ldcg(p.k[0] + o) + (2.0f * __ldcg(p.k[1] + o)) +
+                                         (2.0f * __ldcg(p.k[2] + o)) + acc[b]);
+                p.x[o] = nxt;
+              }
+            }
+            p.xin[o] = nxt;
+          }
+      }
+      if (!coop_grid_sync(p.sync, p.err, epoch)) return;
+      (void)last;
+    }
+  }
+}
+
 class Flow final : public FlowDevice {
  public:
   Flow(std::shared_ptr<DeviceContext> ctx, Precision prec) : ctx_(std::move(ctx)), prec_(prec) {}
@@ -227,6 +428,10 @@ class Flow final : public FlowDevice {
   std::size_t batch_ = 0, steps_ = 0;
   int method_ = 0;
   std::map<std::tuple<std::size_t, int, bool, std::size_t>, cudaGraphExec_t> graphs_;
+  unsigned* fsync_ = nullptr;  // grid-barrier words of the fused small-batch solve
+  // one cooperative launch for `count` steps of a small batch, or false when
+  // the batch / shape does not take the fused kernel
+  bool fused_advance(std::size_t first, std::size_t count, cudaStream_t st, std::string& err, bool& used);
 };
 
 bool Flow::load(const TensorTable& t, std::string& err) {
@@ -370,6 +575,7 @@ int Flow::reserve(std::size_t batch, std::string& err) noexcept {
   plan.add_n<float>(rows * H);                                 // h1
   plan.add_n<float>(rows * static_cast<std::size_t>(c_pad_));  // cin
   plan.add_n<int>(4);
+  plan.add_n<unsigned>(4);
   ws_.release();
   if (!ws_.init(plan.total(), err)) {
     cap_ = 0;
@@ -387,6 +593,7 @@ int Flow::reserve(std::size_t batch, std::string& err) noexcept {
   h1_ = ws_.take(rows * H * 4);
   cin_ = ws_.take(rows * c_pad_ * 4);
   step_ = ws_.take_n<int>(4);
+  fsync_ = ws_.take_n<unsigned>(4);
   if (ws_.overflowed()) {
     err = "internal error: flow workspace arena too small";
     cap_ = 0;
@@ -563,11 +770,80 @@ int Flow::begin(const float* condition, const float* x0, std::size_t batch, std:
   return 0;
 }
 
+bool Flow::fused_advance(std::size_t first, std::size_t count, cudaStream_t st, std::string& err, bool& used) {
+  used = false;
+  const int H = static_cast<int>(cfg_.hidden);
+  if (batch_ > static_cast<std::size_t>(kFuseMaxBatch) || use_tc(batch_) ||
+      layers_.size() > static_cast<std::size_t>(kFuseMaxLayers) || H % 2 != 0)
+    return true;
+  const int ldv = std::max(H, a_pad_);
+  const std::size_t smem = (static_cast<std::size_t>(batch_) * ldv + cfg_.time_dim) * sizeof(float);
+  const bool half = prec_ == Precision::kBF16;
+  const void* fn = half ? reinterpret_cast<const void*>(flow_fused_kernel<true>)
+                        : reinterpret_cast<const void*>(flow_fused_kernel<false>);
+  int per_sm = 0;
+  if (smem > 227 * 1024 || cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                static_cast<int>(smem)) != cudaSuccess ||
+      cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, kFlowThreads, smem) != cudaSuccess || per_sm < 1) {
+    cudaGetLastError();
+    return true;  // not fused: the per-kernel graph runs instead
+  }
+  FlowFusedParams p{};
+  p.B = static_cast<int>(batch_);
+  p.A = static_cast<int>(cfg_.action_dim);
+  p.H = H;
+  p.half = static_cast<int>(cfg_.time_dim / 2);
+  p.layers = static_cast<int>(layers_.size());
+  p.steps = static_cast<int>(steps_);
+  p.method = method_;
+  p.first = static_cast<int>(first);
+  p.count = static_cast<int>(count);
+  p.freqs = freqs_;
+  p.wt = wt_;
+  p.w_in = in_.w;
+  p.ld_in = in_.cols_pad;
+  for (std::size_t i = 0; i < layers_.size(); ++i) p.w_l[i] = layers_[i].w;
+  p.ld_l = layers_.empty() ? 0 : layers_[0].cols_pad;
+  p.w_out = out_.w;
+  p.ld_out = out_.cols_pad;
+  p.cemb = cemb_;
+  p.x = x_;
+  p.probe = probe_;
+  for (int i = 0; i < 4; ++i) p.k[i] = k_[i];
+  p.xin = static_cast<float*>(xin_);
+  p.ld_a = a_pad_;
+  p.h0 = static_cast<float*>(h0_);
+  p.h1 = static_cast<float*>(h1_);
+  p.sync = fsync_;
+  p.err = ctx_->d_err;
+  cudaMemsetAsync(fsync_, 0, 4 * sizeof(unsigned), st);
+  cudaLaunchAttribute attr{};
+  attr.id = cudaLaunchAttributeCooperative;
+  attr.val.cooperative = 1;
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(static_cast<unsigned>(ctx_->sm_count));
+  cfg.blockDim = dim3(kFlowThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cfg.attrs = &attr;
+  cfg.numAttrs = 1;
+  const cudaError_t rc = half ? cudaLaunchKernelEx(&cfg, flow_fused_kernel<true>, p)
+                              : cudaLaunchKernelEx(&cfg, flow_fused_kernel<false>, p);
+  if (rc != cudaSuccess) {
+    err = std::string("fused flow launch: ") + cudaGetErrorString(rc);
+    return false;
+  }
+  used = true;
+  return true;
+}
+
 int Flow::advance(std::size_t first, std::size_t count, float* out, std::string& err) noexcept {
   cudaSetDevice(ctx_->device);
   cudaStream_t st = ctx_->stream;
   const bool tc = use_tc(batch_);
-  if (count > 0) {
+  bool fused = false;
+  if (count > 0 && !fused_advance(first, count, st, err, fused)) return 2;
+  if (count > 0 && !fused) {
     const auto key = std::make_tuple(batch_, method_, tc, steps_);
     auto it = graphs_.find(key);
     if (it == graphs_.end()) {

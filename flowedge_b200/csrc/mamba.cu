@@ -276,39 +276,8 @@ struct DecodeParams {
   int* err;
 };
 
-__device__ bool dec_grid_sync(const DecodeParams& p, unsigned& epoch) {
-  __shared__ int s_ok;
-  __syncthreads();
-  ++epoch;
-  if (threadIdx.x == 0) {
-    volatile unsigned* abort_flag = p.sync + 2;
-    int ok = *abort_flag == 0u;
-    if (ok) {
-      const unsigned target = epoch * gridDim.x;
-      asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(p.sync) : "memory");
-      const uint64_t t0 = global_ns();
-      for (uint32_t spin = 0;; ++spin) {
-        unsigned v;
-        asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p.sync) : "memory");
-        if (v >= target) break;
-        if ((spin & 15u) == 15u) {
-          if (*abort_flag != 0u) {
-            ok = 0;
-            break;
-          }
-          if (global_ns() - t0 > kWaitNs) {
-            atomicCAS(p.err, 0, kErrGridBarrierTimeout);
-            atomicExch(p.sync + 2, 1u);
-            ok = 0;
-            break;
-          }
-        }
-      }
-    }
-    s_ok = ok;
-  }
-  __syncthreads();
-  return s_ok != 0;
+__device__ __forceinline__ bool dec_grid_sync(const DecodeParams& p, unsigned& epoch) {
+  return coop_grid_sync(p.sync, p.err, epoch);
 }
 
 // sum over a row of `n` weights times the shared / global vector v (one warp)
@@ -316,38 +285,28 @@ template <bool HALF>
 __device__ __forceinline__ float warp_dot(const void* w, long long row, int ld, int n, const float* v) {
   float acc = 0.0f;
   const int lane = threadIdx.x & 31;
-  // lane l takes pairs (k, k + 1), k = 2 l + 64 j; four pairs in flight
-  if constexpr (HALF) {
-    const __half* wr = static_cast<const __half*>(w) + row * ld;
-    for (int k0 = lane * 2; k0 < n; k0 += 256) {
-      __half2 h2[4];
+  // lane l takes pairs (k, k + 1), k = 2 l + 64 j; up to 16 pairs (all of a
+  // 1024-long row) in flight before the first multiply
+  constexpr int kPairs = 16;
+  for (int k0 = lane * 2; k0 < n; k0 += 64 * kPairs) {
+    float2 f2[kPairs];
 #pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const int k = k0 + 64 * u;
-        h2[u] = k < n ? *reinterpret_cast<const __half2*>(wr + k) : __floats2half2_rn(0.0f, 0.0f);
-      }
-#pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const int k = k0 + 64 * u;
-        if (k < n) acc = fmaf(__low2float(h2[u]), v[k], acc);
-        if (k + 1 < n) acc = fmaf(__high2float(h2[u]), v[k + 1], acc);
+    for (int u = 0; u < kPairs; ++u) {
+      const int k = k0 + 64 * u;
+      f2[u] = make_float2(0.0f, 0.0f);
+      if (k < n) {
+        if constexpr (HALF) {
+          f2[u] = __half22float2(*reinterpret_cast<const __half2*>(static_cast<const __half*>(w) + row * ld + k));
+        } else {
+          f2[u] = *reinterpret_cast<const float2*>(static_cast<const float*>(w) + row * ld + k);
+        }
       }
     }
-  } else {
-    const float* wr = static_cast<const float*>(w) + row * ld;
-    for (int k0 = lane * 2; k0 < n; k0 += 256) {
-      float2 f2[4];
 #pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const int k = k0 + 64 * u;
-        f2[u] = k < n ? *reinterpret_cast<const float2*>(wr + k) : make_float2(0.0f, 0.0f);
-      }
-#pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const int k = k0 + 64 * u;
-        if (k < n) acc = fmaf(f2[u].x, v[k], acc);
-        if (k + 1 < n) acc = fmaf(f2[u].y, v[k + 1], acc);
-      }
+    for (int u = 0; u < kPairs; ++u) {
+      const int k = k0 + 64 * u;
+      if (k < n) acc = fmaf(f2[u].x, v[k], acc);
+      if (k + 1 < n) acc = fmaf(f2[u].y, v[k + 1], acc);
     }
   }
 #pragma unroll
