@@ -16,6 +16,8 @@
 #include <algorithm>
 #include <cmath>
 #include <cstring>
+#include <map>
+#include <tuple>
 
 #include "runtime.cuh"
 #include "simt.cuh"
@@ -23,7 +25,7 @@
 namespace feb {
 namespace {
 
-constexpr int kTcMinTokens = 256;
+constexpr int kTcMinTokens = 128;
 constexpr int kMaxState = 16;
 constexpr int kMaxRank = 64;
 constexpr int kMaxConv = 8;  // causal conv width limit (register window)
@@ -200,6 +202,113 @@ __global__ void __launch_bounds__(256) scan_kernel(const float* dbl, int wd, con
   if (state != nullptr)
 #pragma unroll
     for (int n = 0; n < DS; ++n) state[(static_cast<long long>(b) * DS + n) * di + c] = h[n];
+}
+
+// Chunked selective scan for few sequences (the sequential kernel above runs
+// one thread per (sequence, channel), so one sequence is 1024 threads walking
+// all L steps).  The recurrence h_t = a_t h_(t-1) + b_t (a_t = exp(dt A),
+// b_t = dt B_t u_t) is split into chunks of kScanChunk steps: thread
+// (chunk w, channel c) first folds its chunk into (P, Q) = (prod a_t, the
+// chunk's h from a zero start), the chunks' (P, Q) are combined in order
+// through shared memory into the state entering each chunk, and a second pass
+// replays the chunk from that state with scan_kernel's expressions.  State n
+// at a time: y_t accumulates D u_t + sum_n h_t[n] C_t[n] in scan_kernel's n
+// order.  A CTA holds kScanCh consecutive channels (coalesced loads) and all
+// L / kScanChunk chunks; `state` (optional) is read as h_0 and receives h_L.
+constexpr int kScanChunk = 8;
+constexpr int kScanCh = 8;
+
+template <int DS, int DR, bool FAST>
+__global__ void scan_chunked_kernel(const float* dbl, int wd, const float* u, const float* xz, int L, int di,
+                                    const float* dt_w, const float* dt_b, const float* a_neg, const float* dsk,
+                                    float* state, float* y, __half* y_bf) {
+  extern __shared__ __align__(16) float sm[];
+  float* sdbl = sm;                  // [L][wd]
+  float* red = sdbl + L * wd;        // [2][nch][kScanCh][P, Q]
+  const int nch = L / kScanChunk;
+  const int b = blockIdx.y;
+  const int w = threadIdx.x / kScanCh, sub = threadIdx.x - w * kScanCh;
+  const int c = blockIdx.x * kScanCh + sub;
+  const float* drow = dbl + static_cast<long long>(b) * L * wd;
+  {
+    // 16-byte copies, eight in flight per thread (wd is a multiple of 4)
+    const int n4 = L * wd / 4;
+    const float4* src = reinterpret_cast<const float4*>(drow);
+    float4* dst = reinterpret_cast<float4*>(sdbl);
+    for (int i0 = threadIdx.x; i0 < n4; i0 += 8 * blockDim.x) {
+      float4 v[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int i = i0 + u * blockDim.x;
+        v[u] = i < n4 ? src[i] : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+      }
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int i = i0 + u * blockDim.x;
+        if (i < n4) dst[i] = v[u];
+      }
+    }
+  }
+  __syncthreads();
+  const bool live = c < di;
+  const int cc = live ? c : 0;
+  const int t0 = w * kScanChunk;
+  float dt[kScanChunk], uv[kScanChunk], yv[kScanChunk];
+  {
+    float wdt[DR];
+#pragma unroll
+    for (int r = 0; r < DR; ++r) wdt[r] = dt_w[cc * DR + r];
+    const float bdt = dt_b[cc], dk = dsk[cc];
+#pragma unroll
+    for (int i = 0; i < kScanChunk; ++i) {
+      const float* row = sdbl + (t0 + i) * wd;
+      float acc = 0.0f;
+#pragma unroll
+      for (int r = 0; r < DR; ++r) acc += row[r] * wdt[r];
+      const float pre = acc + bdt;
+      dt[i] = FAST ? fmaxf(pre, 0.0f) + __logf(1.0f + __expf(-fabsf(pre))) : softplus_f(pre);
+      const long long tok = static_cast<long long>(b) * L + t0 + i;
+      uv[i] = live ? u[tok * di + cc] : 0.0f;
+      yv[i] = dk * uv[i];
+    }
+  }
+  for (int n = 0; n < DS; ++n) {
+    const float an = FAST ? a_neg[n * di + cc] * 1.4426950408889634f : a_neg[n * di + cc];
+    // pass 1: the chunk from a zero state
+    float P = 1.0f, Q = 0.0f;
+#pragma unroll
+    for (int i = 0; i < kScanChunk; ++i) {
+      const float da = FAST ? ex2_approx(dt[i] * an) : expf(dt[i] * an);
+      const float dbu = dt[i] * sdbl[(t0 + i) * wd + DR + n] * uv[i];
+      P *= da;
+      Q = (da * Q) + dbu;
+    }
+    float* rd = red + (n & 1) * nch * kScanCh * 2;
+    rd[(w * kScanCh + sub) * 2] = P;
+    rd[(w * kScanCh + sub) * 2 + 1] = Q;
+    __syncthreads();
+    // state entering this chunk: the earlier chunks in order
+    float h = (state != nullptr && live) ? state[(static_cast<long long>(b) * DS + n) * di + cc] : 0.0f;
+    for (int v = 0; v < w; ++v) h = (rd[(v * kScanCh + sub) * 2] * h) + rd[(v * kScanCh + sub) * 2 + 1];
+    // pass 2: the chunk from that state (scan_kernel's update)
+#pragma unroll
+    for (int i = 0; i < kScanChunk; ++i) {
+      const float da = FAST ? ex2_approx(dt[i] * an) : expf(dt[i] * an);
+      const float dbu = dt[i] * sdbl[(t0 + i) * wd + DR + n] * uv[i];
+      h = (da * h) + dbu;
+      yv[i] += h * sdbl[(t0 + i) * wd + DR + DS + n];
+    }
+    if (state != nullptr && live && w == nch - 1) state[(static_cast<long long>(b) * DS + n) * di + cc] = h;
+  }
+  if (!live) return;
+#pragma unroll
+  for (int i = 0; i < kScanChunk; ++i) {
+    const long long tok = static_cast<long long>(b) * L + t0 + i;
+    const float zv = xz[tok * 2 * di + di + cc];
+    const float out = yv[i] * (FAST ? silu_fast(zv) : (zv / (1.0f + expf(-zv))));
+    y[tok * di + cc] = out;
+    if (y_bf != nullptr) y_bf[tok * di + cc] = to_half_sat(out);
+  }
 }
 
 // hidden[b][t] = embedding[token[b][t]]
@@ -415,6 +524,7 @@ class Mamba final : public MambaDevice {
   Mamba(std::shared_ptr<DeviceContext> ctx, Precision prec) : ctx_(std::move(ctx)), prec_(prec) {}
   ~Mamba() override {
     if (step_graph_ != nullptr) cudaGraphExecDestroy(step_graph_);
+    for (auto& [k, g] : fwd_graphs_) cudaGraphExecDestroy(g);
     if (pinned_ != nullptr) cudaFreeHost(pinned_);
   }
   bool load(const TensorTable& t, std::string& err);
@@ -462,6 +572,9 @@ class Mamba final : public MambaDevice {
   // the decode step as one graph (token upload, every layer, output download);
   // rebuilt after reserve() moves the buffers
   cudaGraphExec_t step_graph_ = nullptr;
+  // prefill kernels (embedding .. last-position gather) as one graph per
+  // (batch, length, destination); rebuilt after reserve() moves the buffers
+  std::map<std::tuple<std::size_t, std::size_t, const float*>, cudaGraphExec_t> fwd_graphs_;
   // fused decode (one cooperative launch per token) when the whole grid fits
   DecodeLayer* dec_layers_ = nullptr;
   unsigned* dec_sync_ = nullptr;
@@ -609,7 +722,13 @@ bool Mamba::load(const TensorTable& t, std::string& err) {
     err = "internal error: Mamba weight arena too small";
     return false;
   }
-  for (const void* k : {reinterpret_cast<const void*>(scan_kernel<16, 32, false>),
+  for (const void* k : {reinterpret_cast<const void*>(scan_chunked_kernel<16, 32, false>),
+                        reinterpret_cast<const void*>(scan_chunked_kernel<16, 32, true>),
+                        reinterpret_cast<const void*>(scan_chunked_kernel<8, 4, false>),
+                        reinterpret_cast<const void*>(scan_chunked_kernel<8, 4, true>),
+                        reinterpret_cast<const void*>(scan_chunked_kernel<4, 4, false>),
+                        reinterpret_cast<const void*>(scan_chunked_kernel<4, 4, true>),
+                        reinterpret_cast<const void*>(scan_kernel<16, 32, false>),
                         reinterpret_cast<const void*>(scan_kernel<16, 32, true>),
                         reinterpret_cast<const void*>(scan_kernel<8, 4, false>),
                         reinterpret_cast<const void*>(scan_kernel<8, 4, true>),
@@ -632,6 +751,8 @@ int Mamba::reserve(std::size_t batch, std::size_t max_len, std::string& err) noe
     cudaGraphExecDestroy(step_graph_);
     step_graph_ = nullptr;
   }
+  for (auto& [k, g] : fwd_graphs_) cudaGraphExecDestroy(g);
+  fwd_graphs_.clear();
   const std::size_t dm = cfg_.d_model, di = cfg_.d_inner, wd = cfg_.dt_rank + 2 * cfg_.d_state;
   const std::size_t rows = (tokens + 255) / 256 * 256;
   std::size_t nsl = 1;
@@ -802,16 +923,30 @@ bool Mamba::run_layers(long long n_tok, int B, int L, bool tc, cudaStream_t st, 
       return false;
     const dim3 grid(static_cast<unsigned>((di + 255) / 256), static_cast<unsigned>(B));
     const std::size_t smem = static_cast<std::size_t>(L) * wd * 4;
-    auto scan = [&](auto kernel) {
-      kernel<<<grid, 256, smem, st>>>(dbl_, wd, u_, xz_, L, di, Ly.dt_w, Ly.dt_b, Ly.a_neg, Ly.d, nullptr, y_,
-                                      tc ? yb_ : nullptr);
+    // few sequences: chunks of the sequence in parallel (when L splits into them)
+    const dim3 cgrid(static_cast<unsigned>((di + kScanCh - 1) / kScanCh), static_cast<unsigned>(B));
+    const unsigned cthreads = static_cast<unsigned>(kScanCh * (L / kScanChunk));
+    const std::size_t csmem =
+        (static_cast<std::size_t>(L) * wd + 2 * static_cast<std::size_t>(L / kScanChunk) * kScanCh * 2) * 4;
+    const bool chunked = L % kScanChunk == 0 && L / kScanChunk <= 64 && static_cast<long long>(B) * di < 32768 &&
+                         csmem <= 200 * 1024 && wd % 4 == 0;
+    auto scan = [&](auto kernel, auto ckernel) {
+      if (chunked)
+        ckernel<<<cgrid, cthreads, csmem, st>>>(dbl_, wd, u_, xz_, L, di, Ly.dt_w, Ly.dt_b, Ly.a_neg, Ly.d, nullptr,
+                                                y_, tc ? yb_ : nullptr);
+      else
+        kernel<<<grid, 256, smem, st>>>(dbl_, wd, u_, xz_, L, di, Ly.dt_w, Ly.dt_b, Ly.a_neg, Ly.d, nullptr, y_,
+                                        tc ? yb_ : nullptr);
     };
     if (ds == 16 && dr == 32)
-      tc ? scan(scan_kernel<16, 32, true>) : scan(scan_kernel<16, 32, false>);
+      tc ? scan(scan_kernel<16, 32, true>, scan_chunked_kernel<16, 32, true>)
+         : scan(scan_kernel<16, 32, false>, scan_chunked_kernel<16, 32, false>);
     else if (ds == 4 && dr == 4)
-      tc ? scan(scan_kernel<4, 4, true>) : scan(scan_kernel<4, 4, false>);
+      tc ? scan(scan_kernel<4, 4, true>, scan_chunked_kernel<4, 4, true>)
+         : scan(scan_kernel<4, 4, false>, scan_chunked_kernel<4, 4, false>);
     else if (ds == 8 && dr == 4)
-      tc ? scan(scan_kernel<8, 4, true>) : scan(scan_kernel<8, 4, false>);
+      tc ? scan(scan_kernel<8, 4, true>, scan_chunked_kernel<8, 4, true>)
+         : scan(scan_kernel<8, 4, false>, scan_chunked_kernel<8, 4, false>);
     else {
       err = "no scan instantiation for this (d_state, dt_rank)";
       return false;
@@ -837,11 +972,37 @@ int Mamba::forward_device(const std::int32_t* tokens, std::size_t batch, std::si
   const bool tc = prec_ == Precision::kBF16 && n_tok >= kTcMinTokens;
   if (tokens != tokens_) cudaMemcpyAsync(tokens_, tokens, n_tok * 4, cudaMemcpyDeviceToDevice, st);
   const int dm = static_cast<int>(cfg_.d_model);
-  embed_kernel<<<ew_grid(n_tok * dm, 256, *ctx_), 256, 0, st>>>(tokens_, n_tok, emb_, dm, hidden_);
-  if (!run_layers(n_tok, static_cast<int>(batch), static_cast<int>(len), tc, st, err)) return 2;
-  gather_last_kernel<<<ew_grid(static_cast<long long>(batch) * dm, 256, *ctx_), 256, 0, st>>>(
-      out_, static_cast<int>(batch), static_cast<int>(len), dm, last_hidden != nullptr ? last_hidden : last_);
-  return cudaGetLastError() == cudaSuccess ? 0 : 2;
+  float* dst = last_hidden != nullptr ? last_hidden : last_;
+  const auto key = std::make_tuple(batch, len, static_cast<const float*>(dst));
+  auto it = fwd_graphs_.find(key);
+  if (it == fwd_graphs_.end()) {
+    cudaStream_t cap = nullptr;
+    cudaStreamCreateWithFlags(&cap, cudaStreamNonBlocking);
+    cudaStreamSynchronize(st);
+    cudaGraph_t graph = nullptr;
+    cudaStreamBeginCapture(cap, cudaStreamCaptureModeThreadLocal);
+    embed_kernel<<<ew_grid(n_tok * dm, 256, *ctx_), 256, 0, cap>>>(tokens_, n_tok, emb_, dm, hidden_);
+    const bool ok = run_layers(n_tok, static_cast<int>(batch), static_cast<int>(len), tc, cap, err);
+    gather_last_kernel<<<ew_grid(static_cast<long long>(batch) * dm, 256, *ctx_), 256, 0, cap>>>(
+        out_, static_cast<int>(batch), static_cast<int>(len), dm, dst);
+    const cudaError_t end = cudaStreamEndCapture(cap, &graph);
+    cudaStreamDestroy(cap);
+    if (!ok || end != cudaSuccess || graph == nullptr) {
+      if (graph != nullptr) cudaGraphDestroy(graph);
+      if (err.empty()) err = "Mamba prefill graph capture failed";
+      cudaGetLastError();
+      return 2;
+    }
+    cudaGraphExec_t exec = nullptr;
+    const cudaError_t inst = cudaGraphInstantiate(&exec, graph, 0);
+    cudaGraphDestroy(graph);
+    if (inst != cudaSuccess) {
+      err = "Mamba prefill graph instantiation failed";
+      return 2;
+    }
+    it = fwd_graphs_.emplace(key, exec).first;
+  }
+  return cudaGraphLaunch(it->second, st) == cudaSuccess ? 0 : 2;
 }
 
 int Mamba::forward(const std::int32_t* tokens, std::size_t batch, std::size_t len, float* hidden, bool last_only,
