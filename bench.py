@@ -445,7 +445,22 @@ def _extras(workdir: Path, device: int):
         e.run_batch(tb[:2])
         t0 = time.perf_counter()
         e.run_batch(tb)
+        # host API: every position's hidden state comes back (1024 x 128 x 512 fp32 = 268 MB)
         out[f"c3_mamba_b1024_prefill128_{prec}_seq_per_s"] = 1024 / (time.perf_counter() - t0)
+        # device buffers, last hidden state only (what feeds the flow head), CUDA events
+        dt_ = torch.from_numpy(tb).cuda()
+        dl = torch.empty((1024, 512), dtype=torch.float32, device="cuda")
+        st = torch.cuda.Stream()
+        for _ in range(2):
+            e.run_device(dt_.data_ptr(), 1024, 128, dl.data_ptr(), st.cuda_stream)
+        st.synchronize()
+        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        ev0.record(st)
+        for _ in range(3):
+            e.run_device(dt_.data_ptr(), 1024, 128, dl.data_ptr(), st.cuda_stream)
+        ev1.record(st)
+        st.synchronize()
+        out[f"c3_mamba_b1024_prefill128_{prec}_device_seq_per_s"] = 3 * 1024 / (ev0.elapsed_time(ev1) / 1000.0)
         e.close()
     # C5: SmolVLA-shaped action expert (bf16 by construction), Euler-10, one
     # fixed 241-slot prefix shared by the batch

@@ -894,6 +894,25 @@ int fe_engine_run(fe_engine* engine, const int32_t* tokens, size_t seq_len, floa
   return fe_engine_run_batch(engine, tokens, 1, seq_len, out);
 }
 
+int fe_engine_run_device(fe_engine* engine, const int32_t* tokens, size_t batch, size_t seq_len, float* last_hidden,
+                         void* stream) {
+  clear_error();
+  if (engine == nullptr || tokens == nullptr || last_hidden == nullptr || seq_len == 0 || batch == 0) {
+    set_error("Invalid arguments to fe_engine_run_device");
+    return FE_STATUS_INVALID_ARGUMENT;
+  }
+  if (!engine->mamba) {
+    set_error("Model has no backbone");
+    return FE_STATUS_UNSUPPORTED_MODEL;
+  }
+  std::string err;
+  if (engine->mamba->forward_device(tokens, batch, seq_len, last_hidden, stream, err) != 0) {
+    set_error("Mamba forward failed: " + err);
+    return FE_STATUS_RESOURCE_EXHAUSTED;
+  }
+  return FE_STATUS_OK;
+}
+
 int fe_engine_sample_batch(fe_engine* engine, const int32_t* tokens, size_t batch, size_t seq_len,
                            const float* noise, size_t steps, int method, float* action) {
   clear_error();

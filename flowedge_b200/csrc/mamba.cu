@@ -82,8 +82,9 @@ __global__ void rmsnorm_kernel(const float* in, const float* w, int rows, int di
 // once).  The window is right-aligned in kMaxConv slots so every index is a
 // compile-time constant; slots before the first step hold zeros, which the
 // taps that reach before t = 0 multiply (the reference skips them: same sum).
-__global__ void causal_conv_kernel(const float* xz, int B, int L, int di, int dc, const float* w, const float* bias,
-                                   float* u, __half* u_bf) {
+__global__ void causal_conv_kernel(const float* __restrict__ xz, int B, int L, int di, int dc,
+                                   const float* __restrict__ w, const float* __restrict__ bias, float* __restrict__ u,
+                                   __half* __restrict__ u_bf) {
   const int q = di >> 2;
   const long long total = static_cast<long long>(B) * q;
   const int first = kMaxConv - dc;
@@ -101,10 +102,13 @@ __global__ void causal_conv_kernel(const float* xz, int B, int L, int di, int dc
 #pragma unroll
     for (int j = 0; j < kMaxConv; ++j) win[j] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
     const long long tok0 = static_cast<long long>(b) * L;
+    // the next step's input is requested one step ahead
+    float4 ahead = __ldg(reinterpret_cast<const float4*>(xz + tok0 * 2 * di + c));
     for (int t = 0; t < L; ++t) {
 #pragma unroll
       for (int j = 0; j + 1 < kMaxConv; ++j) win[j] = win[j + 1];
-      win[kMaxConv - 1] = *reinterpret_cast<const float4*>(xz + (tok0 + t) * 2 * di + c);
+      win[kMaxConv - 1] = ahead;
+      if (t + 1 < L) ahead = __ldg(reinterpret_cast<const float4*>(xz + (tok0 + t + 1) * 2 * di + c));
       float a0 = bv.x, a1 = bv.y, a2 = bv.z, a3 = bv.w;
 #pragma unroll
       for (int j = 0; j < kMaxConv; ++j)

@@ -137,6 +137,7 @@ SIGNATURES = {
     "fe_engine_sample_condition_static": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_size_t, C.c_size_t,
                                                     C.c_int, C.c_void_p, C.c_void_p]),
     "fe_engine_run_batch": (C.c_int, [C.c_void_p, _i32p, C.c_size_t, C.c_size_t, _f32p]),
+    "fe_engine_run_device": (C.c_int, [C.c_void_p, C.c_void_p, C.c_size_t, C.c_size_t, C.c_void_p, C.c_void_p]),
     "fe_engine_sample_batch": (C.c_int, [C.c_void_p, _i32p, C.c_size_t, C.c_size_t, _f32p, C.c_size_t, C.c_int,
                                          _f32p]),
     "fe_engine_smolvla_sample_batch": (C.c_int, [C.c_void_p, _f32p, C.c_size_t, C.c_size_t, C.c_size_t, _f32p,
@@ -367,6 +368,11 @@ class Engine:
         out = np.empty((toks.size, self.d_model), np.float32)
         self._check(self.lib.fe_engine_run(self.handle, toks.ctypes.data_as(_i32p), toks.size, _p(out)))
         return out
+
+    def run_device(self, tokens_ptr: int, batch: int, seq_len: int, last_hidden_ptr: int, stream: int = 0):
+        """Prefill on device buffers (last hidden state of each sequence); asynchronous."""
+        self._check(self.lib.fe_engine_run_device(self.handle, tokens_ptr, batch, seq_len, last_hidden_ptr,
+                                                  stream or None))
 
     def run_batch(self, tokens):
         toks = np.ascontiguousarray(tokens, np.int32)

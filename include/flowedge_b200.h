@@ -322,6 +322,13 @@ int fe_engine_sample_condition_static(fe_engine* engine, const float* condition,
                                       size_t steps, int method, float* action, void* stream);
 /* Batched Mamba prefill: tokens [batch][seq_len], out [batch][seq_len][d_model]. */
 int fe_engine_run_batch(fe_engine* engine, const int32_t* tokens, size_t batch, size_t seq_len, float* out);
+/* Mamba prefill on DEVICE buffers, enqueued on `stream` (NULL = the engine's
+ * stream): tokens [batch][seq_len] (ids are not range-checked on the host),
+ * last_hidden [batch][d_model] = the final-normed hidden state of each
+ * sequence's last position (the flow condition).  Returns before the work
+ * completes; batch * seq_len must fit the reserved capacity. */
+int fe_engine_run_device(fe_engine* engine, const int32_t* tokens, size_t batch, size_t seq_len, float* last_hidden,
+                         void* stream);
 /* Batched fe_engine_sample: tokens [batch][seq_len], noise/action [batch][A]. */
 int fe_engine_sample_batch(fe_engine* engine, const int32_t* tokens, size_t batch, size_t seq_len,
                            const float* noise, size_t steps, int method, float* action);
