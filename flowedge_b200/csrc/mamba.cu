@@ -41,6 +41,7 @@ std::uint16_t bf16_of(float v) {
 struct Mat {
   int rows = 0, rows_pad = 0, cols = 0, cols_pad = 0;
   void* w = nullptr;
+  void* w3 = nullptr;  // fp32 engines: fp16 [rows_pad][3 cols_pad] = [hi | hi | lo] for the tensor path
   SimtSlice* slices = nullptr;
   int nslices = 0;
 };
@@ -56,9 +57,23 @@ struct Layer {
   float* d = nullptr;
 };
 
+// 16-bit GEMM operand of an activation: fp16(v) at [row][c] of a [rows][ld]
+// matrix, or with split = 1 the pair hi = fp16(v) at [row][c], lo = fp16(v - hi)
+// at [row][ld + c] of a [rows][2 ld] matrix (fp32 engines on the tensor cores)
+__device__ __forceinline__ void store_act16(__half* base, long long row, int ld, int c, float v, int split) {
+  const __half hi = to_half_sat(v);
+  if (split) {
+    base[row * 2 * ld + c] = hi;
+    base[row * 2 * ld + ld + c] = __float2half_rn(v - __half2float(hi));
+  } else {
+    base[row * ld + c] = hi;
+  }
+}
+
 // one warp per row; RMSNorm with eps 1e-5 (kernels_scalar.cc:48-60); optional
-// bf16 copy for the tensor-core GEMM
-__global__ void rmsnorm_kernel(const float* in, const float* w, int rows, int dim, float* out, __half* out_bf) {
+// 16-bit copy for the tensor-core GEMM (store_act16)
+__global__ void rmsnorm_kernel(const float* in, const float* w, int rows, int dim, float* out, __half* out_bf,
+                               int split) {
   const int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (row >= rows) return;
@@ -70,7 +85,7 @@ __global__ void rmsnorm_kernel(const float* in, const float* w, int rows, int di
   for (int i = lane; i < dim; i += 32) {
     const float v = x[i] * scale * w[i];
     if (out != nullptr) out[static_cast<long long>(row) * dim + i] = v;
-    if (out_bf != nullptr) out_bf[static_cast<long long>(row) * dim + i] = to_half_sat(v);
+    if (out_bf != nullptr) store_act16(out_bf, row, dim, i, v, split);
   }
 }
 
@@ -84,7 +99,7 @@ __global__ void rmsnorm_kernel(const float* in, const float* w, int rows, int di
 // taps that reach before t = 0 multiply (the reference skips them: same sum).
 __global__ void causal_conv_kernel(const float* __restrict__ xz, int B, int L, int di, int dc,
                                    const float* __restrict__ w, const float* __restrict__ bias, float* __restrict__ u,
-                                   __half* __restrict__ u_bf) {
+                                   __half* __restrict__ u_bf, int split) {
   const int q = di >> 2;
   const long long total = static_cast<long long>(B) * q;
   const int first = kMaxConv - dc;
@@ -122,12 +137,18 @@ __global__ void causal_conv_kernel(const float* __restrict__ xz, int B, int L, i
       const long long o = (tok0 + t) * di + c;
       *reinterpret_cast<float4*>(u + o) = v;
       if (u_bf != nullptr) {
-        const __half2 lo = __halves2half2(to_half_sat(v.x), to_half_sat(v.y));
-        const __half2 hi = __halves2half2(to_half_sat(v.z), to_half_sat(v.w));
-        uint2 packed;
-        packed.x = *reinterpret_cast<const uint32_t*>(&lo);
-        packed.y = *reinterpret_cast<const uint32_t*>(&hi);
-        *reinterpret_cast<uint2*>(u_bf + o) = packed;
+        const __half h0 = to_half_sat(v.x), h1 = to_half_sat(v.y), h2 = to_half_sat(v.z), h3 = to_half_sat(v.w);
+        const __half2 p01 = __halves2half2(h0, h1);
+        const __half2 p23 = __halves2half2(h2, h3);
+        const long long ob = split ? (tok0 + t) * 2 * di + c : o;
+        *reinterpret_cast<uint2*>(u_bf + ob) =
+            make_uint2(*reinterpret_cast<const uint32_t*>(&p01), *reinterpret_cast<const uint32_t*>(&p23));
+        if (split) {
+          const __half2 l01 = __floats2half2_rn(v.x - __half2float(h0), v.y - __half2float(h1));
+          const __half2 l23 = __floats2half2_rn(v.z - __half2float(h2), v.w - __half2float(h3));
+          *reinterpret_cast<uint2*>(u_bf + ob + di) =
+              make_uint2(*reinterpret_cast<const uint32_t*>(&l01), *reinterpret_cast<const uint32_t*>(&l23));
+        }
       }
     }
   }
@@ -135,7 +156,7 @@ __global__ void causal_conv_kernel(const float* __restrict__ xz, int B, int L, i
 
 // Few sequences: one thread per (token, channel), the dc inputs re-read
 __global__ void causal_conv_tok_kernel(const float* xz, int B, int L, int di, int dc, const float* w,
-                                       const float* bias, float* u, __half* u_bf) {
+                                       const float* bias, float* u, __half* u_bf, int split) {
   const long long total = static_cast<long long>(B) * L * di;
   for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
        i += static_cast<long long>(gridDim.x) * blockDim.x) {
@@ -149,7 +170,7 @@ __global__ void causal_conv_tok_kernel(const float* xz, int B, int L, int di, in
     }
     const float v = silu_f(acc);
     u[i] = v;
-    if (u_bf != nullptr) u_bf[i] = to_half_sat(v);
+    if (u_bf != nullptr) store_act16(u_bf, tok, di, c, v, split);
   }
 }
 
@@ -164,7 +185,8 @@ __global__ void causal_conv_tok_kernel(const float* xz, int B, int L, int di, in
 template <int DS, int DR, bool FAST>
 __global__ void __launch_bounds__(256) scan_kernel(const float* dbl, int wd, const float* u, const float* xz, int L,
                                                    int di, const float* dt_w, const float* dt_b, const float* a_neg,
-                                                   const float* dsk, float* state, float* y, __half* y_bf) {
+                                                   const float* dsk, float* state, float* y, __half* y_bf,
+                                                   int split) {
   extern __shared__ float sdbl[];  // [L][wd]
   const int b = blockIdx.y;
   const int c = blockIdx.x * blockDim.x + threadIdx.x;
@@ -201,7 +223,7 @@ __global__ void __launch_bounds__(256) scan_kernel(const float* dbl, int wd, con
     const float zv = xz[tok * 2 * di + di + c];
     const float out = yv * (FAST ? silu_fast(zv) : (zv / (1.0f + expf(-zv))));
     y[tok * di + c] = out;
-    if (y_bf != nullptr) y_bf[tok * di + c] = to_half_sat(out);
+    if (y_bf != nullptr) store_act16(y_bf, tok, di, c, out, split);
   }
   if (state != nullptr)
 #pragma unroll
@@ -225,7 +247,7 @@ constexpr int kScanCh = 8;
 template <int DS, int DR, bool FAST>
 __global__ void scan_chunked_kernel(const float* dbl, int wd, const float* u, const float* xz, int L, int di,
                                     const float* dt_w, const float* dt_b, const float* a_neg, const float* dsk,
-                                    float* state, float* y, __half* y_bf) {
+                                    float* state, float* y, __half* y_bf, int split) {
   extern __shared__ __align__(16) float sm[];
   float* sdbl = sm;                  // [L][wd]
   float* red = sdbl + L * wd;        // [2][nch][kScanCh][P, Q]
@@ -311,7 +333,7 @@ __global__ void scan_chunked_kernel(const float* dbl, int wd, const float* u, co
     const float zv = xz[tok * 2 * di + di + cc];
     const float out = yv[i] * (FAST ? silu_fast(zv) : (zv / (1.0f + expf(-zv))));
     y[tok * di + cc] = out;
-    if (y_bf != nullptr) y_bf[tok * di + cc] = to_half_sat(out);
+    if (y_bf != nullptr) store_act16(y_bf, tok, di, cc, out, split);
   }
 }
 
@@ -623,7 +645,8 @@ bool Mamba::load(const TensorTable& t, std::string& err) {
   const bool bf = prec_ == Precision::kBF16;
   auto mat_bytes = [&](std::size_t rows, std::size_t cols) {
     const std::size_t rp = (rows + 127) / 128 * 128, cp = (cols + 63) / 64 * 64;
-    return rp * cp * (bf ? 2 : 4) + ((cp + 255) / 256) * sizeof(SimtSlice) + 512;
+    // bf16: 16-bit W; fp32: fp32 W (CUDA cores) and the [hi | hi | lo] fp16 copy
+    return rp * cp * (bf ? 2 : 4 + 6) + ((cp + 255) / 256) * sizeof(SimtSlice) + 1024;
   };
   ArenaPlan plan;
   plan.add_n<float>(cfg_.vocab * dm + dm);
@@ -672,6 +695,19 @@ bool Mamba::load(const TensorTable& t, std::string& err) {
       cudaMemcpy(m.w, hb.data(), hb.size() * 2, cudaMemcpyHostToDevice);
     } else {
       m.w = put(padded);
+      // [hi | hi | lo] rows for the fp32 tensor path
+      const std::size_t cp = static_cast<std::size_t>(m.cols_pad);
+      std::vector<std::uint16_t> h3(padded.size() * 3);
+      for (std::size_t r = 0; r < static_cast<std::size_t>(m.rows_pad); ++r)
+        for (std::size_t c = 0; c < cp; ++c) {
+          const float v = padded[r * cp + c];
+          const __half hi = __float2half_rn(v);
+          h3[r * 3 * cp + c] = __half_as_ushort(hi);
+          h3[r * 3 * cp + cp + c] = __half_as_ushort(hi);
+          h3[r * 3 * cp + 2 * cp + c] = __half_as_ushort(__float2half_rn(v - __half2float(hi)));
+        }
+      m.w3 = wts_.take(h3.size() * 2);
+      cudaMemcpy(m.w3, h3.data(), h3.size() * 2, cudaMemcpyHostToDevice);
     }
     std::vector<SimtSlice> sl;
     for (int c = 0; c < m.cols_pad; c += 256) sl.push_back(SimtSlice{0, 0, c, std::min(256, m.cols_pad - c), c});
@@ -776,9 +812,9 @@ int Mamba::reserve(std::size_t batch, std::size_t max_len, std::string& err) noe
   plan.add_n<float>(part_elems_);
   plan.add_n<float>(batch * dm);      // last
   plan.add_n<float>(rows * dm);       // out
-  plan.add_n<__half>(rows * dm);
-  plan.add_n<__half>(rows * di);
-  plan.add_n<__half>(rows * di);
+  plan.add_n<__half>(rows * 2 * dm);
+  plan.add_n<__half>(rows * 2 * di);
+  plan.add_n<__half>(rows * 2 * di);
   plan.add_n<float>(state_floats());
   plan.add_n<float>(dm + 2 * di + di + wd + di + di + dm + 64);
   plan.add_n<DecodeLayer>(layers_.size());
@@ -803,9 +839,9 @@ int Mamba::reserve(std::size_t batch, std::size_t max_len, std::string& err) noe
   part_ = ws_.take_n<float>(part_elems_);
   last_ = ws_.take_n<float>(batch * dm);
   out_ = ws_.take_n<float>(rows * dm);
-  nb_ = ws_.take_n<__half>(rows * dm);
-  ub_ = ws_.take_n<__half>(rows * di);
-  yb_ = ws_.take_n<__half>(rows * di);
+  nb_ = ws_.take_n<__half>(rows * 2 * dm);  // room for hi / lo pairs (fp32 engines)
+  ub_ = ws_.take_n<__half>(rows * 2 * di);
+  yb_ = ws_.take_n<__half>(rows * 2 * di);
   state_ = ws_.take_n<float>(state_floats());
   dh_ = ws_.take_n<float>(dm + 2 * di + di + wd + di + di + dm + 64);
   dec_layers_ = ws_.take_n<DecodeLayer>(layers_.size());
@@ -857,14 +893,23 @@ bool Mamba::gemm(const Mat& m, const void* in, int in_ld, long long n_tok, float
   if (tc) {
     TcLaunch l;
     l.fp16 = true;
-    l.A = m.w;
     l.M_rows = m.rows_pad;
-    l.K = m.cols_pad;
-    l.src[0] = TcSource{in, in_ld, 1, static_cast<int>(cap_rows_)};
     l.L = 1;
     l.n_samples = static_cast<int>(n_tok);
     l.m_valid = m.rows;
-    l.segs = {tc::Seg{0, 0, 0, m.cols_pad / 64, 0}};
+    const int kb = m.cols_pad / 64;
+    if (prec_ != Precision::kBF16) {
+      // fp32 engine: [hi(W) | hi(W) | lo(W)] against [hi(x) | lo(x)] (segments hi, lo, hi)
+      l.A = m.w3;
+      l.K = 3 * m.cols_pad;
+      l.src[0] = TcSource{in, 2 * in_ld, 1, static_cast<int>(cap_rows_)};
+      l.segs = {tc::Seg{0, 0, 0, kb, 0}, tc::Seg{0, 0, in_ld, kb, m.cols_pad}, tc::Seg{0, 0, 0, kb, 2 * m.cols_pad}};
+    } else {
+      l.A = m.w;
+      l.K = m.cols_pad;
+      l.src[0] = TcSource{in, in_ld, 1, static_cast<int>(cap_rows_)};
+      l.segs = {tc::Seg{0, 0, 0, kb, 0}};
+    }
     l.out_f32 = true;
     l.out_accumulate = accumulate;
     l.out = out;
@@ -910,19 +955,23 @@ bool Mamba::run_layers(long long n_tok, int B, int L, bool tc, cudaStream_t st, 
   const int ds = static_cast<int>(cfg_.d_state), dc = static_cast<int>(cfg_.d_conv);
   const int dr = static_cast<int>(cfg_.dt_rank), wd = dr + 2 * ds;
   float* normed = out_;  // fp32 normed rows share the output buffer until the final norm
+  // tensor path: bf16 engines take fp16 operands, fp32 engines fp16 hi / lo splits;
+  // the scan's fast exponentials belong to the bf16 mode only
+  const int split = tc && prec_ != Precision::kBF16 ? 1 : 0;
+  const bool fast = prec_ == Precision::kBF16;
   for (const Layer& Ly : layers_) {
     rmsnorm_kernel<<<static_cast<unsigned>((n_tok * 32 + 255) / 256), 256, 0, st>>>(hidden_, Ly.norm,
                                                                                       static_cast<int>(n_tok), dm,
                                                                                       tc ? nullptr : normed,
-                                                                                      tc ? nb_ : nullptr);
+                                                                                      tc ? nb_ : nullptr, split);
     if (!gemm(Ly.in_proj, tc ? static_cast<const void*>(nb_) : normed, dm, n_tok, xz_, 2 * di, false, tc, st, err))
       return false;
     if (static_cast<long long>(B) * (di / 4) >= 32LL * 32 * ctx_->sm_count)
       causal_conv_kernel<<<ew_grid(static_cast<long long>(B) * (di / 4), 256, *ctx_), 256, 0, st>>>(
-          xz_, B, L, di, dc, Ly.conv_w, Ly.conv_b, u_, tc ? ub_ : nullptr);
+          xz_, B, L, di, dc, Ly.conv_w, Ly.conv_b, u_, tc ? ub_ : nullptr, split);
     else
       causal_conv_tok_kernel<<<ew_grid(n_tok * di, 256, *ctx_), 256, 0, st>>>(xz_, B, L, di, dc, Ly.conv_w, Ly.conv_b,
-                                                                            u_, tc ? ub_ : nullptr);
+                                                                            u_, tc ? ub_ : nullptr, split);
     if (!gemm(Ly.x_proj, tc ? static_cast<const void*>(ub_) : u_, di, n_tok, dbl_, wd, false, tc, st, err))
       return false;
     const dim3 grid(static_cast<unsigned>((di + 255) / 256), static_cast<unsigned>(B));
@@ -937,20 +986,20 @@ bool Mamba::run_layers(long long n_tok, int B, int L, bool tc, cudaStream_t st, 
     auto scan = [&](auto kernel, auto ckernel) {
       if (chunked)
         ckernel<<<cgrid, cthreads, csmem, st>>>(dbl_, wd, u_, xz_, L, di, Ly.dt_w, Ly.dt_b, Ly.a_neg, Ly.d, nullptr,
-                                                y_, tc ? yb_ : nullptr);
+                                                y_, tc ? yb_ : nullptr, split);
       else
         kernel<<<grid, 256, smem, st>>>(dbl_, wd, u_, xz_, L, di, Ly.dt_w, Ly.dt_b, Ly.a_neg, Ly.d, nullptr, y_,
-                                        tc ? yb_ : nullptr);
+                                        tc ? yb_ : nullptr, split);
     };
     if (ds == 16 && dr == 32)
-      tc ? scan(scan_kernel<16, 32, true>, scan_chunked_kernel<16, 32, true>)
-         : scan(scan_kernel<16, 32, false>, scan_chunked_kernel<16, 32, false>);
+      fast ? scan(scan_kernel<16, 32, true>, scan_chunked_kernel<16, 32, true>)
+           : scan(scan_kernel<16, 32, false>, scan_chunked_kernel<16, 32, false>);
     else if (ds == 4 && dr == 4)
-      tc ? scan(scan_kernel<4, 4, true>, scan_chunked_kernel<4, 4, true>)
-         : scan(scan_kernel<4, 4, false>, scan_chunked_kernel<4, 4, false>);
+      fast ? scan(scan_kernel<4, 4, true>, scan_chunked_kernel<4, 4, true>)
+           : scan(scan_kernel<4, 4, false>, scan_chunked_kernel<4, 4, false>);
     else if (ds == 8 && dr == 4)
-      tc ? scan(scan_kernel<8, 4, true>, scan_chunked_kernel<8, 4, true>)
-         : scan(scan_kernel<8, 4, false>, scan_chunked_kernel<8, 4, false>);
+      fast ? scan(scan_kernel<8, 4, true>, scan_chunked_kernel<8, 4, true>)
+           : scan(scan_kernel<8, 4, false>, scan_chunked_kernel<8, 4, false>);
     else {
       err = "no scan instantiation for this (d_state, dt_rank)";
       return false;
@@ -960,7 +1009,7 @@ bool Mamba::run_layers(long long n_tok, int B, int L, bool tc, cudaStream_t st, 
   }
   rmsnorm_kernel<<<static_cast<unsigned>((n_tok * 32 + 255) / 256), 256, 0, st>>>(hidden_, norm_f_,
                                                                                     static_cast<int>(n_tok), dm, out_,
-                                                                                    nullptr);
+                                                                                    nullptr, 0);
   return cudaGetLastError() == cudaSuccess;
 }
 
@@ -973,7 +1022,7 @@ int Mamba::forward_device(const std::int32_t* tokens, std::size_t batch, std::si
   }
   cudaSetDevice(ctx_->device);
   cudaStream_t st = stream != nullptr ? static_cast<cudaStream_t>(stream) : ctx_->stream;
-  const bool tc = prec_ == Precision::kBF16 && n_tok >= kTcMinTokens;
+  const bool tc = n_tok >= kTcMinTokens;
   if (tokens != tokens_) cudaMemcpyAsync(tokens_, tokens, n_tok * 4, cudaMemcpyDeviceToDevice, st);
   const int dm = static_cast<int>(cfg_.d_model);
   float* dst = last_hidden != nullptr ? last_hidden : last_;
@@ -1095,25 +1144,25 @@ bool Mamba::record_step(cudaStream_t st, std::string& err) {
     const Layer& Ly = layers_[li];
     float* window = state_ + li * per;
     float* h = window + static_cast<std::size_t>(di) * dc;
-    rmsnorm_kernel<<<1, 32, 0, st>>>(x, Ly.norm, 1, dm, normed, nullptr);
+    rmsnorm_kernel<<<1, 32, 0, st>>>(x, Ly.norm, 1, dm, normed, nullptr, 0);
     if (!gemm(Ly.in_proj, normed, dm, 1, xz, 2 * di, false, false, st, err)) return false;
     conv_step_kernel<<<(di + 255) / 256, 256, 0, st>>>(xz, di, dc, window, Ly.conv_w, Ly.conv_b, u);
     if (!gemm(Ly.x_proj, u, di, 1, dbl, wd, false, false, st, err)) return false;
     const dim3 grid(static_cast<unsigned>((di + 255) / 256), 1);
     const std::size_t smem = static_cast<std::size_t>(wd) * 4;
     if (ds == 16 && dr == 32)
-      scan_kernel<16, 32, false><<<grid, 256, smem, st>>>(dbl, wd, u, xz, 1, di, Ly.dt_w, Ly.dt_b, Ly.a_neg, Ly.d, h, y, nullptr);
+      scan_kernel<16, 32, false><<<grid, 256, smem, st>>>(dbl, wd, u, xz, 1, di, Ly.dt_w, Ly.dt_b, Ly.a_neg, Ly.d, h, y, nullptr, 0);
     else if (ds == 4 && dr == 4)
-      scan_kernel<4, 4, false><<<grid, 256, smem, st>>>(dbl, wd, u, xz, 1, di, Ly.dt_w, Ly.dt_b, Ly.a_neg, Ly.d, h, y, nullptr);
+      scan_kernel<4, 4, false><<<grid, 256, smem, st>>>(dbl, wd, u, xz, 1, di, Ly.dt_w, Ly.dt_b, Ly.a_neg, Ly.d, h, y, nullptr, 0);
     else if (ds == 8 && dr == 4)
-      scan_kernel<8, 4, false><<<grid, 256, smem, st>>>(dbl, wd, u, xz, 1, di, Ly.dt_w, Ly.dt_b, Ly.a_neg, Ly.d, h, y, nullptr);
+      scan_kernel<8, 4, false><<<grid, 256, smem, st>>>(dbl, wd, u, xz, 1, di, Ly.dt_w, Ly.dt_b, Ly.a_neg, Ly.d, h, y, nullptr, 0);
     else {
       err = "no scan instantiation for this (d_state, dt_rank)";
       return false;
     }
     if (!gemm(Ly.out_proj, y, di, 1, x, dm, true, false, st, err)) return false;
   }
-  rmsnorm_kernel<<<1, 32, 0, st>>>(x, norm_f_, 1, dm, normed, nullptr);
+  rmsnorm_kernel<<<1, 32, 0, st>>>(x, norm_f_, 1, dm, normed, nullptr, 0);
   cudaMemcpyAsync(pinned_ + 1, normed, dm * 4, cudaMemcpyDeviceToHost, st);
   return cudaGetLastError() == cudaSuccess;
 }

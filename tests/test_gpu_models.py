@@ -383,3 +383,21 @@ def test_mamba_c3_bf16_batched_tensor_path(tmp_path):
     expected_act = np.stack([flow.sample(expected[i, -1], x0[i], 10, "euler") for i in range(4)])
     assert np.abs(act - expected_act).max() <= 2e-2
     e.close()
+
+
+def test_mamba_c3_fp32_split_tensor_path_matches_cuda_cores(tmp_path):
+    """fp32 Mamba projections on the tensor cores (fp16 hi/lo split, from 128
+    tokens) against the same engine's CUDA-core fp32 path (below 128 tokens),
+    fp32 tolerance 1e-3."""
+    tensors = _mamba_flow_c3(6)
+    path = tmp_path / "mamba_c3_split.safetensors"
+    ck.write_checkpoint(path, tensors)
+    rng = np.random.default_rng(6)
+    tokens = rng.integers(0, 128, size=(3, 64)).astype(np.int32)
+    e = Engine(path, threads=0, device=0, precision="fp32", max_batch=3)
+    batched = e.run_batch(tokens)  # 192 tokens: tensor-core split path
+    single = np.stack([e.run(tokens[i]) for i in range(3)])  # 64 tokens: CUDA cores
+    err = float(np.abs(batched - single).max())
+    print(f"C3 Mamba fp32 split tensor path vs CUDA cores max-abs {err:.3g}")
+    assert err <= 1e-3
+    e.close()
