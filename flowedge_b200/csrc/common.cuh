@@ -12,6 +12,33 @@
 namespace feb {
 
 // ---------------------------------------------------------------------------
+// Programmatic dependent launch.  A kernel launched by launch_pdl may start
+// while the kernel before it in the stream is still running; it calls
+// griddep_wait() before it reads anything an earlier kernel wrote (the wait
+// returns once the previous grid completed and its writes are visible; it is a
+// no-op for a normal launch).  griddep_launch() lets the next kernel start.
+// Every thread of a PDL kernel passes griddep_wait() before it exits, so the
+// previous grid's completion carries over to the kernels after this one.
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                              Args... args) {
+  cudaLaunchAttribute attr{};
+  attr.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr.val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cfg.attrs = &attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+}
+
+// ---------------------------------------------------------------------------
 // error flags written by device code (never a trap): the host reads them after
 // the launch and turns them into FE_STATUS_RESOURCE_EXHAUSTED.
 enum DeviceError : int {

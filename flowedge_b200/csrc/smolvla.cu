@@ -121,6 +121,8 @@ __device__ __forceinline__ float4 bf16x4_to_f4(uint2 u) {
 }
 __global__ void rms_kernel(float* __restrict__ h, int ld_h, const bf16* __restrict__ proj, int ld_p,
                            const float* __restrict__ w, int W, long long rows, int out_mode, void* out, int ld_out) {
+  griddep_wait();
+  griddep_launch();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const long long r = blockIdx.x * static_cast<long long>(blockDim.x >> 5) + warp;
   if (r >= rows) return;
@@ -196,6 +198,8 @@ __global__ void rms_kernel(float* __restrict__ h, int ld_h, const bf16* __restri
 // input and the step counter.
 __global__ void euler_kernel(const float* v, int ld_v, float* x, int A, long long rows, int steps, __half* x2,
                              int ld2, const int* step_idx, int* step_out) {
+  griddep_wait();
+  griddep_launch();
   const float dt = -1.0f / static_cast<float>(steps);
   const long long total = rows * A;
   for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
@@ -337,6 +341,8 @@ constexpr int kStageBatch = 4;  // independent 8-byte loads in flight per thread
 // gridDim.z slices the tasks so that small batches still fill the GPU.
 template <int G>
 __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const AttnParams p) {
+  griddep_wait();
+  griddep_launch();
   extern __shared__ __align__(16) uint8_t smem[];
   bf16* Ks = reinterpret_cast<bf16*>(smem);                  // [S_pad][kKRow]
   bf16* Vs = Ks + static_cast<long long>(p.S_pad) * kKRow;  // [S_pad][kKRow]
@@ -639,6 +645,8 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const AttnParam
 // bf16 probabilities times V).
 template <int G>
 __global__ void __launch_bounds__(kAttnThreads) attention_rows_kernel(const AttnParams p) {
+  griddep_wait();
+  griddep_launch();
   extern __shared__ __align__(16) uint8_t smem[];
   bf16* Ks = reinterpret_cast<bf16*>(smem);                  // [S_pad][kKRow]
   bf16* Vs = Ks + static_cast<long long>(p.S_pad) * kKRow;  // [S_pad][kKRow]
@@ -918,6 +926,22 @@ __global__ void __launch_bounds__(128) small_gemm_kernel(const SmallGemm g) {
   const int kn = min(kSmallK, g.kp - k0);  // multiple of 16
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int g4 = lane >> 2, t4 = lane & 3;
+  // this warp's weight fragments (K steps warp * 16 and warp * 16 + 64) do not
+  // depend on the previous kernel: loaded before the dependency wait
+  const uint16_t* wrow0 = static_cast<const uint16_t*>(g.w) + static_cast<long long>(mb * 16 + g4) * g.ld_w + k0;
+  const uint16_t* wrow1 = wrow0 + 8LL * g.ld_w;
+  uint32_t a[kSmallK / 64][4];
+#pragma unroll
+  for (int j = 0; j < kSmallK / 64; ++j) {
+    const int kk = warp * 16 + 64 * j;
+    const bool in = kk < kn;
+    a[j][0] = in ? __ldg(reinterpret_cast<const uint32_t*>(wrow0 + kk + 2 * t4)) : 0u;
+    a[j][1] = in ? __ldg(reinterpret_cast<const uint32_t*>(wrow1 + kk + 2 * t4)) : 0u;
+    a[j][2] = in ? __ldg(reinterpret_cast<const uint32_t*>(wrow0 + kk + 2 * t4 + 8)) : 0u;
+    a[j][3] = in ? __ldg(reinterpret_cast<const uint32_t*>(wrow1 + kk + 2 * t4 + 8)) : 0u;
+  }
+  griddep_wait();
+  griddep_launch();
   // stage x[rows][k0 .. k0 + kn) (both planes when split); rows >= g.rows are zero
   const int nq = kn / 8;  // 16-byte groups per row and plane
   for (int i = tid; i < (SPLIT ? 2 : 1) * kSmallRows * nq; i += 128) {
@@ -939,14 +963,11 @@ __global__ void __launch_bounds__(128) small_gemm_kernel(const SmallGemm g) {
     for (int n = 0; n < kSmallRows / 8; ++n)
 #pragma unroll
       for (int e = 0; e < 4; ++e) acc[pl][n][e] = 0.0f;
-  const uint16_t* wrow0 = static_cast<const uint16_t*>(g.w) + static_cast<long long>(mb * 16 + g4) * g.ld_w + k0;
-  const uint16_t* wrow1 = wrow0 + 8LL * g.ld_w;
-  for (int kk = warp * 16; kk < kn; kk += 64) {
-    uint32_t a[4];
-    a[0] = __ldg(reinterpret_cast<const uint32_t*>(wrow0 + kk + 2 * t4));
-    a[1] = __ldg(reinterpret_cast<const uint32_t*>(wrow1 + kk + 2 * t4));
-    a[2] = __ldg(reinterpret_cast<const uint32_t*>(wrow0 + kk + 2 * t4 + 8));
-    a[3] = __ldg(reinterpret_cast<const uint32_t*>(wrow1 + kk + 2 * t4 + 8));
+#pragma unroll
+  for (int j = 0; j < kSmallK / 64; ++j) {
+    const int kk = warp * 16 + 64 * j;
+    if (kk >= kn) break;
+    const uint32_t (&a_)[4] = a[j];
 #pragma unroll
     for (int n = 0; n < kSmallRows / 8; ++n) {
       if (n < nt) {
@@ -959,9 +980,9 @@ __global__ void __launch_bounds__(128) small_gemm_kernel(const SmallGemm g) {
             asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
                 "{%0,%1,%2,%3};"
                 : "+f"(acc[pl][n][0]), "+f"(acc[pl][n][1]), "+f"(acc[pl][n][2]), "+f"(acc[pl][n][3])
-                : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+                : "r"(a_[0]), "r"(a_[1]), "r"(a_[2]), "r"(a_[3]), "r"(b0), "r"(b1));
           } else {
-            mma_bf16_16816(acc[pl][n], a, b0, b1);
+            mma_bf16_16816(acc[pl][n], a_, b0, b1);
           }
         }
       }
@@ -1007,6 +1028,8 @@ struct SmallEpilogue {
 // y = sum of the K slices in slice order + bias + add_vec, then the act and
 // the store of the tcgen05 epilogue (SwiGLU: rows 2f / 2f + 1 are gate / up)
 __global__ void small_epilogue_kernel(const SmallEpilogue e) {
+  griddep_wait();
+  griddep_launch();
   const bool swiglu = e.act == tc::kActSwiGLU;
   const int cols = swiglu ? e.m_valid / 2 : e.m_valid;
   const long long total = static_cast<long long>(e.rows) * cols;
@@ -1519,8 +1542,8 @@ bool SmolVLA::gemm(const Mat& m, const void* src, long long rows, void* out, int
     g.m_pad = pad(m.rows, 16);
     const int nks = (m.kp + kSmallK - 1) / kSmallK;
     const dim3 grid(static_cast<unsigned>(g.m_pad / 16), static_cast<unsigned>(nks));
-    if (m.split) small_gemm_kernel<true><<<grid, 128, 0, st>>>(g);
-    else small_gemm_kernel<false><<<grid, 128, 0, st>>>(g);
+    if (m.split) launch_pdl(small_gemm_kernel<true>, grid, dim3(128), 0, st, g);
+    else launch_pdl(small_gemm_kernel<false>, grid, dim3(128), 0, st, g);
     SmallEpilogue e{};
     e.partial = small_part_;
     e.nks = nks;
@@ -1536,7 +1559,7 @@ bool SmolVLA::gemm(const Mat& m, const void* src, long long rows, void* out, int
     e.lo_off = lo_off;
     e.ch_off = out_ch_off;
     const long long cols = act == tc::kActSwiGLU ? m.rows / 2 : m.rows;
-    small_epilogue_kernel<<<ew_grid(rows * cols, 256, *ctx_), 256, 0, st>>>(e);
+    launch_pdl(small_epilogue_kernel, dim3(ew_grid(rows * cols, 256, *ctx_)), dim3(256), 0, st, e);
     launches_ += 2;
     return cudaGetLastError() == cudaSuccess;
   }
@@ -1688,8 +1711,8 @@ bool SmolVLA::attention(const Layer& Ly, std::size_t li, std::size_t batch, std:
     // enough (sample, head) CTAs to fill the GPU: warps own whole tasks
     const dim3 grid(static_cast<unsigned>(batch), static_cast<unsigned>(cfg_.kv_heads));
     const std::size_t rsmem = attn_rows_smem(p.S_pad, G);
-    if (G == 3) attention_rows_kernel<3><<<grid, kAttnThreads, rsmem, st>>>(p);
-    else attention_rows_kernel<1><<<grid, kAttnThreads, rsmem, st>>>(p);
+    if (G == 3) launch_pdl(attention_rows_kernel<3>, grid, dim3(kAttnThreads), rsmem, st, p);
+    else launch_pdl(attention_rows_kernel<1>, grid, dim3(kAttnThreads), rsmem, st, p);
     ++launches_;
     if (cudaGetLastError() != cudaSuccess) {
       err = "SmolVLA attention launch failed";
@@ -1704,8 +1727,8 @@ bool SmolVLA::attention(const Layer& Ly, std::size_t li, std::size_t batch, std:
   const int tasks = (p.heads / p.kv_heads / G) * (p.chunk_pad / 16);
   const int slices = static_cast<long long>(batch) * p.kv_heads < 2LL * ctx_->sm_count ? tasks : 1;
   const dim3 grid(static_cast<unsigned>(batch), static_cast<unsigned>(cfg_.kv_heads), static_cast<unsigned>(slices));
-  if (G == 3) attention_kernel<3><<<grid, kAttnThreads, smem, st>>>(p);
-  else attention_kernel<1><<<grid, kAttnThreads, smem, st>>>(p);
+  if (G == 3) launch_pdl(attention_kernel<3>, grid, dim3(kAttnThreads), smem, st, p);
+  else launch_pdl(attention_kernel<1>, grid, dim3(kAttnThreads), smem, st, p);
   ++launches_;
   if (cudaGetLastError() != cudaSuccess) {
     err = "SmolVLA attention launch failed";
@@ -1721,12 +1744,12 @@ bool SmolVLA::record_layers(std::size_t batch, std::size_t chunk, bool shared, i
   const bf16* pending = nullptr;  // residual projection not yet added to h
   for (std::size_t li = 0; li < layers_.size(); ++li) {
     const Layer& L = layers_[li];
-    rms_kernel<<<rgrid, 256, 0, st>>>(h_, Wp_, pending, Wp_, L.in_norm, W_, rows, 0, nb_, Wp_);
+    launch_pdl(rms_kernel, dim3(rgrid), dim3(256), 0, st, h_, Wp_, pending, Wp_, L.in_norm, W_, rows, 0, nb_, Wp_);
     ++launches_;
     if (!gemm(L.qkv, nb_, rows, qkv_, qkv_ld_, false, 0, nullptr, nullptr, tc::kActNone, st, err)) return false;
     if (!attention(L, li, batch, chunk, shared, st, err)) return false;
     if (!gemm(L.o, att_, rows, proj_, Wp_, false, 0, nullptr, nullptr, tc::kActNone, st, err)) return false;
-    rms_kernel<<<rgrid, 256, 0, st>>>(h_, Wp_, proj_, Wp_, L.post_norm, W_, rows, 0, nb_, Wp_);
+    launch_pdl(rms_kernel, dim3(rgrid), dim3(256), 0, st, h_, Wp_, proj_, Wp_, L.post_norm, W_, rows, 0, nb_, Wp_);
     ++launches_;
     // act = bf16(bf16(up) * SiLU(bf16(gate))) straight from the GEMM epilogue
     // (gate_silu, kernels_scalar.cc:61-67, smolvla_action_expert.cc:366-372)
@@ -1735,9 +1758,9 @@ bool SmolVLA::record_layers(std::size_t batch, std::size_t chunk, bool shared, i
     pending = proj_;
   }
   if (final_mode == 1)
-    rms_kernel<<<rgrid, 256, 0, st>>>(h_, Wp_, pending, Wp_, final_norm_, W_, rows, 1, fin2_, Wp_);
+    launch_pdl(rms_kernel, dim3(rgrid), dim3(256), 0, st, h_, Wp_, pending, Wp_, final_norm_, W_, rows, 1, fin2_, Wp_);
   else
-    rms_kernel<<<rgrid, 256, 0, st>>>(h_, Wp_, pending, Wp_, final_norm_, W_, rows, 2, io_, W_);
+    launch_pdl(rms_kernel, dim3(rgrid), dim3(256), 0, st, h_, Wp_, pending, Wp_, final_norm_, W_, rows, 2, io_, W_);
   ++launches_;
   return cudaGetLastError() == cudaSuccess;
 }
@@ -1748,8 +1771,8 @@ bool SmolVLA::record_step(std::size_t batch, std::size_t chunk, std::size_t step
   if (!record_embed(rows, nullptr, static_cast<int>(steps), st, err)) return false;
   if (!record_layers(batch, chunk, shared, 1, st, err)) return false;
   if (!gemm(out_, fin2_, rows, v_, Ap_, true, 0, b_out_, nullptr, tc::kActNone, st, err)) return false;
-  euler_kernel<<<ew_grid(rows * A_, 256, *ctx_), 256, 0, st>>>(v_, Ap_, x_, A_, rows, static_cast<int>(steps), x2_,
-                                                                Ap_, step_, step_ + 1);
+  launch_pdl(euler_kernel, dim3(ew_grid(rows * A_, 256, *ctx_)), dim3(256), 0, st, v_, Ap_, x_, A_, rows,
+             static_cast<int>(steps), x2_, Ap_, step_, step_ + 1);
   ++launches_;
   // step_[0] <- step_[1] for the next replay
   cudaMemcpyAsync(step_, step_ + 1, sizeof(int), cudaMemcpyDeviceToDevice, st);
