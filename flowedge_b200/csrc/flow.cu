@@ -945,10 +945,10 @@ int Flow::sample_device(const float* condition, const float* x0, std::size_t bat
 // ---------------------------------------------------------------------------
 // Allocation-free flow solve (fe_engine_sample_condition_static).
 //
-// Some callers cannot call cudaMalloc when they sample: a host application
-// that captures its control step into its own CUDA graph (allocation is not
-// permitted while a stream is being captured), or a real-time loop whose
-// device memory is pre-budgeted by another runtime.  The resident-engine
+// Some callers cannot call cudaMalloc when they sample: a fixed-period
+// control loop, where cudaMalloc may block and synchronise the device and so
+// miss the period, or a host process whose device memory another runtime's
+// pool allocator claimed at start-up.  The resident-engine
 // entry points grow the engine's workspace with cudaMalloc when a batch
 // exceeds the reserved capacity; this variant never allocates: its scratch
 // (solver state, stage slopes, hidden activations, split-K partial sums) is

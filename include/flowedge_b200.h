@@ -309,9 +309,9 @@ int fe_engine_sample_condition_device(fe_engine* engine, const float* condition,
                                       size_t steps, int method, float* action, void* stream);
 /* Allocation-free variant of fe_engine_sample_condition_device (no
  * counterpart in the reference ABI).  For callers that cannot call cudaMalloc
- * while they sample - a host application capturing its control step into its
- * own CUDA graph, or a loop whose device memory another runtime pre-budgets -
- * it runs the flow ODE solve on caller device buffers (condition [batch][C],
+ * while they sample - a fixed-period control loop, where cudaMalloc may block
+ * and synchronise the device, or a host process whose device memory another
+ * runtime's pool allocator claimed at start-up - it runs the flow ODE solve on caller device buffers (condition [batch][C],
  * noise / action [batch][A], enqueued on `stream`) with its scratch in a
  * fixed 4 MiB static device array that every GPU loading the library holds
  * until exit, never touching the engine's reserved workspace.  Requests whose

@@ -1,8 +1,9 @@
 """The allocation-free flow entry point (fe_engine_sample_condition_static).
 
-It exists for callers that cannot call cudaMalloc while they sample (a host
-application capturing its control step into its own CUDA graph, or a loop
-whose device memory another runtime pre-budgets): its scratch is a fixed
+It exists for callers that cannot call cudaMalloc while they sample (a
+fixed-period control loop, where cudaMalloc may block and synchronise the
+device, or a host process whose device memory another runtime's pool
+allocator claimed at start-up): its scratch is a fixed
 static device array instead of the engine's workspace.  This file checks,
 through the C ABI, that two calls in a row match the existing device entry
 point (fe_engine_sample_condition_device) within the flow tolerance of the
