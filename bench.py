@@ -41,6 +41,14 @@ UNIT = "chunks/s"
 GLOBAL_BATCH = int(os.environ.get("FLOWEDGE_BENCH_BATCH", "4096"))
 STEPS = 10
 SEED = 0
+# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of the 36 conv
+# GEMM launches of one denoising forward, per shard size, from one ncu capture
+# of this script's first forward:
+#   FLOWEDGE_BENCH_BATCH=<shard> ncu --metrics gpu__time_duration.sum,dram__bytes_read.sum,dram__bytes_write.sum
+#       --clock-control none -k regex:tc_gemm -c 80 --csv --log-file traffic.csv
+#       python bench.py --steps 1 --warmup 1 --no-cpu-baseline --no-extras
+# (launches 1-36 after the FiLM-condition GEMM).  Other shard sizes report null.
+CONV_TRAFFIC_PER_FORWARD = {4096: 35.45e9, 1024: 7.26e9}
 
 
 def _dist():
@@ -326,7 +334,9 @@ def run_ours(args):
             "device_mallocs_in_timed_region": int(mallocs),
             "roofline": {"bound": "tensor", "kernel": "tc_gemm_kernel (conv GEMMs of one denoise)",
                          "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
-                         "peak_kind": peak_kind, "traffic": None,
+                         "peak_kind": peak_kind, "traffic": CONV_TRAFFIC_PER_FORWARD.get(shard),
+                         "traffic_unit": "DRAM bytes per forward (the 36 conv launches achieved is taken over), "
+                                         "from an ncu capture at this shard size",
                          "conv_share_of_forward": prof["conv_ms"] / prof["forward_ms"],
                          "conv_launches_per_forward": prof["conv_launches"]},
         }

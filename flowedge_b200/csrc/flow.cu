@@ -57,6 +57,8 @@ __device__ __forceinline__ float stage_time(int step, int steps, int method, int
 constexpr int kTimeProjRowsPerBlock = 8;
 __global__ void time_proj_kernel(const int* step_idx, int steps, int method, int stage, const float* freqs, int half,
                                  const float* wt, int H, float* tp) {
+  griddep_wait();
+  griddep_launch();
   extern __shared__ float sinu[];
   const float t = stage_time(*step_idx, steps, method, stage);
   for (int j = threadIdx.x; j < half; j += blockDim.x) {
@@ -93,13 +95,23 @@ struct OdeParams {
 };
 
 __global__ void ode_stage_kernel(const OdeParams p) {
+  griddep_wait();
+  griddep_launch();
   const float dt = 1.0f / static_cast<float>(p.steps);
   const long long total = static_cast<long long>(p.B) * p.A;
   const int last = p.method == 0 ? 0 : (p.method == 1 ? 1 : 3);
+  const bool narrow = total < (1LL << 31);  // 32-bit index division (uniform branch)
   for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
        i += static_cast<long long>(gridDim.x) * blockDim.x) {
-    const int b = static_cast<int>(i / p.A);
-    const int a = static_cast<int>(i - static_cast<long long>(b) * p.A);
+    int b, a;
+    if (narrow) {
+      const int ii = static_cast<int>(i);
+      b = ii / p.A;
+      a = ii - b * p.A;
+    } else {
+      b = static_cast<int>(i / p.A);
+      a = static_cast<int>(i - static_cast<long long>(b) * p.A);
+    }
     const long long o = static_cast<long long>(b) * p.ld + a;
     float nxt;
     if (p.method == 0) {
@@ -683,8 +695,16 @@ bool Flow::record_step(std::size_t batch, int method, bool tc, cudaStream_t st, 
   const int half = static_cast<int>(cfg_.time_dim / 2);
   const int stages = method == 0 ? 1 : (method == 1 ? 2 : 4);
   for (int s = 0; s < stages; ++s) {
-    time_proj_kernel<<<(H + kTimeProjRowsPerBlock - 1) / kTimeProjRowsPerBlock, 32 * kTimeProjRowsPerBlock, static_cast<std::size_t>(2 * half) * 4, st>>>(
-        step_, static_cast<int>(steps_), method, s, freqs_, half, wt_, H, tp_);
+    // later stages follow ode_stage_kernel: a programmatic dependent launch
+    // (the first stage follows the step-index copy, a plain dependency)
+    const dim3 tgrid((H + kTimeProjRowsPerBlock - 1) / kTimeProjRowsPerBlock), tblock(32 * kTimeProjRowsPerBlock);
+    const std::size_t tsmem = static_cast<std::size_t>(2 * half) * 4;
+    if (s > 0)
+      launch_pdl(time_proj_kernel, tgrid, tblock, tsmem, st, static_cast<const int*>(step_), static_cast<int>(steps_),
+                 method, s, static_cast<const float*>(freqs_), half, static_cast<const float*>(wt_), H, tp_);
+    else
+      time_proj_kernel<<<tgrid, tblock, tsmem, st>>>(step_, static_cast<int>(steps_), method, s, freqs_, half, wt_, H,
+                                                     tp_);
     // h = SiLU(W_in x + tp + c_emb)
     void* hin = h0_;
     void* hout = h1_;
@@ -713,7 +733,7 @@ bool Flow::record_step(std::size_t batch, int method, bool tc, cudaStream_t st, 
     p.next_in = xin_;
     p.ld_in = a_pad_;
     p.next_mode = in_mode(tc);
-    ode_stage_kernel<<<ew_grid(static_cast<long long>(batch) * A, 256, *ctx_), 256, 0, st>>>(p);
+    launch_pdl(ode_stage_kernel, dim3(ew_grid(static_cast<long long>(batch) * A, 256, *ctx_)), dim3(256), 0, st, p);
   }
   // step_[0] <- step_[1] (next step index) for the next replay
   cudaMemcpyAsync(step_, step_ + 1, sizeof(int), cudaMemcpyDeviceToDevice, st);

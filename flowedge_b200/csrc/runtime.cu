@@ -362,32 +362,37 @@ cudaError_t tc_gemm(const TcLaunch& l, DeviceContext& ctx, cudaStream_t stream, 
     if (!encode_3d(&tb[i], s, static_cast<std::uint32_t>(l.L), static_cast<std::uint32_t>(p.tile_samples), dtype, err))
       return cudaErrorInvalidValue;
   }
+  // Launched as a programmatic dependent of the previous kernel in the stream
+  // (the kernel waits for that grid before its first global access).
+  cudaLaunchAttribute attrs[2]{};
+  attrs[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attrs[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg{};
+  cfg.blockDim = dim3(tc::THREADS);
+  cfg.dynamicSmemBytes = tc::SMEM_BYTES;
+  cfg.stream = stream;
+  cfg.attrs = attrs;
+  cfg.numAttrs = 1;
   if (p.gn_fuse && l.group_ch == 2 * tc::BM) {
-    cudaLaunchAttribute attr{};
-    attr.id = cudaLaunchAttributeClusterDimension;
-    attr.val.clusterDim.x = 2;
-    attr.val.clusterDim.y = 1;
-    attr.val.clusterDim.z = 1;
-    cudaLaunchConfig_t cfg{};
+    attrs[1].id = cudaLaunchAttributeClusterDimension;
+    attrs[1].val.clusterDim.x = 2;
+    attrs[1].val.clusterDim.y = 1;
+    attrs[1].val.clusterDim.z = 1;
+    cfg.numAttrs = 2;
     cfg.gridDim = dim3(static_cast<unsigned>(2 * std::min(p.total_tiles / 2, ctx.pair_clusters)));
-    cfg.blockDim = dim3(tc::THREADS);
-    cfg.dynamicSmemBytes = tc::SMEM_BYTES;
-    cfg.stream = stream;
-    cfg.attrs = &attr;
-    cfg.numAttrs = 1;
     const cudaError_t rc =
         cudaLaunchKernelEx(&cfg, tc::tc_gemm_kernel<tc::kEpiFused, true>, ta, tb[0], tb[1], tb[2], p);
     if (rc != cudaSuccess) err = std::string("tc_gemm cluster launch: ") + cudaGetErrorString(rc);
     return rc;
   }
-  const int grid = p.total_tiles < ctx.sm_count ? p.total_tiles : ctx.sm_count;
+  cfg.gridDim = dim3(static_cast<unsigned>(p.total_tiles < ctx.sm_count ? p.total_tiles : ctx.sm_count));
+  cudaError_t rc;
   if (p.gn_fuse)
-    tc::tc_gemm_kernel<tc::kEpiFused><<<grid, tc::THREADS, tc::SMEM_BYTES, stream>>>(ta, tb[0], tb[1], tb[2], p);
+    rc = cudaLaunchKernelEx(&cfg, tc::tc_gemm_kernel<tc::kEpiFused>, ta, tb[0], tb[1], tb[2], p);
   else if (p.stats != nullptr)
-    tc::tc_gemm_kernel<tc::kEpiStats><<<grid, tc::THREADS, tc::SMEM_BYTES, stream>>>(ta, tb[0], tb[1], tb[2], p);
+    rc = cudaLaunchKernelEx(&cfg, tc::tc_gemm_kernel<tc::kEpiStats>, ta, tb[0], tb[1], tb[2], p);
   else
-    tc::tc_gemm_kernel<tc::kEpiPlain><<<grid, tc::THREADS, tc::SMEM_BYTES, stream>>>(ta, tb[0], tb[1], tb[2], p);
-  const cudaError_t rc = cudaGetLastError();
+    rc = cudaLaunchKernelEx(&cfg, tc::tc_gemm_kernel<tc::kEpiPlain>, ta, tb[0], tb[1], tb[2], p);
   if (rc != cudaSuccess) err = std::string("tc_gemm launch: ") + cudaGetErrorString(rc);
   return rc;
 }

@@ -552,69 +552,129 @@ __device__ __noinline__ void run_conv(const ConvOp& op_in, uint8_t* smem, uint64
 // ---------------------------------------------------------------------------
 // GroupNorm + Mish (+ FiLM or residual): one CTA per (sample, group)
 
-// y at up to E (token, channel) points at once: every segment of every point
-// is requested before any is added (static bound kMaxSeg).  Same summation
-// order as y_at (bias, then segments in order).
-template <int E>
-__device__ __forceinline__ void y_gather(const YSrc& y, const int (&n)[E], const int (&m)[E], const bool (&ok)[E],
-                                         float (&v)[E]) {
-  const long long stride = static_cast<long long>(y.T) * 16;
-  float t[E][kMaxSeg];
-  int nseg[E];
-#pragma unroll
-  for (int e = 0; e < E; ++e) {
-    v[e] = 0.0f;
-    nseg[e] = 0;
-    const float* p = y.P;
-    if (ok[e]) {
-      const int rb = m[e] >> 4;
-      nseg[e] = __ldg(y.nseg + rb);
-      if (y.bias != nullptr) v[e] = __ldg(y.bias + m[e]);
-      p = y.P + ((static_cast<long long>(rb) * y.seg_max) * y.T + n[e]) * 16 + (m[e] & 15);
-    }
-#pragma unroll
-    for (int s = 0; s < kMaxSeg; ++s) t[e][s] = s < nseg[e] ? __ldcg(p + s * stride) : 0.0f;
-  }
-#pragma unroll
-  for (int e = 0; e < E; ++e)
-#pragma unroll
-    for (int s = 0; s < kMaxSeg; ++s)
-      if (s < nseg[e]) v[e] += t[e][s];
+// The head of a conv output point (token n, channel m): its segment count,
+// its bias (the start of the sum) and the address of its first segment.
+__device__ __forceinline__ void y_head(const YSrc& y, int n, int m, int& nseg, float& v, const float*& p) {
+  const int rb = m >> 4;
+  nseg = __ldg(y.nseg + rb);
+  v = y.bias != nullptr ? __ldg(y.bias + m) : 0.0f;
+  p = y.P + ((static_cast<long long>(rb) * y.seg_max) * y.T + n) * 16 + (m & 15);
 }
 
-__device__ __noinline__ void run_gn(const GnOp& op, int step, const int* step_t) {
+// Each CTA takes whole (sample, group) items; E elements of the group per
+// thread (E * kThreads >= channels per group * L).  With two elements per
+// thread the loads go out in two dependent rounds: first everything that
+// depends on nothing else (segment counts and biases of the conv output and of
+// a conv residual, the affine and FiLM terms, an fp32 residual), then every
+// segment of both conv outputs.  With four, the values in flight would not fit
+// the registers, so the residual and the affine / FiLM terms follow in later
+// rounds.  Sums keep y_at's order: bias, then the segments in order.
+template <int E>
+__device__ __forceinline__ void run_gn_items(const GnOp& op, int step, const int* step_t) {
+  constexpr bool kEarly = E <= 2;  // residual, affine and FiLM loads in the first round
   __shared__ double red[2][kWarps];
   __shared__ float stat[2];
   const int NC = gridDim.x;
   const int cpg = op.C / op.groups;
   const int cnt = cpg * op.L;
   const int items = op.samples * op.groups;
+  const bool res_conv = op.res_mode == 1;
   const float* ft = op.film ? op.film_time + static_cast<long long>(step_t[step]) * op.film_F + op.film_off : nullptr;
+  const long long sy = static_cast<long long>(op.y.T) * 16;
+  const long long sr = static_cast<long long>(op.res.T) * 16;
   for (int item = blockIdx.x; item < items; item += NC) {
     const int b = item / op.groups;
     const int gi = item - b * op.groups;
-    int n[kGnPerThread], c[kGnPerThread];
-    bool ok[kGnPerThread];
+    const float* fc = op.film ? op.film_cond + static_cast<long long>(b) * op.film_F + op.film_off : nullptr;
+    int n[E], c[E];
+    bool ok[E];
 #pragma unroll
-    for (int e = 0; e < kGnPerThread; ++e) {
+    for (int e = 0; e < E; ++e) {
       const int i = threadIdx.x + e * kThreads;
       ok[e] = i < cnt;
       const int t = ok[e] ? i / cpg : 0;
       c[e] = ok[e] ? gi * cpg + (i - t * cpg) : 0;
       n[e] = b * op.L + t;
     }
-    float v[kGnPerThread], r[kGnPerThread];
-    y_gather<kGnPerThread>(op.y, n, c, ok, v);
-    if (op.res_mode == 1) {
-      y_gather<kGnPerThread>(op.res, n, c, ok, r);
-    } else {
+    // the residual (conv output or fp32 tensor): heads or values
+    auto res_heads = [&](int (&nr)[E], float (&r)[E], const float* (&pr)[E]) {
 #pragma unroll
-      for (int e = 0; e < kGnPerThread; ++e)
-        r[e] = (op.res_mode == 2 && ok[e]) ? __ldcg(op.res_tensor + static_cast<long long>(n[e]) * op.C + c[e]) : 0.0f;
+      for (int e = 0; e < E; ++e) {
+        nr[e] = 0;
+        r[e] = 0.0f;
+        pr[e] = op.res.P;
+        if (ok[e]) {
+          if (res_conv) y_head(op.res, n[e], c[e], nr[e], r[e], pr[e]);
+          else if (op.res_mode == 2) r[e] = __ldcg(op.res_tensor + static_cast<long long>(n[e]) * op.C + c[e]);
+        }
+      }
+    };
+    // gamma, beta and the FiLM scale / shift (condition row + time row)
+    auto affine = [&](int e, float& ga, float& be, float& fs, float& fh) {
+      ga = __ldg(op.gamma + c[e]);
+      be = __ldg(op.beta + c[e]);
+      fs = fh = 0.0f;
+      if (op.film) {
+        fs = __ldcg(fc + c[e]) + __ldg(ft + c[e]);
+        fh = __ldcg(fc + op.C + c[e]) + __ldg(ft + op.C + c[e]);
+      }
+    };
+    int ny[E], nr[E];
+    const float* py[E];
+    const float* pr[E];
+    float v[E], r[E], ga[E], be[E], fs[E], fh[E];
+#pragma unroll
+    for (int e = 0; e < E; ++e) {
+      ny[e] = 0;
+      v[e] = 0.0f;
+      py[e] = op.y.P;
+      if (ok[e]) y_head(op.y, n[e], c[e], ny[e], v[e], py[e]);
+    }
+    if constexpr (kEarly) {
+      res_heads(nr, r, pr);
+#pragma unroll
+      for (int e = 0; e < E; ++e)
+        if (ok[e]) affine(e, ga[e], be[e], fs[e], fh[e]);
+      float ty[E][kMaxSeg], tr[E][kMaxSeg];
+#pragma unroll
+      for (int e = 0; e < E; ++e)
+#pragma unroll
+        for (int s = 0; s < kMaxSeg; ++s) {
+          ty[e][s] = s < ny[e] ? __ldcg(py[e] + s * sy) : 0.0f;
+          tr[e][s] = s < nr[e] ? __ldcg(pr[e] + s * sr) : 0.0f;
+        }
+#pragma unroll
+      for (int e = 0; e < E; ++e)
+#pragma unroll
+        for (int s = 0; s < kMaxSeg; ++s) {
+          if (s < ny[e]) v[e] += ty[e][s];
+          if (s < nr[e]) r[e] += tr[e][s];
+        }
+    } else {
+      float t[E][kMaxSeg];
+#pragma unroll
+      for (int e = 0; e < E; ++e)
+#pragma unroll
+        for (int s = 0; s < kMaxSeg; ++s) t[e][s] = s < ny[e] ? __ldcg(py[e] + s * sy) : 0.0f;
+#pragma unroll
+      for (int e = 0; e < E; ++e)
+#pragma unroll
+        for (int s = 0; s < kMaxSeg; ++s)
+          if (s < ny[e]) v[e] += t[e][s];
+      res_heads(nr, r, pr);
+#pragma unroll
+      for (int e = 0; e < E; ++e)
+#pragma unroll
+        for (int s = 0; s < kMaxSeg; ++s) t[e][s] = s < nr[e] ? __ldcg(pr[e] + s * sr) : 0.0f;
+#pragma unroll
+      for (int e = 0; e < E; ++e)
+#pragma unroll
+        for (int s = 0; s < kMaxSeg; ++s)
+          if (s < nr[e]) r[e] += t[e][s];
     }
     double s1 = 0.0, s2 = 0.0;
 #pragma unroll
-    for (int e = 0; e < kGnPerThread; ++e)
+    for (int e = 0; e < E; ++e)
       if (ok[e]) {
         s1 += v[e];
         s2 += static_cast<double>(v[e]) * v[e];
@@ -645,19 +705,25 @@ __device__ __noinline__ void run_gn(const GnOp& op, int step, const int* step_t)
     __syncthreads();
     const float mean = stat[0], inv = stat[1];
 #pragma unroll
-    for (int e = 0; e < kGnPerThread; ++e) {
+    for (int e = 0; e < E; ++e) {
       if (ok[e]) {
-        float z = (v[e] - mean) * (inv * __ldg(op.gamma + c[e])) + __ldg(op.beta + c[e]);
+        if constexpr (!kEarly) affine(e, ga[e], be[e], fs[e], fh[e]);
+        float z = (v[e] - mean) * (inv * ga[e]) + be[e];
         z = mish_f(z);
-        if (op.film) {
-          const float* fc = op.film_cond + static_cast<long long>(b) * op.film_F + op.film_off;
-          z = (__ldcg(fc + c[e]) + __ldg(ft + c[e])) * z + (__ldcg(fc + op.C + c[e]) + __ldg(ft + op.C + c[e]));
-        }
+        if (op.film) z = fs[e] * z + fh[e];
         op.out[static_cast<long long>(n[e]) * op.C + c[e]] = z + r[e];
       }
     }
     __syncthreads();
   }
+}
+
+// GroupNorm + Mish (+ FiLM or residual): two elements per thread when a group
+// holds at most 2 * kThreads of them (every PushT-shaped layer), else four.
+__device__ __noinline__ void run_gn(const GnOp& op, int step, const int* step_t) {
+  static_assert(kGnPerThread == 4, "run_gn instantiates 2 and 4 elements per thread");
+  if ((op.C / op.groups) * op.L <= 2 * kThreads) run_gn_items<2>(op, step, step_t);
+  else run_gn_items<4>(op, step, step_t);
 }
 
 __device__ void run_reduce(const ReduceOp& op) {

@@ -174,6 +174,14 @@ static __global__ void __launch_bounds__(THREADS, 1)
   const uint32_t tmem_base = *tmem_slot;
   // the other CTA's barriers are initialised before anyone arrives on them
   if constexpr (PAIR) cluster_sync_all();
+  // Programmatic dependent launch: the set-up above (barriers, tensor-map
+  // prefetch, TMEM allocation; no global memory) may overlap the previous
+  // kernel's tail.  Nothing below touches global memory before the previous
+  // grid has completed.  Only one CTA of this kernel fits an SM (shared
+  // memory), and no other kernel allocates TMEM, so the early allocation
+  // never waits on another grid.
+  griddep_wait();
+  griddep_launch();
 
   // Tile walk.  Plain: tiles blockIdx.x, +gridDim.x, ...  PAIR: tile pairs
   // (cluster index, +clusters, ...), of which this CTA takes row block
