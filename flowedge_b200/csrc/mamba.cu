@@ -187,11 +187,31 @@ __global__ void __launch_bounds__(256) scan_kernel(const float* dbl, int wd, con
                                                    int di, const float* dt_w, const float* dt_b, const float* a_neg,
                                                    const float* dsk, float* state, float* y, __half* y_bf,
                                                    int split) {
-  extern __shared__ float sdbl[];  // [L][wd]
+  static_assert(DR % 4 == 0 && DS % 4 == 0, "rows of [dt_in | B | C] are read as float4");
+  extern __shared__ __align__(16) float sdbl[];  // [L][wd], wd = DR + 2 DS
   const int b = blockIdx.y;
   const int c = blockIdx.x * blockDim.x + threadIdx.x;
-  const float* drow = dbl + static_cast<long long>(b) * L * wd;
-  for (int i = threadIdx.x; i < L * wd; i += blockDim.x) sdbl[i] = drow[i];
+  {
+    // the sequence's rows as 16-byte copies, eight loads in flight per thread
+    // (wd is a multiple of 4 and dbl 16-byte aligned)
+    const float4* src = reinterpret_cast<const float4*>(dbl + static_cast<long long>(b) * L * wd);
+    float4* dst = reinterpret_cast<float4*>(sdbl);
+    const int n4 = L * wd / 4;
+    constexpr int kBatch = 8;
+    for (int i0 = threadIdx.x; i0 < n4; i0 += kBatch * blockDim.x) {
+      float4 v[kBatch];
+#pragma unroll
+      for (int j = 0; j < kBatch; ++j) {
+        const int i = i0 + j * blockDim.x;
+        if (i < n4) v[j] = __ldg(src + i);
+      }
+#pragma unroll
+      for (int j = 0; j < kBatch; ++j) {
+        const int i = i0 + j * blockDim.x;
+        if (i < n4) dst[i] = v[j];
+      }
+    }
+  }
   __syncthreads();
   if (c >= di) return;
   float wdt[DR], an[DS], h[DS];
@@ -203,27 +223,59 @@ __global__ void __launch_bounds__(256) scan_kernel(const float* dbl, int wd, con
     h[n] = state != nullptr ? state[(static_cast<long long>(b) * DS + n) * di + c] : 0.0f;
   }
   const float bdt = dt_b[c], dk = dsk[c];
-  for (int t = 0; t < L; ++t) {
-    const float* row = sdbl + t * wd;
-    float acc = 0.0f;
+  // u and z of step t are requested kScanAhead steps earlier: the loop is
+  // unrolled by kScanAhead, so slot j holds the values of steps t = j mod
+  // kScanAhead and each load has kScanAhead steps of recurrence to complete
+  constexpr int kScanAhead = 4;
+  const long long tok0 = static_cast<long long>(b) * L;
+  float u_ahead[kScanAhead], z_ahead[kScanAhead];
 #pragma unroll
-    for (int r = 0; r < DR; ++r) acc += row[r] * wdt[r];
-    const float pre = acc + bdt;
-    const float dt = FAST ? fmaxf(pre, 0.0f) + __logf(1.0f + __expf(-fabsf(pre))) : softplus_f(pre);
-    const long long tok = static_cast<long long>(b) * L + t;
-    const float uv = u[tok * di + c];
-    float yv = dk * uv;
+  for (int j = 0; j < kScanAhead; ++j) {
+    u_ahead[j] = j < L ? u[(tok0 + j) * di + c] : 0.0f;
+    z_ahead[j] = j < L ? xz[(tok0 + j) * 2 * di + di + c] : 0.0f;
+  }
+  for (int t0 = 0; t0 < L; t0 += kScanAhead) {
 #pragma unroll
-    for (int n = 0; n < DS; ++n) {
-      const float da = FAST ? ex2_approx(dt * an[n]) : expf(dt * an[n]);
-      const float dbu = dt * row[DR + n] * uv;
-      h[n] = (da * h[n]) + dbu;
-      yv += h[n] * row[DR + DS + n];
+    for (int j = 0; j < kScanAhead; ++j) {
+      const int t = t0 + j;
+      if (t >= L) break;
+      const float uv = u_ahead[j], zv = z_ahead[j];
+      if (t + kScanAhead < L) {
+        u_ahead[j] = u[(tok0 + t + kScanAhead) * di + c];
+        z_ahead[j] = xz[(tok0 + t + kScanAhead) * 2 * di + di + c];
+      }
+      // the row as 16-byte shared-memory reads (same sums, same order)
+      const float4* row4 = reinterpret_cast<const float4*>(sdbl + t * wd);
+      float acc = 0.0f;
+#pragma unroll
+      for (int r = 0; r < DR / 4; ++r) {
+        const float4 v = row4[r];
+        acc += v.x * wdt[4 * r];
+        acc += v.y * wdt[4 * r + 1];
+        acc += v.z * wdt[4 * r + 2];
+        acc += v.w * wdt[4 * r + 3];
+      }
+      const float pre = acc + bdt;
+      const float dt = FAST ? fmaxf(pre, 0.0f) + __logf(1.0f + __expf(-fabsf(pre))) : softplus_f(pre);
+      const long long tok = tok0 + t;
+      float yv = dk * uv;
+#pragma unroll
+      for (int n4 = 0; n4 < DS / 4; ++n4) {
+        const float4 bq = row4[DR / 4 + n4], cq = row4[(DR + DS) / 4 + n4];
+        const float bn[4] = {bq.x, bq.y, bq.z, bq.w}, cn[4] = {cq.x, cq.y, cq.z, cq.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int n = 4 * n4 + i;
+          const float da = FAST ? ex2_approx(dt * an[n]) : expf(dt * an[n]);
+          const float dbu = dt * bn[i] * uv;
+          h[n] = (da * h[n]) + dbu;
+          yv += h[n] * cn[i];
+        }
+      }
+      const float out = yv * (FAST ? silu_fast(zv) : (zv / (1.0f + expf(-zv))));
+      y[tok * di + c] = out;
+      if (y_bf != nullptr) store_act16(y_bf, tok, di, c, out, split);
     }
-    const float zv = xz[tok * 2 * di + di + c];
-    const float out = yv * (FAST ? silu_fast(zv) : (zv / (1.0f + expf(-zv))));
-    y[tok * di + c] = out;
-    if (y_bf != nullptr) store_act16(y_bf, tok, di, c, out, split);
   }
   if (state != nullptr)
 #pragma unroll
