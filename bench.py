@@ -221,7 +221,9 @@ def run_ours(args):
 
         import torch.distributed as dist
 
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
+        # bounded: a rank that fails leaves the others' next collective with an
+        # error instead of a hang (rank 0's checkpoint write precedes the first)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=240),
                                 device_id=torch.device("cuda", local))
     from flowedge_b200 import Engine
     from flowedge_b200.engine import device_malloc_count
