@@ -35,6 +35,7 @@ REPO = Path(__file__).resolve().parent
 sys.path.insert(0, str(REPO))
 
 from flowedge_b200 import checkpoint as ck  # noqa: E402
+from flowedge_b200.shard import gather_rows, max_over_ranks, shard_range, shard_seed  # noqa: E402
 
 METRIC = "DDIM action chunks/s at b=4096 (bimanual U-Net, 10-step DDIM)"
 UNIT = "chunks/s"
@@ -236,9 +237,10 @@ def run_ours(args):
         _checkpoint(path, spec, True)
     if dist is not None:
         dist.barrier()
-    assert GLOBAL_BATCH % world == 0
-    shard = GLOBAL_BATCH // world
-    cond, noise = _inputs(spec, shard, offset=rank * shard)
+    assert GLOBAL_BATCH % world == 0  # equal shards: the actions are all-gathered
+    offset, shard = shard_range(GLOBAL_BATCH, world, rank)
+    seed = shard_seed(SEED, offset)
+    cond, noise = _inputs(spec, shard, offset=offset)
     engine = Engine(path, threads=0, device=local, precision="bf16", max_batch=shard)
 
     # a dedicated (non-default) stream: the engine enqueues on it and the
@@ -251,7 +253,7 @@ def run_ours(args):
 
     def step():
         engine.sample_diffusion_device(d_cond.data_ptr(), d_noise.data_ptr(), shard, d_action.data_ptr(), STEPS,
-                                       "ddim", SEED + rank * shard, stream.cuda_stream)
+                                       "ddim", seed, stream.cuda_stream)
 
     for _ in range(max(args.warmup, 3)):
         step()
@@ -271,47 +273,39 @@ def run_ours(args):
         torch.cuda.synchronize()
     ms = start.elapsed_time(stop)
     launches = engine.kernel_launches - launches0
-    t = torch.tensor([ms], dtype=torch.float64, device="cuda")
     if dist is not None:
         dist.barrier()
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms_max = float(t.item())
+    ms_max = max_over_ranks(ms, dist, "cuda")
     value = GLOBAL_BATCH * args.steps / (ms_max / 1000.0)
     mallocs = device_malloc_count() - mallocs0
 
     # e2e through the host-buffer public API (inputs/outputs in host memory)
     out = np.empty_like(noise)
-    engine.sample_diffusion_batch(cond, noise, STEPS, "ddim", SEED)  # warm the host-API path
+    engine.sample_diffusion_batch(cond, noise, STEPS, "ddim", seed)  # warm the host-API path
     if dist is not None:
         dist.barrier()
     torch.cuda.synchronize()
     e2e_steps = max(1, min(args.steps, 3))
     t0 = time.perf_counter()
     for _ in range(e2e_steps):
-        out[:] = engine.sample_diffusion_batch(cond, noise, STEPS, "ddim", SEED)
+        out[:] = engine.sample_diffusion_batch(cond, noise, STEPS, "ddim", seed)
     e2e_s = time.perf_counter() - t0
-    te = torch.tensor([e2e_s], dtype=torch.float64, device="cuda")
-    if dist is not None:
-        dist.all_reduce(te, op=dist.ReduceOp.MAX)
-    e2e_value = GLOBAL_BATCH * e2e_steps / float(te.item())
+    e2e_value = GLOBAL_BATCH * e2e_steps / max_over_ranks(e2e_s, dist, "cuda")
 
     # results gathered to every rank after the timed region (timed separately)
     gather = None
     if dist is not None:
-        parts = [torch.empty_like(d_action) for _ in range(world)]
         g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        dist.all_gather(parts, d_action)  # untimed: the first gather sets up NCCL's channels
+        gather_rows(d_action, dist)  # untimed: the first gather sets up NCCL's channels
         dist.barrier()
         torch.cuda.synchronize()
         g0.record(stream)
-        dist.all_gather(parts, d_action)
+        gathered = gather_rows(d_action, dist)
         g1.record(stream)
         torch.cuda.synchronize()
-        tg = torch.tensor([g0.elapsed_time(g1)], dtype=torch.float64, device="cuda")
-        dist.all_reduce(tg, op=dist.ReduceOp.MAX)
-        gather = {"op": "all_gather of the actions", "bytes": int(d_action.numel() * 4 * world),
-                  "ms": float(tg.item())}
-        del parts
+        gather = {"op": "all_gather of the actions", "bytes": int(gathered.numel() * 4),
+                  "ms": max_over_ranks(g0.elapsed_time(g1), dist, "cuda")}
+        del gathered
 
     # dominant kernel: the tcgen05 conv GEMMs of one denoise forward
     prof = engine.profile_diffusion(shard)
