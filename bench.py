@@ -1,7 +1,7 @@
 #!/usr/bin/env python3
 """Benchmark of the policy-sampling hot path on B200.
 
-Workload (BASELINE config 4): bimanual Diffusion Policy ConditionalUnet1D
+Workload: bimanual Diffusion Policy ConditionalUnet1D
 (action 14, horizon 64, condition 284, dims 512/1024/2048, kernel 5, 8 groups,
 step embedding 128), bf16 weights / fp32 accumulation, 10-step DDIM (eta 0),
 global batch 4096 sharded over the ranks (strong scaling), seeded synthetic
@@ -15,6 +15,11 @@ launching stream, inputs resident in HBM, max over ranks); `e2e` is the same
 metric through the host-buffer C ABI (host->device inputs and device->host
 actions inside the timed region).  `--impl reference` times the reference's own
 CPU core (oracle/_ref) on the host cores on a bounded sample of the workload.
+
+After the timed region the engine's device error word is read (a bounded
+device wait that timed out fails the run), and the actions of the last timed
+step are checked against the reference core on sampled rows of every rank's
+shard (`parity_max_abs`; the run exits non-zero above the bf16 bar 2e-2).
 """
 
 from __future__ import annotations
@@ -144,37 +149,81 @@ def _peaks():
 # CPU: the reference core on the host cores
 
 
-def _reference_throughput(path: Path, spec, chunks: int, threads: int, rounds: int = 1):
-    """`threads` engines sharing one weight store, threads=0 each (one chunk
-    per engine per round); returns (chunks/s, seconds)."""
-    from oracle import reference
+class ReferencePool:
+    """The reference core on the host cores: `threads` engines sharing one
+    weight store (`fe_weights_load` + `fe_engine_create_from_weights`, one
+    worker thread = the caller each), the throughput form of the CPU baseline
+    (one engine per host thread)."""
 
-    lib = reference.lib()
-    weights = lib.fe_weights_load(str(path).encode())
-    if not weights:
-        raise RuntimeError(lib.fe_engine_last_error().decode())
-    engines = [reference.ReferenceEngine.from_weights(weights, 0) for _ in range(threads)]
-    cond, noise = _inputs(spec, chunks)
-    done = []
+    def __init__(self, path: Path, threads: int):
+        from oracle import reference
 
-    def work(i):
-        e = engines[i % threads]
-        for j in range(i, chunks, threads):
-            e.sample_diffusion(cond[j], noise[j], STEPS)
-            done.append(j)
+        self.lib = reference.lib()
+        self.weights = self.lib.fe_weights_load(str(path).encode())
+        if not self.weights:
+            raise RuntimeError(self.lib.fe_engine_last_error().decode())
+        self.threads = threads
+        self.engines = [reference.ReferenceEngine.from_weights(self.weights, 0) for _ in range(threads)]
 
-    t0 = time.perf_counter()
-    for _ in range(rounds):
-        pool = [threading.Thread(target=work, args=(i,)) for i in range(threads)]
+    def sample(self, cond, noise):
+        """DDIM-10 actions of every row (rows spread round-robin over the
+        engines); returns (actions, seconds)."""
+        out = np.empty_like(noise)
+
+        def work(i):
+            e = self.engines[i]
+            for j in range(i, cond.shape[0], self.threads):
+                out[j] = e.sample_diffusion(cond[j], noise[j], STEPS)
+
+        t0 = time.perf_counter()
+        pool = [threading.Thread(target=work, args=(i,)) for i in range(min(self.threads, cond.shape[0]))]
         for t in pool:
             t.start()
         for t in pool:
             t.join()
-    elapsed = time.perf_counter() - t0
-    for e in engines:
-        e.close()
-    lib.fe_weights_free(weights)
-    return chunks * rounds / elapsed, elapsed
+        return out, time.perf_counter() - t0
+
+    def close(self):
+        for e in self.engines:
+            e.close()
+        self.lib.fe_weights_free(self.weights)
+
+
+def _cpu_model() -> str:
+    try:
+        for line in Path("/proc/cpuinfo").read_text().splitlines():
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+def _reference_leg(path: Path, spec, steps: int, warmup: int):
+    """The C4 reference measurement shared by `--impl reference` and the
+    in-line `cpu_baseline`: one step = one DDIM-10 chunk per host thread (rows
+    0..threads-1 of the global batch), after `warmup` untimed steps of the same
+    size.  Returns (chunks/s, per-step seconds, threads, the rows' actions)."""
+    threads = os.cpu_count() or 1
+    cond, noise = _inputs(spec, threads)
+    pool = ReferencePool(path, threads)
+    for _ in range(warmup):
+        pool.sample(cond, noise)
+    times, actions = [], None
+    for _ in range(steps):
+        actions, secs = pool.sample(cond, noise)
+        times.append(secs)
+    pool.close()
+    return threads * steps / sum(times), times, threads, actions
+
+
+def _reference_rows(path: Path, spec, rows) -> np.ndarray:
+    """Reference-core DDIM-10 actions of the given global rows (parity check)."""
+    cond, noise = _inputs(spec, GLOBAL_BATCH)
+    pool = ReferencePool(path, min(len(rows), os.cpu_count() or 1))
+    out, _ = pool.sample(cond[list(rows)], noise[list(rows)])
+    pool.close()
+    return out
 
 
 def run_reference(args):
@@ -183,28 +232,87 @@ def run_reference(args):
         return 0
     spec = ck.BIMANUAL
     path = _checkpoint(Path(args.workdir) / "bench_c4_bf16w.safetensors", spec, True)
-    threads = os.cpu_count() or 1
-    chunks = threads  # one DDIM-10 chunk per host thread per step
-    for _ in range(args.warmup):
-        _reference_throughput(path, spec, max(1, threads // 4), threads)
-    times = []
-    for _ in range(args.steps):
-        _, secs = _reference_throughput(path, spec, chunks, threads)
-        times.append(secs)
-    total = sum(times)
-    value = chunks * args.steps / total
+    value, times, threads, _ = _reference_leg(path, spec, args.steps, args.warmup)
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": 1000 * total / args.steps, "higher_is_better": True,
+        "warmup": args.warmup, "ms_per_step": 1000 * sum(times) / args.steps, "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "config": {"workload": "C4 bimanual U-Net DDIM-10 (reference fp32 CPU core on the bf16-rounded weights)",
                    "global_batch": GLOBAL_BATCH, "horizon": spec.horizon, "action_dim": spec.action_dim},
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "reference",
-                         "sample": f"{chunks} chunks per step, {threads} engines x 1 thread, shared weights"},
+                         "cpu_model": _cpu_model(),
+                         "sample": f"{threads} chunks per step (rows 0..{threads - 1}), {threads} engines x 1 thread, "
+                                   f"shared weights, {args.warmup} warm-up steps of the same size"},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
     return 0
+
+
+def _latency_cpu(fn, iters: int, warmup: int = 2) -> dict:
+    for _ in range(warmup):
+        fn()
+    times = []
+    for _ in range(iters):
+        t0 = time.perf_counter()
+        fn()
+        times.append((time.perf_counter() - t0) * 1000.0)
+    times.sort()
+    return {"p50_ms": times[len(times) // 2], "p99_ms": times[min(len(times) - 1, int(len(times) * 0.99))],
+            "iters": iters}
+
+
+def _cpu_latency_legs(workdir: Path) -> dict:
+    """Batch-1 latency of the other workloads on the reference core, threads = 1
+    (one engine, caller thread only) and all cores (one engine with
+    min(nproc, 8) workers, the reference's maximum pool): PushT U-Net fp32
+    DDIM-10, flow head Euler-10 / RK4-4 given the condition, Mamba 8 x 512
+    prefill of 128 tokens, and Mamba -> flow Euler-10 (fe_engine_sample)."""
+    from oracle import reference
+
+    nproc = os.cpu_count() or 1
+    rng = np.random.default_rng(7)
+    cond = rng.standard_normal(132).astype(np.float32)
+    noise = rng.standard_normal((16, 2)).astype(np.float32)
+    c = rng.standard_normal(512).astype(np.float32)
+    x0 = rng.standard_normal(350).astype(np.float32)
+    tokens = np.arange(128, dtype=np.int32)
+    pusht, flow, mamba = _latency_checkpoints(workdir)
+    out = {}
+    for label, threads in (("threads_1", 0), ("all_cores", min(nproc, 8))):
+        e = reference.ReferenceEngine(pusht, threads=threads)
+        # one fp32 DDIM-10 call takes about a second on one core: 10 timed calls there
+        out.setdefault("c1_pusht_b1_ddim10_fp32", {})[label] = _latency_cpu(
+            lambda: e.sample_diffusion(cond, noise, 10), 10 if threads == 0 else 20)
+        e.close()
+        e = reference.ReferenceEngine(flow, threads=threads)
+        out.setdefault("c2_flow_b1_euler10_fp32", {})[label] = _latency_cpu(
+            lambda: e.sample_condition(c, x0, 10, "euler"), 50)
+        out.setdefault("c2_flow_b1_rk4_4_fp32", {})[label] = _latency_cpu(
+            lambda: e.sample_condition(c, x0, 4, "rk4"), 50)
+        e.close()
+        e = reference.ReferenceEngine(mamba, threads=threads)
+        out.setdefault("c3_mamba_b1_prefill128_fp32", {})[label] = _latency_cpu(lambda: e.run(tokens, 512), 20)
+        out.setdefault("c3_mamba_flow_b1_sample_euler10_fp32", {})[label] = _latency_cpu(
+            lambda: e.sample(tokens, x0, 10, "euler"), 20)
+        e.close()
+        for leg in out.values():
+            leg[label]["workers"] = threads
+    return out
+
+
+def _latency_checkpoints(workdir: Path):
+    workdir.mkdir(parents=True, exist_ok=True)
+    pusht = _checkpoint(workdir / "bench_c1_pusht.safetensors", ck.PUSHT, False)
+    flow = workdir / "bench_c2_flow.safetensors"
+    if not flow.exists():
+        ck.write_checkpoint(flow, ck.flow_tensors(ck.FLOW_C2, seed=SEED))
+    mamba = workdir / "bench_c3_mamba_flow.safetensors"
+    if not mamba.exists():
+        t = ck.mamba_tensors(ck.MAMBA_C3, seed=SEED)
+        t.update(ck.flow_tensors(ck.FLOW_C2, seed=SEED + 1))
+        ck.write_checkpoint(mamba, t)
+    return pusht, flow, mamba
 
 
 # ---------------------------------------------------------------------------
@@ -273,6 +381,9 @@ def run_ours(args):
         torch.cuda.synchronize()
     ms = start.elapsed_time(stop)
     launches = engine.kernel_launches - launches0
+    # the device error word: a bounded device wait that timed out inside the
+    # timed region fails the run here instead of yielding a throughput number
+    engine.synchronize()
     if dist is not None:
         dist.barrier()
     ms_max = max_over_ranks(ms, dist, "cuda")
@@ -292,6 +403,12 @@ def run_ours(args):
     e2e_s = time.perf_counter() - t0
     e2e_value = GLOBAL_BATCH * e2e_steps / max_over_ranks(e2e_s, dist, "cuda")
 
+    # rows of the last timed step that are checked against the reference core:
+    # rows 0..P-1 of the single shard, or the first two rows of every rank's shard
+    n_par = 0 if args.no_parity else (min(os.cpu_count() or 1, shard) if world == 1 else min(2, shard))
+    par_rows = [r * shard + i for r in range(world) for i in range(n_par)]
+    par_got = d_action[:n_par].cpu().numpy() if world == 1 else None
+
     # results gathered to every rank after the timed region (timed separately)
     gather = None
     if dist is not None:
@@ -305,6 +422,8 @@ def run_ours(args):
         torch.cuda.synchronize()
         gather = {"op": "all_gather of the actions", "bytes": int(gathered.numel() * 4),
                   "ms": max_over_ranks(g0.elapsed_time(g1), dist, "cuda")}
+        if rank == 0 and par_rows:
+            par_got = gathered.reshape(GLOBAL_BATCH, spec.horizon, spec.action_dim)[par_rows].cpu().numpy()
         del gathered
 
     # dominant kernel: the tcgen05 conv GEMMs of one denoise forward
@@ -340,20 +459,52 @@ def run_ours(args):
         line["gather"] = gather
     if world == 1 and not args.no_extras:
         line["extra"] = _extras(Path(args.workdir), local)
+    expected = None
     if world == 1 and not args.no_cpu_baseline:
-        threads = os.cpu_count() or 1
-        cpu_value, secs = _reference_throughput(path, spec, threads, threads)
+        # the same measurement as `--impl reference` (one warm-up step, three timed)
+        cpu_value, times, threads, expected = _reference_leg(path, spec, 3, 1)
         line["cpu_baseline"] = {"value": cpu_value, "unit": UNIT, "cores": threads, "kind": "reference",
-                                "sample": f"{threads} chunks (one per host thread, {secs:.1f} s)"}
+                                "nproc": os.cpu_count(), "cpu_model": _cpu_model(),
+                                "sample": f"{threads} chunks per step (rows 0..{threads - 1}), {threads} engines x 1 "
+                                          f"thread, 1 warm-up + 3 timed steps ({sum(times):.1f} s)"}
+        value_t1 = _reference_single_thread(path, spec)
+        line["cpu_baseline"]["threads_1"] = {"value": value_t1, "unit": UNIT, "cores": 1,
+                                             "sample": "1 chunk (row 0), one engine, caller thread only"}
         if not args.no_extras:
+            line["cpu_baseline"]["latency_b1"] = _cpu_latency_legs(Path(args.workdir))
             line["cpu_baseline"]["c5_smolvla"] = _smolvla_cpu_baseline(threads)
+    parity_bad = False
+    if rank == 0 and par_rows:
+        if expected is None or expected.shape[0] < len(par_rows):
+            expected = _reference_rows(path, spec, par_rows)
+        err = float(np.abs(par_got - expected[:len(par_rows)]).max())
+        parity_bad = not err <= 2e-2
+        line["parity_max_abs"] = err
+        line["parity"] = {"rows": len(par_rows), "bar": 2e-2, "against": "reference CPU core on the same "
+                          "bf16-rounded weights (fp32)", "which": "first rows of every rank's shard, last timed step"}
     engine.close()
     if dist is not None:
         dist.barrier()
         dist.destroy_process_group()
     if line is not None:
         print(json.dumps(line), flush=True)
+    if parity_bad:
+        print(f"parity check failed: max-abs {line['parity_max_abs']:.3g} above 2e-2", file=sys.stderr)
+        return 1
     return 0
+
+
+def _reference_single_thread(path: Path, spec) -> float:
+    """threads = 1: one reference engine, caller thread only, one chunk."""
+    from oracle import reference
+
+    cond, noise = _inputs(spec, 1)
+    e = reference.ReferenceEngine(path, threads=0)
+    t0 = time.perf_counter()
+    e.sample_diffusion(cond[0], noise[0], STEPS)
+    secs = time.perf_counter() - t0
+    e.close()
+    return 1.0 / secs
 
 
 def _latency(fn, iters):
@@ -391,7 +542,8 @@ def _smolvla_flops(spec) -> float:
 
 
 def _extras(workdir: Path, device: int):
-    """The other BASELINE configurations, through the public host-buffer API
+    """The other workloads (PushT U-Net, flow head, Mamba encoder, SmolVLA-shaped
+    expert), through the public host-buffer API
     (synchronous calls: host->device inputs and device->host outputs included)."""
     import torch
 
@@ -400,7 +552,7 @@ def _extras(workdir: Path, device: int):
     out = {}
     rng = np.random.default_rng(7)
     # C1: PushT U-Net, batch 1, DDIM-10 (fp32 weights; and the bf16-weight mode)
-    pusht = _checkpoint(workdir / "bench_c1_pusht.safetensors", ck.PUSHT, False)
+    pusht, flow, mamba = _latency_checkpoints(workdir)
     cond = rng.standard_normal(132).astype(np.float32)
     noise = rng.standard_normal((16, 2)).astype(np.float32)
     for prec in ("fp32", "bf16"):
@@ -408,9 +560,6 @@ def _extras(workdir: Path, device: int):
         out[f"c1_pusht_b1_ddim10_{prec}"] = _latency(lambda: e.sample_diffusion(cond, noise, 10), 1000)
         e.close()
     # C2: flow head 350 / 1024 x 3 / 512, Euler-10 and RK4-4
-    flow = workdir / "bench_c2_flow.safetensors"
-    if not flow.exists():
-        ck.write_checkpoint(flow, ck.flow_tensors(ck.FLOW_C2, seed=SEED))
     c = rng.standard_normal(512).astype(np.float32)
     x0 = rng.standard_normal(350).astype(np.float32)
     for prec in ("fp32", "bf16"):
@@ -435,11 +584,6 @@ def _extras(workdir: Path, device: int):
         out[f"c2_flow_b4096_euler10_{prec}_actions_per_s"] = 4096 * 5 / (ev0.elapsed_time(ev1) / 1000.0)
         e.close()
     # C3: Mamba 8 x 512 (L = 128) -> C2 flow head
-    mamba = workdir / "bench_c3_mamba_flow.safetensors"
-    if not mamba.exists():
-        t = ck.mamba_tensors(ck.MAMBA_C3, seed=SEED)
-        t.update(ck.flow_tensors(ck.FLOW_C2, seed=SEED + 1))
-        ck.write_checkpoint(mamba, t)
     tokens = np.arange(128, dtype=np.int32)
     for prec in ("fp32", "bf16"):
         e = Engine(mamba, threads=0, device=device, precision=prec, max_batch=1024)
@@ -469,7 +613,7 @@ def _extras(workdir: Path, device: int):
         out[f"c3_mamba_b1024_prefill128_{prec}_device_seq_per_s"] = 3 * 1024 / (ev0.elapsed_time(ev1) / 1000.0)
         e.close()
     # C5: SmolVLA-shaped action expert (bf16 by construction), Euler-10, one
-    # fixed 241-slot prefix shared by the batch
+    # fixed 241-slot prefix of width 960 shared by the batch
     spec = ck.SMOLVLA_C5
     sv = workdir / "bench_c5_smolvla.safetensors"
     if not sv.exists():
@@ -512,8 +656,8 @@ def _extras(workdir: Path, device: int):
 
 
 def _smolvla_cpu_baseline(threads: int) -> dict:
-    """The reference cannot load configuration 5's shapes
-    (smolvla_action_expert.cc:120-128), so its CPU figure is the numpy
+    """The reference cannot load the SmolVLA-shaped expert's shapes (12 heads of
+    60, a 960-wide prefix; smolvla_action_expert.cc:120-128), so its CPU figure is the numpy
     restatement of the same algorithm (oracle/restate.py) on the host cores."""
     from oracle import restate
 
@@ -537,6 +681,7 @@ def main():
     ap.add_argument("--workdir", default=os.environ.get("FLOWEDGE_BENCH_DIR", "/tmp/flowedge_bench"))
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-extras", action="store_true", help="skip the C1/C2/C3 latency and throughput extras")
+    ap.add_argument("--no-parity", action="store_true", help="skip the check against the reference core")
     args = ap.parse_args()
     Path(args.workdir).mkdir(parents=True, exist_ok=True)
     if args.impl == "reference":

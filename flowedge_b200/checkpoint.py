@@ -11,10 +11,12 @@ U(-1/sqrt(fan_in), 1/sqrt(fan_in)); GroupNorm weight 1, bias 0).  The same
 arrays written through the reference converter produce an identical file
 content (checked by the golden-fixture tests).
 
-`conv_dtype="bf16"` stores the U-Net conv weights as BF16.  That is a new
-precision mode of this build: the reference loader accepts only F32 convs
-(src/core/heads/diffusion/diffusion.cc:656-660) and casts only 2-D tensors
-(convert/convert.py:602-610).
+`convs="bf16"` stores the U-Net conv weights as BF16, and
+`recast_convs_bf16` does the same to a file the reference converter wrote
+(`python -m flowedge_b200.checkpoint recast-convs SRC DST [--max-batch N]`).
+That is a new precision mode of this build: the reference loader accepts only
+F32 convs (src/core/heads/diffusion/diffusion.cc:656-660) and the reference
+converter casts only 2-D tensors (convert/convert.py:602-610).
 """
 
 from __future__ import annotations
@@ -48,6 +50,7 @@ __all__ = [
     "smolvla_prefix",
     "SMOLVLA_C5",
     "SMOLVLA_REF",
+    "recast_convs_bf16",
 ]
 
 
@@ -126,7 +129,7 @@ def read_safetensors(path) -> tuple[dict, dict]:
 
 
 # ----------------------------------------------------------------------------
-# model specifications (the BASELINE configs are module constants below)
+# model specifications (the benchmarked workloads are module constants below)
 
 
 @dataclass(frozen=True)
@@ -202,7 +205,7 @@ class SmolVLASpec:
         return self.kv_heads * self.head_width
 
 
-# 16 layers, width 720, 12 heads of 60, SwiGLU 2048, 50
+# SmolVLA-shaped expert workload: 16 layers, width 720, 12 heads of 60, SwiGLU 2048, 50
 # action tokens of dim 32, a 241-token prefix of width 960 projected per
 # cross-attention layer (3:1 grouped-query attention, 4 K / V heads).
 SMOLVLA_C5 = SmolVLASpec()
@@ -211,9 +214,9 @@ SMOLVLA_C5 = SmolVLASpec()
 SMOLVLA_REF = SmolVLASpec(expert_width=720, layers=4, heads=15, kv_heads=5, head_width=64, mlp_width=2048,
                           action_dim=32, chunk=10, state_dim=32, vlm_width=960, cache_width=320, prefix=24)
 
-# BASELINE config 1: PushT-shaped U-Net (A 2, H 16, cond 132).
+# PushT-shaped U-Net (A 2, H 16, cond 132).
 PUSHT = DiffusionSpec(action_dim=2, horizon=16, condition_dim=132)
-# BASELINE config 4: bimanual U-Net (A 14, H 64, cond 284).
+# bimanual U-Net (A 14, H 64, cond 284).
 BIMANUAL = DiffusionSpec(action_dim=14, horizon=64, condition_dim=284, action_steps=32)
 FLOW_C2 = FlowSpec()
 MAMBA_C3 = MambaSpec()
@@ -435,6 +438,45 @@ def cast_tensors(tensors: dict, matrices: str = "f32", convs: str = "f32") -> di
     return out
 
 
+def recast_convs_bf16(src, dst, *, max_batch: int | None = None) -> dict:
+    """Re-emit a converted checkpoint (e.g. one written by the reference's
+    convert/convert.py) with its U-Net conv weights in BF16.
+
+    The reference converter casts only 2-D tensors (convert.py:602-610), so its
+    files hold every 3-D `dp.*` conv weight (conv [out][in][k], conv-transpose
+    [in][out][4]) as F32.  This rewrites those tensors as BF16 (round to nearest
+    even), copies every other tensor's bytes and dtype unchanged, keeps the
+    file's metadata, and with `max_batch` adds the metadata key
+    "flowedge.max_batch", which this library's loader takes as the engine's
+    default batch reservation.  Returns {tensor name: "BF16"} for the recast
+    tensors.
+    """
+    data = Path(src).read_bytes()
+    (length,) = struct.unpack("<Q", data[:8])
+    header = json.loads(data[8:8 + length])
+    base = 8 + length
+    metadata = dict(header.pop("__metadata__", {}))
+    if max_batch is not None:
+        if not 1 <= int(max_batch) <= 1 << 24:
+            raise ValueError("max_batch must be from 1 through 16777216")
+        metadata["flowedge.max_batch"] = str(int(max_batch))
+    tensors, recast = {}, {}
+    for name, entry in sorted(header.items(), key=lambda kv: kv[1]["data_offsets"][0]):
+        begin, end = entry["data_offsets"]
+        raw = data[base + begin:base + end]
+        shape = tuple(entry["shape"])
+        if entry["dtype"] == "F32" and len(shape) == 3 and name.startswith("dp."):
+            tensors[name] = ("BF16", to_bf16_bits(np.frombuffer(raw, np.float32).reshape(shape)))
+            recast[name] = "BF16"
+        elif entry["dtype"] in ("F32", "BF16"):
+            dt = np.float32 if entry["dtype"] == "F32" else np.uint16
+            tensors[name] = (entry["dtype"], np.frombuffer(raw, dt).reshape(shape))
+        else:
+            raise ValueError(f"unsupported dtype {entry['dtype']} for {name}")
+    write_safetensors(dst, tensors, metadata)
+    return recast
+
+
 def write_checkpoint(path, *parts, matrices: str = "f32", convs: str = "f32",
                      metadata: dict | None = None) -> Path:
     merged: dict = {}
@@ -442,3 +484,23 @@ def write_checkpoint(path, *parts, matrices: str = "f32", convs: str = "f32",
         merged.update(part)
     write_safetensors(path, cast_tensors(merged, matrices, convs), metadata)
     return Path(path)
+
+
+def _main(argv=None) -> int:
+    import argparse
+
+    ap = argparse.ArgumentParser(prog="python -m flowedge_b200.checkpoint")
+    sub = ap.add_subparsers(dest="cmd", required=True)
+    rc = sub.add_parser("recast-convs", help="re-emit a converted checkpoint with BF16 U-Net conv weights")
+    rc.add_argument("src")
+    rc.add_argument("dst")
+    rc.add_argument("--max-batch", type=int, default=None,
+                    help="default batch reservation recorded in the file's metadata")
+    args = ap.parse_args(argv)
+    recast = recast_convs_bf16(args.src, args.dst, max_batch=args.max_batch)
+    print(f"{args.dst}: {len(recast)} conv tensors as BF16")
+    return 0
+
+
+if __name__ == "__main__":
+    raise SystemExit(_main())

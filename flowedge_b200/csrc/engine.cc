@@ -162,7 +162,8 @@ fe_engine* create_engine(std::shared_ptr<const feb::ModelWeights> weights, const
       return nullptr;
     }
     std::size_t max_batch = opt.max_batch;
-    if (max_batch == 0) max_batch = env_uint("FLOWEDGE_MAX_BATCH").value_or(1);
+    if (max_batch == 0) max_batch = env_uint("FLOWEDGE_MAX_BATCH").value_or(0);
+    if (max_batch == 0) max_batch = std::max<std::size_t>(weights->default_max_batch(), 1);
     std::size_t max_seq = opt.max_sequence == 0 ? kMaxPrefill : opt.max_sequence;
     const feb::TensorTable& t = weights->table();
     if (t.find("dp.meta") != nullptr) {

@@ -486,6 +486,17 @@ bool Flow::load(const TensorTable& t, std::string& err) {
   }
   tc_ok_ = H % 64 == 0;
   const bool bf = prec_ == Precision::kBF16;
+  // every projection but the time projection (fp32 on the device) is held in fp16
+  {
+    std::vector<std::pair<const HostTensor*, std::string>> planes = {
+        {in, "flow.in_proj.weight"}, {cp, "flow.cond_proj.weight"}, {op, "flow.out_proj.weight"}};
+    for (std::size_t n = 0; n < layer_t.size(); ++n)
+      planes.emplace_back(layer_t[n], "flow.layers." + std::to_string(n) + ".weight");
+    for (const auto& [tensor, name] : planes) {
+      const auto w = widen_f32(*tensor);
+      if (!check_fp16_storable(name, w.data(), w.size(), bf, err)) return false;
+    }
+  }
   ArenaPlan plan;
   auto plan_mat = [&](int rows, int cols) {
     const int rp = (rows + 127) / 128 * 128;
@@ -1018,6 +1029,15 @@ int Flow::sample_static(const float* condition, const float* x0, std::size_t bat
   }
   const int H = static_cast<int>(cfg_.hidden), A = static_cast<int>(cfg_.action_dim);
   const int C = static_cast<int>(cfg_.cond_dim), half = static_cast<int>(cfg_.time_dim / 2);
+  // every row needs at least one full-width fp32 row of scratch: reject batches
+  // that cannot fit before any size arithmetic (which then cannot wrap)
+  const std::size_t widest = std::max({static_cast<std::size_t>(a_pad_), static_cast<std::size_t>(H),
+                                       static_cast<std::size_t>(c_pad_)});
+  if (batch > kStaticScratchBytes / (4 * widest)) {
+    err = "batch of " + std::to_string(batch) + " rows cannot fit the " + std::to_string(kStaticScratchBytes) +
+          "-byte static array (use fewer rows)";
+    return 2;
+  }
   const std::size_t rows = batch;
   const std::size_t nsl = static_cast<std::size_t>(std::max({in_.nslices, cond_.nslices, out_.nslices,
                                                              layers_.empty() ? 1 : layers_[0].nslices}));
@@ -1040,9 +1060,24 @@ int Flow::sample_static(const float* condition, const float* x0, std::size_t bat
           std::to_string(kStaticScratchBytes) + "-byte static array (use fewer rows)";
     return 2;
   }
+  // the caller's current device is restored on every return; errors left
+  // pending on this thread by earlier calls are cleared so that the status
+  // below reports this call's launches only
+  int caller_device = -1;
+  cudaGetDevice(&caller_device);
+  struct RestoreDevice {
+    int device;
+    ~RestoreDevice() {
+      if (device >= 0) cudaSetDevice(device);
+    }
+  } restore{caller_device};
   cudaSetDevice(ctx_->device);
+  cudaGetLastError();
   auto* base = static_cast<unsigned char*>(static_scratch_address(ctx_->device, err));
-  if (base == nullptr) return 2;
+  if (base == nullptr) {
+    cudaGetLastError();
+    return 2;
+  }
   auto F = [&](std::size_t off) { return reinterpret_cast<float*>(base + off); };
   float *x = F(o_x), *probe = F(o_probe), *cemb = F(o_cemb), *tp = F(o_tp), *part = F(o_part);
   float *cin = F(o_cin), *xin = F(o_xin), *h0 = F(o_h0), *h1 = F(o_h1);
@@ -1086,7 +1121,11 @@ int Flow::sample_static(const float* condition, const float* x0, std::size_t bat
   linear(cond_, cin, c_pad_, cemb, H, nullptr, nullptr, tc::kActNone);
   load_rows_kernel<<<ew_grid(static_cast<long long>(rows) * a_pad_, 256, *ctx_), 256, 0, st>>>(
       x0, static_cast<int>(rows), A, x, a_pad_, xin, a_pad_, 0);
-  cudaMemsetAsync(step, 0, 2 * sizeof(int), st);
+  if (const cudaError_t rc = cudaMemsetAsync(step, 0, 2 * sizeof(int), st); rc != cudaSuccess) {
+    err = std::string("clearing the static step counter failed: ") + cudaGetErrorString(rc);
+    cudaGetLastError();
+    return 2;
+  }
   const int stages = method == 0 ? 1 : (method == 1 ? 2 : 4);
   for (std::size_t i = 0; i < steps; ++i) {
     for (int s = 0; s < stages; ++s) {
@@ -1117,7 +1156,12 @@ int Flow::sample_static(const float* condition, const float* x0, std::size_t bat
       p.next_mode = 0;
       ode_stage_kernel<<<ew_grid(static_cast<long long>(rows) * A, 256, *ctx_), 256, 0, st>>>(p);
     }
-    cudaMemcpyAsync(step, step + 1, sizeof(int), cudaMemcpyDeviceToDevice, st);
+    if (const cudaError_t rc = cudaMemcpyAsync(step, step + 1, sizeof(int), cudaMemcpyDeviceToDevice, st);
+        rc != cudaSuccess) {
+      err = std::string("advancing the static step counter failed: ") + cudaGetErrorString(rc);
+      cudaGetLastError();
+      return 2;
+    }
   }
   store_rows_kernel<<<ew_grid(static_cast<long long>(rows) * A, 256, *ctx_), 256, 0, st>>>(
       x, static_cast<int>(rows), A, a_pad_, out);

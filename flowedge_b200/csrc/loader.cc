@@ -496,6 +496,19 @@ std::shared_ptr<const ModelWeights> ModelWeights::open(const char* path, std::st
         if (!parse_profile(*profile->string(), p, error)) return nullptr;
         weights->profile_ = std::move(p);
       }
+      if (const Json* mb = entry.get("flowedge.max_batch"); mb != nullptr) {
+        const std::string* text = mb->string();
+        std::size_t value = 0;
+        const char* first = text != nullptr ? text->data() : nullptr;
+        const auto parsed = text != nullptr ? std::from_chars(first, first + text->size(), value)
+                                            : std::from_chars_result{nullptr, std::errc::invalid_argument};
+        if (text == nullptr || parsed.ec != std::errc() || parsed.ptr != first + text->size() || value == 0 ||
+            value > (std::size_t(1) << 24)) {
+          error = "Invalid flowedge.max_batch metadata (a batch count from 1 to 16777216)";
+          return nullptr;
+        }
+        weights->default_max_batch_ = value;
+      }
       continue;
     }
     const Json* dtype = entry.get("dtype");

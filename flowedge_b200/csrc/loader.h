@@ -40,6 +40,11 @@ class ModelWeights {
   [[nodiscard]] const DeploymentProfile* profile() const noexcept { return profile_ ? &*profile_ : nullptr; }
   [[nodiscard]] const Digest& digest() const noexcept { return digest_; }
   [[nodiscard]] std::uint32_t precision() const noexcept { return precision_; }
+  // Batch capacity written into the file by flowedge_b200.checkpoint
+  // (metadata key "flowedge.max_batch"; 0 = none): the default reservation of
+  // engines created from this store when their options and FLOWEDGE_MAX_BATCH
+  // name none.
+  [[nodiscard]] std::size_t default_max_batch() const noexcept { return default_max_batch_; }
 
  private:
   std::vector<std::byte> storage_;
@@ -48,6 +53,7 @@ class ModelWeights {
   std::optional<DeploymentProfile> profile_;
   Digest digest_{};
   std::uint32_t precision_{};
+  std::size_t default_max_batch_{};
 };
 
 // XXH64 of a byte range (the published xxHash 64-bit algorithm).

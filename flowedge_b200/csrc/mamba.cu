@@ -724,6 +724,10 @@ bool Mamba::load(const TensorTable& t, std::string& err) {
         return false;
       }
     out = widen_f32(*h);
+    // the in / x / out projections are held in fp16 (dt_proj stays fp32)
+    if (allow_bf16 && sub.find("_proj.weight") != std::string::npos && sub.find("dt_proj") == std::string::npos &&
+        !check_fp16_storable(name, out.data(), out.size(), bf, err))
+      return false;
     return true;
   };
   auto put = [&](const std::vector<float>& h) {

@@ -1,3 +1,5 @@
+#include <algorithm>
+#include <cmath>
 #include <cstring>
 #include <mutex>
 
@@ -242,6 +244,49 @@ std::uint16_t fp16_bits_of_bf16_rounded(float v) {
   std::memcpy(&r, &u, 4);
   const __half h = __float2half_rn(r);
   return __half_as_ushort(h);
+}
+
+bool check_fp16_storable(const std::string& name, const float* w, std::size_t n, bool bf16_mode, std::string& err) {
+  double max_abs = 0.0, max_err = 0.0;
+  for (std::size_t i = 0; i < n; ++i) {
+    const float v = w[i];
+    if (!std::isfinite(v)) {
+      err = "tensor " + name + " holds a non-finite value at element " + std::to_string(i);
+      return false;
+    }
+    double target, stored;
+    if (bf16_mode) {
+      const std::uint16_t h = fp16_bits_of_bf16_rounded(v);
+      std::uint32_t u;
+      std::memcpy(&u, &v, 4);
+      u = (u + 0x7FFFu + ((u >> 16) & 1u)) & 0xFFFF0000u;
+      float r;
+      std::memcpy(&r, &u, 4);
+      target = r;
+      stored = __half2float(__ushort_as_half(h));
+    } else {
+      const __half hi = __float2half_rn(v);
+      const float hf = __half2float(hi);
+      target = v;
+      stored = static_cast<double>(hf) + static_cast<double>(__half2float(__float2half_rn(v - hf)));
+    }
+    if (!std::isfinite(stored)) {
+      err = "tensor " + name + " holds " + std::to_string(v) + " at element " + std::to_string(i) +
+            ", beyond the fp16 range (65504) of this build's " + (bf16_mode ? "bf16" : "fp32") +
+            " weight storage";
+      return false;
+    }
+    max_abs = std::max(max_abs, std::fabs(target));
+    max_err = std::max(max_err, std::fabs(stored - target));
+  }
+  const double bound = bf16_mode ? 1.0 / 512.0 : 1.0 / 65536.0;
+  if (max_err > bound * max_abs) {
+    err = "tensor " + name + " cannot be stored in fp16 to " + (bf16_mode ? "2^-9" : "2^-16") +
+          " of its largest magnitude " + std::to_string(max_abs) + " (fp16 subnormal range); largest error " +
+          std::to_string(max_err);
+    return false;
+  }
+  return true;
 }
 
 cudaError_t tc_gemm(const TcLaunch& l, DeviceContext& ctx, cudaStream_t stream, std::string& err) {

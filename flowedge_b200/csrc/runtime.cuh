@@ -146,4 +146,15 @@ std::vector<float> widen_f32(const HostTensor& t);
 // throughput.
 std::uint16_t fp16_bits_of_bf16_rounded(float v);
 
+// Load-time range check of a weight tensor that the device holds in fp16:
+// bf16 mode stores fp16(bf16(w)); fp32 mode stores the pair hi = fp16(w),
+// lo = fp16(w - hi), which is within max(2^-22 |w|, 2^-25) of w.  Fails with a
+// message naming the tensor when a value cannot be stored (|w| beyond the fp16
+// range 65504, or not finite), or when the stored values miss the intended
+// ones (bf16(w), or w) by more than 2^-9 (bf16 mode) or 2^-16 (fp32 mode) of
+// the tensor's largest magnitude; that happens only for a tensor whose values
+// all lie far below 1 (under about 2^-16 in bf16 mode, 2^-9 in fp32 mode),
+// where fp16's subnormal spacing 2^-24 is no longer small against them.
+bool check_fp16_storable(const std::string& name, const float* w, std::size_t n, bool bf16_mode, std::string& err);
+
 }  // namespace feb

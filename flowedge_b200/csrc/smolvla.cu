@@ -1,5 +1,5 @@
-// SmolVLA-shaped flow action expert on sm_100a (BASELINE configuration 5 and
-// the reference's own shapes).
+// SmolVLA-shaped flow action expert on sm_100a (12 heads of 60 over a 960-wide
+// prefix, and the reference's own shapes).
 //
 // The reference runs the expert on the host with bf16 rounding at every
 // boundary (src/core/models/smolvla/smolvla_action_expert.cc:209-477).  Here a
@@ -1330,7 +1330,16 @@ bool SmolVLA::load(const TensorTable& t, std::string& err) {
   if (!wts_.init(plan.total(), err)) return false;
 
   // bf16 [rows_pad][kp] or split fp16 [rows_pad][2 kp] from row blocks (each [rows][cols])
-  auto put_mat = [&](Mat& m, const std::vector<const std::vector<float>*>& blocks, int cols, bool split) {
+  // split matrices hold fp16(bf16(w)): check their range first
+  bool planes_ok = true;
+  auto put_mat = [&](Mat& m, const std::vector<const std::vector<float>*>& blocks, int cols, bool split,
+                     const std::string& name = std::string()) {
+    if (split && planes_ok)
+      for (const auto* b : blocks)
+        if (!check_fp16_storable(name, b->data(), b->size(), true, err)) {
+          planes_ok = false;
+          return;
+        }
     int rows = 0;
     for (const auto* b : blocks) rows += static_cast<int>(b->size() / static_cast<std::size_t>(cols));
     m.rows = rows;
@@ -1369,8 +1378,8 @@ bool SmolVLA::load(const TensorTable& t, std::string& err) {
     L.cross = l % 2 == 1;
     if (L.cross) {
       put_mat(L.qkv, {&s.q}, W_, false);
-      put_mat(L.k, {&s.k}, Cw_, true);
-      put_mat(L.v, {&s.v}, Cw_, true);
+      put_mat(L.k, {&s.k}, Cw_, true, pre + std::to_string(l) + ".self_attn.k_proj.weight");
+      put_mat(L.v, {&s.v}, Cw_, true, pre + std::to_string(l) + ".self_attn.v_proj.weight");
     } else {
       put_mat(L.qkv, {&s.q, &s.k, &s.v}, W_, false);
     }
@@ -1393,10 +1402,11 @@ bool SmolVLA::load(const TensorTable& t, std::string& err) {
       wa[m * W + j] = wtin[m * 2 * W + j];
       wt[m * W + j] = wtin[m * 2 * W + W + j];
     }
-  put_mat(in_, {&win}, A_, true);
-  put_mat(tin_, {&wa}, W_, true);
-  put_mat(tout_, {&wtout}, W_, true);
-  put_mat(out_, {&wout}, W_, true);
+  put_mat(in_, {&win}, A_, true, "model.action_in_proj.weight");
+  put_mat(tin_, {&wa}, W_, true, "model.action_time_mlp_in.weight");
+  put_mat(tout_, {&wtout}, W_, true, "model.action_time_mlp_out.weight");
+  put_mat(out_, {&wout}, W_, true, "model.action_out_proj.weight");
+  if (!planes_ok) return false;
   wt_ = put_vec(wt);
   b_in_ = put_vec(widen_f32(*bin));
   b_tin_ = put_vec(widen_f32(*btin));

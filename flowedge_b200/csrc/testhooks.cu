@@ -1,5 +1,6 @@
 // Test hooks (include/flowedge_b200_testing.h): one tcgen05 GEMM / conv on
 // host buffers, for kernel-level numerics tests.
+#include <algorithm>
 #include <cstring>
 #include <vector>
 
@@ -136,4 +137,16 @@ extern "C" int febtest_conv_16(const uint16_t* x, int B, int L, int C, const uin
   cudaFree(dbias);
   cudaFree(dst);
   return rc;
+}
+
+extern "C" int febtest_check_fp16_storable(const char* name, const float* w, size_t n, int bf16_mode, char* message,
+                                           size_t message_len) {
+  std::string err;
+  const bool ok = feb::check_fp16_storable(name != nullptr ? name : "", w, n, bf16_mode != 0, err);
+  if (message != nullptr && message_len > 0) {
+    const size_t len = std::min(err.size(), message_len - 1);
+    std::memcpy(message, err.data(), len);
+    message[len] = '\0';
+  }
+  return ok ? 0 : 1;
 }

@@ -463,6 +463,11 @@ bool Unet::load(const TensorTable& t, std::string& err) {
         return false;
       }
     out = widen_f32(*h);
+    // conv and FiLM weights live on the device in fp16 planes (the time MLP
+    // stays fp32: it is tabulated at load)
+    if (allow_bf16 && shape.size() >= 2 && name.rfind("dp.te", 0) != 0 &&
+        !check_fp16_storable(name, out.data(), out.size(), bf16_weights(), err))
+      return false;
     return true;
   };
   // Conv weights: the reference accepts F32 only; BF16 convs are this build's

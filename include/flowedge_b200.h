@@ -195,7 +195,7 @@ int fe_engine_smolvla_embed_suffix(fe_engine* engine, const float* noisy_actions
 /* engine.h:148-161: the expert's layers over a caller-supplied prefix cache
  * [expert_layers][prefix_length][cache_width] (cache_width = the K / V width in
  * the reference's layout; this build also accepts a wider cache that the
- * cross-attention layers project) */
+ * cross-attention layers project, e.g. a 960-wide prefix for 12 heads of 60) */
 int fe_engine_smolvla_run_expert(fe_engine* engine, const float* suffix, size_t chunk_size,
                                  const float* prefix_keys, const float* prefix_values, const uint8_t* prefix_mask,
                                  size_t prefix_length, float* out);

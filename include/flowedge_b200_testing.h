@@ -7,6 +7,7 @@
 #ifndef FLOWEDGE_B200_TESTING_H
 #define FLOWEDGE_B200_TESTING_H
 
+#include <stddef.h>
 #include <stdint.h>
 
 #ifdef __cplusplus
@@ -31,6 +32,14 @@ int febtest_gemm_16(const uint16_t* A, int M, int K, const uint16_t* B, int N, f
  * bf16 rounding), groups = OC / group_ch (group_ch = 0: no statistics). */
 int febtest_conv_16(const uint16_t* x, int B, int L, int C, const uint16_t* W, const float* bias, int OC, int k,
                     int group_ch, float* y, double* stats, int fp16);
+
+/* The load-time range check applied to every weight tensor that the device
+ * holds in fp16 (bf16 mode when `bf16_mode` != 0, else the fp32 hi / lo
+ * split).  Returns 0 when `w` can be stored, else 1 with the loader's message
+ * (naming `name`) in `message` (NUL-terminated, truncated to `message_len`).
+ * Host only: needs no GPU. */
+int febtest_check_fp16_storable(const char* name, const float* w, size_t n, int bf16_mode, char* message,
+                                size_t message_len);
 
 #if defined(__GNUC__)
 #pragma GCC visibility pop

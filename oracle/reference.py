@@ -15,18 +15,20 @@ import numpy as np
 
 HERE = Path(__file__).resolve().parent
 LIB_PATH = HERE / "_ref" / "liboracle.so"
-REFERENCE_ROOT = Path(os.environ.get("FLOWEDGE_REFERENCE", "/root/reference"))
+# the reference checkout, given by FLOWEDGE_REFERENCE (needed only to build)
+REFERENCE_ROOT = Path(os.environ["FLOWEDGE_REFERENCE"]) if os.environ.get("FLOWEDGE_REFERENCE") else None
 
 _f32p = C.POINTER(C.c_float)
 
 
-def build() -> Path:
-    """Compile the reference core (only where its sources exist)."""
+def build(root: Path | None = None) -> Path:
+    """Compile the reference core from the checkout at `root` (default:
+    FLOWEDGE_REFERENCE) unless it is built already."""
     if not LIB_PATH.exists():
-        if not (REFERENCE_ROOT / "src" / "core").is_dir():
-            raise FileNotFoundError(f"{LIB_PATH} missing and no reference sources to build it")
-        subprocess.run(["make", "-C", str(HERE), f"REF={REFERENCE_ROOT}", "-j8"],
-                       check=True, stdout=subprocess.DEVNULL)
+        root = root if root is not None else REFERENCE_ROOT
+        if root is None or not (Path(root) / "src" / "core").is_dir():
+            raise FileNotFoundError(f"{LIB_PATH} missing: set FLOWEDGE_REFERENCE to a reference checkout to build it")
+        subprocess.run(["make", "-C", str(HERE), f"REF={root}", "-j8"], check=True, stdout=subprocess.DEVNULL)
     return LIB_PATH
 
 

@@ -1,10 +1,10 @@
 #!/usr/bin/env python3
 """Regenerate the golden fixtures in this directory from the reference itself.
 
-Run in a container that has the reference checkout (default /root/reference,
-override with FLOWEDGE_REFERENCE) and PyTorch:
+Run where the reference checkout and PyTorch are available, with
+FLOWEDGE_REFERENCE naming the checkout:
 
-    python tests/golden/make_golden.py [fixture names]
+    FLOWEDGE_REFERENCE=<path to FlowEdge> python tests/golden/make_golden.py [fixture names]
 
 For each fixture it
   1. builds a small seeded model in the *source* layout the reference converter
@@ -35,7 +35,9 @@ from safetensors.torch import save_file
 
 HERE = Path(__file__).resolve().parent
 REPO = HERE.parents[1]
-REF = Path(os.environ.get("FLOWEDGE_REFERENCE", "/root/reference"))
+if not os.environ.get("FLOWEDGE_REFERENCE"):
+    sys.exit("set FLOWEDGE_REFERENCE to the reference FlowEdge checkout")
+REF = Path(os.environ["FLOWEDGE_REFERENCE"])
 sys.path.insert(0, str(REPO))
 
 from oracle import reference as oracle_ref  # noqa: E402

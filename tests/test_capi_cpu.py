@@ -149,3 +149,85 @@ def test_gaussian_stream_random_access_matches_sequential():
         seq = restate.GaussianGenerator(seed).fill(37)
         ra = np.array([at(seed, j) for j in range(37)], np.float32)
         np.testing.assert_array_equal(seq, ra)
+
+
+def _fp16_check(lib, w, bf16_mode, name=b"dp.d0.r0.c1.w"):
+    fn = lib.febtest_check_fp16_storable
+    fn.restype = C.c_int
+    fn.argtypes = [C.c_char_p, C.POINTER(C.c_float), C.c_size_t, C.c_int, C.c_char_p, C.c_size_t]
+    w = np.ascontiguousarray(w, np.float32)
+    msg = C.create_string_buffer(512)
+    rc = fn(name, w.ctypes.data_as(C.POINTER(C.c_float)), w.size, int(bf16_mode), msg, len(msg))
+    return rc, msg.value.decode()
+
+
+@pytest.mark.parametrize("bf16_mode", [True, False])
+def test_fp16_weight_storage_range_check(lib, bf16_mode):
+    """Weights the device holds in fp16 (bf16 mode: fp16(bf16(w)); fp32 mode:
+    fp16 hi + lo) are range-checked at load: a value beyond 65504, a non-finite
+    value, or a tensor whose values all sit in fp16's subnormal range is
+    rejected with a message naming the tensor; ordinary PyTorch-default inits
+    (down to 1/sqrt(20480) for the widest conv) pass."""
+    rng = np.random.default_rng(0)
+    bound = 1.0 / np.sqrt(20480.0)
+    ok = rng.uniform(-bound, bound, 4096).astype(np.float32)
+    ok[:10] = 0.0  # exact zeros and tiny values inside an ordinary tensor are fine
+    ok[10:20] = 1e-9
+    assert _fp16_check(lib, ok, bf16_mode) == (0, "")
+    # 65504 is fp16's largest value; bf16 rounds it up to 65536, beyond fp16
+    assert _fp16_check(lib, np.array([65504.0, -3.0], np.float32), bf16_mode)[0] == (1 if bf16_mode else 0)
+    big = ok.copy()
+    big[123] = 70000.0
+    rc, msg = _fp16_check(lib, big, bf16_mode)
+    assert rc == 1 and "dp.d0.r0.c1.w" in msg and "65504" in msg and "123" in msg
+    nan = ok.copy()
+    nan[7] = np.nan
+    rc, msg = _fp16_check(lib, nan, bf16_mode)
+    assert rc == 1 and "non-finite" in msg
+    tiny = (ok * 1e-6).astype(np.float32)  # every value below 2^-17: fp16 subnormals only
+    rc, msg = _fp16_check(lib, tiny, bf16_mode)
+    assert rc == 1 and "subnormal" in msg
+
+
+def test_fp16_weight_storage_error_bounds_match_the_documented_split(lib):
+    """fp32 mode's hi / lo pair is within max(2^-22 |w|, 2^-25) of w, so the
+    check accepts a tensor of scale 2^-8 and rejects one of scale 2^-17."""
+    rng = np.random.default_rng(1)
+    w = rng.uniform(-1, 1, 8192).astype(np.float32) * np.float32(2.0 ** -8)
+    assert _fp16_check(lib, w, False)[0] == 0
+    assert _fp16_check(lib, w * np.float32(2.0 ** -9), False)[0] == 1
+
+
+def test_recast_reference_converted_convs_to_bf16(lib, tmp_path):
+    """A file written by the reference converter (the golden fixture, made by
+    its convert/convert.py, which keeps 3-D convs F32) re-emitted with BF16
+    conv weights: every 3-D dp.* tensor becomes the nearest-even bf16 of the
+    original, every other tensor and the metadata are unchanged, the optional
+    batch reservation lands in the metadata, and the loader accepts the file
+    (and rejects a malformed reservation)."""
+    src = REPO / "tests/golden/unet_small.safetensors"
+    dst = tmp_path / "unet_small_bf16conv.safetensors"
+    recast = ck.recast_convs_bf16(src, dst, max_batch=32)
+    before, meta0 = ck.read_safetensors(src)
+    after, meta1 = ck.read_safetensors(dst)
+    convs = [k for k, v in before.items() if v.ndim == 3 and k.startswith("dp.")]
+    assert sorted(recast) == sorted(convs) and len(convs) > 20
+    for k, v in before.items():
+        if k in recast:
+            np.testing.assert_array_equal(after[k], ck.bf16_bits_to_f32(ck.to_bf16_bits(v)))
+        else:
+            np.testing.assert_array_equal(after[k], v)
+    assert meta1 == dict(meta0, **{"flowedge.max_batch": "32"})
+    w = lib.fe_weights_load(str(dst).encode())
+    assert w
+    w_src = lib.fe_weights_load(str(src).encode())
+    assert lib.fe_weights_size_bytes(w) < lib.fe_weights_size_bytes(w_src)
+    lib.fe_weights_free(w)
+    lib.fe_weights_free(w_src)
+    bad = tmp_path / "bad_meta.safetensors"
+    t, m = ck.read_safetensors(src)
+    ck.write_safetensors(bad, t, dict(m, **{"flowedge.max_batch": "0"}))
+    assert not lib.fe_weights_load(str(bad).encode())
+    assert b"flowedge.max_batch" in lib.fe_engine_last_error()
+    with pytest.raises(ValueError):
+        ck.recast_convs_bf16(src, tmp_path / "x.safetensors", max_batch=0)

@@ -3,7 +3,7 @@
 * golden fixtures (tests/golden/): the reference's own outputs on its own
   converted checkpoints - fp32 mode must match within 1e-4..1e-3;
 * the compiled reference core (oracle/_ref) on a PushT-shaped checkpoint
-  (BASELINE config 1) - DDIM-10 actions within max-abs 1e-3 (fp32);
+  (PushT U-Net) - DDIM-10 actions within max-abs 1e-3 (fp32);
 * bf16 mode (this build's added precision) within max-abs 2e-2 of the fp32
   reference, as the north star sets for bf16 weights with fp32 accumulation.
 """
@@ -176,7 +176,7 @@ def _needs_reference():
 
 
 def test_pusht_fp32_ddim10_matches_reference_core(tmp_path):
-    """BASELINE config 1 (PushT U-Net, fp32, batch 1) at full size against the
+    """PushT U-Net (fp32, batch 1) at full size against the
     compiled reference core: epsilon within 1e-4, DDIM-10 actions within 1e-3."""
     _needs_reference()
     tensors, meta = ck.diffusion_tensors(ck.PUSHT, seed=0)
@@ -230,7 +230,7 @@ def test_pusht_bf16_paths_match_reference_on_same_weights(tmp_path):
 
 
 def test_bimanual_c4_bf16_tensor_path_matches_reference_on_same_weights(tmp_path):
-    """BASELINE config 4 (the bench's bimanual U-Net: A14, H64, dims
+    """The bench's bimanual U-Net (A14, H64, dims
     512/1024/2048, 8 groups) in bf16 mode, on bf16-representable weights,
     against the reference core on the same weights: DDIM-10 actions within
     max-abs 2e-2.  Batch 8 x horizon 64 takes the tensor path, where every
@@ -263,7 +263,7 @@ def _round_bf16(tensors):
 
 
 def test_flow_c2_fp32_matches_reference_core(tmp_path):
-    """BASELINE config 2 (flow head 350 / 1024 x 3 / cond 512), fp32, batch 1:
+    """Flow head (350 / 1024 x 3 / cond 512), fp32, batch 1:
     Euler-10 and RK4-4 against the compiled reference core (bar 1e-3)."""
     _needs_reference()
     from oracle import reference
@@ -339,7 +339,7 @@ def _mamba_flow_c3(seed):
 
 
 def test_mamba_c3_fp32_matches_reference_core(tmp_path):
-    """BASELINE config 3 (Mamba 8 x 512, di 1024, ds 16, L = 128) feeding the
+    """Mamba 8 x 512 (di 1024, ds 16, L = 128) feeding the
     C2 flow head, fp32 batch 1, against the compiled reference core."""
     _needs_reference()
     from oracle import reference

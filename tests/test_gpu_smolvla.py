@@ -1,4 +1,4 @@
-"""SmolVLA action expert on the GPU (BASELINE configuration 5 and the
+"""SmolVLA action expert on the GPU (12 heads of 60, 960-wide prefix, and the
 reference's shapes) through the C ABI.
 
 Parity: against the reference's own outputs (golden fixtures, reference
@@ -106,7 +106,7 @@ def test_smolvla_c5_large_batch_matches_restatement(tmp_path):
 
 
 def test_smolvla_c5_full_depth_matches_restatement(tmp_path):
-    """BASELINE configuration 5 at full depth (16 layers), batch 1, Euler-10."""
+    """The SmolVLA-shaped workload at full depth (16 layers), batch 1, Euler-10."""
     spec = ck.SMOLVLA_C5
     tensors, e = _engine(tmp_path, spec, 31)
     model = restate.SmolVLAExpert(tensors)

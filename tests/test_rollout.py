@@ -1,25 +1,40 @@
 """Host-side deployment contract (flowedge_b200/rollout.py): the LeRobot action
-slice and the control-period miss policy of the reference's rollout loop
-(integrations/lerobot/src/flowedge_lerobot/rollout.py:95-124), driven with a fake
-engine, a fake robot and a fake step clock (no GPU)."""
+slice and the control-period miss policy (`--on-miss hold|drop|raise`) of the
+reference's rollout loop (integrations/lerobot/src/flowedge_lerobot/rollout.py:95-124),
+driven with a fake engine that spends time on a fake clock, and a fake robot
+(no GPU)."""
 
 import numpy as np
 import pytest
 
-from flowedge_b200.rollout import DeadlineMissed, DiffusionPolicy, run_rollout
+from flowedge_b200.rollout import ControlLoop, DeadlineMissed, DiffusionPolicy, MissPolicy, run_rollout
 
 META = {"condition_dim": 4, "action_dim": 2, "horizon": 6, "action_steps": 3, "observation_steps": 2}
 
 
+class FakeClock:
+    """Nanosecond clock that only moves when a fake sample call spends time."""
+
+    def __init__(self):
+        self.t = 0
+
+    def __call__(self):
+        return self.t
+
+
 class FakeEngine:
-    """Horizon row t is filled with (seed * 10 + t, condition[0])."""
+    """Horizon row t is filled with (seed * 10 + t, condition[0]); call i takes
+    durations_ms[i] on the fake clock."""
 
     diffusion_metadata = META
 
-    def __init__(self):
+    def __init__(self, clock=None, durations_ms=()):
         self.calls = []
+        self.clock, self.durations = clock, list(durations_ms)
 
     def sample_diffusion_into(self, condition, noise, output, steps=10, scheduler="ddim", seed=0):
+        if self.clock is not None and len(self.calls) < len(self.durations):
+            self.clock.t += int(self.durations[len(self.calls)] * 1e6)
         self.calls.append((steps, scheduler, seed))
         output[:, 0] = seed * 10 + np.arange(output.shape[0])
         output[:, 1] = condition[0]
@@ -42,21 +57,6 @@ class FakeRobot:
         self.events.append("stop")
 
 
-class StepClock:
-    """Each sample call takes the next duration (ms) of `durations`."""
-
-    def __init__(self, durations):
-        self.durations, self.t, self.i, self.n = durations, 0, 0, 0
-
-    def __call__(self):
-        self.n += 1
-        # calls: start, then (t0, t1) per step, then end
-        if self.n > 1 and self.n % 2 == 1 and self.i < len(self.durations):
-            self.t += int(self.durations[self.i] * 1e6)
-            self.i += 1
-        return self.t
-
-
 def test_action_slice_is_the_lerobot_contract():
     eng = FakeEngine()
     pol = DiffusionPolicy(eng)
@@ -76,8 +76,9 @@ def test_action_slice_is_the_lerobot_contract():
 @pytest.mark.parametrize("on_miss", ["hold", "drop"])
 def test_missed_periods_hold_or_drop(on_miss):
     robot = FakeRobot()
-    clock = StepClock([1, 9, 1, 9, 9, 1])  # ms per step; period 5 ms -> steps 1, 3, 4 miss
-    res = run_rollout(DiffusionPolicy(FakeEngine()), robot, lambda obs: obs, steps=6, period_ms=5.0,
+    clock = FakeClock()
+    engine = FakeEngine(clock, [1, 9, 1, 9, 9, 1])  # ms per step; period 5 ms -> steps 1, 3, 4 miss
+    res = run_rollout(DiffusionPolicy(engine), robot, lambda obs: obs, steps=6, period_ms=5.0,
                       on_miss=on_miss, clock_ns=clock)
     assert res.steps == 6 and res.missed_deadlines == 3 and robot.events == ["reset", "stop"]
     if on_miss == "hold":
@@ -94,9 +95,10 @@ def test_missed_periods_hold_or_drop(on_miss):
 
 def test_raise_stops_the_robot():
     robot = FakeRobot()
+    clock = FakeClock()
     with pytest.raises(DeadlineMissed):
-        run_rollout(DiffusionPolicy(FakeEngine()), robot, lambda o: o, steps=4, period_ms=5.0, on_miss="raise",
-                    clock_ns=StepClock([1, 7, 1, 1]))
+        run_rollout(DiffusionPolicy(FakeEngine(clock, [1, 7, 1, 1])), robot, lambda o: o, steps=4, period_ms=5.0,
+                    on_miss="raise", clock_ns=clock)
     assert robot.events == ["reset", "stop"] and len(robot.sent) == 1
 
 
@@ -109,3 +111,17 @@ def test_seeds_noise_and_argument_checks():
                dict(steps=2, diffusion_steps=0)):
         with pytest.raises(ValueError):
             run_rollout(DiffusionPolicy(eng), FakeRobot(), lambda o: o, **kw)
+
+
+def test_hold_before_any_send_holds_zeros_and_report_fields():
+    robot = FakeRobot()
+    clock = FakeClock()
+    loop = ControlLoop(DiffusionPolicy(FakeEngine(clock, [8, 1, 8])), robot, lambda o: o, period_ms=5.0,
+                       clock_ns=clock)
+    rep = loop.run(3, seed=2)
+    np.testing.assert_array_equal(robot.sent[0], [0, 0])  # nothing was sent yet: the held action is zeros
+    assert robot.sent[1][0] == 31 and robot.sent[2][0] == 31  # step 1 (seed 3) sent, then held
+    assert rep.steps == 3 and rep.missed_deadlines == 2 and rep.on_miss == "hold" and rep.stopped
+    assert rep.latencies_ns.tolist() == [8_000_000, 1_000_000, 8_000_000]
+    assert rep.elapsed_ms == pytest.approx(17.0) and rep.max_ms == pytest.approx(8.0)
+    assert MissPolicy("drop") is MissPolicy.DROP

@@ -64,6 +64,38 @@ def test_static_scratch_flow_matches_device_entry_point(golden):
     e.close()
 
 
+@pytest.mark.parametrize("precision", ["fp32", "bf16"])
+def test_static_scratch_runs_past_the_reserved_capacity(precision):
+    """An engine reserved for one row serves 17 rows (the 16-row tile plus a
+    ragged one) from the static array without allocating, and matches the
+    device entry point after that entry point's workspace was grown to 17."""
+    batch, steps = 17, 6
+    rng = np.random.default_rng(17)
+    e = Engine(GOLD, threads=0, device=0, precision=precision, max_batch=1)
+    lib = e.lib
+    cond = torch.from_numpy(rng.standard_normal((batch, 16), dtype=np.float32)).cuda()
+    noise = torch.from_numpy(rng.standard_normal((batch, 6), dtype=np.float32)).cuda()
+    stream = torch.cuda.Stream()
+    got = []
+    before = device_malloc_count()
+    for _ in range(2):
+        out = torch.full_like(noise, float("nan"))
+        rc = lib.fe_engine_sample_condition_static(e.handle, _ptr(cond), _ptr(noise), batch, steps, 2, _ptr(out),
+                                                   C.c_void_p(stream.cuda_stream))
+        assert rc == 0, lib.fe_engine_last_error()
+        stream.synchronize()
+        got.append(out.cpu().numpy())
+    assert device_malloc_count() == before
+    e.reserve_batch(batch)
+    expected = torch.empty_like(noise)
+    assert lib.fe_engine_sample_condition_device(e.handle, _ptr(cond), _ptr(noise), batch, steps, 2, _ptr(expected),
+                                                 C.c_void_p(stream.cuda_stream)) == 0
+    stream.synchronize()
+    for g in got:
+        np.testing.assert_allclose(g, expected.cpu().numpy(), atol=2e-5, rtol=1e-4)
+    e.close()
+
+
 def test_static_scratch_rejects_oversized_requests():
     e = Engine(GOLD, threads=0, device=0, precision="fp32")
     big = 1 << 16  # rows whose scratch cannot fit the 4 MiB array
@@ -74,5 +106,17 @@ def test_static_scratch_rejects_oversized_requests():
     rc = e.lib.fe_engine_sample_condition_static(e.handle, _ptr(cond), _ptr(noise), big, 4, 0, _ptr(out), None)
     assert rc == 2
     assert b"static array" in e.lib.fe_engine_last_error()
+    # a row count whose scratch size would wrap around size_t is rejected the
+    # same way, before any launch (the buffers are never read)
+    huge = (1 << 64) // 8 - 1
+    rc = e.lib.fe_engine_sample_condition_static(e.handle, _ptr(cond), _ptr(noise), huge, 4, 0, _ptr(out), None)
+    assert rc == 2
+    assert b"static array" in e.lib.fe_engine_last_error()
     assert device_malloc_count() == before
+    # the engine's current device is left as the caller had it, and a valid
+    # call after the rejections succeeds (no stale error is reported)
+    assert torch.cuda.current_device() == 0
+    rc = e.lib.fe_engine_sample_condition_static(e.handle, _ptr(cond), _ptr(noise), 2, 4, 0, _ptr(out), None)
+    assert rc == 0, e.lib.fe_engine_last_error()
+    e.synchronize()
     e.close()
