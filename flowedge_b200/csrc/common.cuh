@@ -49,6 +49,7 @@ enum DeviceError : int {
   kErrTmemAlloc = 4,
   kErrGridBarrierTimeout = 5,
   kErrProgramLayout = 6,
+  kErrDependencyTimeout = 7,
 };
 
 // Every mbarrier wait gives up after kWaitNs of wall time (read from the

@@ -173,6 +173,7 @@ const char* device_error_text(int code) noexcept {
     case kErrTmemAlloc: return "tensor memory allocation failed";
     case kErrGridBarrierTimeout: return "a device grid barrier timed out";
     case kErrProgramLayout: return "internal error: small-batch program layout check failed";
+    case kErrDependencyTimeout: return "a small-batch program dependency wait timed out";
     default: return "a device pipeline wait timed out";
   }
 }

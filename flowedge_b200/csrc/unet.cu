@@ -20,6 +20,7 @@
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <deque>
 #include <map>
 #include <numbers>
 #include <tuple>
@@ -209,7 +210,7 @@ class Unet final : public UnetDevice {
   Unet(std::shared_ptr<DeviceContext> ctx, Precision prec) : ctx_(std::move(ctx)), prec_(prec) {}
   ~Unet() override {
     write_trace();
-    if (trace_ != nullptr) cudaFreeHost(trace_);
+    if (trace_ != nullptr) cudaFree(trace_);
     for (auto& [key, g] : graphs_) {
       cudaGraphExecDestroy(g.exec);
       if (g.tables != nullptr) cudaFree(g.tables);
@@ -360,7 +361,8 @@ class Unet final : public UnetDevice {
   struct StreamProg {
     void* dev = nullptr;  // ops, partial-sum buffers, segment tables, barrier words
     const sp::Op* ops = nullptr;
-    unsigned* sync = nullptr;
+    unsigned* sync = nullptr;  // abort word and completion counters, zeroed at every call
+    std::size_t sync_words = 0;
     int n_pre = 0, n_step = 0;
     std::size_t smem = 0;
     bool ok = false;
@@ -368,7 +370,8 @@ class Unet final : public UnetDevice {
   std::map<std::size_t, StreamProg> progs_;
   // FLOWEDGE_PROGRAM_TRACE=<file>: op timeline of the last program call
   // (mapped host memory, CTA 0's global-timer stamps), written at close
-  unsigned long long* trace_ = nullptr;
+  unsigned long long* trace_ = nullptr;  // device stamps (FLOWEDGE_PROGRAM_TRACE)
+  std::size_t trace_bytes_ = 0;
   std::vector<int> trace_kinds_;
   void write_trace() noexcept;
   bool use_stream(std::size_t batch);
@@ -1356,7 +1359,7 @@ namespace {
 // per-step tables of a recorded program: int timestep[steps], then StepScalars[steps]
 std::size_t stream_table_off(std::size_t steps) { return (steps * sizeof(int) + 255) & ~std::size_t(255); }
 
-// CTA whose unit range [U c / NC, U (c + 1) / NC) holds unit u (host twin of sp::cta_of)
+// CTA whose range [U c / NC, U (c + 1) / NC) holds item u (host twin of sp::cta_of)
 int cta_of_host(long long u, long long U, int NC) {
   int c = static_cast<int>((u * NC) / U);
   while (c + 1 < NC && (U * (c + 1)) / NC <= u) ++c;
@@ -1365,12 +1368,33 @@ int cta_of_host(long long u, long long U, int NC) {
 }
 }  // namespace
 
+// One line per (executed op, CTA) of the last traced call: op index, kind
+// (10 + kind for the once-per-call ops), CTA, then the sp::kTracePhases stamps
+// of stream.cuh in ns from the call's first stamp (-1: the CTA had no such
+// phase in that op).
 void Unet::write_trace() noexcept {
   const char* path = std::getenv("FLOWEDGE_PROGRAM_TRACE");
   if (trace_ == nullptr || path == nullptr) return;
+  const std::size_t grid = static_cast<std::size_t>(ctx_->sm_count);
+  constexpr std::size_t kPh = sp::kTracePhases;
+  std::vector<unsigned long long> h(trace_kinds_.size() * grid * kPh);
+  if (cudaMemcpy(h.data(), trace_, h.size() * sizeof(unsigned long long), cudaMemcpyDeviceToHost) != cudaSuccess)
+    return;
+  unsigned long long t0 = ~0ull;
+  for (unsigned long long v : h)
+    if (v != 0) t0 = std::min(t0, v);
   if (std::FILE* f = std::fopen(path, "w")) {
-    for (std::size_t i = 0; i + 1 < trace_kinds_.size() + 1 && trace_[i + 1] != 0; ++i)
-      std::fprintf(f, "%zu %d %llu\n", i, trace_kinds_[i % trace_kinds_.size()], trace_[i + 1] - trace_[i]);
+    for (std::size_t i = 0; i < trace_kinds_.size(); ++i) {
+      if (h[(i * grid) * kPh + kPh - 1] == 0) break;  // past the last executed op
+      for (std::size_t c = 0; c < grid; ++c) {
+        std::fprintf(f, "%zu %d %zu", i, trace_kinds_[i], c);
+        for (std::size_t ph = 0; ph < kPh; ++ph) {
+          const unsigned long long v = h[(i * grid + c) * kPh + ph];
+          std::fprintf(f, " %lld", v == 0 ? -1ll : static_cast<long long>(v - t0));
+        }
+        std::fprintf(f, "\n");
+      }
+    }
     std::fclose(f);
   }
 }
@@ -1396,10 +1420,11 @@ bool Unet::use_stream(std::size_t batch) {
   return it->second.ok;
 }
 
-// Builds the op list of one sampling call for `batch` samples: it mirrors the
-// weight-streaming forward op by op (same buffers, fp32 activations).  Two
-// passes over the same emission code: the first sizes the device buffer, the
-// second fills in its addresses.
+// Builds the op list of one sampling call for `batch` samples (the dataflow
+// program of stream.cuh): the forward of the weight-streaming path conv by
+// conv, with GroupNorm + Mish + FiLM / residual folded into the staging of the
+// conv that reads them.  Two passes over the same emission code: the first
+// sizes the device buffer, the second fills in its addresses.
 bool Unet::build_stream(std::size_t batch, StreamProg& out) {
   const int NC = ctx_->sm_count;
   const int planes = stream_planes(bf16_weights());
@@ -1410,6 +1435,23 @@ bool Unet::build_stream(std::size_t batch, StreamProg& out) {
   int dev_smem_max = 0;
   cudaDeviceGetAttribute(&dev_smem_max, cudaDevAttrMaxSharedMemoryPerBlockOptin, ctx_->device);
   std::size_t total = 0;
+  // a tensor as the convs that read it stage it, and what they wait on
+  struct VT {
+    sp::StageSrc src{};
+    std::vector<sp::Dep> deps;
+  };
+  auto add_deps = [](std::vector<sp::Dep>& into, const std::vector<sp::Dep>& from) {
+    for (const sp::Dep& d : from) {
+      bool have = false;
+      for (sp::Dep& e : into)
+        if (e.ctr == d.ctr) {
+          e.base = std::max(e.base, d.base);
+          e.per_step = std::max(e.per_step, d.per_step);
+          have = true;
+        }
+      if (!have) into.push_back(d);
+    }
+  };
   for (int pass = 0; pass < 2; ++pass) {
     const std::uintptr_t base = reinterpret_cast<std::uintptr_t>(out.dev);
     std::size_t used = 0;
@@ -1423,29 +1465,70 @@ bool Unet::build_stream(std::size_t batch, StreamProg& out) {
       return off;
     };
     auto at = [&](std::size_t off) { return base + off; };
+    // completion counters: one block, zeroed at every call (index 2 is the abort word)
+    constexpr int kCtrBase = 4;
+    constexpr int kMaxCtrs = 252;
+    const std::size_t ctr_off = take((kCtrBase + kMaxCtrs) * sizeof(unsigned));
+    int n_ctrs = 0;
+    auto counter = [&]() {
+      if (n_ctrs >= kMaxCtrs) fits = false;
+      const int i = std::min(n_ctrs++, kMaxCtrs - 1);
+      return reinterpret_cast<unsigned*>(at(ctr_off)) + kCtrBase + i;
+    };
     std::vector<sp::Op> pre, step;
     std::vector<sp::Op>* cur = &pre;
+    bool in_step = false;
+    int next_cta = 0;  // first CTA of the next conv (rotating)
+    unsigned* upd_ctr = counter();
+    unsigned* film_ctr = counter();
+    auto done_dep = [&](unsigned* ctr, int per) {
+      return sp::Dep{ctr, static_cast<unsigned>(per), in_step ? static_cast<unsigned>(per) : 0u};
+    };
+    auto set_deps = [&](sp::Op& op, const std::vector<sp::Dep>& deps) {
+      if (deps.size() > static_cast<std::size_t>(sp::kMaxDeps)) fits = false;
+      op.ndeps = static_cast<int>(std::min<std::size_t>(deps.size(), sp::kMaxDeps));
+      for (int i = 0; i < op.ndeps; ++i) op.deps[i] = deps[static_cast<std::size_t>(i)];
+    };
 
-    auto conv = [&](const ConvDev& c, const std::vector<Act>& srcs, int L_in, int L_out, bool barrier) {
+    auto conv = [&](const ConvDev& c, const std::vector<VT*>& ins, int L_in, int L_out) {
       sp::Op op{};
       op.kind = sp::kOpConv;
-      op.barrier_after = barrier ? 1 : 0;
       sp::ConvOp& o = op.conv;
       o.w = static_cast<const uint4*>(c.sw);
       o.planes = planes;
       o.rbs = c.s_rbs;
       o.ks = c.s_ks;
       o.ic_pad = c.ic_total;
-      o.src0 = static_cast<const float*>(srcs[0].p);
-      o.c0 = srcs[0].C;
-      if (srcs.size() > 1) {
-        o.src1 = static_cast<const float*>(srcs[1].p);
-        o.c1 = srcs[1].C;
+      std::vector<sp::Dep> deps;
+      int csum = 0, gn_c = 0;
+      if (ins.empty() || ins.size() > 2) fits = false;
+      for (std::size_t k = 0; k < ins.size() && k < 2; ++k) {
+        const int C = ins[k]->src.C;
+        if (C < 4 || C % 4 != 0 || ins[k]->src.kind == sp::kSrcNone) {  // also a conv that did not fit
+          fits = false;
+          return VT{};
+        }
+        o.src[k] = ins[k]->src;
+        o.src[k].Cpad = (C + 63) / 64 * 64;  // the staged rows keep the activations' 64-channel padding
+        csum += o.src[k].Cpad;
+        add_deps(deps, ins[k]->deps);
+        if (ins[k]->src.kind == sp::kSrcGn) {
+          // one normalised source, first: its buffer aliases the staged rows
+          if (k != 0) fits = false;
+          gn_c = C;
+          const int groups = ins[k]->src.groups;
+          // stage_gn: a thread owns one channel quad of kGnQuads tokens
+          if (groups < 1 || gn_c % groups != 0 || (gn_c / groups) % 4 != 0 || B * groups > sp::kMaxStats ||
+              gn_c / 4 > sp::kThreads || sp::kThreads % (gn_c / 4) != 0 ||
+              B * L_in > sp::kGnQuads * (sp::kThreads / (gn_c / 4)))
+            fits = false;
+        }
+        if (ins[k]->src.kind == sp::kSrcRaw && ins[k]->src.phases == 2 && L_in % 2 != 0) fits = false;
       }
-      if (o.c0 + o.c1 != o.ic_pad || c.tap_off.empty() || c.tap_off.size() > static_cast<std::size_t>(sp::kMaxTaps) ||
+      if (csum != o.ic_pad || c.tap_off.empty() || c.tap_off.size() > static_cast<std::size_t>(sp::kMaxTaps) ||
           o.ic_pad % 16 != 0 || o.ks < 1 || o.rbs < 1 || c.sw == nullptr) {
         fits = false;
-        return sp::YSrc{};
+        return VT{};
       }
       o.samples = B;
       o.L_in = L_in;
@@ -1462,24 +1545,55 @@ bool Unet::build_stream(std::size_t batch, StreamProg& out) {
       o.rows = L_in + o.halo_lo + std::max(0, (L_out - 1) * o.stride + hi - (L_in - 1));
       o.T = B * L_out;
       if (o.T > sp::kMaxTok) fits = false;
-      const long long U = static_cast<long long>(o.rbs) * o.ks;
-      // CTAs the units are split over: all of them, unless a row block would
-      // then meet more than kMaxSeg CTAs (tiny convs with few row blocks)
-      const int nct = static_cast<int>(
-          std::max<long long>(1, std::min<long long>(NC, static_cast<long long>(o.rbs) * (sp::kMaxSeg - 1))));
+      // units are taken in groups of sp::kGroupBytes (that never cross a tap
+      // or a row block)
+      const int G = sp::kGroupBytes / (planes * 512);
+      if (o.ks % G != 0 || o.ic_pad % (16 * G) != 0) fits = false;
+      const long long gpr = std::max(1, o.ks / G);
+      const long long Ug = static_cast<long long>(o.rbs) * gpr;
+      // CTAs the groups are split over.  With at most as many row blocks as
+      // CTAs, each row block's K goes to s CTAs (s segments), s the smallest
+      // factor that brings a CTA's weights down to what its ring holds or
+      // the largest that keeps s * rbs CTAs (other CTAs stay free to fetch
+      // the next convs' weights); a conv that still leaves a CTA more than its
+      // ring goes to all CTAs.  With more row blocks than CTAs, the largest
+      // divisor of the row blocks up to the CTA count (no row block split),
+      // else all CTAs.
+      const std::size_t row_block_bytes = static_cast<std::size_t>(o.ks) * planes * 512;
+      constexpr std::size_t kRingTarget = std::size_t(4) * sp::kChunk;
+      int nct = o.rbs;
+      if (o.rbs <= NC) {
+        int split = 1;
+        while (o.rbs * (split + 1) <= NC && row_block_bytes / split > kRingTarget && split < static_cast<int>(gpr))
+          ++split;
+        nct = o.rbs * split;
+        // still more than a ring per CTA: every CTA streams a share (row blocks
+        // then meet up to two or three CTAs)
+        if (row_block_bytes / split > kRingTarget && nct < NC) nct = NC;
+      } else {
+        nct = NC;
+        for (int d = NC; d >= NC / 2; --d)
+          if (o.rbs % d == 0) {
+            nct = d;
+            break;
+          }
+      }
+      nct = static_cast<int>(std::min<long long>(nct, Ug));
       o.nct = nct;
+      o.cta0 = next_cta;
+      next_cta = (next_cta + nct) % NC;
       std::vector<int> nseg(static_cast<std::size_t>(o.rbs));
       int seg_max = 1;
       for (int rb = 0; rb < o.rbs; ++rb) {
-        const long long u0 = static_cast<long long>(rb) * o.ks;
-        nseg[static_cast<std::size_t>(rb)] = cta_of_host(u0 + o.ks - 1, U, nct) - cta_of_host(u0, U, nct) + 1;
+        const long long g0 = static_cast<long long>(rb) * gpr;
+        nseg[static_cast<std::size_t>(rb)] = cta_of_host(g0 + gpr - 1, Ug, nct) - cta_of_host(g0, Ug, nct) + 1;
         seg_max = std::max(seg_max, nseg[static_cast<std::size_t>(rb)]);
       }
-      // row blocks one CTA's units meet (a slot per compute warp each)
+      // row blocks one CTA's groups meet (a slot per compute warp each)
       int nslots = 1;
       for (int ci = 0; ci < nct; ++ci) {
-        const long long a = (U * ci) / nct, b = (U * (ci + 1)) / nct;
-        if (b > a) nslots = std::max(nslots, static_cast<int>((b - 1) / o.ks - a / o.ks + 1));
+        const long long a = (Ug * ci) / nct, b = (Ug * (ci + 1)) / nct;
+        if (b > a) nslots = std::max(nslots, static_cast<int>((b - 1) / gpr - a / gpr + 1));
       }
       if (nslots > sp::kMaxSlots) fits = false;
       o.nslots = nslots;
@@ -1489,8 +1603,14 @@ bool Unet::build_stream(std::size_t batch, StreamProg& out) {
       const std::size_t noff = take(static_cast<std::size_t>(o.rbs) * sizeof(int));
       tables.emplace_back(noff, std::move(nseg));
       o.P = reinterpret_cast<float*>(at(poff));
-      // shared memory: staged input (fp16 hi / lo), per-warp slots, then the weight ring
-      const std::size_t head = static_cast<std::size_t>(2) * (B * o.rows + 1) * (o.ic_pad + sp::kRowPad) * 2 +
+      o.done = counter();
+      // shared memory: staged input (fp16 hi / lo; a normalised source's fp32
+      // values alias it), per-warp slots, then the weight ring
+      const std::size_t staged = static_cast<std::size_t>(2) * (B * o.rows + 1) * (o.ic_pad + sp::kRowPad) * 2;
+      // a normalised source's per-quad (double2) sums take as much as its fp32 values
+      const std::size_t temp = static_cast<std::size_t>(B) * L_in * gn_c * sizeof(float);
+      o.slots_off = static_cast<int>((std::max(staged, temp) + 127) & ~std::size_t(127));
+      const std::size_t head = static_cast<std::size_t>(o.slots_off) +
                                static_cast<std::size_t>(sp::kComputeWarps) * nslots * 16 * o.T * sizeof(float) +
                                static_cast<std::size_t>(sp::kWarps) * nslots * sizeof(int);
       o.ring_off = static_cast<int>((head + 127) & ~std::size_t(127));
@@ -1498,123 +1618,148 @@ bool Unet::build_stream(std::size_t batch, StreamProg& out) {
       // as many stages as the launch's shared memory (sized in the first pass) leaves
       o.stages = pass == 0 ? sp::kMinStages
                            : static_cast<int>(std::min<std::size_t>(sp::kMaxStages, (out.smem - o.ring_off) / sp::kChunk));
+      set_deps(op, deps);
       cur->push_back(op);
-      sp::YSrc y{};
-      y.P = o.P;
-      y.nseg = reinterpret_cast<const int*>(at(noff));
-      y.bias = c.bias;
-      y.ks = o.ks;
-      y.units = U;
-      y.seg_max = seg_max;
-      y.T = o.T;
+      const sp::Dep mine = done_dep(o.done, nct);
+      // a block output is written out by its first consumer; later ones read that copy
+      for (VT* in : ins)
+        if (in->src.kind == sp::kSrcGn && in->src.materialize != nullptr) {
+          VT m;
+          m.src.kind = sp::kSrcMat;
+          m.src.C = in->src.C;
+          m.src.mat = in->src.materialize;
+          m.deps = {mine};
+          *in = m;
+        }
+      VT y;
+      y.src.kind = sp::kSrcRaw;
+      y.src.C = c.oc;
+      y.src.phases = 1;
+      y.src.raw[0] = sp::RawSrc{o.P, reinterpret_cast<const int*>(at(noff)), c.bias, seg_max, o.T};
+      y.deps = {mine};
       return y;
     };
-    auto gn = [&](const sp::YSrc& y, int C, int groups, int L, const float* gamma, const float* beta,
-                  const BlockDev* film_blk, int res_mode, const sp::YSrc* res, const void* res_tensor, void* dst) {
-      if ((C / groups) * L > sp::kGnPerThread * sp::kThreads) fits = false;
-      sp::Op op{};
-      op.kind = sp::kOpGn;
-      op.barrier_after = 1;
-      sp::GnOp& o = op.gn;
-      o.y = y;
-      o.C = C;
-      o.groups = groups;
-      o.samples = B;
-      o.L = L;
-      o.gamma = gamma;
-      o.beta = beta;
+    // mish(GroupNorm(y)) with FiLM or a residual, as its consumer stages it
+    auto gn = [&](const VT& y, const float* gamma, const float* beta, int groups, const BlockDev* film_blk,
+                  const VT* res, void* materialize) {
+      VT v;
+      v.src.kind = sp::kSrcGn;
+      v.src.C = y.src.C;
+      v.src.raw[0] = y.src.raw[0];
+      v.src.gamma = gamma;
+      v.src.beta = beta;
+      v.src.groups = groups;
+      v.deps = y.deps;
+      if (y.src.kind != sp::kSrcRaw || y.src.phases != 1) fits = false;
       if (film_blk != nullptr) {
-        o.film = 1;
-        o.film_cond = film_cond_;
-        o.film_time = film_time_;
-        o.film_F = F_;
-        o.film_off = film_blk->film_off;
+        v.src.film = 1;
+        v.src.film_off = film_blk->film_off;
+        add_deps(v.deps, {sp::Dep{film_ctr, static_cast<unsigned>(NC), 0u}});
       }
-      o.res_mode = res_mode;
-      if (res != nullptr) o.res = *res;
-      o.res_tensor = static_cast<const float*>(res_tensor);
-      o.out = static_cast<float*>(dst);
-      cur->push_back(op);
+      if (res != nullptr) {
+        if (res->src.kind == sp::kSrcRaw && res->src.phases == 1) {
+          v.src.res_kind = 1;
+          v.src.res = res->src.raw[0];
+        } else if (res->src.kind == sp::kSrcMat) {
+          v.src.res_kind = 2;
+          v.src.mat = res->src.mat;
+        } else {
+          fits = false;
+        }
+        if (res->src.C != v.src.C) fits = false;
+        add_deps(v.deps, res->deps);
+      }
+      v.src.materialize = static_cast<float*>(materialize);
+      return v;
     };
-    auto reduce = [&](const sp::YSrc& y, int M, int L, int tmul, int tadd, void* dst, bool barrier) {
-      sp::Op op{};
-      op.kind = sp::kOpReduce;
-      op.barrier_after = barrier ? 1 : 0;
-      op.reduce.y = y;
-      op.reduce.M = M;
-      op.reduce.L = L;
-      op.reduce.tmul = tmul;
-      op.reduce.tadd = tadd;
-      op.reduce.out = static_cast<float*>(dst);
-      cur->push_back(op);
-    };
-    auto block = [&](const BlockDev& blk, const std::vector<Act>& in, int L, Act o) {
-      const int oc = blk.oc;
-      const sp::YSrc y1 = conv(blk.c1, in, L, L, true);
-      gn(y1, oc, G, L, blk.g1, blk.b1, &blk, 0, nullptr, nullptr, h1_);
-      sp::YSrc yr{};
-      if (blk.has_res) yr = conv(blk.res, in, L, L, false);
-      const sp::YSrc y2 = conv(blk.c2, {Act{h1_, oc, L}}, L, L, true);
-      if (blk.has_res) gn(y2, oc, G, L, blk.g2, blk.b2, nullptr, 1, &yr, nullptr, o.p);
-      else gn(y2, oc, G, L, blk.g2, blk.b2, nullptr, 2, nullptr, in[0].p, o.p);
+    auto block = [&](const BlockDev& blk, const std::vector<VT*>& in, int L, void* dst) {
+      const VT y1 = conv(blk.c1, in, L, L);
+      VT yr;
+      if (blk.has_res) yr = conv(blk.res, in, L, L);
+      VT h1 = gn(y1, blk.g1, blk.b1, G, &blk, nullptr, nullptr);
+      const VT y2 = conv(blk.c2, {&h1}, L, L);
+      if (!blk.has_res && in.size() != 1) fits = false;
+      return gn(y2, blk.g2, blk.b2, G, nullptr, blk.has_res ? &yr : in[0], dst);
     };
 
     // once per call: FiLM condition part W_c * mish(cond) + b -> film_cond_
-    const sp::YSrc yf = conv(film_, {Act{mcond_, cond_pad_, 1}}, 1, 1, true);
-    reduce(yf, F_, 1, 1, 0, film_cond_, true);
+    {
+      VT mc;
+      mc.src.kind = sp::kSrcMat;
+      mc.src.C = cond_pad_;
+      mc.src.mat = static_cast<const float*>(mcond_);
+      const VT yf = conv(film_, {&mc}, 1, 1);
+      sp::Op op{};
+      op.kind = sp::kOpReduce;
+      op.reduce.y = yf.src.raw[0];
+      op.reduce.M = F_;
+      op.reduce.T = B;
+      op.reduce.out = film_cond_;
+      op.reduce.done = film_ctr;
+      set_deps(op, yf.deps);
+      pre.push_back(op);
+    }
     // every step: the forward and the update
     cur = &step;
+    in_step = true;
+    std::deque<VT> keep;  // tensors referred to later (skips), at stable addresses
     std::size_t li = 0;
     int L = H;
-    Act x{x_in_, cin_pad_, H};
-    std::vector<Act> skips(static_cast<std::size_t>(S));
+    keep.emplace_back();
+    keep.back().src.kind = sp::kSrcMat;
+    keep.back().src.C = cin_pad_;
+    keep.back().src.mat = static_cast<const float*>(x_in_);
+    keep.back().deps = {sp::Dep{upd_ctr, 0u, 1u}};  // step s reads the input the update of step s - 1 wrote
+    VT* x = &keep.back();
+    std::vector<VT*> skips(static_cast<std::size_t>(S));
     for (int st = 0; st < S; ++st) {
-      const int oc = static_cast<int>(cfg_.dims[static_cast<std::size_t>(st)]);
-      const Act o0{acts_[li], oc, L}, o1{acts_[li + 1], oc, L};
+      keep.push_back(block(down_[static_cast<std::size_t>(st)][0], {x}, L, acts_[li]));
+      VT* o0 = &keep.back();
+      keep.push_back(block(down_[static_cast<std::size_t>(st)][1], {o0}, L, acts_[li + 1]));
       li += 2;
-      block(down_[static_cast<std::size_t>(st)][0], {x}, L, o0);
-      block(down_[static_cast<std::size_t>(st)][1], {o0}, L, o1);
-      skips[static_cast<std::size_t>(st)] = o1;
-      x = o1;
+      skips[static_cast<std::size_t>(st)] = x = &keep.back();
       if (st + 1 < S) {
-        const Act d{acts_[li++], oc, L / 2};
-        const sp::YSrc yd = conv(ds_[static_cast<std::size_t>(st)], {x}, L, L / 2, true);
-        reduce(yd, oc, L / 2, 1, 0, d.p, true);
-        x = d;
+        keep.push_back(conv(ds_[static_cast<std::size_t>(st)], {x}, L, L / 2));
+        x = &keep.back();
+        ++li;
         L /= 2;
       } else {
         ++li;
       }
     }
     for (int m = 0; m < 2; ++m) {
-      const Act o{acts_[li++], x.C, L};
-      block(mid_[static_cast<std::size_t>(m)], {x}, L, o);
-      x = o;
+      keep.push_back(block(mid_[static_cast<std::size_t>(m)], {x}, L, acts_[li++]));
+      x = &keep.back();
     }
     for (int st = 0; st + 1 < S; ++st) {
-      const Act skip = skips[static_cast<std::size_t>(S - 1 - st)];
-      const int low = static_cast<int>(cfg_.dims[static_cast<std::size_t>(S - 2 - st)]);
-      const Act o0{acts_[li], low, L}, o1{acts_[li + 1], low, L};
-      li += 2;
-      block(up_[static_cast<std::size_t>(st)][0], {x, skip}, L, o0);
-      block(up_[static_cast<std::size_t>(st)][1], {o0}, L, o1);
-      const Act u{acts_[li++], low, 2 * L};
-      const sp::YSrc y0 = conv(us_[static_cast<std::size_t>(st)][0], {o1}, L, L, false);
-      const sp::YSrc y1 = conv(us_[static_cast<std::size_t>(st)][1], {o1}, L, L, true);
-      reduce(y0, low, L, 2, 0, u.p, false);
-      reduce(y1, low, L, 2, 1, u.p, true);
-      x = u;
+      VT* skip = skips[static_cast<std::size_t>(S - 1 - st)];
+      keep.push_back(block(up_[static_cast<std::size_t>(st)][0], {x, skip}, L, acts_[li]));
+      VT* o0 = &keep.back();
+      keep.push_back(block(up_[static_cast<std::size_t>(st)][1], {o0}, L, acts_[li + 1]));
+      VT* o1 = &keep.back();
+      li += 3;
+      const VT y0 = conv(us_[static_cast<std::size_t>(st)][0], {o1}, L, L);
+      const VT y1 = conv(us_[static_cast<std::size_t>(st)][1], {o1}, L, L);
+      keep.emplace_back();
+      VT& u = keep.back();
+      u.src.kind = sp::kSrcRaw;
+      u.src.C = y0.src.C;
+      u.src.phases = 2;
+      u.src.raw[0] = y0.src.raw[0];
+      u.src.raw[1] = y1.src.raw[0];
+      u.deps = y0.deps;
+      add_deps(u.deps, y1.deps);
+      x = &u;
       L *= 2;
     }
-    const int c0 = static_cast<int>(cfg_.dims[0]);
-    const sp::YSrc yc = conv(fc_, {x}, H, H, true);
-    gn(yc, c0, static_cast<int>(kFinalNormGroups), H, fn_g_, fn_b_, nullptr, 0, nullptr, nullptr, h1_);
-    const sp::YSrc ye = conv(fo_s_, {Act{h1_, c0, H}}, H, H, true);
+    const VT yc = conv(fc_, {x}, H, H);
+    VT hf = gn(yc, fn_g_, fn_b_, static_cast<int>(kFinalNormGroups), nullptr, nullptr, nullptr);
+    const VT ye = conv(fo_s_, {&hf}, H, H);
     {
       sp::Op op{};
       op.kind = sp::kOpUpdate;
-      op.barrier_after = 1;
-      op.update.y = ye;
+      op.update.y = ye.src.raw[0];
+      op.update.cta = next_cta;  // a CTA outside the output conv's
       op.update.A = A;
       op.update.H = H;
       op.update.Cin = cin_pad_;
@@ -1622,6 +1767,8 @@ bool Unet::build_stream(std::size_t batch, StreamProg& out) {
       op.update.x_master = x_master_;
       op.update.x_in = static_cast<float*>(x_in_);
       op.update.seeds = seeds_;
+      op.update.done = upd_ctr;
+      set_deps(op, ye.deps);
       step.push_back(op);
     }
     // L2 prefetch chain: each conv names the next conv's weights (the last
@@ -1640,11 +1787,11 @@ bool Unet::build_stream(std::size_t batch, StreamProg& out) {
     }
     const std::size_t n_ops = pre.size() + step.size();
     const std::size_t ops_off = take(n_ops * sizeof(sp::Op));
-    const std::size_t sync_off = take(4 * sizeof(unsigned));
     if (pass == 0) {
       // use all the shared memory a CTA may have: deeper rings for the smaller convs
-      if (!fits || smem > static_cast<std::size_t>(dev_smem_max) - 1024) return false;
-      smem = std::max(smem, static_cast<std::size_t>(dev_smem_max) - 1024);
+      constexpr std::size_t kStaticSmem = 4096;  // the kernel's static shared memory (2.8 KB), with margin
+      if (!fits || smem > static_cast<std::size_t>(dev_smem_max) - kStaticSmem) return false;
+      smem = std::max(smem, static_cast<std::size_t>(dev_smem_max) - kStaticSmem);
       total = used;
       if (counted_malloc(&out.dev, total) != cudaSuccess) {
         cudaGetLastError();
@@ -1662,19 +1809,21 @@ bool Unet::build_stream(std::size_t batch, StreamProg& out) {
     for (const auto& [off, tab] : tables) cudaMemcpy(dev + off, tab.data(), tab.size() * sizeof(int), cudaMemcpyHostToDevice);
     out.ops = reinterpret_cast<const sp::Op*>(dev + ops_off);
     if (std::getenv("FLOWEDGE_PROGRAM_TRACE") != nullptr && trace_ == nullptr) {
-      // one stamp per op of a call of up to train_timesteps steps
-      const std::size_t n = 2 + pre.size() + cfg_.train_timesteps * step.size();
-      if (cudaHostAlloc(reinterpret_cast<void**>(&trace_), n * sizeof(unsigned long long), cudaHostAllocMapped) !=
-          cudaSuccess)
+      // stamps per (op, CTA) of a call of up to train_timesteps steps
+      const std::size_t n =
+          (pre.size() + cfg_.train_timesteps * step.size()) * static_cast<std::size_t>(NC) * sp::kTracePhases;
+      trace_bytes_ = n * sizeof(unsigned long long);
+      if (cudaMalloc(reinterpret_cast<void**>(&trace_), trace_bytes_) != cudaSuccess) {
+        cudaGetLastError();
         trace_ = nullptr;
-      else
-        std::memset(trace_, 0, n * sizeof(unsigned long long));
+      }
       trace_kinds_.clear();
       for (const auto& op : pre) trace_kinds_.push_back(10 + op.kind);
       for (std::size_t r = 0; r < cfg_.train_timesteps; ++r)
         for (const auto& op : step) trace_kinds_.push_back(op.kind);
     }
-    out.sync = reinterpret_cast<unsigned*>(dev + sync_off);
+    out.sync = reinterpret_cast<unsigned*>(dev + ctr_off);
+    out.sync_words = static_cast<std::size_t>(kCtrBase + n_ctrs);
     out.n_pre = static_cast<int>(pre.size());
     out.n_step = static_cast<int>(step.size());
   }
@@ -1705,7 +1854,7 @@ bool Unet::record_stream(std::size_t batch, std::size_t steps, const void* table
   launch(prep_cond_kernel, dim3(ew_grid(static_cast<long long>(batch) * cond_pad_, 256, *ctx_)), dim3(256), 0, st,
          static_cast<const float*>(in_cond_), static_cast<int>(batch), static_cast<int>(cfg_.condition_dim),
          mcond_, cond_pad_, 0);
-  cudaMemsetAsync(pg.sync, 0, 4 * sizeof(unsigned), st);
+  cudaMemsetAsync(pg.sync, 0, pg.sync_words * sizeof(unsigned), st);
   sp::Program prog{};
   prog.ops = pg.ops;
   prog.n_pre = pg.n_pre;
@@ -1713,9 +1862,13 @@ bool Unet::record_stream(std::size_t batch, std::size_t steps, const void* table
   prog.steps = static_cast<int>(steps);
   prog.step_t = static_cast<const int*>(tables);
   prog.scalars = reinterpret_cast<const StepScalars*>(static_cast<const char*>(tables) + stream_table_off(steps));
+  prog.film_cond = film_cond_;
+  prog.film_time = film_time_;
+  prog.film_F = F_;
   prog.sync = pg.sync;
   prog.err = ctx_->d_err;
   prog.trace = trace_;
+  if (trace_ != nullptr) cudaMemsetAsync(trace_, 0, trace_bytes_, st);
   cudaLaunchAttribute attr{};
   attr.id = cudaLaunchAttributeCooperative;
   attr.val.cooperative = 1;
