@@ -239,12 +239,17 @@ __device__ __forceinline__ float y_at(const RawSrc& y, int n, int m) {
   return v;
 }
 
-// The same for the four channels m .. m + 3 (m a multiple of 4): the segment
-// layout keeps them in one 16-byte vector; the sums are y_at's, per channel.
+// The bias quad of channels m .. m + 3 (zeros without a bias).
+__device__ __forceinline__ float4 bias_quad(const RawSrc& y, int m) {
+  return y.bias != nullptr ? __ldg(reinterpret_cast<const float4*>(y.bias + m)) : make_float4(0.f, 0.f, 0.f, 0.f);
+}
+
+// The same for the four channels m .. m + 3 (m a multiple of 4), starting
+// from the bias quad `v`: the segment layout keeps them in one 16-byte
+// vector; the sums are y_at's, per channel.
 template <int SEG>
-__device__ __forceinline__ float4 y_quad(const RawSrc& y, int n, int m) {
+__device__ __forceinline__ float4 y_quad_from(const RawSrc& y, int n, int m, float4 v) {
   const int rb = m >> 4;
-  float4 v = y.bias != nullptr ? __ldg(reinterpret_cast<const float4*>(y.bias + m)) : make_float4(0.f, 0.f, 0.f, 0.f);
   const float* p = y.P + ((static_cast<long long>(rb) * y.seg_max) * y.T + n) * 16 + (m & 15);
   const long long stride = static_cast<long long>(y.T) * 16;
   float4 t[SEG];
@@ -260,6 +265,11 @@ __device__ __forceinline__ float4 y_quad(const RawSrc& y, int n, int m) {
       v.w += t[s].w;
     }
   return v;
+}
+
+template <int SEG>
+__device__ __forceinline__ float4 y_quad(const RawSrc& y, int n, int m) {
+  return y_quad_from<SEG>(y, n, m, bias_quad(y, m));
 }
 
 // Trace stamp `phase` of the executed op `exec` (FLOWEDGE_PROGRAM_TRACE)
@@ -421,6 +431,14 @@ __device__ __noinline__ void stage_gn(int si, int off, int step, int rel, int ex
   const float4 be = __ldg(reinterpret_cast<const float4*>(s.beta + c));
   const float4 ts = s.film ? __ldg(reinterpret_cast<const float4*>(ft + c)) : zero4;
   const float4 th = s.film ? __ldg(reinterpret_cast<const float4*>(ft + C + c)) : zero4;
+  // the thread's channel quad is the same for all its tokens: its bias, and
+  // (batch 1) its FiLM condition rows, are loaded once
+  const float4 yb = bias_quad(s.raw[0], c);
+  const float4 rb = s.res_kind == 1 ? bias_quad(s.res, c) : zero4;
+  const bool one_sample = op.samples == 1;
+  const float* fc0 = s.film ? sp_pg.film_cond + s.film_off : nullptr;
+  const float4 fs0 = s.film && one_sample ? __ldcg(reinterpret_cast<const float4*>(fc0 + c)) : zero4;
+  const float4 fh0 = s.film && one_sample ? __ldcg(reinterpret_cast<const float4*>(fc0 + C + c)) : zero4;
   // y: conv values; a1 / a2: the FiLM condition rows (scale / shift), or a1 the residual
   float4 y[kGnQuads], a1[kGnQuads], a2[kGnQuads];
 #pragma unroll
@@ -430,13 +448,18 @@ __device__ __noinline__ void stage_gn(int si, int off, int step, int rel, int ex
       const int n = n0 + j * dn;
       y[j] = a1[j] = a2[j] = zero4;
       if (n < T_in) {
-        y[j] = y_quad<SEG>(s.raw[0], n, c);
+        y[j] = y_quad_from<SEG>(s.raw[0], n, c, yb);
         if (s.film) {
-          const float* fc = sp_pg.film_cond + static_cast<long long>(n / L) * F + s.film_off;
-          a1[j] = __ldcg(reinterpret_cast<const float4*>(fc + c));
-          a2[j] = __ldcg(reinterpret_cast<const float4*>(fc + C + c));
+          if (one_sample) {
+            a1[j] = fs0;
+            a2[j] = fh0;
+          } else {
+            const float* fc = fc0 + static_cast<long long>(n / L) * F;
+            a1[j] = __ldcg(reinterpret_cast<const float4*>(fc + c));
+            a2[j] = __ldcg(reinterpret_cast<const float4*>(fc + C + c));
+          }
         } else if (s.res_kind == 1) {
-          a1[j] = y_quad<SEG>(s.res, n, c);
+          a1[j] = y_quad_from<SEG>(s.res, n, c, rb);
         } else if (s.res_kind == 2) {
           a1[j] = __ldcg(reinterpret_cast<const float4*>(s.mat + static_cast<long long>(n) * C + c));
         }
@@ -876,7 +899,7 @@ __device__ __noinline__ bool run_conv(int step, int exec) {
     if (rbi < nslots)
       for (int w = 1; w < kWarps; ++w)
         if (touched[w * nslots + rbi]) v += slots[((w - 1) * nslots + rbi) * slot_floats + e];
-    const int seg = cta - cta_of(static_cast<long long>(rb) * gpr, Ug, NC);
+    const int seg = op.seg_max == 1 ? 0 : cta - cta_of(static_cast<long long>(rb) * gpr, Ug, NC);
     const int m = e / T, n = e - m * T;
     op.P[((static_cast<long long>(rb) * op.seg_max + seg) * T + n) * 16 + m] = v;
   }
