@@ -210,6 +210,9 @@ static __global__ void __launch_bounds__(THREADS, 1)
   if (warp == 0) {
     // ---------------- TMA producer ----------------
     if (lane == 0) {
+      // the weights (A) are read by every N tile: keep them in L2 past the
+      // streaming activations and residuals
+      const uint64_t keep_a = l2_policy_evict_last();
       uint32_t kb_iter = 0;
       uint32_t armed = 0, armed_phase = 0;  // per-stage bits: armed at least once / parity of its last arm
       bool ok = true;
@@ -231,7 +234,7 @@ static __global__ void __launch_bounds__(THREADS, 1)
             mbar_arrive_expect_tx(&full[stage], STAGE_BYTES);
             armed |= 1u << stage;
             armed_phase = (armed_phase & ~(1u << stage)) | (phase << stage);
-            tma_load_2d(a_dst, &tmA, sg.a_k + kb * BK, m_blk * BM, &full[stage]);
+            tma_load_2d_hint(a_dst, &tmA, sg.a_k + kb * BK, m_blk * BM, &full[stage], keep_a);
             tma_load_3d(b_dst, mapB, sg.ch_off + kb * BK, sg.t_off, n_blk * p.tile_samples, &full[stage]);
           }
         }
