@@ -52,9 +52,9 @@ SEED = 0
 # of this script's first forward:
 #   FLOWEDGE_BENCH_BATCH=<shard> ncu --metrics gpu__time_duration.sum,dram__bytes_read.sum,dram__bytes_write.sum
 #       --clock-control none -k regex:tc_gemm -c 80 --csv --log-file traffic.csv
-#       python bench.py --steps 1 --warmup 1 --no-cpu-baseline --no-extras
+#       python bench.py --steps 1 --warmup 1 --no-cpu-baseline --no-extras --no-parity
 # (launches 1-36 after the FiLM-condition GEMM).  Other shard sizes report null.
-CONV_TRAFFIC_PER_FORWARD = {4096: 35.45e9, 1024: 7.26e9}
+CONV_TRAFFIC_PER_FORWARD = {4096: 34.79e9, 1024: 7.26e9}
 
 
 def _dist():
