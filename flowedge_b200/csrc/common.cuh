@@ -50,6 +50,7 @@ enum DeviceError : int {
   kErrGridBarrierTimeout = 5,
   kErrProgramLayout = 6,
   kErrDependencyTimeout = 7,
+  kErrStageTimeout = 8,
 };
 
 // Every mbarrier wait gives up after kWaitNs of wall time (read from the
@@ -110,6 +111,15 @@ __device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t pari
       : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns)
       : "memory");
   return ok != 0;
+}
+
+// Bulk copy of `bytes` (a multiple of 16; both addresses 16-byte aligned)
+// from global to this CTA's shared memory, completing on `bar`'s tx count.
+__device__ __forceinline__ void bulk_load_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   smem_u32(dst)),
+               "l"(src), "r"(bytes), "r"(smem_u32(bar))
+               : "memory");
 }
 
 // Bounded wait: returns false (and never hangs) once kWaitNs elapsed or
@@ -446,6 +456,33 @@ __device__ __forceinline__ float ex2_approx(float x) {
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
 }
+// 2^x for a pair of x <= 0 on the FMA pipe, so that a kernel bound by the
+// MUFU unit can move some of its exponentials off it.  Range reduction
+// x = k + r, k = round(x), r in [-0.5, 0.5], by the 1.5 * 2^23 rounding
+// constant (its low mantissa bits then hold k); 2^r by the degree-5
+// Chebyshev interpolant of 2^r on [-0.5, 0.5] in monomial form (nodes of
+// degree 5, coefficients rounded to fp32; max relative error 2.4e-7 over the
+// interval in fp32 Horner evaluation, against ex2.approx's 2^-22); 2^k added
+// to the exponent field.  x is clamped at -125 so the exponent stays normal;
+// 2^-125 stands in for the flushed-to-zero values of ex2.approx.ftz below it.
+__device__ __forceinline__ float2 exp2_poly2(float2 x) {
+  constexpr float kRound = 12582912.0f;  // 1.5 * 2^23
+  x.x = fmaxf(x.x, -125.0f);
+  x.y = fmaxf(x.y, -125.0f);
+  const float2 t = __fadd2_rn(x, make_float2(kRound, kRound));
+  const float2 k = __fadd2_rn(t, make_float2(-kRound, -kRound));
+  const float2 r = __ffma2_rn(k, make_float2(-1.0f, -1.0f), x);
+  float2 p = __ffma2_rn(make_float2(1.3390863e-3f, 1.3390863e-3f), r, make_float2(9.6760318e-3f, 9.6760318e-3f));
+  p = __ffma2_rn(p, r, make_float2(5.5503570e-2f, 5.5503570e-2f));
+  p = __ffma2_rn(p, r, make_float2(2.4022107e-1f, 2.4022107e-1f));
+  p = __ffma2_rn(p, r, make_float2(6.9314718e-1f, 6.9314718e-1f));
+  p = __ffma2_rn(p, r, make_float2(1.0000001f, 1.0000001f));
+  // the low 9 bits of kRound's encoding are zero, so t's bits shifted by 23
+  // are k in the exponent field
+  return make_float2(__int_as_float(__float_as_int(p.x) + (__float_as_int(t.x) << 23)),
+                     __int_as_float(__float_as_int(p.y) + (__float_as_int(t.y) << 23)));
+}
+
 __device__ __forceinline__ float softplus_f(float x) { return fmaxf(x, 0.0f) + log1pf(expf(-fabsf(x))); }
 
 __device__ __forceinline__ float half_lo(uint32_t packed) {

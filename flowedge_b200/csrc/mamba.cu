@@ -282,6 +282,235 @@ __global__ void __launch_bounds__(256) scan_kernel(const float* dbl, int wd, con
     for (int n = 0; n < DS; ++n) state[(static_cast<long long>(b) * DS + n) * di + c] = h[n];
 }
 
+// Selective scan for many sequences with staged inputs: one thread per
+// (sequence, channel) as in scan_kernel, one CTA per (sequence, kScanThreads
+// channels).  The sequence's [dt_in | B | C] rows and the CTA's u and z
+// columns arrive by bulk copies in tiles of kScanTile steps, two tiles in
+// flight.  A tile runs in two passes per thread:
+//   A. for every step of the tile (independent of the state, so the steps
+//      overlap): dt = softplus(dt_in . W_dt + b_dt) into the thread's slot of
+//      a per-CTA buffer, the gate SiLU(z) over z in the stage;
+//   B. the recurrence h_n = exp(dt A_n) h_n + dt B_n u, y = (D u + sum_n h_n
+//      C_n) * gate, step after step.
+// No CTA barrier per tile: each warp counts itself done with a stage on a
+// shared-memory counter, and the warp that completes the count requests the
+// stage's next tile.  Every warp waits on every tile's full barrier, so none
+// runs more than one tile ahead of the slowest.
+// FAST (the bf16 mode) runs on packed fp32 pairs (FFMA2 / FMUL2): the dt dot
+// product as two interleaved pair sums, the states two at a time, sum_n h_n
+// C_n as two pair sums, dt B u as (dt u) B; POLY of the DS / 2 state pairs take
+// their exponential from exp2_poly2 on the FMA pipe rather than the MUFU unit,
+// which carries the other 14 state exponentials and the 4 of softplus and
+// SiLU per (token, channel).  The fp32 mode (!FAST) evaluates scan_kernel's
+// expressions in scan_kernel's order.  y (fp32) is written only when given:
+// the tensor-core out-projection reads the 16-bit copy.  A full-barrier wait
+// that times out records kErrStageTimeout and ends every warp's loop; the
+// CTA waits (bounded) for the copies it issued and returns.
+constexpr int kScanTile = 16;
+constexpr int kScanThreads = 256;
+constexpr int kScanWarps = kScanThreads / 32;
+constexpr int kScanPolyPairs = 1;  // state pairs of the 16-state bf16 scan on exp2_poly2
+
+// floats of one stage ([kScanTile][dr + 2 ds] dbl rows, then u and z
+// [kScanTile][kScanThreads]), and of the whole dynamic shared memory (two
+// stages and the dt buffer [kScanTile][kScanThreads])
+__host__ __device__ constexpr int scan_stage_floats(int ds, int dr) {
+  return kScanTile * (dr + 2 * ds + 2 * kScanThreads);
+}
+__host__ __device__ constexpr int scan_smem_floats(int ds, int dr) {
+  return 2 * scan_stage_floats(ds, dr) + kScanTile * kScanThreads;
+}
+
+template <int DS, int DR, bool FAST, int POLY>
+__global__ void __launch_bounds__(kScanThreads, 2)
+    scan_staged_kernel(const float* __restrict__ dbl, const float* __restrict__ u, const float* __restrict__ xz, int L,
+                       int di, const float* __restrict__ dt_w, const float* __restrict__ dt_b,
+                       const float* __restrict__ a_neg, const float* __restrict__ dsk, float* __restrict__ y,
+                       __half* __restrict__ y_bf, int split, int* err) {
+  static_assert(DR % 4 == 0 && DS % 4 == 0 && POLY >= 0 && POLY <= DS / 2, "rows are read as float4");
+  constexpr int WD = DR + 2 * DS;
+  constexpr int kStage = scan_stage_floats(DS, DR);
+  extern __shared__ __align__(128) float sst[];
+  float* sdt = sst + 2 * kStage;  // [kScanTile][kScanThreads] dt of the current tile, per thread
+  __shared__ uint64_t full[2];
+  __shared__ int done_warps[2], last_req[2], abort_word, zero_word;
+  const int b = blockIdx.y, c0 = blockIdx.x * kScanThreads, tid = threadIdx.x, lane = tid & 31;
+  const int nch = min(kScanThreads, di - c0);
+  const int c = c0 + tid;
+  const long long tok0 = static_cast<long long>(b) * L;
+  const int ntiles = (L + kScanTile - 1) / kScanTile;
+  if (tid == 0) {
+    mbar_init(&full[0], 1);
+    mbar_init(&full[1], 1);
+    done_warps[0] = done_warps[1] = 0;
+    last_req[0] = last_req[1] = -1;
+    abort_word = zero_word = 0;
+    fence_mbar_init();
+  }
+  __syncthreads();
+  // one warp: tile `tile` into stage tile % 2 (lane 0 the dbl rows, lane j
+  // the u and z row slices of step j; 16-byte aligned since di % 4 == 0)
+  auto request = [&](int tile) {
+    const int s = tile & 1, t0 = tile * kScanTile, n = min(kScanTile, L - t0);
+    float* sd = sst + s * kStage;
+    float* su = sd + kScanTile * WD;
+    float* sz = su + kScanTile * kScanThreads;
+    if (lane == 0) {
+      last_req[s] = tile;
+      mbar_arrive_expect_tx(&full[s], static_cast<uint32_t>(n * WD * 4 + 2 * n * nch * 4));
+    }
+    __syncwarp();
+    if (lane == 0) bulk_load_g2s(sd, dbl + (tok0 + t0) * WD, static_cast<uint32_t>(n * WD * 4), &full[s]);
+    if (lane < n) {
+      const long long tok = tok0 + t0 + lane;
+      bulk_load_g2s(su + lane * kScanThreads, u + tok * di + c0, static_cast<uint32_t>(nch * 4), &full[s]);
+      bulk_load_g2s(sz + lane * kScanThreads, xz + tok * 2 * di + di + c0, static_cast<uint32_t>(nch * 4), &full[s]);
+    }
+  };
+  if (tid < 32) {
+    request(0);
+    if (ntiles > 1) request(1);
+  }
+  const bool active = tid < nch;
+  const int cc = active ? c : c0;  // idle threads of a ragged last CTA read channel c0's constants
+  float wdt[DR], an[DS], h[DS];
+#pragma unroll
+  for (int r = 0; r < DR; ++r) wdt[r] = dt_w[cc * DR + r];
+#pragma unroll
+  for (int n = 0; n < DS; ++n) {
+    an[n] = FAST ? a_neg[n * di + cc] * 1.4426950408889634f : a_neg[n * di + cc];
+    h[n] = 0.0f;
+  }
+  const float bdt = dt_b[cc], dk = dsk[cc];
+  bool failed = false;
+  for (int tile = 0; tile < ntiles; ++tile) {
+    const int s = tile & 1, t0 = tile * kScanTile, n = min(kScanTile, L - t0);
+    const bool ok = __all_sync(0xffffffffu, mbar_wait(&full[s], static_cast<uint32_t>(tile >> 1) & 1u, &abort_word));
+    if (!ok) {
+      if (lane == 0) {
+        atomicCAS(err, 0, kErrStageTimeout);
+        atomicExch(&abort_word, 1);
+      }
+      failed = true;
+      break;
+    }
+    const float* sd = sst + s * kStage;
+    const float* su = sd + kScanTile * WD;
+    float* sz = sst + s * kStage + kScanTile * WD + kScanTile * kScanThreads;
+    if (active) {
+      // A: dt and the gate of every step of the tile
+#pragma unroll 4
+      for (int j = 0; j < n; ++j) {
+        const float4* row4 = reinterpret_cast<const float4*>(sd + j * WD);
+        const float zv = sz[j * kScanThreads + tid];
+        float dt, gate;
+        if constexpr (FAST) {
+          float2 acc0 = make_float2(0.0f, 0.0f), acc1 = make_float2(0.0f, 0.0f);
+#pragma unroll
+          for (int r = 0; r < DR / 4; ++r) {
+            const float4 v = row4[r];
+            acc0 = __ffma2_rn(make_float2(v.x, v.y), make_float2(wdt[4 * r], wdt[4 * r + 1]), acc0);
+            acc1 = __ffma2_rn(make_float2(v.z, v.w), make_float2(wdt[4 * r + 2], wdt[4 * r + 3]), acc1);
+          }
+          const float pre = ((acc0.x + acc1.x) + (acc0.y + acc1.y)) + bdt;
+          dt = fmaxf(pre, 0.0f) + __logf(1.0f + __expf(-fabsf(pre)));
+          gate = silu_fast(zv);
+        } else {
+          float acc = 0.0f;
+#pragma unroll
+          for (int r = 0; r < DR / 4; ++r) {
+            const float4 v = row4[r];
+            acc += v.x * wdt[4 * r];
+            acc += v.y * wdt[4 * r + 1];
+            acc += v.z * wdt[4 * r + 2];
+            acc += v.w * wdt[4 * r + 3];
+          }
+          dt = softplus_f(acc + bdt);
+          gate = zv / (1.0f + expf(-zv));
+        }
+        sdt[j * kScanThreads + tid] = dt;
+        sz[j * kScanThreads + tid] = gate;
+      }
+      // B: the recurrence
+#pragma unroll 2
+      for (int j = 0; j < n; ++j) {
+        const float4* row4 = reinterpret_cast<const float4*>(sd + j * WD);
+        const float dt = sdt[j * kScanThreads + tid], uv = su[j * kScanThreads + tid];
+        const float gate = sz[j * kScanThreads + tid];
+        float out;
+        if constexpr (FAST) {
+          const float dtu = dt * uv;
+          const float2 dt2 = make_float2(dt, dt), dtu2 = make_float2(dtu, dtu);
+          float2 y0 = make_float2(dk * uv, 0.0f), y1 = make_float2(0.0f, 0.0f);
+#pragma unroll
+          for (int q = 0; q < DS / 4; ++q) {
+            const float4 bq = row4[DR / 4 + q], cq = row4[(DR + DS) / 4 + q];
+#pragma unroll
+            for (int half = 0; half < 2; ++half) {
+              const int pr = 2 * q + half;  // states 2 pr and 2 pr + 1
+              const float2 e = __fmul2_rn(dt2, make_float2(an[2 * pr], an[2 * pr + 1]));
+              const float2 da = pr >= DS / 2 - POLY ? exp2_poly2(e) : make_float2(ex2_approx(e.x), ex2_approx(e.y));
+              const float2 bn = half ? make_float2(bq.z, bq.w) : make_float2(bq.x, bq.y);
+              const float2 cn = half ? make_float2(cq.z, cq.w) : make_float2(cq.x, cq.y);
+              const float2 hn = __ffma2_rn(da, make_float2(h[2 * pr], h[2 * pr + 1]), __fmul2_rn(dtu2, bn));
+              h[2 * pr] = hn.x;
+              h[2 * pr + 1] = hn.y;
+              if (half)
+                y1 = __ffma2_rn(hn, cn, y1);
+              else
+                y0 = __ffma2_rn(hn, cn, y0);
+            }
+          }
+          out = ((y0.x + y1.x) + (y0.y + y1.y)) * gate;
+        } else {
+          float yv = dk * uv;
+#pragma unroll
+          for (int q = 0; q < DS / 4; ++q) {
+            const float4 bq = row4[DR / 4 + q], cq = row4[(DR + DS) / 4 + q];
+            const float bn[4] = {bq.x, bq.y, bq.z, bq.w}, cn[4] = {cq.x, cq.y, cq.z, cq.w};
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              const int st = 4 * q + i;
+              const float da = expf(dt * an[st]);
+              const float dbu = dt * bn[i] * uv;
+              h[st] = (da * h[st]) + dbu;
+              yv += h[st] * cn[i];
+            }
+          }
+          out = yv * gate;
+        }
+        const long long tok = tok0 + t0 + j;
+        if (y != nullptr) y[tok * di + c] = out;
+        if (y_bf != nullptr) store_act16(y_bf, tok, di, c, out, split);
+      }
+    }
+    // this warp is done with the stage; the warp completing the count requests
+    // the stage's next tile (the gates were written into the stage by the
+    // generic proxy, the copies write it through the async proxy)
+    __syncwarp();
+    int last = 0;
+    if (lane == 0) {
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      __threadfence_block();
+      last = atomicAdd(&done_warps[s], 1) == kScanWarps * ((tile >> 1) + 1) - 1;
+      __threadfence_block();
+    }
+    last = __shfl_sync(0xffffffffu, last, 0);
+    if (last && tile + 2 < ntiles) {
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      request(tile + 2);
+    }
+  }
+  if (__syncthreads_or(failed)) {
+    // the copies this CTA issued may still be in flight: wait for each
+    // stage's last request (bounded) before the shared memory is released
+    if (tid == 0)
+      for (int s = 0; s < 2; ++s)
+        if (last_req[s] >= 0) mbar_wait(&full[s], static_cast<uint32_t>(last_req[s] >> 1) & 1u, &zero_word);
+    __syncthreads();
+  }
+}
+
 // Chunked selective scan for few sequences (the sequential kernel above runs
 // one thread per (sequence, channel), so one sequence is 1024 threads walking
 // all L steps).  The recurrence h_t = a_t h_(t-1) + b_t (a_t = exp(dt A),
@@ -829,7 +1058,13 @@ bool Mamba::load(const TensorTable& t, std::string& err) {
                         reinterpret_cast<const void*>(scan_kernel<8, 4, false>),
                         reinterpret_cast<const void*>(scan_kernel<8, 4, true>),
                         reinterpret_cast<const void*>(scan_kernel<4, 4, false>),
-                        reinterpret_cast<const void*>(scan_kernel<4, 4, true>)})
+                        reinterpret_cast<const void*>(scan_kernel<4, 4, true>),
+                        reinterpret_cast<const void*>(scan_staged_kernel<16, 32, false, 0>),
+                        reinterpret_cast<const void*>(scan_staged_kernel<16, 32, true, kScanPolyPairs>),
+                        reinterpret_cast<const void*>(scan_staged_kernel<8, 4, false, 0>),
+                        reinterpret_cast<const void*>(scan_staged_kernel<8, 4, true, 0>),
+                        reinterpret_cast<const void*>(scan_staged_kernel<4, 4, false, 0>),
+                        reinterpret_cast<const void*>(scan_staged_kernel<4, 4, true, 0>)})
     cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
   if (cudaDeviceSynchronize() != cudaSuccess) {
     err = "Mamba weight upload failed";
@@ -1039,23 +1274,32 @@ bool Mamba::run_layers(long long n_tok, int B, int L, bool tc, cudaStream_t st, 
         (static_cast<std::size_t>(L) * wd + 2 * static_cast<std::size_t>(L / kScanChunk) * kScanCh * 2) * 4;
     const bool chunked = L % kScanChunk == 0 && L / kScanChunk <= 64 && static_cast<long long>(B) * di < 32768 &&
                          csmem <= 200 * 1024 && wd % 4 == 0;
-    auto scan = [&](auto kernel, auto ckernel) {
+    // many sequences: the staged kernel (bulk copies need di % 4 == 0); the
+    // fp32 y is read only by the CUDA-core out-projection
+    const bool staged = di % 4 == 0;
+    const dim3 sgrid(static_cast<unsigned>((di + kScanThreads - 1) / kScanThreads), static_cast<unsigned>(B));
+    auto scan = [&](auto kernel, auto ckernel, auto skernel, int sds, int sdr) {
       if (chunked)
         ckernel<<<cgrid, cthreads, csmem, st>>>(dbl_, wd, u_, xz_, L, di, Ly.dt_w, Ly.dt_b, Ly.a_neg, Ly.d, nullptr,
                                                 y_, tc ? yb_ : nullptr, split);
+      else if (staged)
+        skernel<<<sgrid, kScanThreads, static_cast<std::size_t>(scan_smem_floats(sds, sdr)) * 4, st>>>(dbl_, u_, xz_, L, di, Ly.dt_w, Ly.dt_b, Ly.a_neg, Ly.d, tc ? nullptr : y_,
+                        tc ? yb_ : nullptr, split, ctx_->d_err);
       else
         kernel<<<grid, 256, smem, st>>>(dbl_, wd, u_, xz_, L, di, Ly.dt_w, Ly.dt_b, Ly.a_neg, Ly.d, nullptr, y_,
                                         tc ? yb_ : nullptr, split);
     };
     if (ds == 16 && dr == 32)
-      fast ? scan(scan_kernel<16, 32, true>, scan_chunked_kernel<16, 32, true>)
-           : scan(scan_kernel<16, 32, false>, scan_chunked_kernel<16, 32, false>);
+      fast ? scan(scan_kernel<16, 32, true>, scan_chunked_kernel<16, 32, true>,
+                  scan_staged_kernel<16, 32, true, kScanPolyPairs>, 16, 32)
+           : scan(scan_kernel<16, 32, false>, scan_chunked_kernel<16, 32, false>, scan_staged_kernel<16, 32, false, 0>,
+                  16, 32);
     else if (ds == 4 && dr == 4)
-      fast ? scan(scan_kernel<4, 4, true>, scan_chunked_kernel<4, 4, true>)
-           : scan(scan_kernel<4, 4, false>, scan_chunked_kernel<4, 4, false>);
+      fast ? scan(scan_kernel<4, 4, true>, scan_chunked_kernel<4, 4, true>, scan_staged_kernel<4, 4, true, 0>, 4, 4)
+           : scan(scan_kernel<4, 4, false>, scan_chunked_kernel<4, 4, false>, scan_staged_kernel<4, 4, false, 0>, 4, 4);
     else if (ds == 8 && dr == 4)
-      fast ? scan(scan_kernel<8, 4, true>, scan_chunked_kernel<8, 4, true>)
-           : scan(scan_kernel<8, 4, false>, scan_chunked_kernel<8, 4, false>);
+      fast ? scan(scan_kernel<8, 4, true>, scan_chunked_kernel<8, 4, true>, scan_staged_kernel<8, 4, true, 0>, 8, 4)
+           : scan(scan_kernel<8, 4, false>, scan_chunked_kernel<8, 4, false>, scan_staged_kernel<8, 4, false, 0>, 8, 4);
     else {
       err = "no scan instantiation for this (d_state, dt_rank)";
       return false;

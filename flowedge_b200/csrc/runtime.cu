@@ -174,6 +174,7 @@ const char* device_error_text(int code) noexcept {
     case kErrGridBarrierTimeout: return "a device grid barrier timed out";
     case kErrProgramLayout: return "internal error: small-batch program layout check failed";
     case kErrDependencyTimeout: return "a small-batch program dependency wait timed out";
+    case kErrStageTimeout: return "a staged-input wait of the selective scan timed out";
     default: return "a device pipeline wait timed out";
   }
 }

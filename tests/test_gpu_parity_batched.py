@@ -3,12 +3,14 @@ compiled reference core (oracle/_ref) on sampled rows of the same inputs.
 
 * Mamba (the 8 x 512 encoder: d_inner 1024, d_state 16, d_conv 4, dt_rank 32):
   - 64 sequences of 128 tokens reach the many-sequence selective scan
-    (`scan_kernel<16, 32, *>`, chosen when batch * d_inner >= 32768) at the
-    bench's sequence length;
+    (`scan_staged_kernel<16, 32, *>`, chosen when batch * d_inner >= 32768:
+    eight 16-step tiles) at the bench's sequence length;
   - 640 sequences of 16 tokens also reach the register-window causal conv
     (`causal_conv_kernel`, chosen when batch * d_inner / 4 >= 1024 * SMs);
   - 2 sequences of 13 tokens reach the many-sequence scan at a small batch,
-    because 13 steps do not split into the chunked scan's 8-step chunks.
+    because 13 steps do not split into the chunked scan's 8-step chunks (one
+    ragged tile), and 3 sequences of 37 tokens run it over two whole tiles
+    and a ragged third.
   Each in fp32 mode (tensor cores on fp16 hi / lo splits, bar 1e-3) and in bf16
   mode on bf16-rounded weights (bar 2e-2), per-row against the reference's
   `Mamba::forward` (src/core/models/mamba/mamba.cc:232-315; scan at
@@ -54,6 +56,7 @@ CASES = [  # (batch, seq_len, rows compared with the reference)
     (64, 128, (0, 37, 63)),
     (640, 16, (0, 1, 318, 638, 639)),
     (2, 13, (0, 1)),
+    (3, 37, (0, 2)),
 ]
 
 
