@@ -498,6 +498,36 @@ __device__ __forceinline__ float bf16_hi(uint32_t packed) { return __uint_as_flo
 // fp16 operand storage saturates at the largest finite value (never inf)
 __device__ __forceinline__ __half to_half_sat(float v) { return __float2half_rn(fminf(fmaxf(v, -65504.0f), 65504.0f)); }
 
+// fp16 of v with saturation at +-65504 in one conversion (cvt.rn.satfinite)
+__device__ __forceinline__ __half half_satfinite(float v) {
+  unsigned short r;
+  asm("cvt.rn.satfinite.f16.f32 %0, %1;" : "=h"(r) : "f"(v));
+  return __ushort_as_half(r);
+}
+
+// fp16 pair {lo, hi} with saturation at +-65504 (cvt.rn.satfinite; NaN stays NaN)
+__device__ __forceinline__ uint32_t pack_half2_sat(float lo, float hi) {
+  uint32_t r;
+  asm("cvt.rn.satfinite.f16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+
+// Mish of a pair, x * n / (n + 2) with n = e (e + 2), e = 2^(min(x, 20) log2 e)
+// by the hardware ex2 and reciprocal approximations; above 20 the quotient
+// rounds to 1 in fp32, so the clamp changes nothing.  For values rounded to
+// fp16 right afterwards (relative error ~1e-6).
+__device__ __forceinline__ float2 mish2(float2 x) {
+  constexpr float kLog2e = 1.4426950408889634f;
+  const float2 t = __fmul2_rn(make_float2(fminf(x.x, 20.0f), fminf(x.y, 20.0f)), make_float2(kLog2e, kLog2e));
+  const float2 e = make_float2(ex2_approx(t.x), ex2_approx(t.y));
+  const float2 n = __fmul2_rn(e, __fadd2_rn(e, make_float2(2.0f, 2.0f)));
+  const float2 d = __fadd2_rn(n, make_float2(2.0f, 2.0f));
+  float2 r;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r.x) : "f"(d.x));
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r.y) : "f"(d.y));
+  return __fmul2_rn(x, __fmul2_rn(n, r));
+}
+
 __device__ __forceinline__ uint32_t pack_half(float lo, float hi) {
   __half2 v = __halves2half2(to_half_sat(lo), to_half_sat(hi));
   return *reinterpret_cast<uint32_t*>(&v);

@@ -128,7 +128,9 @@ std::shared_ptr<DeviceContext> make_device_context(int device, std::string& err)
       cudaFuncSetAttribute(tc::tc_gemm_kernel<tc::kEpiStats>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                            tc::SMEM_BYTES) != cudaSuccess ||
       cudaFuncSetAttribute(tc::tc_gemm_kernel<tc::kEpiFused>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           tc::SMEM_BYTES) != cudaSuccess) {
+                           tc::SMEM_BYTES) != cudaSuccess ||
+      cudaFuncSetAttribute(tc::tc_gemm_kernel<tc::kEpiFused, false, true>,
+                           cudaFuncAttributeMaxDynamicSharedMemorySize, tc::SMEM_BYTES) != cudaSuccess) {
     err = "cannot enable the tensor-core kernel's shared memory";
     return nullptr;
   }
@@ -376,11 +378,35 @@ cudaError_t tc_gemm(const TcLaunch& l, DeviceContext& ctx, cudaStream_t stream, 
   p.groups = l.groups;
   p.parts = l.group_ch > tc::BM ? l.group_ch / tc::BM : 1;
   p.err = ctx.d_err;
+  // Fused GroupNorm convs run with tokens on the accumulator rows (TOKM)
+  // when the layout allows its 16-byte accesses: 128-token tiles (L in
+  // [8, 128]), groups inside a 256-channel tile, bias without add terms, an
+  // fp32 residual (or none), and every per-channel vector, row stride and base
+  // 16-byte aligned.
+  const auto al16 = [](const void* ptr) { return (reinterpret_cast<std::uintptr_t>(ptr) & 15u) == 0; };
+  // Only the convs whose groups span 256 channels take it (they would
+  // otherwise run as 2-CTA pairs) and only without an fp32 residual or twin:
+  // with tokens on the lanes each 16-byte access of a warp lands in a
+  // different token row, four to eight times the L1 line requests of the
+  // channel-per-lane layout, which the fp32 residual stream makes the bound.
+  const bool tokm =
+      l.gn_fuse && l.L >= 8 && l.L <= tc::BM && l.group_ch == 256 && l.res_f32 == nullptr &&
+      l.res16 == nullptr && l.out_twin == nullptr &&
+      l.M_rows >= tc::BN && l.bias != nullptr && l.add_vec == nullptr && p.out_cs % 8 == 0 && p.out_base % 8 == 0 &&
+      al16(l.out) && al16(l.bias) && al16(l.gamma) && al16(l.beta) && al16(l.out_twin) && al16(l.res_f32) &&
+      (l.res16 == nullptr || l.res_f32 != nullptr) &&
+      (l.film_cond == nullptr || (al16(l.film_cond) && al16(l.film_time) && l.film_F % 4 == 0 &&
+                                  l.film_off % 4 == 0 && l.film_C % 4 == 0)) &&
+      [&] {
+        for (int i = 0; i < 3; ++i)
+          if (l.src[i].ptr != nullptr && l.src[i].samples < tc::BM / l.L) return false;
+        return true;
+      }();
   if (l.gn_fuse) {
     const bool in_tile = l.group_ch >= 32 && l.group_ch <= tc::BM && tc::BM % l.group_ch == 0 &&
                          tc::BM / l.group_ch <= tc::MAX_TILE_GROUPS;
     const bool paired = l.group_ch == 2 * tc::BM && p.n_tiles_m % 2 == 0 && ctx.pair_clusters > 0;
-    if (l.stats != nullptr || l.out_f32 || !(in_tile || paired) || p.tile_samples > tc::MAX_TILE_SAMPLES || l.L < 8 ||
+    if (l.stats != nullptr || l.out_f32 || !(in_tile || paired || tokm) || p.tile_samples > tc::MAX_TILE_SAMPLES || l.L < 8 ||
         l.gamma == nullptr ||
         l.beta == nullptr || l.act != tc::kActNone || l.add_tok != nullptr || !l.fp16) {
       err = "tc_gemm: unsupported fused GroupNorm geometry";
@@ -400,9 +426,16 @@ cudaError_t tc_gemm(const TcLaunch& l, DeviceContext& ctx, cudaStream_t stream, 
     p.out_twin = l.out_twin;
   }
 
+  if (tokm) {
+    p.tile_samples = tc::BM / l.L;
+    p.n_tiles_m = (l.n_samples + p.tile_samples - 1) / p.tile_samples;
+    p.n_tiles_n = (l.M_rows + tc::BN - 1) / tc::BN;
+    p.total_tiles = p.n_tiles_m * p.n_tiles_n;
+  }
+
   CUtensorMap ta{}, tb[3]{};
-  if (!encode_2d(&ta, l.A, static_cast<std::uint64_t>(l.K), static_cast<std::uint64_t>(l.M_rows), 64, tc::BM, dtype,
-                 err))
+  if (!encode_2d(&ta, l.A, static_cast<std::uint64_t>(l.K), static_cast<std::uint64_t>(l.M_rows), 64,
+                 tokm ? tc::BN : tc::BM, dtype, err))
     return cudaErrorInvalidValue;
   for (int i = 0; i < 3; ++i) {
     const TcSource& s = l.src[i].ptr != nullptr ? l.src[i] : l.src[0];
@@ -420,6 +453,13 @@ cudaError_t tc_gemm(const TcLaunch& l, DeviceContext& ctx, cudaStream_t stream, 
   cfg.stream = stream;
   cfg.attrs = attrs;
   cfg.numAttrs = 1;
+  if (tokm) {
+    cfg.gridDim = dim3(static_cast<unsigned>(p.total_tiles < ctx.sm_count ? p.total_tiles : ctx.sm_count));
+    const cudaError_t rc =
+        cudaLaunchKernelEx(&cfg, tc::tc_gemm_kernel<tc::kEpiFused, false, true>, ta, tb[0], tb[1], tb[2], p);
+    if (rc != cudaSuccess) err = std::string("tc_gemm launch: ") + cudaGetErrorString(rc);
+    return rc;
+  }
   if (p.gn_fuse && l.group_ch == 2 * tc::BM) {
     attrs[1].id = cudaLaunchAttributeClusterDimension;
     attrs[1].val.clusterDim.x = 2;

@@ -1128,8 +1128,8 @@ class SmolVLA final : public SmolVLADevice {
   bool attention(const Layer& L, std::size_t li, std::size_t batch, std::size_t chunk, bool shared, cudaStream_t st,
                  std::string& err);
   int finish(cudaStream_t st, std::string& err);
-  // heads per attention task: 3 (the reference's 15 / 5 and configuration 5's
-  // 12 / 4) when the batch fills the GPU, else 1 (more, smaller CTAs)
+  // heads per attention task: 3 (the reference's 15 / 5 and the SmolVLA-shaped
+  // expert's 12 / 4) when the batch fills the GPU, else 1 (more, smaller CTAs)
   int attn_g(std::size_t batch) const {
     return cfg_.heads / cfg_.kv_heads % 3 == 0 && batch * cfg_.kv_heads >= static_cast<std::size_t>(ctx_->sm_count)
                ? 3

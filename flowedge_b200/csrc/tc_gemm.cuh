@@ -45,6 +45,8 @@ constexpr int EPI_COLS = BN / EPI_PARTS;    // tile columns per epilogue warp
 constexpr int THREADS = 64 + EPI_THREADS;
 constexpr int TMEM_COLS = 512;
 constexpr int MAX_TILE_GROUPS = 4;   // groups of >= 32 channels inside a 128-row tile
+constexpr int BP_SAMPLES = 32;       // samples of a tile in the per-slice statistics (L >= 8)
+static_assert(2 * 16 * BP_SAMPLES <= 4 * 4 * MAX_TILE_SAMPLES, "per-slice partials fit the partials buffer");
 constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + 256 + 4 * EPI_PARTS * MAX_TILE_SAMPLES * 16 +
                            MAX_TILE_SAMPLES * MAX_TILE_GROUPS * 8 + 3 * MAX_TILE_SAMPLES * 16;
 static_assert(SMEM_BYTES <= 232448, "shared memory above the 227 KB per-CTA limit");
@@ -123,7 +125,17 @@ enum EpiMode : int { kEpiPlain = 0, kEpiStats = 1, kEpiFused = 2 };
 // its per-sample partial sums into the other's shared memory and arrives on
 // the other's mbarrier (release, cluster scope); each then waits (bounded) for
 // the other's partials and normalises with the whole group's statistics.
-template <int MODE, bool PAIR = false>
+//
+// TOKM (fused mode only, no PAIR): tokens on the accumulator rows.  The
+// activation tile (128 tokens x 64 channels, box {64, L, 128 / L}) is the MMA's
+// A operand and the weight tile (256 output channels x 64) its B operand, in
+// the same stage buffers (16 KB + 32 KB) and with the same UMMA shape and TMEM
+// footprint; tile t covers channel tile t % n_tiles_n of token tile
+// t / n_tiles_n, so the CTAs running at once share token tiles in L2.  An
+// epilogue thread then owns one token and 64 consecutive output channels:
+// GroupNorm groups of up to 256 channels lie inside one tile, and the
+// per-channel work runs on packed fp32 pairs with 16-byte loads and stores.
+template <int MODE, bool PAIR = false, bool TOKM = false>
 static __global__ void __launch_bounds__(THREADS, 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB0,
                    const __grid_constant__ CUtensorMap tmB1, const __grid_constant__ CUtensorMap tmB2,
@@ -190,8 +202,12 @@ static __global__ void __launch_bounds__(THREADS, 1)
   const int walk_first = PAIR ? static_cast<int>(cluster_index()) : static_cast<int>(blockIdx.x);
   const int walk_stride = PAIR ? static_cast<int>(cluster_count()) : static_cast<int>(gridDim.x);
   const int walk_count = PAIR ? p.total_tiles / 2 : p.total_tiles;
+  static_assert(!TOKM || (MODE == kEpiFused && !PAIR), "tokens on the rows: fused GroupNorm epilogue, unpaired");
   auto tile_mn = [&](int t, int& m_blk, int& n_blk) {
-    if constexpr (PAIR) {
+    if constexpr (TOKM) {
+      n_blk = t % p.n_tiles_n;
+      m_blk = t / p.n_tiles_n;
+    } else if constexpr (PAIR) {
       const int npm = p.n_tiles_m >> 1;
       m_blk = (t % npm) * 2 + rank;
       n_blk = t / npm;
@@ -234,8 +250,13 @@ static __global__ void __launch_bounds__(THREADS, 1)
             mbar_arrive_expect_tx(&full[stage], STAGE_BYTES);
             armed |= 1u << stage;
             armed_phase = (armed_phase & ~(1u << stage)) | (phase << stage);
-            tma_load_2d_hint(a_dst, &tmA, sg.a_k + kb * BK, m_blk * BM, &full[stage], keep_a);
-            tma_load_3d(b_dst, mapB, sg.ch_off + kb * BK, sg.t_off, n_blk * p.tile_samples, &full[stage]);
+            if constexpr (TOKM) {
+              tma_load_3d(a_dst, mapB, sg.ch_off + kb * BK, sg.t_off, m_blk * p.tile_samples, &full[stage]);
+              tma_load_2d_hint(b_dst, &tmA, sg.a_k + kb * BK, n_blk * BN, &full[stage], keep_a);
+            } else {
+              tma_load_2d_hint(a_dst, &tmA, sg.a_k + kb * BK, m_blk * BM, &full[stage], keep_a);
+              tma_load_3d(b_dst, mapB, sg.ch_off + kb * BK, sg.t_off, n_blk * p.tile_samples, &full[stage]);
+            }
           }
         }
       }
@@ -295,6 +316,194 @@ static __global__ void __launch_bounds__(THREADS, 1)
       for (uint32_t spin = 0; spin < kSpinLimit && !mbar_try_wait(drain, 0); ++spin) {
       }
     }
+  } else if constexpr (TOKM) {
+    // ---------------- epilogue, tokens on the accumulator rows ----------------
+    // Thread (quadrant q, lane) owns token row q*32 + lane of the tile and the
+    // 64 channel columns [64 part, 64 part + 64).  Pass 1 sums y = acc + bias
+    // over the thread's channels of each GroupNorm group (fp32), then over the
+    // sample's lanes (double, shuffles); one double2 per (warp, sample of the
+    // warp, group piece) goes to shared memory, buffered by accumulator parity,
+    // and after one epilogue barrier every thread adds up the entries of its
+    // (sample, group) in a fixed order.  Pass 2: z = Mish(GN(y)), then FiLM or
+    // + residual, stored as fp16 (and fp32 when out_twin is set).
+    const int q = warp & 3;
+    const int part = (warp - 2) >> 2;
+    const int row = q * 32 + lane;
+    const int col0 = part * EPI_COLS;
+    const uint32_t lane_base = static_cast<uint32_t>(q * 32) << 16;
+    const int lps = p.L < 32 ? p.L : 32;                 // lanes of one sample in a warp (L >= 8)
+    const int qps = p.L > 32 ? p.L >> 5 : 1;             // quadrants of one sample
+    const int pieces = p.group_ch < EPI_COLS ? EPI_COLS / p.group_ch : 1;  // groups in the slice (1 or 2)
+    const int ppg = p.group_ch > EPI_COLS ? p.group_ch / EPI_COLS : 1;    // slices of one group
+    const double inv_cnt = 1.0 / (static_cast<double>(p.group_ch) * p.L);
+    const bool film = p.film_cond != nullptr;
+    // [acc][warp slot q * EPI_PARTS + part][sample of the warp][piece]
+    auto red_at = [&](int a, int qq, int pp, int siw, int pc) -> double2& {
+      return red[((a * EPI_WARPS + qq * EPI_PARTS + pp) * 4 + siw) * 2 + pc];
+    };
+    uint32_t acc_iter = 0;
+    for (int tile = walk_first; tile < walk_count; tile += walk_stride, ++acc_iter) {
+      int m_blk, n_blk;
+      tile_mn(tile, m_blk, n_blk);
+      const int acc = acc_iter & 1;
+      const uint32_t acc_phase = (acc_iter >> 1) & 1;
+      const bool waited = bar_and(2, EPI_THREADS, mbar_wait(&tfull[acc], acc_phase, abort_flag));
+      if (!waited) {
+        atomicCAS(p.err, 0, kErrWaitTimeoutEpilogue);
+        *abort_flag = 1;
+        break;
+      }
+      tc_fence_after();
+      const int tok = m_blk * BM + row;
+      const int smp = tok >> p.L_shift;
+      const bool tok_ok = smp < p.n_samples;
+      const int smp_c = tok_ok ? smp : p.n_samples - 1;  // in-range sample for the FiLM loads
+      const int ch0 = n_blk * BN + col0;                 // output channel of this slice's column 0
+      const int nval = min(max(p.m_valid - ch0, 0), EPI_COLS);
+      const uint32_t tbase = tmem_base + lane_base + acc * BN + col0;
+
+      // pass 1: per-piece sums of y over this thread's channels (piece 1 is
+      // channels 32-63 when a group has 32 channels)
+      float2 s1[2] = {make_float2(0.0f, 0.0f), make_float2(0.0f, 0.0f)};
+      float2 s2[2] = {make_float2(0.0f, 0.0f), make_float2(0.0f, 0.0f)};
+#pragma unroll 1
+      for (int c = 0; c < EPI_COLS / 16; ++c) {
+        float v[16];
+        tmem_ld16(tbase + c * 16, v);
+        float2 c1 = make_float2(0.0f, 0.0f), c2 = make_float2(0.0f, 0.0f);
+        if (c * 16 + 16 <= nval) {
+          const float4* b4 = reinterpret_cast<const float4*>(p.bias + ch0 + c * 16);
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const float4 b = b4[k];
+            const float2 y0 = __fadd2_rn(make_float2(v[4 * k], v[4 * k + 1]), make_float2(b.x, b.y));
+            const float2 y1 = __fadd2_rn(make_float2(v[4 * k + 2], v[4 * k + 3]), make_float2(b.z, b.w));
+            c1 = __fadd2_rn(c1, __fadd2_rn(y0, y1));
+            c2 = __ffma2_rn(y0, y0, c2);
+            c2 = __ffma2_rn(y1, y1, c2);
+          }
+        } else {
+#pragma unroll
+          for (int j = 0; j < 16; j += 2) {
+            const float y0 = c * 16 + j < nval ? v[j] + p.bias[ch0 + c * 16 + j] : 0.0f;
+            const float y1 = c * 16 + j + 1 < nval ? v[j + 1] + p.bias[ch0 + c * 16 + j + 1] : 0.0f;
+            c1 = __fadd2_rn(c1, make_float2(y0, y1));
+            c2 = __ffma2_rn(make_float2(y0, y1), make_float2(y0, y1), c2);
+          }
+        }
+        if (c >= 2 && pieces == 2) {
+          s1[1] = __fadd2_rn(s1[1], c1);
+          s2[1] = __fadd2_rn(s2[1], c2);
+        } else {
+          s1[0] = __fadd2_rn(s1[0], c1);
+          s2[0] = __fadd2_rn(s2[0], c2);
+        }
+      }
+      const int siw = p.L < 32 ? lane / lps : 0;  // sample of this lane within the warp
+#pragma unroll
+      for (int pc = 0; pc < 2; ++pc) {
+        if (pc < pieces) {
+          double d1 = static_cast<double>(s1[pc].x) + static_cast<double>(s1[pc].y);
+          double d2 = static_cast<double>(s2[pc].x) + static_cast<double>(s2[pc].y);
+          for (int off = 1; off < lps; off <<= 1) {
+            d1 += __shfl_xor_sync(0xffffffffu, d1, off);
+            d2 += __shfl_xor_sync(0xffffffffu, d2, off);
+          }
+          if ((lane & (lps - 1)) == 0) red_at(acc, q, part, siw, pc) = make_double2(d1, d2);
+        }
+      }
+      named_barrier(1, EPI_THREADS);
+      // statistics of this thread's (sample, group) per piece: the sample's
+      // quadrants, then the group's slices, in that order
+      float2 st[2];
+#pragma unroll
+      for (int pc = 0; pc < 2; ++pc) {
+        st[pc] = make_float2(0.0f, 1.0f);
+        if (pc < pieces) {
+          const int qs0 = p.L > 32 ? ((row >> p.L_shift) << p.L_shift) >> 5 : q;
+          const int pg0 = ppg > 1 ? (part / ppg) * ppg : part;
+          const int ppc = pieces == 2 ? pc : 0;
+          double d1 = 0.0, d2 = 0.0;
+          for (int qq = qs0; qq < qs0 + qps; ++qq)
+            for (int pp = pg0; pp < pg0 + ppg; ++pp) {
+              const double2 r = red_at(acc, qq, pp, siw, ppc);
+              d1 += r.x;
+              d2 += r.y;
+            }
+          const double mean = d1 * inv_cnt;
+          const double var = fmax(0.0, d2 * inv_cnt - mean * mean);
+          st[pc] = make_float2(static_cast<float>(mean), rsqrtf(static_cast<float>(var + 1e-5)));
+        }
+      }
+
+      // pass 2, eight channels at a time
+      const long long o_tok = static_cast<long long>(tok) * p.out_cs + p.out_base + ch0;
+      const float* fcs = film ? p.film_cond + (static_cast<long long>(smp_c) * p.film_F + p.film_off + ch0) : nullptr;
+      const float* fts = film ? p.film_time + (p.film_off + ch0) : nullptr;
+      const float* rf = p.res_f32 != nullptr ? p.res_f32 + o_tok : nullptr;
+      __half* o16 = static_cast<__half*>(p.out) + o_tok;
+      float* tw = p.out_twin != nullptr ? p.out_twin + o_tok : nullptr;
+#pragma unroll 1
+      for (int cb = 0; cb < EPI_COLS; cb += 8) {
+        float v[8];
+        tmem_ld8(tbase + cb, v);
+        const float2 sg = (pieces == 2 && cb >= 32) ? st[1] : st[0];
+        if (tok_ok && cb + 8 <= nval) {
+          const float2 inv2 = make_float2(sg.y, sg.y), nmean2 = make_float2(-sg.x, -sg.x);
+          uint32_t h[4];
+#pragma unroll
+          for (int k = 0; k < 2; ++k) {
+            const float4 b = reinterpret_cast<const float4*>(p.bias + ch0 + cb)[k];
+            const float4 g = reinterpret_cast<const float4*>(p.gamma + ch0 + cb)[k];
+            const float4 be = reinterpret_cast<const float4*>(p.beta + ch0 + cb)[k];
+            // GN(y) = y * sc + of with sc = inv * gamma, of = (bias - mean) * sc + beta
+            const float2 sc0 = __fmul2_rn(inv2, make_float2(g.x, g.y));
+            const float2 sc1 = __fmul2_rn(inv2, make_float2(g.z, g.w));
+            const float2 of0 = __ffma2_rn(__fadd2_rn(make_float2(b.x, b.y), nmean2), sc0, make_float2(be.x, be.y));
+            const float2 of1 = __ffma2_rn(__fadd2_rn(make_float2(b.z, b.w), nmean2), sc1, make_float2(be.z, be.w));
+            float2 z0 = mish2(__ffma2_rn(make_float2(v[4 * k], v[4 * k + 1]), sc0, of0));
+            float2 z1 = mish2(__ffma2_rn(make_float2(v[4 * k + 2], v[4 * k + 3]), sc1, of1));
+            if (film) {
+              const float4 cs4 = reinterpret_cast<const float4*>(fcs + cb)[k];
+              const float4 ts4 = reinterpret_cast<const float4*>(fts + cb)[k];
+              const float4 ch4 = reinterpret_cast<const float4*>(fcs + p.film_C + cb)[k];
+              const float4 th4 = reinterpret_cast<const float4*>(fts + p.film_C + cb)[k];
+              z0 = __ffma2_rn(__fadd2_rn(make_float2(cs4.x, cs4.y), make_float2(ts4.x, ts4.y)), z0,
+                              __fadd2_rn(make_float2(ch4.x, ch4.y), make_float2(th4.x, th4.y)));
+              z1 = __ffma2_rn(__fadd2_rn(make_float2(cs4.z, cs4.w), make_float2(ts4.z, ts4.w)), z1,
+                              __fadd2_rn(make_float2(ch4.z, ch4.w), make_float2(th4.z, th4.w)));
+            }
+            if (rf != nullptr) {
+              const float4 r = __ldcs(reinterpret_cast<const float4*>(rf + cb) + k);
+              z0 = __fadd2_rn(z0, make_float2(r.x, r.y));
+              z1 = __fadd2_rn(z1, make_float2(r.z, r.w));
+            }
+            if (tw != nullptr) reinterpret_cast<float4*>(tw + cb)[k] = make_float4(z0.x, z0.y, z1.x, z1.y);
+            h[2 * k] = pack_half2_sat(z0.x, z0.y);
+            h[2 * k + 1] = pack_half2_sat(z1.x, z1.y);
+          }
+          *reinterpret_cast<uint4*>(o16 + cb) = make_uint4(h[0], h[1], h[2], h[3]);
+        } else if (tok_ok) {
+          // ragged channel slice (fewer than 8 valid channels left): scalar, masked
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const int ch = cb + j;
+            if (ch < nval) {
+              const float sc = sg.y * p.gamma[ch0 + ch];
+              const float of = fmaf(p.bias[ch0 + ch] - sg.x, sc, p.beta[ch0 + ch]);
+              const float m = mish_sel(fmaf(v[j], sc, of));
+              const float fsc = film ? fcs[ch] + fts[ch] : 1.0f;
+              const float fsh = film ? fcs[p.film_C + ch] + fts[p.film_C + ch] : 0.0f;
+              const float z = fmaf(fsc, m, fsh) + (rf != nullptr ? rf[ch] : 0.0f);
+              o16[ch] = to_half_sat(z);
+              if (tw != nullptr) tw[ch] = z;
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&tempty[acc]);
+    }
   } else {
     // ---------------- epilogue (warps 2 .. 2 + EPI_WARPS - 1) ----------------
     // Thread (quadrant q, lane) owns accumulator row q*32 + lane (one output
@@ -317,6 +526,14 @@ static __global__ void __launch_bounds__(THREADS, 1)
     const uint32_t lane_base = static_cast<uint32_t>(q * 32) << 16;
     const int lmask = p.L - 1;
     const int cs = p.out_cs;
+    // Fused, unpaired, every sample inside one column slice (L <= EPI_COLS):
+    // the GroupNorm statistics of a slice's samples come from that slice's
+    // four warps (one per TMEM lane quadrant) only, so each slice combines
+    // them behind its own 128-thread named barrier (3 + part) and the slices
+    // run independently of one another.
+    const bool by_part = MODE == kEpiFused && !PAIR && p.L <= EPI_COLS;
+    const int bp_wpg = p.group_ch >= BM ? 4 : p.group_ch / 32;  // quadrants (warps) of one group
+    const double bp_inv_cnt = 1.0 / (static_cast<double>(p.group_ch) * p.L);
     uint32_t acc_iter = 0;
     for (int tile = walk_first; tile < walk_count; tile += walk_stride, ++acc_iter) {
       int m_blk, n_blk;
@@ -325,7 +542,8 @@ static __global__ void __launch_bounds__(THREADS, 1)
       const uint32_t acc_phase = (acc_iter >> 1) & 1;
       bool waited = mbar_wait(&tfull[acc], acc_phase, abort_flag);
       // modes with named barriers below take the same decision in every thread
-      if constexpr (kStats) waited = bar_and(2, EPI_THREADS, waited);
+      // that shares them: the whole epilogue, or one column slice (by_part)
+      if constexpr (kStats) waited = by_part ? bar_and(3 + part, 128, waited) : bar_and(2, EPI_THREADS, waited);
       if (!waited) {
         atomicCAS(p.err, 0, kErrWaitTimeoutEpilogue);
         *abort_flag = 1;
@@ -368,7 +586,13 @@ static __global__ void __launch_bounds__(THREADS, 1)
                   d1 += __shfl_xor_sync(0xffffffffu, d1, off);
                   d2 += __shfl_xor_sync(0xffffffffu, d2, off);
                 }
-                if (lane == 0) red[(q * EPI_PARTS + part) * MAX_TILE_SAMPLES + (col >> p.L_shift)] = make_double2(d1, d2);
+                if (lane == 0) {
+                  // by_part: [acc][warp][sample of the tile], so the next
+                  // tile's partials never overwrite ones still being read
+                  const int slot = by_part ? ((acc * EPI_WARPS + q * EPI_PARTS + part) * BP_SAMPLES + (col >> p.L_shift))
+                                           : (q * EPI_PARTS + part) * MAX_TILE_SAMPLES + (col >> p.L_shift);
+                  red[slot] = make_double2(d1, d2);
+                }
                 s1 = 0.0f;
                 s2 = 0.0f;
               }
@@ -441,7 +665,28 @@ static __global__ void __launch_bounds__(THREADS, 1)
         tc_fence_before();
         mbar_arrive(&tempty[acc]);
       }
-      if constexpr (kStats) {
+      // by_part: a warp's 32 channels lie in one group, so lane i combines the
+      // partials of the slice's sample i (the group's quadrants in quadrant
+      // order; E[y^2] - E[y]^2 in double, clamped at 0, eps 1e-5) and pass 2
+      // takes them by shuffle: one barrier of the slice's four warps is all
+      // the statistics take
+      float2 st_lane = make_float2(0.0f, 1.0f);
+      if (kStats && by_part) {
+        named_barrier(3 + part, 128);
+        const int gw = (q * 32) / p.group_ch;  // this warp's group within the tile
+        if (lane < (EPI_COLS >> p.L_shift)) {
+          const int ls = (col0 >> p.L_shift) + lane;
+          double d1 = 0.0, d2 = 0.0;
+          for (int w = 0; w < bp_wpg; ++w) {
+            const double2 r = red[(acc * EPI_WARPS + (gw * bp_wpg + w) * EPI_PARTS + part) * BP_SAMPLES + ls];
+            d1 += r.x;
+            d2 += r.y;
+          }
+          const double mean = d1 * bp_inv_cnt;
+          const double var = fmax(0.0, fma(-mean, mean, d2 * bp_inv_cnt));
+          st_lane = make_float2(static_cast<float>(mean), rsqrtf(static_cast<float>(var) + 1e-5f));
+        }
+      } else if constexpr (kStats) {
         named_barrier(1, EPI_THREADS);
         // combine the partials of the quadrants (and column slices) of each
         // (sample, group) of the tile
@@ -533,8 +778,15 @@ static __global__ void __launch_bounds__(THREADS, 1)
             }
           }
         };
+        // all EPI_COLS columns stored (every full tile): running pointers, no
+        // per-element predicates
+        const bool full = lim == EPI_COLS;
         auto load_res = [&](int c, float (&r)[CH]) {
-          if (rf != nullptr) {
+          if (rf != nullptr && full) {
+            const float* rp = rf + static_cast<long long>(c) * cs;
+#pragma unroll
+            for (int j = 0; j < CH; ++j, rp += cs) r[j] = *rp;
+          } else if (rf != nullptr) {
 #pragma unroll
             for (int j = 0; j < CH; ++j) r[j] = c + j < lim ? rf[static_cast<long long>(c + j) * cs] : 0.0f;
           } else if (rh != nullptr) {
@@ -558,25 +810,50 @@ static __global__ void __launch_bounds__(THREADS, 1)
           float v[CH];
           tmem_ld16(tbase + c, v);
           float z[CH];
+          // consecutive columns (tokens) of this channel in packed pairs
 #pragma unroll
           for (int h = 0; h < CH / 8; ++h) {
             const int ls = (col0 + c + 8 * h) >> p.L_shift;
-            const float2 st = stat[ls * MAX_TILE_GROUPS + gl];
+            float2 st;
+            if (by_part) {
+              st.x = __shfl_sync(0xffffffffu, st_lane.x, ls - (col0 >> p.L_shift));
+              st.y = __shfl_sync(0xffffffffu, st_lane.y, ls - (col0 >> p.L_shift));
+            } else {
+              st = stat[ls * MAX_TILE_GROUPS + gl];
+            }
             const float sc = st.y * gam;
             const float of = fmaf(bb - st.x, sc, bet);
+            const float2 sc2 = make_float2(sc, sc), of2 = make_float2(of, of);
+            const float2 fs2 = make_float2(f_cur[h].x, f_cur[h].x), fh2 = make_float2(f_cur[h].y, f_cur[h].y);
 #pragma unroll
-            for (int j = 0; j < 8; ++j)
-              z[8 * h + j] = fmaf(f_cur[h].x, mish_sel(fmaf(v[8 * h + j], sc, of)), f_cur[h].y) + r_cur[8 * h + j];
+            for (int j = 0; j < 8; j += 2) {
+              const int i = 8 * h + j;
+              const float2 mz = mish2(__ffma2_rn(make_float2(v[i], v[i + 1]), sc2, of2));
+              const float2 zz = __fadd2_rn(__ffma2_rn(fs2, mz, fh2), make_float2(r_cur[i], r_cur[i + 1]));
+              z[i] = zz.x;
+              z[i + 1] = zz.y;
+            }
           }
-          __half* o = o16 + static_cast<long long>(c) * cs;
+          if (full) {
+            __half* o = o16 + static_cast<long long>(c) * cs;
 #pragma unroll
-          for (int j = 0; j < CH; ++j)
-            if (c + j < lim) o[j * cs] = to_half_sat(z[j]);
-          if (tw != nullptr) {
-            float* t = tw + static_cast<long long>(c) * cs;
+            for (int j = 0; j < CH; ++j, o += cs) *o = half_satfinite(z[j]);
+            if (tw != nullptr) {
+              float* t = tw + static_cast<long long>(c) * cs;
+#pragma unroll
+              for (int j = 0; j < CH; ++j, t += cs) *t = z[j];
+            }
+          } else {
+            __half* o = o16 + static_cast<long long>(c) * cs;
 #pragma unroll
             for (int j = 0; j < CH; ++j)
-              if (c + j < lim) t[j * cs] = z[j];
+              if (c + j < lim) o[j * cs] = half_satfinite(z[j]);
+            if (tw != nullptr) {
+              float* t = tw + static_cast<long long>(c) * cs;
+#pragma unroll
+              for (int j = 0; j < CH; ++j)
+                if (c + j < lim) t[j * cs] = z[j];
+            }
           }
 #pragma unroll
           for (int h = 0; h < CH / 8; ++h) f_cur[h] = f_nxt[h];
