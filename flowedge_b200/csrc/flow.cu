@@ -13,11 +13,14 @@
 // terms in its epilogue.
 #include <algorithm>
 #include <cmath>
+#include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <map>
 #include <mutex>
 #include <tuple>
 
+#include "flow_program.cuh"
 #include "runtime.cuh"
 #include "simt.cuh"
 
@@ -75,6 +78,32 @@ __global__ void time_proj_kernel(const int* step_idx, int steps, int method, int
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
     if (lane == 0) tp[h] = acc;
+  }
+}
+
+// time_proj_kernel for every evaluation of steps first .. first + count - 1
+// at once (blockIdx.y = evaluation e = (step - first) * stages + stage), into
+// tp[e][h], for the persistent tensor-core solve
+__global__ void time_proj_all_kernel(int first, int steps, int method, int stages, const float* freqs, int half,
+                                     const float* wt, int H, float* tp) {
+  extern __shared__ float sinu[];
+  const int e = blockIdx.y;
+  const float t = stage_time(first + e / stages, steps, method, e % stages);
+  for (int j = threadIdx.x; j < half; j += blockDim.x) {
+    sinu[j] = sinf(t * freqs[j]);
+    sinu[half + j] = cosf(t * freqs[j]);
+  }
+  __syncthreads();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int warps = blockDim.x >> 5;
+  float* out = tp + static_cast<long long>(e) * H;
+  for (int h = blockIdx.x * warps + warp; h < H; h += gridDim.x * warps) {
+    const float* w = wt + static_cast<long long>(h) * 2 * half;
+    float acc = 0.0f;
+    for (int j = lane; j < 2 * half; j += 32) acc = fmaf(w[j], sinu[j], acc);
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+    if (lane == 0) out[h] = acc;
   }
 }
 
@@ -394,6 +423,12 @@ class Flow final : public FlowDevice {
   Flow(std::shared_ptr<DeviceContext> ctx, Precision prec) : ctx_(std::move(ctx)), prec_(prec) {}
   ~Flow() override {
     for (auto& [k, g] : graphs_) cudaGraphExecDestroy(g);
+    for (auto& [k, pr] : programs_) {
+      cudaFree(pr.table);
+      cudaFree(pr.ctr);
+      cudaFree(pr.tp);
+      cudaFree(pr.trace);
+    }
     if (pinned_ != nullptr) cudaFreeHost(pinned_);
   }
   bool load(const TensorTable& t, std::string& err);
@@ -441,6 +476,19 @@ class Flow final : public FlowDevice {
   int method_ = 0;
   std::map<std::tuple<std::size_t, int, bool, std::size_t>, cudaGraphExec_t> graphs_;
   unsigned* fsync_ = nullptr;  // grid-barrier words of the fused small-batch solve
+  // persistent tensor-core solve (flow_program_kernel): one layer table per
+  // (batch, first step, steps run, method, total steps), its block counters
+  // and the time projections of its evaluations
+  struct Program {
+    fp::Layer* table = nullptr;
+    int* ctr = nullptr;
+    float* tp = nullptr;
+    unsigned long long* trace = nullptr;  // FLOWEDGE_FLOW_TRACE=<file>: per-tile stamps of the last call
+    int n_layers = 0, total_tiles = 0, tiles_n = 0, n_evals = 0;
+    std::vector<int> tiles_m;             // per layer
+  };
+  std::map<std::tuple<std::size_t, std::size_t, std::size_t, int, std::size_t>, Program> programs_;
+  bool program_solve(std::size_t first, std::size_t count, cudaStream_t st, std::string& err, bool& used);
   // one cooperative launch for `count` steps of a small batch, or false when
   // the batch / shape does not take the fused kernel
   bool fused_advance(std::size_t first, std::size_t count, cudaStream_t st, std::string& err, bool& used);
@@ -484,7 +532,9 @@ bool Flow::load(const TensorTable& t, std::string& err) {
     err = "flow hidden width must be a multiple of 8";
     return false;
   }
-  tc_ok_ = H % 64 == 0;
+  tc_ok_ = H % 64 == 0 &&
+           cudaFuncSetAttribute(fp::flow_program_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                fp::SMEM_BYTES) == cudaSuccess;
   const bool bf = prec_ == Precision::kBF16;
   // every projection but the time projection (fp32 on the device) is held in fp16
   {
@@ -868,12 +918,172 @@ bool Flow::fused_advance(std::size_t first, std::size_t count, cudaStream_t st, 
   return true;
 }
 
+bool Flow::program_solve(std::size_t first, std::size_t count, cudaStream_t st, std::string& err, bool& used) {
+  used = false;
+  // bf16 mode only: with the fp32 engines' hi / lo splits every GEMM has three
+  // times the K blocks, each tile's operand stream from L2 is the bound, and
+  // the per-launch graph (256-token tiles, one wave per GEMM) measured faster
+  if (!use_tc(batch_) || split() || count == 0 || first + count > steps_) return true;
+  const int H = static_cast<int>(cfg_.hidden);
+  const int stages = method_ == 0 ? 1 : (method_ == 1 ? 2 : 4);
+  const auto key = std::make_tuple(batch_, first, count, method_, steps_);
+  auto it = programs_.find(key);
+  if (it == programs_.end()) {
+    Program pr;
+    pr.n_evals = static_cast<int>(count) * stages;
+    pr.tiles_n = static_cast<int>((batch_ + fp::BN - 1) / fp::BN);
+    const bool sp = split();
+    std::vector<fp::Layer> host;
+    int tiles = 0;
+    // one GEMM layer reading `in` (row width in_ld, hi / lo halves when split)
+    auto add_layer = [&](const Mat& m, const void* in, int in_ld, fp::Layer& L) -> bool {
+      L.tiles_m = m.rows_pad / fp::BM;
+      L.tiles_n = pr.tiles_n;
+      L.tile0 = tiles;
+      const int kb = m.cols_pad / fp::BK;
+      if (sp) {
+        L.nseg = 3;
+        const int bcol[3] = {0, in_ld, 0}, acol[3] = {0, m.cols_pad, 2 * m.cols_pad};
+        for (int i = 0; i < 3; ++i) {
+          L.seg_kb[i] = kb;
+          L.seg_bcol[i] = bcol[i];
+          L.seg_acol[i] = acol[i];
+        }
+      } else {
+        L.nseg = 1;
+        L.seg_kb[0] = kb;
+        L.seg_bcol[0] = 0;
+        L.seg_acol[0] = 0;
+      }
+      L.kb_total = L.nseg * kb;
+      L.m_valid = m.rows;
+      L.n_tokens = static_cast<int>(batch_);
+      L.dep = host.empty() ? -1 : static_cast<int>(host.size()) - 1;
+      L.dep_target = host.empty() ? 0 : host.back().tiles_m;
+      tiles += L.tiles_m * L.tiles_n;
+      const std::uint64_t a_cols = static_cast<std::uint64_t>(sp ? 3 * m.cols_pad : m.cols_pad);
+      const std::uint64_t b_cols = static_cast<std::uint64_t>(sp ? 2 * in_ld : in_ld);
+      return encode_tmap_2d(&L.a, sp ? m.w3 : m.w, a_cols, static_cast<std::uint64_t>(m.rows_pad), fp::BK, fp::BM,
+                            true, err) &&
+             encode_tmap_2d(&L.b, in, b_cols, static_cast<std::uint64_t>(cap_rows_), fp::BK, fp::BN, true, err);
+    };
+    const int hld = sp ? 2 * H : H;
+    for (int e = 0; e < pr.n_evals; ++e) {
+      void* hin = h0_;
+      void* hout = h1_;
+      fp::Layer L{};
+      if (!add_layer(in_, xin_, a_pad_, L)) return false;
+      L.act = tc::kActSilu;
+      L.add_tok = cemb_;
+      L.add_ld = H;
+      L.out = static_cast<__half*>(hin);
+      L.out_ld = hld;
+      L.out_lo = sp ? H : 0;
+      host.push_back(L);
+      L.add_vec = nullptr;  // set once the time-projection buffer exists
+      for (const Mat& m : layers_) {
+        fp::Layer Lh{};
+        if (!add_layer(m, hin, H, Lh)) return false;
+        Lh.act = tc::kActSilu;
+        Lh.out = static_cast<__half*>(hout);
+        Lh.out_ld = hld;
+        Lh.out_lo = sp ? H : 0;
+        host.push_back(Lh);
+        std::swap(hin, hout);
+      }
+      fp::Layer Lo{};
+      if (!add_layer(out_, hin, H, Lo)) return false;
+      Lo.ode = 1;
+      Lo.method = method_;
+      Lo.stage = e % stages;
+      Lo.steps = static_cast<int>(steps_);
+      Lo.x = x_;
+      Lo.probe = probe_;
+      for (int i = 0; i < 4; ++i) Lo.k[i] = k_[i];
+      Lo.ld = a_pad_;
+      Lo.next_in = static_cast<__half*>(xin_);
+      Lo.ld_in = a_pad_;
+      Lo.next_mode = in_mode(true);
+      host.push_back(Lo);
+    }
+    pr.n_layers = static_cast<int>(host.size());
+    pr.total_tiles = tiles;
+    for (const fp::Layer& L : host) pr.tiles_m.push_back(L.tiles_m);
+    if (std::getenv("FLOWEDGE_FLOW_TRACE") != nullptr &&
+        counted_malloc(reinterpret_cast<void**>(&pr.trace),
+                       static_cast<std::size_t>(tiles) * fp::kTraceStamps * sizeof(unsigned long long)) != cudaSuccess)
+      pr.trace = nullptr;
+    if (counted_malloc(reinterpret_cast<void**>(&pr.table), host.size() * sizeof(fp::Layer)) != cudaSuccess ||
+        counted_malloc(reinterpret_cast<void**>(&pr.ctr), host.size() * pr.tiles_n * sizeof(int)) != cudaSuccess ||
+        counted_malloc(reinterpret_cast<void**>(&pr.tp), static_cast<std::size_t>(pr.n_evals) * H * sizeof(float)) !=
+            cudaSuccess) {
+      cudaFree(pr.table);
+      cudaFree(pr.ctr);
+      err = "device allocation failed (flow program)";
+      return false;
+    }
+    const std::size_t per_eval = layers_.size() + 2;
+    for (int e = 0; e < pr.n_evals; ++e) host[static_cast<std::size_t>(e) * per_eval].add_vec = pr.tp + static_cast<std::size_t>(e) * H;
+    if (cudaMemcpy(pr.table, host.data(), host.size() * sizeof(fp::Layer), cudaMemcpyHostToDevice) != cudaSuccess) {
+      err = "flow program upload failed";
+      return false;
+    }
+    it = programs_.emplace(key, pr).first;
+  }
+  const Program& pr = it->second;
+  const int half = static_cast<int>(cfg_.time_dim / 2);
+  time_proj_all_kernel<<<dim3((H + kTimeProjRowsPerBlock - 1) / kTimeProjRowsPerBlock, pr.n_evals),
+                         32 * kTimeProjRowsPerBlock, static_cast<std::size_t>(2 * half) * 4, st>>>(
+      static_cast<int>(first), static_cast<int>(steps_), method_, stages, freqs_, half, wt_, H, pr.tp);
+  cudaMemsetAsync(pr.ctr, 0, static_cast<std::size_t>(pr.n_layers) * pr.tiles_n * sizeof(int), st);
+  const int grid = std::min(pr.total_tiles, ctx_->sm_count);
+  if (pr.trace != nullptr)
+    cudaMemsetAsync(pr.trace, 0, static_cast<std::size_t>(pr.total_tiles) * fp::kTraceStamps * 8, st);
+  fp::flow_program_kernel<<<grid, fp::THREADS, fp::SMEM_BYTES, st>>>(pr.table, pr.n_layers, pr.total_tiles, pr.ctr,
+                                                                      pr.tiles_n, ctx_->d_err, pr.trace);
+  if (cudaGetLastError() != cudaSuccess) {
+    err = "flow program launch failed";
+    return false;
+  }
+  if (pr.trace != nullptr) {
+    // profiling only: wait for the call and write "tile layer m n" and the
+    // five stamps (ns from the first producer start) per line
+    std::vector<unsigned long long> h(static_cast<std::size_t>(pr.total_tiles) * fp::kTraceStamps);
+    cudaStreamSynchronize(st);
+    cudaMemcpy(h.data(), pr.trace, h.size() * 8, cudaMemcpyDeviceToHost);
+    unsigned long long t0 = ~0ull;
+    for (std::size_t i = 0; i < h.size(); i += fp::kTraceStamps)
+      if (h[i] != 0) t0 = std::min(t0, h[i]);
+    if (FILE* f = std::fopen(std::getenv("FLOWEDGE_FLOW_TRACE"), "w")) {
+      std::fprintf(f, "tile layer m n start dep_met mma_issued epi_start published\n");
+      int layer = 0, base = 0;
+      for (int t = 0; t < pr.total_tiles; ++t) {
+        while (layer + 1 < pr.n_layers && t >= base + pr.tiles_m[static_cast<std::size_t>(layer)] * pr.tiles_n) {
+          base += pr.tiles_m[static_cast<std::size_t>(layer)] * pr.tiles_n;
+          ++layer;
+        }
+        const int tm = pr.tiles_m[static_cast<std::size_t>(layer)];
+        std::fprintf(f, "%d %d %d %d", t, layer, (t - base) % tm, (t - base) / tm);
+        for (int k = 0; k < fp::kTraceStamps; ++k) {
+          const unsigned long long v = h[static_cast<std::size_t>(t) * fp::kTraceStamps + k];
+          std::fprintf(f, " %lld", v == 0 ? -1LL : static_cast<long long>(v - t0));
+        }
+        std::fprintf(f, "\n");
+      }
+      std::fclose(f);
+    }
+  }
+  used = true;
+  return true;
+}
+
 int Flow::advance(std::size_t first, std::size_t count, float* out, std::string& err) noexcept {
   cudaSetDevice(ctx_->device);
   cudaStream_t st = ctx_->stream;
   const bool tc = use_tc(batch_);
   bool fused = false;
   if (count > 0 && !fused_advance(first, count, st, err, fused)) return 2;
+  if (count > 0 && !fused && !program_solve(first, count, st, err, fused)) return 2;
   if (count > 0 && !fused) {
     const auto key = std::make_tuple(batch_, method_, tc, steps_);
     auto it = graphs_.find(key);
@@ -946,6 +1156,13 @@ int Flow::sample_device(const float* condition, const float* x0, std::size_t bat
   method_ = method;
   if (!prepare(condition, x0, batch, true, true, st, err)) return 2;
   const bool tc = use_tc(batch);
+  bool programmed = false;
+  if (!program_solve(0, steps, st, err, programmed)) return 2;
+  if (programmed) {
+    store_rows_kernel<<<ew_grid(static_cast<long long>(batch) * cfg_.action_dim, 256, *ctx_), 256, 0, st>>>(
+        x_, static_cast<int>(batch), static_cast<int>(cfg_.action_dim), a_pad_, out);
+    return cudaGetLastError() == cudaSuccess ? 0 : 2;
+  }
   const auto key = std::make_tuple(batch, method, tc, steps);
   auto it = graphs_.find(key);
   if (it == graphs_.end()) {

@@ -63,6 +63,12 @@ bool encode_3d(CUtensorMap* map, const TcSource& s, std::uint32_t box_l, std::ui
 
 }  // namespace
 
+bool encode_tmap_2d(CUtensorMap* map, const void* ptr, std::uint64_t inner, std::uint64_t outer,
+                    std::uint32_t box_inner, std::uint32_t box_outer, bool fp16, std::string& err) {
+  return encode_2d(map, ptr, inner, outer, box_inner, box_outer,
+                   fp16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, err);
+}
+
 std::uint64_t device_malloc_count() noexcept { return g_device_mallocs.load(); }
 std::uint64_t host_malloc_count() noexcept { return g_host_mallocs.load(); }
 
@@ -175,7 +181,7 @@ const char* device_error_text(int code) noexcept {
     case kErrTmemAlloc: return "tensor memory allocation failed";
     case kErrGridBarrierTimeout: return "a device grid barrier timed out";
     case kErrProgramLayout: return "internal error: small-batch program layout check failed";
-    case kErrDependencyTimeout: return "a small-batch program dependency wait timed out";
+    case kErrDependencyTimeout: return "a program dependency wait timed out (small-batch U-Net or tensor-core flow solve)";
     case kErrStageTimeout: return "a staged-input wait of the selective scan timed out";
     default: return "a device pipeline wait timed out";
   }

@@ -123,6 +123,12 @@ struct TcLaunch {
 
 cudaError_t tc_gemm(const TcLaunch& launch, DeviceContext& ctx, cudaStream_t stream, std::string& err);
 
+// 2-D tensor map of a 16-bit row-major matrix [outer][inner] (128-byte
+// swizzle, box {box_inner, box_outer}), for kernels that keep their maps in
+// device memory.
+bool encode_tmap_2d(CUtensorMap* map, const void* ptr, std::uint64_t inner, std::uint64_t outer,
+                    std::uint32_t box_inner, std::uint32_t box_outer, bool fp16, std::string& err);
+
 // grid size for grid-stride elementwise kernels
 inline int ew_grid(long long total, int threads, const DeviceContext& ctx) {
   long long blocks = (total + threads - 1) / threads;

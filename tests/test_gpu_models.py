@@ -286,8 +286,10 @@ def test_flow_c2_fp32_matches_reference_core(tmp_path):
 
 
 def test_flow_c2_bf16_batched_tensor_path(tmp_path):
-    """C2 at batch 256 in bf16 mode (tcgen05 GEMMs, fp16 operands) against the
-    restatement on the same bf16-rounded weights (bar 2e-2)."""
+    """C2 at batch 256 in bf16 mode (the persistent tcgen05 solve: fp16
+    operands, the ODE stage in the output projection's epilogue) against the
+    restatement on the same bf16-rounded weights (bar 2e-2), for each solver
+    and for a ragged batch of 300 rows."""
     tensors = _round_bf16(ck.flow_tensors(ck.FLOW_C2, seed=3))
     path = tmp_path / "flow_c2_bf16w.safetensors"
     ck.write_checkpoint(path, tensors)
@@ -295,13 +297,20 @@ def test_flow_c2_bf16_batched_tensor_path(tmp_path):
     cond = rng.standard_normal((256, 512)).astype(np.float32)
     x0 = rng.standard_normal((256, 350)).astype(np.float32)
     flow = restate.FlowModel(tensors)
-    e = Engine(path, threads=0, device=0, precision="bf16", max_batch=256)
-    for solver, steps in (("euler", 10), ("rk4", 4)):
+    e = Engine(path, threads=0, device=0, precision="bf16", max_batch=300)
+    for solver, steps in (("euler", 10), ("rk4", 4), ("heun", 3)):
         got = e.sample_condition_batch(cond, x0, steps=steps, method=solver)
         expected = flow.sample(cond, x0, steps, solver)
         err = float(np.abs(got - expected).max())
         print(f"C2 flow bf16 batch-256 {solver}-{steps} max-abs vs restatement: {err:.3g}")
         assert err <= 2e-2
+    # a ragged token block (300 rows: one full 256-row block and 44 rows)
+    cond3 = rng.standard_normal((300, 512)).astype(np.float32)
+    x3 = rng.standard_normal((300, 350)).astype(np.float32)
+    got3 = e.sample_condition_batch(cond3, x3, steps=5, method="euler")
+    err3 = float(np.abs(got3 - flow.sample(cond3, x3, 5, "euler")).max())
+    print(f"C2 flow bf16 batch-300 euler-5 max-abs vs restatement: {err3:.3g}")
+    assert err3 <= 2e-2
     # the small-batch (weight-streaming) path on the same engine
     got1 = e.sample_condition(cond[0], x0[0], steps=10, method="euler")
     assert np.abs(got1 - flow.sample(cond[:1], x0[:1], 10, "euler")[0]).max() <= 1e-3
@@ -320,7 +329,7 @@ def test_flow_c2_fp32_batched_split_tensor_path(tmp_path):
     x0 = rng.standard_normal((256, 350)).astype(np.float32)
     flow = restate.FlowModel(tensors)
     e = Engine(path, threads=0, device=0, precision="fp32", max_batch=256)
-    for solver, steps in (("euler", 10), ("rk4", 4)):
+    for solver, steps in (("euler", 10), ("rk4", 4), ("heun", 3)):
         got = e.sample_condition_batch(cond, x0, steps=steps, method=solver)
         expected = flow.sample(cond, x0, steps, solver)
         err = float(np.abs(got - expected).max())
