@@ -54,7 +54,7 @@ SEED = 0
 #       --clock-control none -k regex:tc_gemm -c 80 --csv --log-file traffic.csv
 #       python bench.py --steps 1 --warmup 1 --no-cpu-baseline --no-extras --no-parity
 # (launches 1-36 after the FiLM-condition GEMM).  Other shard sizes report null.
-CONV_TRAFFIC_PER_FORWARD = {4096: 34.79e9, 1024: 7.26e9}
+CONV_TRAFFIC_PER_FORWARD = {4096: 32.39e9, 1024: 7.22e9}
 
 
 def _dist():
