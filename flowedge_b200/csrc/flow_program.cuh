@@ -150,6 +150,140 @@ __device__ __forceinline__ void ode_chunk(const Ode& o, int b0, int n, int a, co
   }
 }
 
+// Epilogue of one tile, one function per kind of layer: each allocates its
+// own registers, so the output projection's state and the input projection's
+// condition-row prefetch do not spill the hidden layers' loop.  Chunks of 16
+// columns: the next chunk's global loads (condition rows, or the ODE state)
+// are in flight while this chunk is computed, and this chunk's TMEM load
+// overlaps them; the layer's fields are read into registers first (the
+// stores cannot alias them).
+
+// The solver fields of an output projection tile.
+__device__ __forceinline__ Ode ode_fields(const Layer& L) {
+  Ode ode{};
+  ode.method = L.method;
+  ode.stage = L.stage;
+  ode.ld = L.ld;
+  ode.ld_in = L.ld_in;
+  ode.next_mode = L.next_mode;
+  ode.dt = 1.0f / static_cast<float>(L.steps);
+  ode.x = L.x;
+  ode.probe = L.probe;
+  ode.k0 = L.k[0];
+  ode.k1 = L.k[1];
+  ode.k2 = L.k[2];
+  ode.next_in = L.next_in;
+  return ode;
+}
+
+// Euler: x += dt v, the next input from x.
+__device__ __noinline__ void epi_euler(const Layer& L, int m, int tok0, int lim, uint32_t tbase) {
+  const Ode ode = ode_fields(L);
+  float g_cur[16], g_nxt[16];
+  auto load_x = [&](int c, float (&g)[16]) {
+    const int n = min(max(lim - c, 0), 16);
+#pragma unroll
+    for (int j = 0; j < 16; ++j) g[j] = j < n ? ode.x[static_cast<long long>(tok0 + c + j) * ode.ld + m] : 0.0f;
+  };
+  load_x(0, g_cur);
+#pragma unroll 1
+  for (int c = 0; c < EPI_COLS; c += 16) {
+    uint32_t r[16];
+    tmem_ld16_async(tbase + c, r);
+    if (c + 16 < EPI_COLS) load_x(c + 16, g_nxt);
+    const int n = min(max(lim - c, 0), 16);
+    tmem_wait_ld(r);
+#pragma unroll
+    for (int j = 0; j < 16; ++j)
+      if (j < n) {
+        const int b = tok0 + c + j;
+        const float nxt = g_cur[j] + ode.dt * __uint_as_float(r[j]);
+        ode.x[static_cast<long long>(b) * ode.ld + m] = nxt;
+        const __half hi = to_half_sat(nxt);
+        if (ode.next_mode == 2) {
+          const long long ii = static_cast<long long>(b) * 2 * ode.ld_in + m;
+          ode.next_in[ii] = hi;
+          ode.next_in[ii + ode.ld_in] = __float2half_rn(nxt - __half2float(hi));
+        } else {
+          ode.next_in[static_cast<long long>(b) * ode.ld_in + m] = hi;
+        }
+      }
+#pragma unroll
+    for (int j = 0; j < 16; ++j) g_cur[j] = g_nxt[j];
+  }
+}
+
+// Heun and RK4 stages, eight tokens at a time.
+__device__ __noinline__ void epi_stage(const Layer& L, int m, bool m_ok, int tok0, int lim, uint32_t tbase) {
+  const Ode ode = ode_fields(L);
+#pragma unroll 1
+  for (int c = 0; c < EPI_COLS; c += 8) {
+    float v[8];
+    tmem_ld8(tbase + c, v);
+    if (m_ok) ode_chunk<8>(ode, tok0 + c, min(max(lim - c, 0), 8), m, v);
+  }
+}
+
+// Hidden layers, and with TOK the input projection (+ the condition rows).
+template <bool TOK>
+__device__ __noinline__ void epi_plain(const Layer& L, int m, int mm, int tok0, int lim, uint32_t tbase) {
+  const float addv = L.add_vec != nullptr ? L.add_vec[mm] : 0.0f;
+  const float* __restrict__ add_tok = L.add_tok;
+  const int add_ld = L.add_ld, out_ld = L.out_ld, out_lo = L.out_lo;
+  const bool silu = L.act == tc::kActSilu;
+  __half* __restrict__ out = L.out;
+  // the condition rows (input projection only) one chunk ahead
+  float g_cur[16], g_nxt[16];
+  constexpr bool has_tok = TOK;
+  auto load_g = [&](int c, float (&g)[16]) {
+    const int n = min(max(lim - c, 0), 16);
+    const float* ap = add_tok + (static_cast<long long>(tok0 + c) * add_ld + mm);
+#pragma unroll
+    for (int j = 0; j < 16; ++j) g[j] = j < n ? ap[static_cast<long long>(j) * add_ld] : 0.0f;
+  };
+  if constexpr (has_tok) load_g(0, g_cur);
+#pragma unroll 1
+  for (int c = 0; c < EPI_COLS; c += 16) {
+    uint32_t r[16];
+    tmem_ld16_async(tbase + c, r);
+    if (has_tok && c + 16 < EPI_COLS) load_g(c + 16, g_nxt);
+    const int n = min(max(lim - c, 0), 16);
+    tmem_wait_ld(r);
+    float y[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      y[j] = __uint_as_float(r[j]) + addv;
+      if (has_tok) y[j] += g_cur[j];
+      if (silu) y[j] = silu_fast(y[j]);
+    }
+    __half* o = out + (static_cast<long long>(tok0 + c) * out_ld + m);
+    if (n == 16) {
+      if (out_lo != 0) {
+#pragma unroll
+        for (int j = 0; j < 16; ++j, o += out_ld) {
+          const __half hi = to_half_sat(y[j]);
+          o[0] = hi;
+          o[out_lo] = __float2half_rn(y[j] - __half2float(hi));
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < 16; ++j, o += out_ld) *o = half_satfinite(y[j]);
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 16; ++j)
+        if (j < n) {
+          const __half hi = to_half_sat(y[j]);
+          o[static_cast<long long>(j) * out_ld] = hi;
+          if (out_lo != 0) o[static_cast<long long>(j) * out_ld + out_lo] = __float2half_rn(y[j] - __half2float(hi));
+        }
+    }
+    if (has_tok)
+#pragma unroll
+      for (int j = 0; j < 16; ++j) g_cur[j] = g_nxt[j];
+  }
+}
+
 __device__ __forceinline__ void fence_proxy_async_global() {
   asm volatile("fence.proxy.async.global;" ::: "memory");
 }
@@ -376,123 +510,14 @@ __global__ void __launch_bounds__(THREADS, 1)
       const int tok0 = n_blk * BN + col0;
       const int lim = m_ok ? min(max(L.n_tokens - tok0, 0), EPI_COLS) : 0;
       const uint32_t tbase = tmem_base + lane_base + acc * BN + col0;
-      // chunks of 16 columns: the next chunk's global loads (condition rows,
-      // or the ODE state) are in flight while this chunk is computed, and this
-      // chunk's TMEM load overlaps them.  The two kinds of layer run separate
-      // loops, each with its own fields in registers (the stores cannot alias
-      // them).
-      if (L.ode != 0) {
-        Ode ode{};
-        ode.method = L.method;
-        ode.stage = L.stage;
-        ode.ld = L.ld;
-        ode.ld_in = L.ld_in;
-        ode.next_mode = L.next_mode;
-        ode.dt = 1.0f / static_cast<float>(L.steps);
-        ode.x = L.x;
-        ode.probe = L.probe;
-        ode.k0 = L.k[0];
-        ode.k1 = L.k[1];
-        ode.k2 = L.k[2];
-        ode.next_in = L.next_in;
-        if (ode.method == 0) {
-          // Euler: x += dt v, the next input from x
-          float g_cur[16], g_nxt[16];
-          auto load_x = [&](int c, float (&g)[16]) {
-            const int n = min(max(lim - c, 0), 16);
-#pragma unroll
-            for (int j = 0; j < 16; ++j) g[j] = j < n ? ode.x[static_cast<long long>(tok0 + c + j) * ode.ld + m] : 0.0f;
-          };
-          load_x(0, g_cur);
-#pragma unroll 1
-          for (int c = 0; c < EPI_COLS; c += 16) {
-            uint32_t r[16];
-            tmem_ld16_async(tbase + c, r);
-            if (c + 16 < EPI_COLS) load_x(c + 16, g_nxt);
-            const int n = min(max(lim - c, 0), 16);
-            tmem_wait_ld(r);
-#pragma unroll
-            for (int j = 0; j < 16; ++j)
-              if (j < n) {
-                const int b = tok0 + c + j;
-                const float nxt = g_cur[j] + ode.dt * __uint_as_float(r[j]);
-                ode.x[static_cast<long long>(b) * ode.ld + m] = nxt;
-                const __half hi = to_half_sat(nxt);
-                if (ode.next_mode == 2) {
-                  const long long ii = static_cast<long long>(b) * 2 * ode.ld_in + m;
-                  ode.next_in[ii] = hi;
-                  ode.next_in[ii + ode.ld_in] = __float2half_rn(nxt - __half2float(hi));
-                } else {
-                  ode.next_in[static_cast<long long>(b) * ode.ld_in + m] = hi;
-                }
-              }
-#pragma unroll
-            for (int j = 0; j < 16; ++j) g_cur[j] = g_nxt[j];
-          }
-        } else {
-#pragma unroll 1
-          for (int c = 0; c < EPI_COLS; c += 8) {
-            float v[8];
-            tmem_ld8(tbase + c, v);
-            if (m_ok) ode_chunk<8>(ode, tok0 + c, min(max(lim - c, 0), 8), m, v);
-          }
-        }
+      if (L.ode != 0 && L.method == 0) {
+        epi_euler(L, m, tok0, lim, tbase);
+      } else if (L.ode != 0) {
+        epi_stage(L, m, m_ok, tok0, lim, tbase);
+      } else if (L.add_tok != nullptr) {
+        epi_plain<true>(L, m, mm, tok0, lim, tbase);
       } else {
-        const float addv = L.add_vec != nullptr ? L.add_vec[mm] : 0.0f;
-        const float* __restrict__ add_tok = L.add_tok;
-        const int add_ld = L.add_ld, out_ld = L.out_ld, out_lo = L.out_lo;
-        const bool silu = L.act == tc::kActSilu;
-        __half* __restrict__ out = L.out;
-        // the condition rows (input projection only) one chunk ahead
-        float g_cur[16], g_nxt[16];
-        const bool has_tok = add_tok != nullptr;
-        auto load_g = [&](int c, float (&g)[16]) {
-          const int n = min(max(lim - c, 0), 16);
-          const float* ap = add_tok + (static_cast<long long>(tok0 + c) * add_ld + mm);
-#pragma unroll
-          for (int j = 0; j < 16; ++j) g[j] = j < n ? ap[static_cast<long long>(j) * add_ld] : 0.0f;
-        };
-        if (has_tok) load_g(0, g_cur);
-#pragma unroll 1
-        for (int c = 0; c < EPI_COLS; c += 16) {
-          uint32_t r[16];
-          tmem_ld16_async(tbase + c, r);
-          if (has_tok && c + 16 < EPI_COLS) load_g(c + 16, g_nxt);
-          const int n = min(max(lim - c, 0), 16);
-          tmem_wait_ld(r);
-          float y[16];
-#pragma unroll
-          for (int j = 0; j < 16; ++j) {
-            y[j] = __uint_as_float(r[j]) + addv;
-            if (has_tok) y[j] += g_cur[j];
-            if (silu) y[j] = silu_fast(y[j]);
-          }
-          __half* o = out + (static_cast<long long>(tok0 + c) * out_ld + m);
-          if (n == 16) {
-            if (out_lo != 0) {
-#pragma unroll
-              for (int j = 0; j < 16; ++j, o += out_ld) {
-                const __half hi = to_half_sat(y[j]);
-                o[0] = hi;
-                o[out_lo] = __float2half_rn(y[j] - __half2float(hi));
-              }
-            } else {
-#pragma unroll
-              for (int j = 0; j < 16; ++j, o += out_ld) *o = half_satfinite(y[j]);
-            }
-          } else {
-#pragma unroll
-            for (int j = 0; j < 16; ++j)
-              if (j < n) {
-                const __half hi = to_half_sat(y[j]);
-                o[static_cast<long long>(j) * out_ld] = hi;
-                if (out_lo != 0) o[static_cast<long long>(j) * out_ld + out_lo] = __float2half_rn(y[j] - __half2float(hi));
-              }
-          }
-          if (has_tok)
-#pragma unroll
-            for (int j = 0; j < 16; ++j) g_cur[j] = g_nxt[j];
-        }
+        epi_plain<false>(L, m, mm, tok0, lim, tbase);
       }
       tc_fence_before();
       mbar_arrive(&tempty[acc]);
