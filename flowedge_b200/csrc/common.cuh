@@ -474,7 +474,7 @@ __device__ __forceinline__ float ex2_approx(float x) {
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
 }
-// 2^x for a pair of x <= 0 on the FMA pipe, so that a kernel bound by the
+// 2^x for a pair of x <= 126 on the FMA pipe, so that a kernel bound by the
 // MUFU unit can move some of its exponentials off it.  Range reduction
 // x = k + r, k = round(x), r in [-0.5, 0.5], by the 1.5 * 2^23 rounding
 // constant (its low mantissa bits then hold k); 2^r by the degree-5
@@ -499,6 +499,21 @@ __device__ __forceinline__ float2 exp2_poly2(float2 x) {
   // are k in the exponent field
   return make_float2(__int_as_float(__float_as_int(p.x) + (__float_as_int(t.x) << 23)),
                      __int_as_float(__float_as_int(p.y) + (__float_as_int(t.y) << 23)));
+}
+
+// SiLU of a pair with one MUFU operation per element: x / (1 + 2^(-x log2 e)),
+// the power by exp2_poly2 on the FMA pipe (argument clamped at 126: for
+// x < -87 silu(x) is -0 to fp32 precision, and 1 + 2^126 keeps the reciprocal
+// finite), the reciprocal by rcp.approx.  For values rounded to fp16 right
+// afterwards (relative error ~1e-6).
+__device__ __forceinline__ float2 silu2_fma(float2 x) {
+  constexpr float kLog2e = 1.4426950408889634f;
+  const float2 e = exp2_poly2(make_float2(fminf(-x.x * kLog2e, 126.0f), fminf(-x.y * kLog2e, 126.0f)));
+  const float2 d = __fadd2_rn(e, make_float2(1.0f, 1.0f));
+  float2 r;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r.x) : "f"(d.x));
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r.y) : "f"(d.y));
+  return __fmul2_rn(x, r);
 }
 
 __device__ __forceinline__ float softplus_f(float x) { return fmaxf(x, 0.0f) + log1pf(expf(-fabsf(x))); }

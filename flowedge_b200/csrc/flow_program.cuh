@@ -251,10 +251,12 @@ __device__ __noinline__ void epi_plain(const Layer& L, int m, int mm, int tok0, 
     tmem_wait_ld(r);
     float y[16];
 #pragma unroll
-    for (int j = 0; j < 16; ++j) {
-      y[j] = __uint_as_float(r[j]) + addv;
-      if (has_tok) y[j] += g_cur[j];
-      if (silu) y[j] = silu_fast(y[j]);
+    for (int j = 0; j < 16; j += 2) {
+      float2 v2 = make_float2(__uint_as_float(r[j]) + addv, __uint_as_float(r[j + 1]) + addv);
+      if (has_tok) v2 = __fadd2_rn(v2, make_float2(g_cur[j], g_cur[j + 1]));
+      if (silu) v2 = silu2_fma(v2);  // one MUFU operation per element (the epilogue's bound otherwise)
+      y[j] = v2.x;
+      y[j + 1] = v2.y;
     }
     __half* o = out + (static_cast<long long>(tok0 + c) * out_ld + m);
     if (n == 16) {
