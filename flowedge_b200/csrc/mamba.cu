@@ -154,6 +154,80 @@ __global__ void causal_conv_kernel(const float* __restrict__ xz, int B, int L, i
   }
 }
 
+// causal_conv_kernel for a compile-time width DC (4 for the encoders here):
+// the window and weights take DC instead of kMaxConv registers, and each
+// thread keeps its next kConvAhead inputs in flight (a ring of registers, the
+// step loop unrolled by kConvAhead), so more threads per SM each with more
+// loads outstanding.  Same expressions in the same order as
+// causal_conv_kernel (window oldest to newest against weights 0 .. DC - 1).
+constexpr int kConvAhead = 4;
+template <int DC>
+__global__ void __launch_bounds__(256) causal_conv_fixed_kernel(const float* __restrict__ xz, int B, int L, int di,
+                                                                const float* __restrict__ w,
+                                                                const float* __restrict__ bias, float* __restrict__ u,
+                                                                __half* __restrict__ u_bf, int split) {
+  const int q = di >> 2;
+  const long long total = static_cast<long long>(B) * q;
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const int b = static_cast<int>(i / q);
+    const int c = static_cast<int>(i - static_cast<long long>(b) * q) * 4;
+    float wk[4][DC];
+#pragma unroll
+    for (int j = 0; j < DC; ++j)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) wk[e][j] = w[(c + e) * DC + j];
+    const float4 bv = *reinterpret_cast<const float4*>(bias + c);
+    float4 win[DC];
+#pragma unroll
+    for (int j = 0; j < DC; ++j) win[j] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    const long long tok0 = static_cast<long long>(b) * L;
+    const float* src = xz + tok0 * 2 * di + c;
+    float4 ahead[kConvAhead];
+#pragma unroll
+    for (int k = 0; k < kConvAhead; ++k)
+      ahead[k] = k < L ? __ldg(reinterpret_cast<const float4*>(src + static_cast<long long>(k) * 2 * di))
+                       : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    for (int t0 = 0; t0 < L; t0 += kConvAhead) {
+#pragma unroll
+      for (int k = 0; k < kConvAhead; ++k) {
+        const int t = t0 + k;
+        if (t >= L) break;
+#pragma unroll
+        for (int j = 0; j + 1 < DC; ++j) win[j] = win[j + 1];
+        win[DC - 1] = ahead[k];
+        if (t + kConvAhead < L)
+          ahead[k] = __ldg(reinterpret_cast<const float4*>(src + static_cast<long long>(t + kConvAhead) * 2 * di));
+        float a0 = bv.x, a1 = bv.y, a2 = bv.z, a3 = bv.w;
+#pragma unroll
+        for (int j = 0; j < DC; ++j) {
+          a0 += wk[0][j] * win[j].x;
+          a1 += wk[1][j] * win[j].y;
+          a2 += wk[2][j] * win[j].z;
+          a3 += wk[3][j] * win[j].w;
+        }
+        const float4 v = make_float4(silu_f(a0), silu_f(a1), silu_f(a2), silu_f(a3));
+        const long long o = (tok0 + t) * di + c;
+        *reinterpret_cast<float4*>(u + o) = v;
+        if (u_bf != nullptr) {
+          const __half h0 = to_half_sat(v.x), h1 = to_half_sat(v.y), h2 = to_half_sat(v.z), h3 = to_half_sat(v.w);
+          const __half2 p01 = __halves2half2(h0, h1);
+          const __half2 p23 = __halves2half2(h2, h3);
+          const long long ob = split ? (tok0 + t) * 2 * di + c : o;
+          *reinterpret_cast<uint2*>(u_bf + ob) =
+              make_uint2(*reinterpret_cast<const uint32_t*>(&p01), *reinterpret_cast<const uint32_t*>(&p23));
+          if (split) {
+            const __half2 l01 = __floats2half2_rn(v.x - __half2float(h0), v.y - __half2float(h1));
+            const __half2 l23 = __floats2half2_rn(v.z - __half2float(h2), v.w - __half2float(h3));
+            *reinterpret_cast<uint2*>(u_bf + ob + di) =
+                make_uint2(*reinterpret_cast<const uint32_t*>(&l01), *reinterpret_cast<const uint32_t*>(&l23));
+          }
+        }
+      }
+    }
+  }
+}
+
 // Few sequences: one thread per (token, channel), the dc inputs re-read
 __global__ void causal_conv_tok_kernel(const float* xz, int B, int L, int di, int dc, const float* w,
                                        const float* bias, float* u, __half* u_bf, int split) {
@@ -1257,7 +1331,10 @@ bool Mamba::run_layers(long long n_tok, int B, int L, bool tc, cudaStream_t st, 
                                                                                       tc ? nb_ : nullptr, split);
     if (!gemm(Ly.in_proj, tc ? static_cast<const void*>(nb_) : normed, dm, n_tok, xz_, 2 * di, false, tc, st, err))
       return false;
-    if (static_cast<long long>(B) * (di / 4) >= 32LL * 32 * ctx_->sm_count)
+    if (static_cast<long long>(B) * (di / 4) >= 32LL * 32 * ctx_->sm_count && dc == 4)
+      causal_conv_fixed_kernel<4><<<ew_grid(static_cast<long long>(B) * (di / 4), 256, *ctx_), 256, 0, st>>>(
+          xz_, B, L, di, Ly.conv_w, Ly.conv_b, u_, tc ? ub_ : nullptr, split);
+    else if (static_cast<long long>(B) * (di / 4) >= 32LL * 32 * ctx_->sm_count)
       causal_conv_kernel<<<ew_grid(static_cast<long long>(B) * (di / 4), 256, *ctx_), 256, 0, st>>>(
           xz_, B, L, di, dc, Ly.conv_w, Ly.conv_b, u_, tc ? ub_ : nullptr, split);
     else
