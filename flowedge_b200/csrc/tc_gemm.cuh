@@ -629,9 +629,15 @@ static __global__ void __launch_bounds__(THREADS, 1)
           } else if (p.out_f32) {
             float* o = static_cast<float*>(p.out) + oc;
             if (p.out_accumulate) {
+              // the chunk's previous values all requested before its first
+              // store (in place, the compiler cannot tell the rows apart, so
+              // `o[j * cs] += y[j]` would wait out one round trip per element)
+              float prev[CH];
+#pragma unroll
+              for (int j = 0; j < CH; ++j) prev[j] = c + j < lim ? o[j * cs] : 0.0f;
 #pragma unroll
               for (int j = 0; j < CH; ++j)
-                if (c + j < lim) o[j * cs] += y[j];
+                if (c + j < lim) o[j * cs] = prev[j] + y[j];
             } else {
 #pragma unroll
               for (int j = 0; j < CH; ++j)
