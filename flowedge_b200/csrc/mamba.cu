@@ -3,7 +3,10 @@
 // Per layer, tokens of all sequences at once (token-major [B*L][width]):
 //   normed = RMSNorm(hidden)                     rmsnorm_kernel
 //   [x | z] = normed W_in^T                      GEMM (fp32 out)
-//   u = SiLU(causal depthwise conv(x) + b)       causal_conv_kernel
+//   u = SiLU(causal depthwise conv(x) + b)       causal_conv_kernel, or the
+//                                                in-projection's epilogue
+//                                                (bf16 tensor path, sequences
+//                                                that tile its token blocks)
 //   [dt_in | B | C] = u W_x^T                    GEMM (fp32 out)
 //   scan: dt = softplus(dt_in W_dt^T + b_dt) fused into the selective scan,
 //         y = (D u + sum_n h_n C_n) * SiLU(z)   scan_kernel
@@ -926,8 +929,10 @@ class Mamba final : public MambaDevice {
   int write_state(const float* src, std::string& err) noexcept override;
 
  private:
+  // conv: the layer whose causal conv runs in the epilogue (tensor path,
+  // in-projection; sequences of conv_seq tokens)
   bool gemm(const Mat& m, const void* in, int in_ld, long long n_tok, float* out, int out_ld, bool accumulate,
-            bool tc, cudaStream_t st, std::string& err);
+            bool tc, cudaStream_t st, std::string& err, const Layer* conv = nullptr, int conv_seq = 0);
   bool run_layers(long long n_tok, int B, int L, bool tc, cudaStream_t st, std::string& err);
   // one decode token: the token from pinned_[0], the normed output to pinned_ + 1
   bool record_step(cudaStream_t st, std::string& err);
@@ -1254,7 +1259,7 @@ int Mamba::reserve(std::size_t batch, std::size_t max_len, std::string& err) noe
 }
 
 bool Mamba::gemm(const Mat& m, const void* in, int in_ld, long long n_tok, float* out, int out_ld, bool accumulate,
-                 bool tc, cudaStream_t st, std::string& err) {
+                 bool tc, cudaStream_t st, std::string& err, const Layer* conv, int conv_seq) {
   if (tc) {
     TcLaunch l;
     l.fp16 = true;
@@ -1279,6 +1284,17 @@ bool Mamba::gemm(const Mat& m, const void* in, int in_ld, long long n_tok, float
     l.out_accumulate = accumulate;
     l.out = out;
     l.out_ld = out_ld;
+    if (conv != nullptr) {
+      // in-projection with the causal conv in its epilogue: x half -> u (fp32
+      // and the fp16 operand of the x-projection), z half -> out
+      l.conv_w = conv->conv_w;
+      l.conv_b = conv->conv_b;
+      l.conv_u = u_;
+      l.conv_u16 = ub_;
+      l.conv_rows = static_cast<int>(cfg_.d_inner);
+      l.conv_seq = conv_seq;
+      l.conv_ld = static_cast<int>(cfg_.d_inner);
+    }
     return tc_gemm(l, *ctx_, st, err) == cudaSuccess;
   }
   // CUDA-core path, chunks of <= 4096 tokens through the partial buffer
@@ -1324,22 +1340,29 @@ bool Mamba::run_layers(long long n_tok, int B, int L, bool tc, cudaStream_t st, 
   // the scan's fast exponentials belong to the bf16 mode only
   const int split = tc && prec_ != Precision::kBF16 ? 1 : 0;
   const bool fast = prec_ == Precision::kBF16;
+  // bf16 tensor path with sequences that tile the GEMM's token blocks: the
+  // causal conv runs in the in-projection's epilogue, and only z goes to xz
+  const bool conv_fused = tc && split == 0 && dc == 4 && di % tc::BM == 0 && L <= tc::BN && tc::BN % L == 0;
   for (const Layer& Ly : layers_) {
     rmsnorm_kernel<<<static_cast<unsigned>((n_tok * 32 + 255) / 256), 256, 0, st>>>(hidden_, Ly.norm,
                                                                                       static_cast<int>(n_tok), dm,
                                                                                       tc ? nullptr : normed,
                                                                                       tc ? nb_ : nullptr, split);
-    if (!gemm(Ly.in_proj, tc ? static_cast<const void*>(nb_) : normed, dm, n_tok, xz_, 2 * di, false, tc, st, err))
-      return false;
-    if (static_cast<long long>(B) * (di / 4) >= 32LL * 32 * ctx_->sm_count && dc == 4)
-      causal_conv_fixed_kernel<4><<<ew_grid(static_cast<long long>(B) * (di / 4), 256, *ctx_), 256, 0, st>>>(
-          xz_, B, L, di, Ly.conv_w, Ly.conv_b, u_, tc ? ub_ : nullptr, split);
-    else if (static_cast<long long>(B) * (di / 4) >= 32LL * 32 * ctx_->sm_count)
-      causal_conv_kernel<<<ew_grid(static_cast<long long>(B) * (di / 4), 256, *ctx_), 256, 0, st>>>(
-          xz_, B, L, di, dc, Ly.conv_w, Ly.conv_b, u_, tc ? ub_ : nullptr, split);
-    else
-      causal_conv_tok_kernel<<<ew_grid(n_tok * di, 256, *ctx_), 256, 0, st>>>(xz_, B, L, di, dc, Ly.conv_w, Ly.conv_b,
-                                                                            u_, tc ? ub_ : nullptr, split);
+    if (conv_fused) {
+      if (!gemm(Ly.in_proj, nb_, dm, n_tok, xz_, 2 * di, false, tc, st, err, &Ly, L)) return false;
+    } else {
+      if (!gemm(Ly.in_proj, tc ? static_cast<const void*>(nb_) : normed, dm, n_tok, xz_, 2 * di, false, tc, st, err))
+        return false;
+      if (static_cast<long long>(B) * (di / 4) >= 32LL * 32 * ctx_->sm_count && dc == 4)
+        causal_conv_fixed_kernel<4><<<ew_grid(static_cast<long long>(B) * (di / 4), 256, *ctx_), 256, 0, st>>>(
+            xz_, B, L, di, Ly.conv_w, Ly.conv_b, u_, tc ? ub_ : nullptr, split);
+      else if (static_cast<long long>(B) * (di / 4) >= 32LL * 32 * ctx_->sm_count)
+        causal_conv_kernel<<<ew_grid(static_cast<long long>(B) * (di / 4), 256, *ctx_), 256, 0, st>>>(
+            xz_, B, L, di, dc, Ly.conv_w, Ly.conv_b, u_, tc ? ub_ : nullptr, split);
+      else
+        causal_conv_tok_kernel<<<ew_grid(n_tok * di, 256, *ctx_), 256, 0, st>>>(xz_, B, L, di, dc, Ly.conv_w,
+                                                                              Ly.conv_b, u_, tc ? ub_ : nullptr, split);
+    }
     if (!gemm(Ly.x_proj, tc ? static_cast<const void*>(ub_) : u_, di, n_tok, dbl_, wd, false, tc, st, err))
       return false;
     const dim3 grid(static_cast<unsigned>((di + 255) / 256), static_cast<unsigned>(B));

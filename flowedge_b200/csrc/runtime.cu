@@ -135,6 +135,8 @@ std::shared_ptr<DeviceContext> make_device_context(int device, std::string& err)
                            tc::SMEM_BYTES) != cudaSuccess ||
       cudaFuncSetAttribute(tc::tc_gemm_kernel<tc::kEpiFused>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                            tc::SMEM_BYTES) != cudaSuccess ||
+      cudaFuncSetAttribute(tc::tc_gemm_kernel<tc::kEpiConv>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           tc::SMEM_BYTES) != cudaSuccess ||
       cudaFuncSetAttribute(tc::tc_gemm_kernel<tc::kEpiFused, false, true>,
                            cudaFuncAttributeMaxDynamicSharedMemorySize, tc::SMEM_BYTES) != cudaSuccess) {
     err = "cannot enable the tensor-core kernel's shared memory";
@@ -372,6 +374,23 @@ cudaError_t tc_gemm(const TcLaunch& l, DeviceContext& ctx, cudaStream_t stream, 
     err = "tc_gemm: the SwiGLU epilogue needs interleaved rows and a plain bf16 output";
     return cudaErrorInvalidValue;
   }
+  if (l.conv_w != nullptr) {
+    if (!l.out_f32 || l.out_accumulate || l.act != tc::kActNone || l.bias != nullptr || l.add_vec != nullptr ||
+        l.add_tok != nullptr || l.stats != nullptr || l.gn_fuse || l.L != 1 || l.conv_b == nullptr ||
+        l.conv_u == nullptr || l.conv_u16 == nullptr || l.conv_rows % tc::BM != 0 || l.conv_seq < 1 ||
+        l.conv_seq > tc::BN || tc::BN % l.conv_seq != 0 || l.n_samples % l.conv_seq != 0 ||
+        static_cast<long long>(l.conv_ld) * tc::BN >= (1LL << 31)) {
+      err = "tc_gemm: the conv epilogue needs a plain fp32 GEMM over whole sequences that tile the token blocks";
+      return cudaErrorInvalidValue;
+    }
+    p.conv_w = l.conv_w;
+    p.conv_b = l.conv_b;
+    p.conv_u = l.conv_u;
+    p.conv_u16 = l.conv_u16;
+    p.conv_rows = l.conv_rows;
+    p.conv_seq = l.conv_seq;
+    p.conv_ld = l.conv_ld;
+  }
   if (l.out_bf16) {
     if (l.out_f32 || l.gn_fuse || l.stats != nullptr || l.out_lo_off != 0) {
       err = "tc_gemm: a bf16 output needs a plain 16-bit epilogue";
@@ -484,6 +503,8 @@ cudaError_t tc_gemm(const TcLaunch& l, DeviceContext& ctx, cudaStream_t stream, 
     rc = cudaLaunchKernelEx(&cfg, tc::tc_gemm_kernel<tc::kEpiFused>, ta, tb[0], tb[1], tb[2], p);
   else if (p.stats != nullptr)
     rc = cudaLaunchKernelEx(&cfg, tc::tc_gemm_kernel<tc::kEpiStats>, ta, tb[0], tb[1], tb[2], p);
+  else if (p.conv_w != nullptr)
+    rc = cudaLaunchKernelEx(&cfg, tc::tc_gemm_kernel<tc::kEpiConv>, ta, tb[0], tb[1], tb[2], p);
   else
     rc = cudaLaunchKernelEx(&cfg, tc::tc_gemm_kernel<tc::kEpiPlain>, ta, tb[0], tb[1], tb[2], p);
   if (rc != cudaSuccess) err = std::string("tc_gemm launch: ") + cudaGetErrorString(rc);

@@ -119,6 +119,13 @@ struct TcLaunch {
   const float* res_f32 = nullptr;
   const void* res16 = nullptr;
   float* out_twin = nullptr;
+  // causal conv + SiLU epilogue on the rows < conv_rows (see
+  // tc::Params::conv_w): plain fp32 GEMM, L = 1, sequences of conv_seq tokens
+  const float* conv_w = nullptr;
+  const float* conv_b = nullptr;
+  float* conv_u = nullptr;
+  __half* conv_u16 = nullptr;
+  int conv_rows = 0, conv_seq = 0, conv_ld = 0;
 };
 
 cudaError_t tc_gemm(const TcLaunch& launch, DeviceContext& ctx, cudaStream_t stream, std::string& err);

@@ -108,6 +108,17 @@ struct Params {
   const float* res_f32;    // residual rows laid out like the output, or null
   const void* res16;       // 16-bit residual (used when res_f32 is null), or null
   float* out_twin;         // fp32 copy of z, or null
+  // causal depthwise conv of 4 taps over each sequence's tokens, then SiLU,
+  // for the rows < conv_rows (kEpiConv; the Mamba in-projection's x half):
+  // u = SiLU(conv_b[m] + sum_j conv_w[m][j] y[t - 3 + j]), taps before the
+  // sequence's first token zero, stored fp32 to conv_u and fp16 to conv_u16
+  // at element token * conv_ld + m; rows >= conv_rows take the plain store.
+  // Sequences of conv_seq tokens (a power of two dividing BN) tile the tokens.
+  const float* conv_w;     // [conv_rows][4]
+  const float* conv_b;
+  float* conv_u;
+  __half* conv_u16;
+  int conv_rows, conv_seq, conv_ld;
   int* err;
 };
 
@@ -116,7 +127,60 @@ struct Params {
 //   kEpiPlain: bias (+ add terms, activation), fp32 or 16-bit store
 //   kEpiStats: as plain, plus GroupNorm partial sums to p.stats
 //   kEpiFused: GroupNorm + Mish (+ FiLM / residual) applied in the epilogue
-enum EpiMode : int { kEpiPlain = 0, kEpiStats = 1, kEpiFused = 2 };
+//   kEpiConv:  plain fp32, with the causal conv + SiLU of Params::conv_* on
+//              the rows below conv_rows
+enum EpiMode : int { kEpiPlain = 0, kEpiStats = 1, kEpiFused = 2, kEpiConv = 3 };
+
+// kEpiConv rows: the causal conv and SiLU over this warp's EPI_COLS tokens,
+// straight from the accumulator (tbase: the warp's first column), in the
+// reference's order (kernels_scalar.cc:10-27): the bias, then the taps oldest
+// to newest, each one fused multiply-add.  A sequence that began in an
+// earlier column slice of the tile takes its last three inputs from the
+// TMEM columns before this slice (the accumulator is released only after
+// every epilogue warp is done with it).
+static __device__ __noinline__ void epi_conv(const Params& p, uint32_t tbase, int m, bool m_ok, int tok0, int lim) {
+  constexpr int CH = 16;
+  const int mm = m_ok ? m : 0;
+  const float4 w = *reinterpret_cast<const float4*>(p.conv_w + static_cast<long long>(mm) * 4);
+  const float cb = p.conv_b[mm];
+  const int smask = p.conv_seq - 1;
+  float x1 = 0.0f, x2 = 0.0f, x3 = 0.0f;  // inputs of steps t - 1, t - 2, t - 3
+  const int r = tok0 & smask;              // the same for the whole warp
+  if (r != 0) {
+    float pv[CH];
+    tmem_ld16(tbase - CH, pv);
+    x1 = pv[CH - 1];
+    x2 = r >= 2 ? pv[CH - 2] : 0.0f;
+    x3 = r >= 3 ? pv[CH - 3] : 0.0f;
+  }
+  const long long ld = p.conv_ld;
+  float* ou = p.conv_u + static_cast<long long>(tok0) * ld + m;
+  __half* oh = p.conv_u16 + static_cast<long long>(tok0) * ld + m;
+#pragma unroll 1
+  for (int c = 0; c < EPI_COLS; c += CH) {
+    float v[CH];
+    tmem_ld16(tbase + c, v);
+#pragma unroll
+    for (int j = 0; j < CH; ++j) {
+      if (((tok0 + c + j) & smask) == 0) x1 = x2 = x3 = 0.0f;
+      float a = fmaf(w.x, x3, cb);
+      a = fmaf(w.y, x2, a);
+      a = fmaf(w.z, x1, a);
+      a = fmaf(w.w, v[j], a);
+      x3 = x2;
+      x2 = x1;
+      x1 = v[j];
+      v[j] = silu_f(a);
+    }
+    const long long oc = static_cast<long long>(c) * ld;
+#pragma unroll
+    for (int j = 0; j < CH; ++j)
+      if (c + j < lim) {
+        ou[oc + j * ld] = v[j];
+        oh[oc + j * ld] = to_half_sat(v[j]);
+      }
+  }
+}
 
 // PAIR (fused mode, GroupNorm groups of 256 channels): the kernel runs as
 // clusters of 2 CTAs.  Both CTAs of a cluster walk the same sequence of tile
@@ -512,7 +576,7 @@ static __global__ void __launch_bounds__(THREADS, 1)
     // token, so column c of this warp lives at element o0 + c * out_cs.  Each
     // TMEM load brings CH columns; all per-element work is branch-free and
     // the only branches are per chunk and uniform across the warp.
-    constexpr bool kStats = MODE != kEpiPlain;
+    constexpr bool kStats = MODE == kEpiStats || MODE == kEpiFused;
     constexpr int CH = 16;
     const int q = warp & 3;                    // TMEM lane quadrant this warp may access
     const int part = (warp - 2) >> 2;          // which COLS-wide slice of the tile's columns
@@ -562,10 +626,16 @@ static __global__ void __launch_bounds__(THREADS, 1)
       const int sample0 = n_blk * p.tile_samples;
       const uint32_t tbase = tmem_base + lane_base + acc * BN + col0;
 
+      bool conv_rows = false;
+      if constexpr (MODE == kEpiConv) {
+        conv_rows = m_blk * BM < p.conv_rows;  // whole tiles: conv_rows % BM == 0
+        if (conv_rows) epi_conv(p, tbase, m, m_ok, tok0, lim);
+      }
+
       // pass 1: GroupNorm partial sums (stats / fused) and the plain store
       float s1 = 0.0f, s2 = 0.0f;
 #pragma unroll 1
-      for (int c = 0; c < EPI_COLS; c += CH) {
+      for (int c = 0; c < (conv_rows ? 0 : EPI_COLS); c += CH) {
         float v[CH];
         tmem_ld16(tbase + c, v);
         if constexpr (kStats) {

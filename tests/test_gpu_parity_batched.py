@@ -10,7 +10,13 @@ compiled reference core (oracle/_ref) on sampled rows of the same inputs.
   - 2 sequences of 13 tokens reach the many-sequence scan at a small batch,
     because 13 steps do not split into the chunked scan's 8-step chunks (one
     ragged tile), and 3 sequences of 37 tokens run it over two whole tiles
-    and a ragged third.
+    and a ragged third;
+  - in bf16 mode the tensor-path in-projection takes the causal conv into its
+    epilogue when the sequence length divides its 256-token blocks: 64 x 128
+    and 640 x 16 run that way, 2 x 256 has a whole block per sequence (three
+    of the four column slices of every tile continue a sequence begun in the
+    slice before), and 4 x 37 (148 tokens: tensor path, 37 does not divide
+    the block) keeps the separate conv kernel.
   Each in fp32 mode (tensor cores on fp16 hi / lo splits, bar 1e-3) and in bf16
   mode on bf16-rounded weights (bar 2e-2), per-row against the reference's
   `Mamba::forward` (src/core/models/mamba/mamba.cc:232-315; scan at
@@ -57,6 +63,8 @@ CASES = [  # (batch, seq_len, rows compared with the reference)
     (640, 16, (0, 1, 318, 638, 639)),
     (2, 13, (0, 1)),
     (3, 37, (0, 2)),
+    (2, 256, (0, 1)),
+    (4, 37, (0, 3)),
 ]
 
 
