@@ -380,7 +380,9 @@ __global__ void __launch_bounds__(256) scan_kernel(const float* dbl, int wd, con
 // which carries the other 14 state exponentials and the 4 of softplus and
 // SiLU per (token, channel).  The fp32 mode (!FAST) evaluates scan_kernel's
 // expressions in scan_kernel's order.  y (fp32) is written only when given:
-// the tensor-core out-projection reads the 16-bit copy.  A full-barrier wait
+// the tensor-core out-projection reads the 16-bit copy.  U16 (bf16 mode with
+// the conv in the in-projection's epilogue) stages u from its fp16 copy, the
+// x-projection's operand, so the fp32 u is never written.  A full-barrier wait
 // that times out records kErrStageTimeout and ends every warp's loop; the
 // CTA waits (bounded) for the copies it issued and returns.
 constexpr int kScanTile = 16;
@@ -398,13 +400,14 @@ __host__ __device__ constexpr int scan_smem_floats(int ds, int dr) {
   return 2 * scan_stage_floats(ds, dr) + kScanTile * kScanThreads;
 }
 
-template <int DS, int DR, bool FAST, int POLY>
+template <int DS, int DR, bool FAST, int POLY, bool U16 = false>
 __global__ void __launch_bounds__(kScanThreads, 2)
-    scan_staged_kernel(const float* __restrict__ dbl, const float* __restrict__ u, const float* __restrict__ xz, int L,
+    scan_staged_kernel(const float* __restrict__ dbl, const void* __restrict__ u, const float* __restrict__ xz, int L,
                        int di, const float* __restrict__ dt_w, const float* __restrict__ dt_b,
                        const float* __restrict__ a_neg, const float* __restrict__ dsk, float* __restrict__ y,
                        __half* __restrict__ y_bf, int split, int* err) {
   static_assert(DR % 4 == 0 && DS % 4 == 0 && POLY >= 0 && POLY <= DS / 2, "rows are read as float4");
+  static_assert(!U16 || FAST, "the fp16 u belongs to the bf16 mode");
   constexpr int WD = DR + 2 * DS;
   constexpr int kStage = scan_stage_floats(DS, DR);
   extern __shared__ __align__(128) float sst[];
@@ -426,7 +429,8 @@ __global__ void __launch_bounds__(kScanThreads, 2)
   }
   __syncthreads();
   // one warp: tile `tile` into stage tile % 2 (lane 0 the dbl rows, lane j
-  // the u and z row slices of step j; 16-byte aligned since di % 4 == 0)
+  // the u and z row slices of step j; 16-byte aligned since di % 4 == 0, and
+  // di % 8 == 0 for the fp16 u)
   auto request = [&](int tile) {
     const int s = tile & 1, t0 = tile * kScanTile, n = min(kScanTile, L - t0);
     float* sd = sst + s * kStage;
@@ -434,13 +438,18 @@ __global__ void __launch_bounds__(kScanThreads, 2)
     float* sz = su + kScanTile * kScanThreads;
     if (lane == 0) {
       last_req[s] = tile;
-      mbar_arrive_expect_tx(&full[s], static_cast<uint32_t>(n * WD * 4 + 2 * n * nch * 4));
+      mbar_arrive_expect_tx(&full[s], static_cast<uint32_t>(n * WD * 4 + n * nch * (U16 ? 6 : 8)));
     }
     __syncwarp();
     if (lane == 0) bulk_load_g2s(sd, dbl + (tok0 + t0) * WD, static_cast<uint32_t>(n * WD * 4), &full[s]);
     if (lane < n) {
       const long long tok = tok0 + t0 + lane;
-      bulk_load_g2s(su + lane * kScanThreads, u + tok * di + c0, static_cast<uint32_t>(nch * 4), &full[s]);
+      if constexpr (U16)
+        bulk_load_g2s(reinterpret_cast<__half*>(su) + lane * kScanThreads,
+                      static_cast<const __half*>(u) + tok * di + c0, static_cast<uint32_t>(nch * 2), &full[s]);
+      else
+        bulk_load_g2s(su + lane * kScanThreads, static_cast<const float*>(u) + tok * di + c0,
+                      static_cast<uint32_t>(nch * 4), &full[s]);
       bulk_load_g2s(sz + lane * kScanThreads, xz + tok * 2 * di + di + c0, static_cast<uint32_t>(nch * 4), &full[s]);
     }
   };
@@ -512,7 +521,9 @@ __global__ void __launch_bounds__(kScanThreads, 2)
 #pragma unroll 2
       for (int j = 0; j < n; ++j) {
         const float4* row4 = reinterpret_cast<const float4*>(sd + j * WD);
-        const float dt = sdt[j * kScanThreads + tid], uv = su[j * kScanThreads + tid];
+        const float dt = sdt[j * kScanThreads + tid];
+        const float uv = U16 ? __half2float(reinterpret_cast<const __half*>(su)[j * kScanThreads + tid])
+                             : su[j * kScanThreads + tid];
         const float gate = sz[j * kScanThreads + tid];
         float out;
         if constexpr (FAST) {
@@ -930,9 +941,11 @@ class Mamba final : public MambaDevice {
 
  private:
   // conv: the layer whose causal conv runs in the epilogue (tensor path,
-  // in-projection; sequences of conv_seq tokens)
+  // in-projection; sequences of conv_seq tokens; u to u_ (fp32, when
+  // conv_u32) and ub_ (fp16))
   bool gemm(const Mat& m, const void* in, int in_ld, long long n_tok, float* out, int out_ld, bool accumulate,
-            bool tc, cudaStream_t st, std::string& err, const Layer* conv = nullptr, int conv_seq = 0);
+            bool tc, cudaStream_t st, std::string& err, const Layer* conv = nullptr, int conv_seq = 0,
+            bool conv_u32 = true);
   bool run_layers(long long n_tok, int B, int L, bool tc, cudaStream_t st, std::string& err);
   // one decode token: the token from pinned_[0], the normed output to pinned_ + 1
   bool record_step(cudaStream_t st, std::string& err);
@@ -1140,6 +1153,9 @@ bool Mamba::load(const TensorTable& t, std::string& err) {
                         reinterpret_cast<const void*>(scan_kernel<4, 4, true>),
                         reinterpret_cast<const void*>(scan_staged_kernel<16, 32, false, 0>),
                         reinterpret_cast<const void*>(scan_staged_kernel<16, 32, true, kScanPolyPairs>),
+                        reinterpret_cast<const void*>(scan_staged_kernel<16, 32, true, kScanPolyPairs, true>),
+                        reinterpret_cast<const void*>(scan_staged_kernel<8, 4, true, 0, true>),
+                        reinterpret_cast<const void*>(scan_staged_kernel<4, 4, true, 0, true>),
                         reinterpret_cast<const void*>(scan_staged_kernel<8, 4, false, 0>),
                         reinterpret_cast<const void*>(scan_staged_kernel<8, 4, true, 0>),
                         reinterpret_cast<const void*>(scan_staged_kernel<4, 4, false, 0>),
@@ -1259,7 +1275,7 @@ int Mamba::reserve(std::size_t batch, std::size_t max_len, std::string& err) noe
 }
 
 bool Mamba::gemm(const Mat& m, const void* in, int in_ld, long long n_tok, float* out, int out_ld, bool accumulate,
-                 bool tc, cudaStream_t st, std::string& err, const Layer* conv, int conv_seq) {
+                 bool tc, cudaStream_t st, std::string& err, const Layer* conv, int conv_seq, bool conv_u32) {
   if (tc) {
     TcLaunch l;
     l.fp16 = true;
@@ -1289,7 +1305,7 @@ bool Mamba::gemm(const Mat& m, const void* in, int in_ld, long long n_tok, float
       // and the fp16 operand of the x-projection), z half -> out
       l.conv_w = conv->conv_w;
       l.conv_b = conv->conv_b;
-      l.conv_u = u_;
+      l.conv_u = conv_u32 ? u_ : nullptr;
       l.conv_u16 = ub_;
       l.conv_rows = static_cast<int>(cfg_.d_inner);
       l.conv_seq = conv_seq;
@@ -1343,13 +1359,29 @@ bool Mamba::run_layers(long long n_tok, int B, int L, bool tc, cudaStream_t st, 
   // bf16 tensor path with sequences that tile the GEMM's token blocks: the
   // causal conv runs in the in-projection's epilogue, and only z goes to xz
   const bool conv_fused = tc && split == 0 && dc == 4 && di % tc::BM == 0 && L <= tc::BN && tc::BN % L == 0;
+  const dim3 grid(static_cast<unsigned>((di + 255) / 256), static_cast<unsigned>(B));
+  const std::size_t smem = static_cast<std::size_t>(L) * wd * 4;
+  // few sequences: chunks of the sequence in parallel (when L splits into them)
+  const dim3 cgrid(static_cast<unsigned>((di + kScanCh - 1) / kScanCh), static_cast<unsigned>(B));
+  const unsigned cthreads = static_cast<unsigned>(kScanCh * (L / kScanChunk));
+  const std::size_t csmem =
+      (static_cast<std::size_t>(L) * wd + 2 * static_cast<std::size_t>(L / kScanChunk) * kScanCh * 2) * 4;
+  const bool chunked = L % kScanChunk == 0 && L / kScanChunk <= 64 && static_cast<long long>(B) * di < 32768 &&
+                       csmem <= 200 * 1024 && wd % 4 == 0;
+  // many sequences: the staged kernel (bulk copies need di % 4 == 0); the
+  // fp32 y is read only by the CUDA-core out-projection
+  const bool staged = di % 4 == 0;
+  const dim3 sgrid(static_cast<unsigned>((di + kScanThreads - 1) / kScanThreads), static_cast<unsigned>(B));
+  // with the conv fused, the staged scan reads u from its fp16 copy and the
+  // fp32 u is not written
+  const bool u16 = conv_fused && !chunked && staged && di % 8 == 0;
   for (const Layer& Ly : layers_) {
     rmsnorm_kernel<<<static_cast<unsigned>((n_tok * 32 + 255) / 256), 256, 0, st>>>(hidden_, Ly.norm,
                                                                                       static_cast<int>(n_tok), dm,
                                                                                       tc ? nullptr : normed,
                                                                                       tc ? nb_ : nullptr, split);
     if (conv_fused) {
-      if (!gemm(Ly.in_proj, nb_, dm, n_tok, xz_, 2 * di, false, tc, st, err, &Ly, L)) return false;
+      if (!gemm(Ly.in_proj, nb_, dm, n_tok, xz_, 2 * di, false, tc, st, err, &Ly, L, !u16)) return false;
     } else {
       if (!gemm(Ly.in_proj, tc ? static_cast<const void*>(nb_) : normed, dm, n_tok, xz_, 2 * di, false, tc, st, err))
         return false;
@@ -1365,41 +1397,37 @@ bool Mamba::run_layers(long long n_tok, int B, int L, bool tc, cudaStream_t st, 
     }
     if (!gemm(Ly.x_proj, tc ? static_cast<const void*>(ub_) : u_, di, n_tok, dbl_, wd, false, tc, st, err))
       return false;
-    const dim3 grid(static_cast<unsigned>((di + 255) / 256), static_cast<unsigned>(B));
-    const std::size_t smem = static_cast<std::size_t>(L) * wd * 4;
-    // few sequences: chunks of the sequence in parallel (when L splits into them)
-    const dim3 cgrid(static_cast<unsigned>((di + kScanCh - 1) / kScanCh), static_cast<unsigned>(B));
-    const unsigned cthreads = static_cast<unsigned>(kScanCh * (L / kScanChunk));
-    const std::size_t csmem =
-        (static_cast<std::size_t>(L) * wd + 2 * static_cast<std::size_t>(L / kScanChunk) * kScanCh * 2) * 4;
-    const bool chunked = L % kScanChunk == 0 && L / kScanChunk <= 64 && static_cast<long long>(B) * di < 32768 &&
-                         csmem <= 200 * 1024 && wd % 4 == 0;
-    // many sequences: the staged kernel (bulk copies need di % 4 == 0); the
-    // fp32 y is read only by the CUDA-core out-projection
-    const bool staged = di % 4 == 0;
-    const dim3 sgrid(static_cast<unsigned>((di + kScanThreads - 1) / kScanThreads), static_cast<unsigned>(B));
-    auto scan = [&](auto kernel, auto ckernel, auto skernel, int sds, int sdr) {
+    auto scan = [&](auto kernel, auto ckernel, auto skernel, auto skernel16, int sds, int sdr) {
       if (chunked)
         ckernel<<<cgrid, cthreads, csmem, st>>>(dbl_, wd, u_, xz_, L, di, Ly.dt_w, Ly.dt_b, Ly.a_neg, Ly.d, nullptr,
                                                 y_, tc ? yb_ : nullptr, split);
       else if (staged)
-        skernel<<<sgrid, kScanThreads, static_cast<std::size_t>(scan_smem_floats(sds, sdr)) * 4, st>>>(dbl_, u_, xz_, L, di, Ly.dt_w, Ly.dt_b, Ly.a_neg, Ly.d, tc ? nullptr : y_,
-                        tc ? yb_ : nullptr, split, ctx_->d_err);
+        (u16 ? skernel16 : skernel)<<<sgrid, kScanThreads, static_cast<std::size_t>(scan_smem_floats(sds, sdr)) * 4,
+                                      st>>>(dbl_, u16 ? static_cast<const void*>(ub_) : u_, xz_, L, di, Ly.dt_w,
+                                            Ly.dt_b, Ly.a_neg, Ly.d, tc ? nullptr : y_, tc ? yb_ : nullptr, split,
+                                            ctx_->d_err);
       else
         kernel<<<grid, 256, smem, st>>>(dbl_, wd, u_, xz_, L, di, Ly.dt_w, Ly.dt_b, Ly.a_neg, Ly.d, nullptr, y_,
                                         tc ? yb_ : nullptr, split);
     };
+    // (u16 implies the bf16 mode: the fp32 instantiations pass their own
+    // staged kernel twice)
     if (ds == 16 && dr == 32)
       fast ? scan(scan_kernel<16, 32, true>, scan_chunked_kernel<16, 32, true>,
-                  scan_staged_kernel<16, 32, true, kScanPolyPairs>, 16, 32)
+                  scan_staged_kernel<16, 32, true, kScanPolyPairs>, scan_staged_kernel<16, 32, true, kScanPolyPairs, true>,
+                  16, 32)
            : scan(scan_kernel<16, 32, false>, scan_chunked_kernel<16, 32, false>, scan_staged_kernel<16, 32, false, 0>,
-                  16, 32);
+                  scan_staged_kernel<16, 32, false, 0>, 16, 32);
     else if (ds == 4 && dr == 4)
-      fast ? scan(scan_kernel<4, 4, true>, scan_chunked_kernel<4, 4, true>, scan_staged_kernel<4, 4, true, 0>, 4, 4)
-           : scan(scan_kernel<4, 4, false>, scan_chunked_kernel<4, 4, false>, scan_staged_kernel<4, 4, false, 0>, 4, 4);
+      fast ? scan(scan_kernel<4, 4, true>, scan_chunked_kernel<4, 4, true>, scan_staged_kernel<4, 4, true, 0>,
+                  scan_staged_kernel<4, 4, true, 0, true>, 4, 4)
+           : scan(scan_kernel<4, 4, false>, scan_chunked_kernel<4, 4, false>, scan_staged_kernel<4, 4, false, 0>,
+                  scan_staged_kernel<4, 4, false, 0>, 4, 4);
     else if (ds == 8 && dr == 4)
-      fast ? scan(scan_kernel<8, 4, true>, scan_chunked_kernel<8, 4, true>, scan_staged_kernel<8, 4, true, 0>, 8, 4)
-           : scan(scan_kernel<8, 4, false>, scan_chunked_kernel<8, 4, false>, scan_staged_kernel<8, 4, false, 0>, 8, 4);
+      fast ? scan(scan_kernel<8, 4, true>, scan_chunked_kernel<8, 4, true>, scan_staged_kernel<8, 4, true, 0>,
+                  scan_staged_kernel<8, 4, true, 0, true>, 8, 4)
+           : scan(scan_kernel<8, 4, false>, scan_chunked_kernel<8, 4, false>, scan_staged_kernel<8, 4, false, 0>,
+                  scan_staged_kernel<8, 4, false, 0>, 8, 4);
     else {
       err = "no scan instantiation for this (d_state, dt_rank)";
       return false;

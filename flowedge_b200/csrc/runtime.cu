@@ -377,7 +377,7 @@ cudaError_t tc_gemm(const TcLaunch& l, DeviceContext& ctx, cudaStream_t stream, 
   if (l.conv_w != nullptr) {
     if (!l.out_f32 || l.out_accumulate || l.act != tc::kActNone || l.bias != nullptr || l.add_vec != nullptr ||
         l.add_tok != nullptr || l.stats != nullptr || l.gn_fuse || l.L != 1 || l.conv_b == nullptr ||
-        l.conv_u == nullptr || l.conv_u16 == nullptr || l.conv_rows % tc::BM != 0 || l.conv_seq < 1 ||
+        l.conv_u16 == nullptr || l.conv_rows % tc::BM != 0 || l.conv_seq < 1 ||
         l.conv_seq > tc::BN || tc::BN % l.conv_seq != 0 || l.n_samples % l.conv_seq != 0 ||
         static_cast<long long>(l.conv_ld) * tc::BN >= (1LL << 31)) {
       err = "tc_gemm: the conv epilogue needs a plain fp32 GEMM over whole sequences that tile the token blocks";

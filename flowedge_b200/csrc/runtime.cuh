@@ -120,7 +120,8 @@ struct TcLaunch {
   const void* res16 = nullptr;
   float* out_twin = nullptr;
   // causal conv + SiLU epilogue on the rows < conv_rows (see
-  // tc::Params::conv_w): plain fp32 GEMM, L = 1, sequences of conv_seq tokens
+  // tc::Params::conv_w): plain fp32 GEMM, L = 1, sequences of conv_seq
+  // tokens; conv_u may be null (only the fp16 copy is stored)
   const float* conv_w = nullptr;
   const float* conv_b = nullptr;
   float* conv_u = nullptr;

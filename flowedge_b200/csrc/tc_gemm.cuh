@@ -111,8 +111,9 @@ struct Params {
   // causal depthwise conv of 4 taps over each sequence's tokens, then SiLU,
   // for the rows < conv_rows (kEpiConv; the Mamba in-projection's x half):
   // u = SiLU(conv_b[m] + sum_j conv_w[m][j] y[t - 3 + j]), taps before the
-  // sequence's first token zero, stored fp32 to conv_u and fp16 to conv_u16
-  // at element token * conv_ld + m; rows >= conv_rows take the plain store.
+  // sequence's first token zero, stored fp32 to conv_u (when not null) and
+  // fp16 to conv_u16 at element token * conv_ld + m; rows >= conv_rows take
+  // the plain store.
   // Sequences of conv_seq tokens (a power of two dividing BN) tile the tokens.
   const float* conv_w;     // [conv_rows][4]
   const float* conv_b;
@@ -154,7 +155,7 @@ static __device__ __noinline__ void epi_conv(const Params& p, uint32_t tbase, in
     x3 = r >= 3 ? pv[CH - 3] : 0.0f;
   }
   const long long ld = p.conv_ld;
-  float* ou = p.conv_u + static_cast<long long>(tok0) * ld + m;
+  float* ou = p.conv_u != nullptr ? p.conv_u + static_cast<long long>(tok0) * ld + m : nullptr;
   __half* oh = p.conv_u16 + static_cast<long long>(tok0) * ld + m;
 #pragma unroll 1
   for (int c = 0; c < EPI_COLS; c += CH) {
@@ -176,7 +177,7 @@ static __device__ __noinline__ void epi_conv(const Params& p, uint32_t tbase, in
 #pragma unroll
     for (int j = 0; j < CH; ++j)
       if (c + j < lim) {
-        ou[oc + j * ld] = v[j];
+        if (ou != nullptr) ou[oc + j * ld] = v[j];
         oh[oc + j * ld] = to_half_sat(v[j]);
       }
   }

@@ -16,7 +16,9 @@ compiled reference core (oracle/_ref) on sampled rows of the same inputs.
     and 640 x 16 run that way, 2 x 256 has a whole block per sequence (three
     of the four column slices of every tile continue a sequence begun in the
     slice before), and 4 x 37 (148 tokens: tensor path, 37 does not divide
-    the block) keeps the separate conv kernel.
+    the block) keeps the separate conv kernel. With the conv fused the
+    many-sequence scan stages u from its fp16 copy (64 x 128, 640 x 16, and
+    600 x 8: one ragged 8-step tile).
   Each in fp32 mode (tensor cores on fp16 hi / lo splits, bar 1e-3) and in bf16
   mode on bf16-rounded weights (bar 2e-2), per-row against the reference's
   `Mamba::forward` (src/core/models/mamba/mamba.cc:232-315; scan at
@@ -65,6 +67,7 @@ CASES = [  # (batch, seq_len, rows compared with the reference)
     (3, 37, (0, 2)),
     (2, 256, (0, 1)),
     (4, 37, (0, 3)),
+    (600, 8, (0, 299, 599)),
 ]
 
 
