@@ -135,7 +135,9 @@ enum EpiMode : int { kEpiPlain = 0, kEpiStats = 1, kEpiFused = 2, kEpiConv = 3 }
 // kEpiConv rows: the causal conv and SiLU over this warp's EPI_COLS tokens,
 // straight from the accumulator (tbase: the warp's first column), in the
 // reference's order (kernels_scalar.cc:10-27): the bias, then the taps oldest
-// to newest, each one fused multiply-add.  A sequence that began in an
+// to newest, each one fused multiply-add; the SiLU with one MUFU operation
+// per element (silu2_fma, ~1e-6 relative, far below the fp16 rounding of the
+// u that the x-projection and the scan read).  A sequence that began in an
 // earlier column slice of the tile takes its last three inputs from the
 // TMEM columns before this slice (the accumulator is released only after
 // every epilogue warp is done with it).
@@ -171,7 +173,13 @@ static __device__ __noinline__ void epi_conv(const Params& p, uint32_t tbase, in
       x3 = x2;
       x2 = x1;
       x1 = v[j];
-      v[j] = silu_f(a);
+      v[j] = a;
+    }
+#pragma unroll
+    for (int j = 0; j < CH; j += 2) {
+      const float2 sj = silu2_fma(make_float2(v[j], v[j + 1]));
+      v[j] = sj.x;
+      v[j + 1] = sj.y;
     }
     const long long oc = static_cast<long long>(c) * ld;
 #pragma unroll
