@@ -18,6 +18,7 @@
 // last, then [ds][di] state).
 #include <algorithm>
 #include <cmath>
+#include <cstdint>
 #include <cstring>
 #include <map>
 #include <tuple>
@@ -90,6 +91,76 @@ __global__ void rmsnorm_kernel(const float* in, const float* w, int rows, int di
     if (out != nullptr) out[static_cast<long long>(row) * dim + i] = v;
     if (out_bf != nullptr) store_act16(out_bf, row, dim, i, v, split);
   }
+}
+
+// rmsnorm_kernel for rows of 128 * NV floats: lane l holds the float4s at
+// columns 4 l + 128 k of its row, all requested before the sum of squares
+// (the per-lane partial sums run over k, then the warp reduction; the same
+// value up to the order of that sum), and the 16-bit copy goes out 4 halves
+// per store.
+template <int NV>
+__global__ void __launch_bounds__(256) rmsnorm_vec_kernel(const float* __restrict__ in, const float* __restrict__ w,
+                                                          int rows, float* __restrict__ out,
+                                                          __half* __restrict__ out_bf, int split) {
+  constexpr int kDim = 128 * NV;
+  const int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  const float4* x = reinterpret_cast<const float4*>(in + static_cast<long long>(row) * kDim) + lane;
+  float4 v[NV];
+#pragma unroll
+  for (int k = 0; k < NV; ++k) v[k] = x[32 * k];
+  float ss = 0.0f;
+#pragma unroll
+  for (int k = 0; k < NV; ++k) {
+    ss = fmaf(v[k].x, v[k].x, ss);
+    ss = fmaf(v[k].y, v[k].y, ss);
+    ss = fmaf(v[k].z, v[k].z, ss);
+    ss = fmaf(v[k].w, v[k].w, ss);
+  }
+  for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+  const float scale = 1.0f / sqrtf((ss / static_cast<float>(kDim)) + 1e-5f);
+#pragma unroll
+  for (int k = 0; k < NV; ++k) {
+    const int c = 4 * (lane + 32 * k);
+    const float4 wk = *reinterpret_cast<const float4*>(w + c);
+    const float4 r = make_float4(v[k].x * scale * wk.x, v[k].y * scale * wk.y, v[k].z * scale * wk.z,
+                                 v[k].w * scale * wk.w);
+    if (out != nullptr) *reinterpret_cast<float4*>(out + static_cast<long long>(row) * kDim + c) = r;
+    if (out_bf != nullptr) {
+      const __half h0 = to_half_sat(r.x), h1 = to_half_sat(r.y), h2 = to_half_sat(r.z), h3 = to_half_sat(r.w);
+      const __half2 p01 = __halves2half2(h0, h1), p23 = __halves2half2(h2, h3);
+      const long long ob = split ? static_cast<long long>(row) * 2 * kDim + c : static_cast<long long>(row) * kDim + c;
+      *reinterpret_cast<uint2*>(out_bf + ob) =
+          make_uint2(*reinterpret_cast<const uint32_t*>(&p01), *reinterpret_cast<const uint32_t*>(&p23));
+      if (split) {
+        const __half2 l01 = __floats2half2_rn(r.x - __half2float(h0), r.y - __half2float(h1));
+        const __half2 l23 = __floats2half2_rn(r.z - __half2float(h2), r.w - __half2float(h3));
+        *reinterpret_cast<uint2*>(out_bf + ob + kDim) =
+            make_uint2(*reinterpret_cast<const uint32_t*>(&l01), *reinterpret_cast<const uint32_t*>(&l23));
+      }
+    }
+  }
+}
+
+// RMSNorm of many rows: the vector kernel for widths 128, 256, 512 and 1024
+// (all pointers 16-byte aligned), else rmsnorm_kernel
+void launch_rmsnorm(const float* in, const float* w, long long rows, int dim, float* out, __half* out_bf, int split,
+                    cudaStream_t st) {
+  const unsigned grid = static_cast<unsigned>((rows * 32 + 255) / 256);
+  const bool al = (reinterpret_cast<std::uintptr_t>(in) | reinterpret_cast<std::uintptr_t>(w) |
+                   reinterpret_cast<std::uintptr_t>(out) | reinterpret_cast<std::uintptr_t>(out_bf)) % 16 == 0;
+  const int r = static_cast<int>(rows);
+  if (al && dim == 512)
+    rmsnorm_vec_kernel<4><<<grid, 256, 0, st>>>(in, w, r, out, out_bf, split);
+  else if (al && dim == 1024)
+    rmsnorm_vec_kernel<8><<<grid, 256, 0, st>>>(in, w, r, out, out_bf, split);
+  else if (al && dim == 256)
+    rmsnorm_vec_kernel<2><<<grid, 256, 0, st>>>(in, w, r, out, out_bf, split);
+  else if (al && dim == 128)
+    rmsnorm_vec_kernel<1><<<grid, 256, 0, st>>>(in, w, r, out, out_bf, split);
+  else
+    rmsnorm_kernel<<<grid, 256, 0, st>>>(in, w, r, dim, out, out_bf, split);
 }
 
 // u[b][t][c] = SiLU(bias[c] + sum_k w[c][k] * x[b][t - (dc-1) + k][c]), x is the
@@ -1376,10 +1447,7 @@ bool Mamba::run_layers(long long n_tok, int B, int L, bool tc, cudaStream_t st, 
   // fp32 u is not written
   const bool u16 = conv_fused && !chunked && staged && di % 8 == 0;
   for (const Layer& Ly : layers_) {
-    rmsnorm_kernel<<<static_cast<unsigned>((n_tok * 32 + 255) / 256), 256, 0, st>>>(hidden_, Ly.norm,
-                                                                                      static_cast<int>(n_tok), dm,
-                                                                                      tc ? nullptr : normed,
-                                                                                      tc ? nb_ : nullptr, split);
+    launch_rmsnorm(hidden_, Ly.norm, n_tok, dm, tc ? nullptr : normed, tc ? nb_ : nullptr, split, st);
     if (conv_fused) {
       if (!gemm(Ly.in_proj, nb_, dm, n_tok, xz_, 2 * di, false, tc, st, err, &Ly, L, !u16)) return false;
     } else {
@@ -1435,9 +1503,7 @@ bool Mamba::run_layers(long long n_tok, int B, int L, bool tc, cudaStream_t st, 
     if (!gemm(Ly.out_proj, tc ? static_cast<const void*>(yb_) : y_, di, n_tok, hidden_, dm, true, tc, st, err))
       return false;
   }
-  rmsnorm_kernel<<<static_cast<unsigned>((n_tok * 32 + 255) / 256), 256, 0, st>>>(hidden_, norm_f_,
-                                                                                    static_cast<int>(n_tok), dm, out_,
-                                                                                    nullptr, 0);
+  launch_rmsnorm(hidden_, norm_f_, n_tok, dm, out_, nullptr, 0, st);
   return cudaGetLastError() == cudaSuccess;
 }
 
