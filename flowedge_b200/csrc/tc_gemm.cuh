@@ -163,17 +163,34 @@ static __device__ __noinline__ void epi_conv(const Params& p, uint32_t tbase, in
   for (int c = 0; c < EPI_COLS; c += CH) {
     float v[CH];
     tmem_ld16(tbase + c, v);
+    // tok0 + c is a multiple of CH: sequences of >= CH tokens begin only at
+    // a chunk's first column, shorter ones anywhere in it
+    if (smask >= CH - 1) {
+      if (((tok0 + c) & smask) == 0) x1 = x2 = x3 = 0.0f;
 #pragma unroll
-    for (int j = 0; j < CH; ++j) {
-      if (((tok0 + c + j) & smask) == 0) x1 = x2 = x3 = 0.0f;
-      float a = fmaf(w.x, x3, cb);
-      a = fmaf(w.y, x2, a);
-      a = fmaf(w.z, x1, a);
-      a = fmaf(w.w, v[j], a);
-      x3 = x2;
-      x2 = x1;
-      x1 = v[j];
-      v[j] = a;
+      for (int j = 0; j < CH; ++j) {
+        float a = fmaf(w.x, x3, cb);
+        a = fmaf(w.y, x2, a);
+        a = fmaf(w.z, x1, a);
+        a = fmaf(w.w, v[j], a);
+        x3 = x2;
+        x2 = x1;
+        x1 = v[j];
+        v[j] = a;
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < CH; ++j) {
+        if (((tok0 + c + j) & smask) == 0) x1 = x2 = x3 = 0.0f;
+        float a = fmaf(w.x, x3, cb);
+        a = fmaf(w.y, x2, a);
+        a = fmaf(w.z, x1, a);
+        a = fmaf(w.w, v[j], a);
+        x3 = x2;
+        x2 = x1;
+        x1 = v[j];
+        v[j] = a;
+      }
     }
 #pragma unroll
     for (int j = 0; j < CH; j += 2) {
